@@ -1,0 +1,14 @@
+"""esolearn_b200: B200-native int8 Llama decode for scry-llm (Slush97/esolearn).
+
+The numeric path lives in libscryb200.so (hand-written sm_100a CUDA behind the
+C ABI in include/sb_api.h); this package is the host-side mirror of the
+reference's model / generation API.
+"""
+from . import _native
+from .llama import (LlamaConfig, LlamaKvCacheHandle, QuantLlamaB200, QWeight, RopeScaling, Rng,
+                    SamplingConfig, argmax_last, generate, matmul_i8_f32, quantize_symmetric, sample_token)
+
+__all__ = [
+    "LlamaConfig", "RopeScaling", "QuantLlamaB200", "LlamaKvCacheHandle", "QWeight", "SamplingConfig", "Rng",
+    "generate", "sample_token", "argmax_last", "matmul_i8_f32", "quantize_symmetric", "_native",
+]

@@ -1,0 +1,30 @@
+// Paged, GQA-aware decode attention over a bf16 (or f32) KV cache.
+#pragma once
+
+#include "sb_common.cuh"
+
+namespace sb {
+
+struct AttnArgs {
+    const float *q = nullptr;  // [B, n_heads*hd], RoPE'd and scaled by 1/sqrt(hd)
+    const void *kc = nullptr;  // [pages][n_kv][page_size][hd]
+    const void *vc = nullptr;
+    int kv_f32 = 0;
+    const int *page_table = nullptr;  // [B, max_pages]
+    int max_pages = 0;
+    const int *len = nullptr;  // [B] device: context length, or position when len_is_pos
+    int len_is_pos = 0;        // context = len[b] + 1 (the position just written)
+    int B = 1, n_heads = 0, n_kv = 0, hd = 0, page_size = 0;
+    int n_splits = 1;   // context splits per (sequence, kv head)
+    int max_chunk = 0;  // upper bound of positions per split (shared-memory sizing)
+    float *out = nullptr;           // [B, n_heads*hd]
+    float *part = nullptr;          // scratch [B][n_heads][n_splits][hd+2]
+    unsigned *counters = nullptr;   // scratch [B][n_kv], zero between launches
+};
+
+// Splits per (sequence, kv head) for a given max context on this device.
+int attn_pick_splits(int B, int n_kv, int max_ctx);
+size_t attn_scratch_floats(int B, int n_heads, int n_splits, int hd);
+int attn_launch(const AttnArgs &a, cudaStream_t st, bool pdl);
+
+}  // namespace sb

@@ -1,0 +1,808 @@
+// The quantized Llama decode engine behind sb_llama_* (sb_api.h).
+//
+// Replaces LlamaModel::forward_with_llama_cache (llama.rs:744-763) and the
+// generate() loop (generate.rs:51-89) for int8 weights.  One decode step of
+// `M` sequences is 5 kernels per layer plus embedding, lm_head and argmax:
+//
+//   embed -> [ QKV GEMV (input RMSNorm fused; RoPE, q scale, K/V page write
+//              in the epilogue) -> paged GQA attention -> O GEMV (+residual)
+//              -> gate/up GEMV (post-attention RMSNorm fused; SwiGLU in the
+//              epilogue) -> down GEMV (+residual) ] x L
+//   -> lm_head GEMV (final RMSNorm fused; logits + per-tile argmax)
+//   -> argmax (token bookkeeping on device)
+//
+// The step reads every position-dependent value (token, position, page
+// table) from device memory, so it is captured once per batch size as a
+// CUDA graph and replayed; consecutive kernels use programmatic dependent
+// launch so the next GEMV starts streaming its weights while the previous
+// kernel drains.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "attention.cuh"
+#include "misc.cuh"
+#include "qgemv.cuh"
+
+namespace sb {
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+
+}  // namespace sb
+
+using namespace sb;
+
+struct sb_llama {
+    sb_llama_config cfg{};
+    int dev = 0;
+    int h = 0, F = 0, V = 0, L = 0, nh = 0, nkv = 0, hd = 0, q_dim = 0, kv_dim = 0, qkv_dim = 0;
+    int B = 1, P = 64, pps = 0;
+    cudaStream_t st = nullptr;
+    std::vector<void *> allocs;
+
+    // weights
+    struct Layer {
+        QWeightDesc qkv, o, gu, down;
+        bool has[5] = {false, false, false, false, false};
+    };
+    std::vector<Layer> layers;
+    QWeightDesc lm;
+    bool has_lm = false;
+    float *embed = nullptr, *norm_in = nullptr, *norm_post = nullptr, *norm_final = nullptr;
+    int8_t *stage = nullptr;  // gate staging for gate/up pairing
+    size_t stage_bytes = 0;
+    int staged_gate_layer = -1;
+    float staged_gate_scale = 0.0f;
+    unsigned *amax = nullptr;
+    float *scale_dev = nullptr;
+
+    // KV cache
+    void *kc = nullptr, *vc = nullptr;
+    size_t layer_kv_elems = 0;
+    int kv_f32 = 0;
+    int *page_table = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+
+    // activations
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *cand_val = nullptr;
+    int *cand_idx = nullptr;
+    float *att_part = nullptr;
+    unsigned *att_cnt = nullptr;
+    int att_splits = 1, att_chunk = 1;
+
+    // sequence state
+    SeqState seq;
+    int *d_tok = nullptr, *d_pos = nullptr, *d_prompt = nullptr, *d_plen = nullptr, *d_out = nullptr,
+        *d_ngen = nullptr, *d_last = nullptr;
+    int active = 0;  // batch of the current begin()
+    int steps = 0;   // steps queued since begin()
+
+    // graphs per batch size
+    std::vector<cudaGraphExec_t> graphs;
+    bool trace = false;
+    float *trace_buf = nullptr;
+    int trace_batch = 0;
+};
+
+namespace {
+
+int dalloc(sb_llama *m, void **p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(SB_ERR_OOM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    }
+    m->allocs.push_back(*p);
+    SB_CUDA_TRY(cudaMemsetAsync(*p, 0, bytes, m->st));
+    return SB_OK;
+}
+
+template <typename T>
+int dalloc_t(sb_llama *m, T **p, size_t count) {
+    return dalloc(m, reinterpret_cast<void **>(p), count * sizeof(T));
+}
+
+int make_qweight(sb_llama *m, QWeightDesc &d, int K, int N, int min_tn) {
+    d.K = K;
+    d.N = N;
+    d.KS = ceil_div(K, 16);
+    d.TN = qgemv_pick_tn(N, K, min_tn);
+    d.ntiles = ceil_div(N, d.TN);
+    d.group = 0;
+    void *p = nullptr;
+    SB_TRY(dalloc(m, &p, qweight_bytes(K, N, d.TN)));
+    d.w = reinterpret_cast<const uint4 *>(p);
+    return SB_OK;
+}
+
+void host_rope_tables(const sb_llama_config &c, int hd, std::vector<float> &cs, std::vector<float> &sn) {
+    // compute_rope_freqs (llama.rs:1035-1067) in f64, cast to f32 (llama.rs:621),
+    // then cos/sin of pos * f64(freq) in f64 rounded to f32 (cpu.rs:650-653).
+    const int half = hd / 2;
+    std::vector<double> fr(half);
+    const double th = (double)c.rope_theta;
+    for (int i = 0; i < half; i++) fr[i] = 1.0 / std::pow(th, 2.0 * (double)i / (double)hd);
+    if (c.has_rope_scaling) {
+        const double factor = c.rope_scaling[0], low = c.rope_scaling[1], high = c.rope_scaling[2],
+                     old_ctx = c.rope_scaling[3];
+        const double low_wl = old_ctx / low, high_wl = old_ctx / high;
+        for (int i = 0; i < half; i++) {
+            const double wl = 2.0 * 3.14159265358979323846 / fr[i];
+            double sf;
+            if (wl < high_wl) sf = 1.0;
+            else if (wl > low_wl) sf = factor;
+            else {
+                const double smooth = (old_ctx / wl - low) / (high - low);
+                sf = 1.0 / ((1.0 - smooth) / factor + smooth);
+            }
+            fr[i] /= sf;
+        }
+    }
+    cs.resize((size_t)c.max_seq_len * half);
+    sn.resize((size_t)c.max_seq_len * half);
+    for (int p = 0; p < c.max_seq_len; p++)
+        for (int i = 0; i < half; i++) {
+            const double angle = (double)p * (double)(float)fr[i];
+            cs[(size_t)p * half + i] = (float)std::cos(angle);
+            sn[(size_t)p * half + i] = (float)std::sin(angle);
+        }
+}
+
+QGemvArgs gemv_common(const QWeightDesc &w, int M, const void *x, int ldx) {
+    QGemvArgs a;
+    a.w = w;
+    a.M = M;
+    a.x = x;
+    a.ldx = ldx;
+    return a;
+}
+
+// Per-kernel event timing of an eager step (sb_llama_profile_step).
+struct StepProfiler {
+    std::vector<cudaEvent_t> ev;  // pairs
+    std::vector<int> cls;         // 0 gemv, 1 attention, 2 other
+    cudaStream_t st = nullptr;
+    int begin(int c) {
+        cudaEvent_t a, b;
+        SB_CUDA_TRY(cudaEventCreate(&a));
+        SB_CUDA_TRY(cudaEventCreate(&b));
+        ev.push_back(a);
+        ev.push_back(b);
+        cls.push_back(c);
+        SB_CUDA_TRY(cudaEventRecord(a, st));
+        return SB_OK;
+    }
+    int end() {
+        SB_CUDA_TRY(cudaEventRecord(ev.back(), st));
+        return SB_OK;
+    }
+    ~StepProfiler() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+};
+
+#define SB_PROF(p, c, expr)                \
+    do {                                   \
+        if (p) SB_TRY((p)->begin(c));      \
+        SB_TRY(expr);                      \
+        if (p) SB_TRY((p)->end());         \
+    } while (0)
+
+// Enqueue one decode step for M sequences on st.
+int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, StepProfiler *prof = nullptr) {
+    SB_PROF(prof, 2, embed_launch(m->embed, m->h, m->V, m->seq, M, m->x, st, pdl));
+    for (int l = 0; l < m->L; l++) {
+        const sb_llama::Layer &ly = m->layers[l];
+        const size_t kvoff = (size_t)l * m->layer_kv_elems * (m->kv_f32 ? 4 : 2);
+        {
+            QGemvArgs a = gemv_common(ly.qkv, M, m->x, m->h);
+            a.norm_w = m->norm_in + (size_t)l * m->h;
+            a.eps = m->cfg.rms_norm_eps;
+            a.q_out = m->q;
+            a.q_dim = m->q_dim;
+            a.kv_dim = m->kv_dim;
+            a.hd = m->hd;
+            a.n_kv = m->nkv;
+            a.kcache = (char *)m->kc + kvoff;
+            a.vcache = (char *)m->vc + kvoff;
+            a.kv_f32 = m->kv_f32;
+            a.page_size = m->P;
+            a.max_pages = m->pps;
+            a.page_table = m->page_table;
+            a.pos = m->d_pos;
+            a.max_pos = m->cfg.max_seq_len;
+            a.rope_cos = m->rope_cos;
+            a.rope_sin = m->rope_sin;
+            a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
+            SB_PROF(prof, 0, qgemv_launch(QEPI_QKV, a, st, pdl));
+        }
+        {
+            AttnArgs a;
+            a.q = m->q;
+            a.kc = (char *)m->kc + kvoff;
+            a.vc = (char *)m->vc + kvoff;
+            a.kv_f32 = m->kv_f32;
+            a.page_table = m->page_table;
+            a.max_pages = m->pps;
+            a.len = m->d_pos;
+            a.len_is_pos = 1;
+            a.B = M;
+            a.n_heads = m->nh;
+            a.n_kv = m->nkv;
+            a.hd = m->hd;
+            a.page_size = m->P;
+            a.n_splits = m->att_splits;
+            a.max_chunk = m->att_chunk;
+            a.out = m->attn;
+            a.part = m->att_part;
+            a.counters = m->att_cnt;
+            SB_PROF(prof, 1, attn_launch(a, st, pdl));
+        }
+        {
+            QGemvArgs a = gemv_common(ly.o, M, m->attn, m->q_dim);
+            a.out = m->x;
+            a.ldo = m->h;
+            SB_PROF(prof, 0, qgemv_launch(QEPI_RESID, a, st, pdl));
+        }
+        {
+            QGemvArgs a = gemv_common(ly.gu, M, m->x, m->h);
+            a.norm_w = m->norm_post + (size_t)l * m->h;
+            a.eps = m->cfg.rms_norm_eps;
+            a.out = m->act;
+            a.ldo = m->F;
+            a.F = m->F;
+            SB_PROF(prof, 0, qgemv_launch(QEPI_SWIGLU, a, st, pdl));
+        }
+        {
+            QGemvArgs a = gemv_common(ly.down, M, m->act, m->F);
+            a.out = m->x;
+            a.ldo = m->h;
+            SB_PROF(prof, 0, qgemv_launch(QEPI_RESID, a, st, pdl));
+        }
+        if (trace)
+            SB_CUDA_TRY(cudaMemcpyAsync(m->trace_buf + (size_t)l * M * m->h, m->x, sizeof(float) * M * m->h,
+                                        cudaMemcpyDeviceToDevice, st));
+    }
+    {
+        QGemvArgs a = gemv_common(m->lm, M, m->x, m->h);
+        a.norm_w = m->norm_final;
+        a.eps = m->cfg.rms_norm_eps;
+        a.out = m->logits;
+        a.ldo = m->V;
+        a.cand_val = m->cand_val;
+        a.cand_idx = m->cand_idx;
+        SB_PROF(prof, 0, qgemv_launch(QEPI_LOGITS, a, st, pdl));
+    }
+    SB_PROF(prof, 2, argmax_step_launch(m->cand_val, m->cand_idx, m->lm.ntiles, m->seq, M, st, pdl));
+    return SB_OK;
+}
+
+int check_ready(sb_llama *m) {
+    for (int l = 0; l < m->L; l++)
+        for (int s = 0; s < 5; s++)
+            SB_CHECK(m->layers[l].has[s], SB_ERR_STATE, "weight (layer %d, slot %d) not loaded", l, s);
+    SB_CHECK(m->has_lm, SB_ERR_STATE, "lm_head not loaded");
+    return SB_OK;
+}
+
+int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const int32_t *plen);
+
+int get_graph(sb_llama *m, int M, cudaGraphExec_t *out) {
+    if (m->graphs[M]) {
+        *out = m->graphs[M];
+        return SB_OK;
+    }
+    // Warm up once outside capture (sets kernel attributes, loads modules)
+    // from a valid state; callers set their own state afterwards.
+    std::vector<int32_t> zero(M, 0);
+    SB_TRY(set_state(m, M, zero.data(), zero.data(), zero.data()));
+    SB_TRY(enqueue_step(m, M, m->st, true, false));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    cudaGraph_t g = nullptr;
+    SB_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, M, m->st, true, false);
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc != SB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    SB_CUDA_TRY(e);
+    cudaGraphExec_t ge = nullptr;
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    SB_CUDA_TRY(e);
+    m->graphs[M] = ge;
+    *out = ge;
+    return SB_OK;
+}
+
+// Put sequences 0..M-1 at the given start state (host arrays).
+int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const int32_t *plen) {
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, tok, sizeof(int) * M, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_pos, pos, sizeof(int) * M, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_plen, plen, sizeof(int) * M, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaMemsetAsync(m->d_ngen, 0, sizeof(int) * m->B, m->st));
+    return SB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
+    SB_CHECK(cfg && out, SB_ERR_ARG, "sb_llama_create: null argument");
+    const sb_llama_config &c = *cfg;
+    SB_CHECK(c.hidden_size > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.n_layers > 0 && c.vocab_size > 0 &&
+                 c.intermediate_size > 0 && c.max_seq_len > 0,
+             SB_ERR_SHAPE, "sb_llama_create: non-positive dimension");
+    SB_CHECK(c.hidden_size % c.n_heads == 0 && c.n_heads % c.n_kv_heads == 0, SB_ERR_SHAPE,
+             "sb_llama_create: hidden %% heads or heads %% kv_heads != 0");
+    SB_CHECK(c.max_batch >= 1 && c.max_batch <= QG_MAX_M, SB_ERR_UNSUPPORTED,
+             "sb_llama_create: max_batch %d outside 1..%d", c.max_batch, QG_MAX_M);
+    const int hd = c.hidden_size / c.n_heads;
+    SB_CHECK(hd == 64 || hd == 128, SB_ERR_UNSUPPORTED, "sb_llama_create: head_dim %d not in {64,128}", hd);
+
+    sb_llama *m = new sb_llama();
+    m->cfg = c;
+    cudaGetDevice(&m->dev);
+    m->h = c.hidden_size;
+    m->F = c.intermediate_size;
+    m->V = c.vocab_size;
+    m->L = c.n_layers;
+    m->nh = c.n_heads;
+    m->nkv = c.n_kv_heads;
+    m->hd = hd;
+    m->q_dim = m->nh * hd;
+    m->kv_dim = m->nkv * hd;
+    m->qkv_dim = m->q_dim + 2 * m->kv_dim;
+    m->B = c.max_batch;
+    m->P = c.page_size > 0 ? c.page_size : 64;
+    m->pps = ceil_div(c.max_seq_len, m->P);
+    m->kv_f32 = c.kv_dtype == SB_KV_F32;
+    m->graphs.assign(m->B + 1, nullptr);
+    auto fail = [&](int rc) {
+        sb_llama_destroy(m);
+        return rc;
+    };
+    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_error(SB_ERR_CUDA, "cudaStreamCreate failed"));
+
+    int rc = SB_OK;
+    m->layers.resize(m->L);
+    const int gu_cols = ceil_div(m->F, 16) * 32;  // gate/up interleaved in blocks of 16
+    for (int l = 0; l < m->L && rc == SB_OK; l++) {
+        sb_llama::Layer &ly = m->layers[l];
+        if ((rc = make_qweight(m, ly.qkv, m->h, m->qkv_dim, 16)) != SB_OK) break;
+        if ((rc = make_qweight(m, ly.o, m->q_dim, m->h, 16)) != SB_OK) break;
+        if ((rc = make_qweight(m, ly.gu, m->h, gu_cols, 32)) != SB_OK) break;
+        if ((rc = make_qweight(m, ly.down, m->F, m->h, 16)) != SB_OK) break;
+    }
+    if (rc == SB_OK) rc = make_qweight(m, m->lm, m->h, m->V, 16);
+    if (rc == SB_OK) rc = dalloc_t(m, &m->embed, (size_t)m->V * m->h);
+    if (rc == SB_OK) rc = dalloc_t(m, &m->norm_in, (size_t)m->L * m->h);
+    if (rc == SB_OK) rc = dalloc_t(m, &m->norm_post, (size_t)m->L * m->h);
+    if (rc == SB_OK) rc = dalloc_t(m, &m->norm_final, (size_t)m->h);
+    if (rc != SB_OK) return fail(rc);
+    {
+        // RMSNorm::new initialises weights to 1.0 (rmsnorm.rs:17-22).
+        std::vector<float> ones((size_t)m->L * m->h, 1.0f);
+        cudaMemcpyAsync(m->norm_in, ones.data(), sizeof(float) * ones.size(), cudaMemcpyHostToDevice, m->st);
+        cudaMemcpyAsync(m->norm_post, ones.data(), sizeof(float) * ones.size(), cudaMemcpyHostToDevice, m->st);
+        cudaMemcpyAsync(m->norm_final, ones.data(), sizeof(float) * m->h, cudaMemcpyHostToDevice, m->st);
+        cudaStreamSynchronize(m->st);
+    }
+    // staging for gate/up pairing and for on-device generation
+    m->stage_bytes = std::max<size_t>((size_t)2 * m->h * m->F, (size_t)m->V * m->h);
+    m->stage_bytes = std::max<size_t>(m->stage_bytes, (size_t)m->h * m->qkv_dim);
+    if ((rc = dalloc(m, (void **)&m->stage, m->stage_bytes)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->amax, 4)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->scale_dev, 4)) != SB_OK) return fail(rc);
+
+    // KV cache: pages [B*pps][n_kv][P][hd] per layer; sequence b owns pages b*pps...
+    m->layer_kv_elems = (size_t)m->B * m->pps * m->nkv * m->P * m->hd;
+    const size_t esz = m->kv_f32 ? 4 : 2;
+    if ((rc = dalloc(m, &m->kc, m->layer_kv_elems * esz * m->L)) != SB_OK) return fail(rc);
+    if ((rc = dalloc(m, &m->vc, m->layer_kv_elems * esz * m->L)) != SB_OK) return fail(rc);
+    {
+        std::vector<int> pt((size_t)m->B * m->pps);
+        for (int b = 0; b < m->B; b++)
+            for (int i = 0; i < m->pps; i++) pt[(size_t)b * m->pps + i] = b * m->pps + i;
+        if ((rc = dalloc_t(m, &m->page_table, pt.size())) != SB_OK) return fail(rc);
+        cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->st);
+        std::vector<float> cs, sn;
+        host_rope_tables(c, hd, cs, sn);
+        if ((rc = dalloc_t(m, &m->rope_cos, cs.size())) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->rope_sin, sn.size())) != SB_OK) return fail(rc);
+        cudaMemcpyAsync(m->rope_cos, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice, m->st);
+        cudaMemcpyAsync(m->rope_sin, sn.data(), sizeof(float) * sn.size(), cudaMemcpyHostToDevice, m->st);
+        cudaStreamSynchronize(m->st);
+    }
+    // activations
+    const int B = m->B;
+    if ((rc = dalloc_t(m, &m->x, (size_t)B * m->h)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->q, (size_t)B * m->q_dim)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->attn, (size_t)B * m->q_dim)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->act, (size_t)B * m->F)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->logits, (size_t)B * m->V)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->cand_val, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->cand_idx, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
+    m->att_splits = attn_pick_splits(B, m->nkv, c.max_seq_len);
+    m->att_chunk = ceil_div(c.max_seq_len, m->att_splits);
+    if ((rc = dalloc_t(m, &m->att_part, attn_scratch_floats(B, m->nh, m->att_splits, hd))) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->att_cnt, (size_t)B * m->nkv)) != SB_OK) return fail(rc);
+    // sequence state
+    if ((rc = dalloc_t(m, &m->d_tok, B)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_pos, B)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_plen, B)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_prompt, (size_t)B * c.max_seq_len)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_out, (size_t)B * c.max_seq_len)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_ngen, B)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_last, B)) != SB_OK) return fail(rc);
+    m->seq.tok = m->d_tok;
+    m->seq.pos = m->d_pos;
+    m->seq.prompt = m->d_prompt;
+    m->seq.prompt_len = m->d_plen;
+    m->seq.max_prompt = c.max_seq_len;
+    m->seq.out = m->d_out;
+    m->seq.ngen = m->d_ngen;
+    m->seq.max_gen = c.max_seq_len;
+    m->seq.last = m->d_last;
+    if ((rc = dalloc_t(m, &m->trace_buf, (size_t)m->L * B * m->h)) != SB_OK) return fail(rc);
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    *out = m;
+    return SB_OK;
+}
+
+sb_status sb_llama_destroy(sb_llama *m) {
+    if (!m) return SB_OK;
+    if (m->st) cudaStreamSynchronize(m->st);
+    for (auto g : m->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+    return SB_OK;
+}
+
+sb_status sb_llama_load_f32(sb_llama *m, int which, int layer, const float *data) {
+    SB_CHECK(m && data, SB_ERR_ARG, "sb_llama_load_f32: null argument");
+    float *dst = nullptr;
+    size_t n = m->h;
+    switch (which) {
+    case SB_F_EMBED: dst = m->embed, n = (size_t)m->V * m->h; break;
+    case SB_F_NORM_IN:
+        SB_CHECK(layer >= 0 && layer < m->L, SB_ERR_ARG, "bad layer %d", layer);
+        dst = m->norm_in + (size_t)layer * m->h;
+        break;
+    case SB_F_NORM_POST:
+        SB_CHECK(layer >= 0 && layer < m->L, SB_ERR_ARG, "bad layer %d", layer);
+        dst = m->norm_post + (size_t)layer * m->h;
+        break;
+    case SB_F_NORM_FINAL: dst = m->norm_final; break;
+    default: return set_error(SB_ERR_ARG, "sb_llama_load_f32: unknown tensor %d", which);
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(dst, data, sizeof(float) * n, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *q, float scale) {
+    SB_CHECK(m && q, SB_ERR_ARG, "sb_llama_load_qweight: null argument");
+    if (layer < 0) {  // lm_head, [V,h] like llama.rs:943-948
+        SB_CUDA_TRY(cudaMemcpyAsync(m->stage, q, (size_t)m->V * m->h, cudaMemcpyHostToDevice, m->st));
+        SB_TRY(qweight_pack(m->stage, m->h, m->V, m->lm.TN, 0, 1, const_cast<uint4 *>(m->lm.w), m->st));
+        m->lm.scale = scale;
+        m->has_lm = true;
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        return SB_OK;
+    }
+    SB_CHECK(layer < m->L && slot >= 0 && slot < 5, SB_ERR_ARG, "bad layer %d / slot %d", layer, slot);
+    sb_llama::Layer &ly = m->layers[layer];
+    QWeightDesc *d = nullptr;
+    int K = 0, N = 0;
+    switch (slot) {
+    case SB_W_QKV: d = &ly.qkv, K = m->h, N = m->qkv_dim; break;
+    case SB_W_O: d = &ly.o, K = m->q_dim, N = m->h; break;
+    case SB_W_DOWN: d = &ly.down, K = m->F, N = m->h; break;
+    case SB_W_GATE:
+        SB_CUDA_TRY(cudaMemcpyAsync(m->stage, q, (size_t)m->h * m->F, cudaMemcpyHostToDevice, m->st));
+        m->staged_gate_layer = layer;
+        m->staged_gate_scale = scale;
+        ly.has[SB_W_GATE] = true;
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        return SB_OK;
+    case SB_W_UP:
+        SB_CHECK(m->staged_gate_layer == layer, SB_ERR_STATE,
+                 "sb_llama_load_qweight: load gate before up for layer %d", layer);
+        SB_CUDA_TRY(cudaMemcpyAsync(m->stage + (size_t)m->h * m->F, q, (size_t)m->h * m->F,
+                                    cudaMemcpyHostToDevice, m->st));
+        SB_TRY(qweight_pack(m->stage, m->h, ly.gu.N, ly.gu.TN, m->F, 0, const_cast<uint4 *>(ly.gu.w), m->st));
+        ly.gu.scale = m->staged_gate_scale;
+        ly.gu.scale_up = scale;
+        ly.has[SB_W_UP] = true;
+        m->staged_gate_layer = -1;
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        return SB_OK;
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(m->stage, q, (size_t)K * N, cudaMemcpyHostToDevice, m->st));
+    SB_TRY(qweight_pack(m->stage, K, N, d->TN, 0, 0, const_cast<uint4 *>(d->w), m->st));
+    d->scale = scale;
+    ly.has[slot] = true;
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_get_qweight(sb_llama *m, int layer, int slot, int8_t *q, float *scale) {
+    SB_CHECK(m && q && scale, SB_ERR_ARG, "sb_llama_get_qweight: null argument");
+    if (layer < 0) {
+        SB_TRY(qweight_unpack(m->lm.w, m->h, m->V, m->lm.TN, 0, m->stage, m->st));
+        std::vector<int8_t> hv((size_t)m->h * m->V);
+        SB_CUDA_TRY(cudaMemcpyAsync(hv.data(), m->stage, hv.size(), cudaMemcpyDeviceToHost, m->st));
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        for (int k = 0; k < m->h; k++)
+            for (int n = 0; n < m->V; n++) q[(size_t)n * m->h + k] = hv[(size_t)k * m->V + n];
+        *scale = m->lm.scale;
+        return SB_OK;
+    }
+    SB_CHECK(layer < m->L && slot >= 0 && slot < 5, SB_ERR_ARG, "bad layer %d / slot %d", layer, slot);
+    const sb_llama::Layer &ly = m->layers[layer];
+    const size_t kf = (size_t)m->h * m->F;
+    switch (slot) {
+    case SB_W_QKV:
+        SB_TRY(qweight_unpack(ly.qkv.w, ly.qkv.K, ly.qkv.N, ly.qkv.TN, 0, m->stage, m->st));
+        *scale = ly.qkv.scale;
+        SB_CUDA_TRY(cudaMemcpyAsync(q, m->stage, (size_t)ly.qkv.K * ly.qkv.N, cudaMemcpyDeviceToHost, m->st));
+        break;
+    case SB_W_O:
+        SB_TRY(qweight_unpack(ly.o.w, ly.o.K, ly.o.N, ly.o.TN, 0, m->stage, m->st));
+        *scale = ly.o.scale;
+        SB_CUDA_TRY(cudaMemcpyAsync(q, m->stage, (size_t)ly.o.K * ly.o.N, cudaMemcpyDeviceToHost, m->st));
+        break;
+    case SB_W_DOWN:
+        SB_TRY(qweight_unpack(ly.down.w, ly.down.K, ly.down.N, ly.down.TN, 0, m->stage, m->st));
+        *scale = ly.down.scale;
+        SB_CUDA_TRY(cudaMemcpyAsync(q, m->stage, (size_t)ly.down.K * ly.down.N, cudaMemcpyDeviceToHost, m->st));
+        break;
+    default:  // gate / up
+        SB_TRY(qweight_unpack(ly.gu.w, ly.gu.K, ly.gu.N, ly.gu.TN, m->F, m->stage, m->st));
+        *scale = slot == SB_W_GATE ? ly.gu.scale : ly.gu.scale_up;
+        SB_CUDA_TRY(cudaMemcpyAsync(q, m->stage + (slot == SB_W_GATE ? 0 : kf), kf, cudaMemcpyDeviceToHost, m->st));
+        break;
+    }
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_init_random(sb_llama *m, uint64_t seed) {
+    // LlamaModel::new (llama.rs:593-680) draw order: embed [V*h]; per layer
+    // q, k, v, o, gate, up, down; lm_head [V*h] when untied.
+    SB_CHECK(m, SB_ERR_ARG, "sb_llama_init_random: null model");
+    const int h = m->h, F = m->F, V = m->V;
+    uint64_t sample = 0;
+    SB_TRY(gen_normal_f32(seed, sample, (size_t)V * h, m->embed, m->st));
+    sample += (uint64_t)V * h;
+    float scale = 0.0f;
+    auto quant_pack = [&](GenSpec &g, QWeightDesc &d, int pair_F, int8_t *dst_stage, bool pack, float *sc) -> int {
+        SB_TRY(gen_absmax(g, seed, m->amax, m->st));
+        SB_TRY(gen_quantize(g, seed, m->amax, dst_stage, m->scale_dev, m->st));
+        SB_CUDA_TRY(cudaMemcpyAsync(sc, m->scale_dev, 4, cudaMemcpyDeviceToHost, m->st));
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        if (pack) SB_TRY(qweight_pack(m->stage, d.K, d.N, d.TN, pair_F, 0, const_cast<uint4 *>(d.w), m->st));
+        return SB_OK;
+    };
+    for (int l = 0; l < m->L; l++) {
+        sb_llama::Layer &ly = m->layers[l];
+        GenSpec g;
+        g.K = h;
+        g.N = m->qkv_dim;
+        g.nseg = 3;
+        g.c0[0] = 0, g.c0[1] = m->q_dim, g.c0[2] = m->q_dim + m->kv_dim;
+        g.width[0] = m->q_dim, g.width[1] = m->kv_dim, g.width[2] = m->kv_dim;
+        g.base[0] = sample;
+        g.base[1] = sample + (uint64_t)h * m->q_dim;
+        g.base[2] = g.base[1] + (uint64_t)h * m->kv_dim;
+        sample = g.base[2] + (uint64_t)h * m->kv_dim;
+        SB_TRY(quant_pack(g, ly.qkv, 0, m->stage, true, &scale));
+        ly.qkv.scale = scale;
+        GenSpec go;
+        go.K = m->q_dim;
+        go.N = h;
+        go.width[0] = h;
+        go.base[0] = sample;
+        sample += (uint64_t)m->q_dim * h;
+        SB_TRY(quant_pack(go, ly.o, 0, m->stage, true, &scale));
+        ly.o.scale = scale;
+        GenSpec gg;
+        gg.K = h;
+        gg.N = F;
+        gg.width[0] = F;
+        gg.base[0] = sample;
+        sample += (uint64_t)h * F;
+        float sg = 0.0f, su = 0.0f;
+        SB_TRY(quant_pack(gg, ly.gu, 0, m->stage, false, &sg));
+        GenSpec gu = gg;
+        gu.base[0] = sample;
+        sample += (uint64_t)h * F;
+        SB_TRY(quant_pack(gu, ly.gu, 0, m->stage + (size_t)h * F, false, &su));
+        SB_TRY(qweight_pack(m->stage, h, ly.gu.N, ly.gu.TN, F, 0, const_cast<uint4 *>(ly.gu.w), m->st));
+        ly.gu.scale = sg;
+        ly.gu.scale_up = su;
+        GenSpec gd;
+        gd.K = F;
+        gd.N = h;
+        gd.width[0] = h;
+        gd.base[0] = sample;
+        sample += (uint64_t)F * h;
+        SB_TRY(quant_pack(gd, ly.down, 0, m->stage, true, &scale));
+        ly.down.scale = scale;
+        for (int s = 0; s < 5; s++) ly.has[s] = true;
+    }
+    GenSpec gl;
+    gl.K = h;
+    gl.N = V;
+    gl.transposed = 1;  // target [h,V] from the [V,h] stream order
+    if (m->cfg.tie_word_embeddings) {
+        gl.src = m->embed;
+    } else {
+        gl.base[0] = sample;
+        sample += (uint64_t)V * h;
+    }
+    SB_TRY(quant_pack(gl, m->lm, 0, m->stage, false, &scale));
+    // gen_quantize wrote [h,V] row-major (K x N) into stage: pack as untransposed.
+    SB_TRY(qweight_pack(m->stage, h, V, m->lm.TN, 0, 0, const_cast<uint4 *>(m->lm.w), m->st));
+    m->lm.scale = scale;
+    m->has_lm = true;
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_reset(sb_llama *m) {
+    SB_CHECK(m, SB_ERR_ARG, "sb_llama_reset: null model");
+    SB_CUDA_TRY(cudaMemsetAsync(m->d_pos, 0, sizeof(int) * m->B, m->st));
+    SB_CUDA_TRY(cudaMemsetAsync(m->d_ngen, 0, sizeof(int) * m->B, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_set_trace(sb_llama *m, int enabled) {
+    SB_CHECK(m, SB_ERR_ARG, "null model");
+    m->trace = enabled != 0;
+    return SB_OK;
+}
+
+sb_status sb_llama_get_trace(sb_llama *m, float *out) {
+    SB_CHECK(m && out, SB_ERR_ARG, "null argument");
+    SB_CHECK(m->trace_batch > 0, SB_ERR_STATE, "no traced step yet");
+    SB_CUDA_TRY(cudaMemcpy(out, m->trace_buf, sizeof(float) * (size_t)m->L * m->trace_batch * m->h,
+                           cudaMemcpyDeviceToHost));
+    return SB_OK;
+}
+
+sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const int32_t *pos, float *logits,
+                           int32_t *argmax) {
+    SB_CHECK(m && tokens && pos, SB_ERR_ARG, "sb_llama_forward: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    for (int b = 0; b < batch; b++) {
+        SB_CHECK(pos[b] >= 0 && pos[b] < m->cfg.max_seq_len, SB_ERR_SHAPE, "position %d beyond cache %d", pos[b],
+                 m->cfg.max_seq_len);
+        SB_CHECK(tokens[b] >= 0 && tokens[b] < m->V, SB_ERR_ARG, "token %d outside vocab %d", tokens[b], m->V);
+    }
+    SB_TRY(check_ready(m));
+    std::vector<int32_t> zero(batch, 0);
+    SB_TRY(set_state(m, batch, tokens, pos, zero.data()));
+    if (m->trace) {
+        SB_TRY(enqueue_step(m, batch, m->st, false, true));
+        m->trace_batch = batch;
+    } else {
+        cudaGraphExec_t g = nullptr;
+        SB_TRY(get_graph(m, batch, &g));
+        // get_graph may have run a warm-up step: restore the inputs.
+        SB_TRY(set_state(m, batch, tokens, pos, zero.data()));
+        SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
+    }
+    m->active = 0;
+    if (logits)
+        SB_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * (size_t)batch * m->V, cudaMemcpyDeviceToHost,
+                                    m->st));
+    if (argmax) SB_CUDA_TRY(cudaMemcpyAsync(argmax, m->d_last, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt) {
+    SB_CHECK(m && prompts, SB_ERR_ARG, "sb_llama_begin: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    SB_CHECK(n_prompt >= 1 && n_prompt <= m->cfg.max_seq_len, SB_ERR_SHAPE, "prompt length %d", n_prompt);
+    for (size_t i = 0; i < (size_t)batch * n_prompt; i++)
+        SB_CHECK(prompts[i] >= 0 && prompts[i] < m->V, SB_ERR_ARG, "prompt token %d outside vocab", prompts[i]);
+    SB_TRY(check_ready(m));
+    cudaGraphExec_t g = nullptr;
+    SB_TRY(get_graph(m, batch, &g));
+    for (int b = 0; b < batch; b++)
+        SB_CUDA_TRY(cudaMemcpyAsync(m->d_prompt + (size_t)b * m->cfg.max_seq_len, prompts + (size_t)b * n_prompt,
+                                    sizeof(int) * n_prompt, cudaMemcpyHostToDevice, m->st));
+    std::vector<int32_t> tok(batch, 0), pos(batch, 0), plen(batch, n_prompt);
+    SB_TRY(set_state(m, batch, tok.data(), pos.data(), plen.data()));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    m->active = batch;
+    m->steps = 0;
+    return SB_OK;
+}
+
+sb_status sb_llama_step(sb_llama *m, int n_steps) {
+    SB_CHECK(m && m->active > 0, SB_ERR_STATE, "sb_llama_step: call sb_llama_begin first");
+    cudaGraphExec_t g = nullptr;
+    SB_CHECK(n_steps >= 0 && (long long)m->steps + n_steps <= m->cfg.max_seq_len, SB_ERR_SHAPE,
+             "sb_llama_step: %d + %d steps exceed the cache (%d positions)", m->steps, n_steps, m->cfg.max_seq_len);
+    SB_TRY(get_graph(m, m->active, &g));
+    for (int i = 0; i < n_steps; i++) SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
+    m->steps += n_steps;
+    return SB_OK;
+}
+
+sb_status sb_llama_tokens(sb_llama *m, int32_t *out, int max_tokens, int *n_out) {
+    SB_CHECK(m && out && n_out && m->active > 0, SB_ERR_STATE, "sb_llama_tokens: no active batch");
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    std::vector<int> ngen(m->active);
+    SB_CUDA_TRY(cudaMemcpy(ngen.data(), m->d_ngen, sizeof(int) * m->active, cudaMemcpyDeviceToHost));
+    int n = max_tokens;
+    for (int b = 0; b < m->active; b++) n = std::min(n, ngen[b]);
+    n = std::max(n, 0);
+    for (int b = 0; b < m->active; b++)
+        SB_CUDA_TRY(cudaMemcpy(out + (size_t)b * max_tokens, m->d_out + (size_t)b * m->cfg.max_seq_len,
+                               sizeof(int) * n, cudaMemcpyDeviceToHost));
+    *n_out = n;
+    return SB_OK;
+}
+
+void *sb_llama_stream(sb_llama *m) { return m ? (void *)m->st : nullptr; }
+
+sb_status sb_llama_generate_greedy(sb_llama *m, int batch, const int32_t *prompts, int n_prompt, int max_tokens,
+                                   int32_t *out) {
+    SB_CHECK(m && out, SB_ERR_ARG, "sb_llama_generate_greedy: null argument");
+    SB_CHECK(max_tokens >= 1, SB_ERR_ARG, "max_tokens must be >= 1");
+    SB_CHECK(n_prompt + max_tokens - 1 <= m->cfg.max_seq_len, SB_ERR_SHAPE,
+             "prompt %d + %d tokens exceed the cache (%d positions)", n_prompt, max_tokens, m->cfg.max_seq_len);
+    SB_TRY(sb_llama_begin(m, batch, prompts, n_prompt));
+    SB_TRY(sb_llama_step(m, n_prompt + max_tokens - 1));
+    int n = 0;
+    SB_TRY(sb_llama_tokens(m, out, max_tokens, &n));
+    SB_CHECK(n == max_tokens, SB_ERR_STATE, "generated %d of %d tokens", n, max_tokens);
+    return SB_OK;
+}
+
+sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, float *other_ms, int *launches) {
+    SB_CHECK(m && m->active > 0, SB_ERR_STATE, "sb_llama_profile_step: call sb_llama_begin first");
+    SB_CHECK(m->steps + 1 <= m->cfg.max_seq_len, SB_ERR_SHAPE, "sb_llama_profile_step: cache full");
+    StepProfiler p;
+    p.st = m->st;
+    SB_TRY(enqueue_step(m, m->active, m->st, false, false, &p));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    float t[3] = {0, 0, 0};
+    for (size_t i = 0; i < p.cls.size(); i++) {
+        float ms = 0;
+        SB_CUDA_TRY(cudaEventElapsedTime(&ms, p.ev[2 * i], p.ev[2 * i + 1]));
+        t[p.cls[i]] += ms;
+    }
+    m->steps += 1;
+    if (gemv_ms) *gemv_ms = t[0];
+    if (attn_ms) *attn_ms = t[1];
+    if (other_ms) *other_ms = t[2];
+    if (launches) *launches = (int)p.cls.size();
+    return SB_OK;
+}
+
+sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_bytes_per_pos) {
+    SB_CHECK(m, SB_ERR_ARG, "null model");
+    const double h = m->h, F = m->F, V = m->V;
+    const double per_layer = h * m->qkv_dim + (double)m->q_dim * h + 2.0 * h * F + F * h;
+    if (weight_bytes) *weight_bytes = per_layer * m->L + V * h;  // int8 bytes (+ negligible scalar scales)
+    if (kv_bytes_per_pos) *kv_bytes_per_pos = 2.0 * m->L * m->kv_dim * (m->kv_f32 ? 4.0 : 2.0);
+    return SB_OK;
+}
+
+}  // extern "C"

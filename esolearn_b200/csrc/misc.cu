@@ -1,0 +1,303 @@
+// Embedding, argmax, standalone MathBackend ops, device quantizer and the
+// seeded on-device weight generator.
+#include "misc.cuh"
+
+#include <algorithm>
+
+namespace sb {
+
+// ---------------------------------------------------------------------------
+// embedding / argmax around the decode step
+
+__global__ void embed_kernel(const float *__restrict__ embed, int h, int V, SeqState s, float *x) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x;
+    const int pos = s.pos[b];
+    int tok = (s.prompt_len && pos < s.prompt_len[b]) ? s.prompt[(size_t)b * s.max_prompt + pos] : s.tok[b];
+    tok = min(max(tok, 0), V - 1);  // the reference asserts idx < vocab (cpu.rs:486-491)
+    const float *src = embed + (size_t)tok * h;
+    float *dst = x + (size_t)b * h;
+    for (int i = threadIdx.x; i < h; i += blockDim.x) dst[i] = src[i];
+}
+
+int embed_launch(const float *embed, int h, int V, SeqState s, int B, float *x, cudaStream_t st, bool pdl) {
+    SB_CUDA_TRY(launch(embed_kernel, dim3(B), dim3(256), 0, st, pdl, embed, h, V, s, x));
+    return SB_OK;
+}
+
+// (value, index) pair reduction: larger value wins; equal values -> larger index.
+__device__ __forceinline__ void amax_merge(float &v, int &i, float ov, int oi) {
+    if (oi < 0) return;
+    if (i < 0 || ov > v || (ov == v && oi > i)) v = ov, i = oi;
+}
+
+__device__ void block_amax(float &v, int &i) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        amax_merge(v, i, ov, oi);
+    }
+    if (lane == 0) sv[warp] = v, si[warp] = i;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        v = lane < nw ? sv[lane] : -INFINITY;
+        i = lane < nw ? si[lane] : -1;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            amax_merge(v, i, ov, oi);
+        }
+    }
+}
+
+__global__ void argmax_step_kernel(const float *__restrict__ cv, const int *__restrict__ ci, int ntiles,
+                                   SeqState s) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x;
+    float v = -INFINITY;
+    int idx = -1;
+    for (int t = threadIdx.x; t < ntiles; t += blockDim.x)
+        amax_merge(v, idx, cv[(size_t)b * ntiles + t], ci[(size_t)b * ntiles + t]);
+    block_amax(v, idx);
+    if (threadIdx.x == 0) {
+        const int next = idx < 0 ? 0 : idx;
+        const int pos = s.pos[b];
+        const int plen = s.prompt_len ? s.prompt_len[b] : 0;
+        s.last[b] = next;
+        if (pos >= plen - 1) {  // generate.rs:72-75: sample after the last prompt token
+            const int g = s.ngen[b];
+            if (g < s.max_gen) s.out[(size_t)b * s.max_gen + g] = next;
+            s.ngen[b] = g + 1;
+        }
+        s.tok[b] = next;
+        s.pos[b] = pos + 1;
+    }
+}
+
+int argmax_step_launch(const float *cand_val, const int *cand_idx, int ntiles, SeqState s, int B,
+                       cudaStream_t st, bool pdl) {
+    SB_CUDA_TRY(launch(argmax_step_kernel, dim3(B), dim3(256), 0, st, pdl, cand_val, cand_idx, ntiles, s));
+    return SB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// standalone ops
+
+__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int d, float eps,
+                               float *__restrict__ out) {
+    // cpu.rs:574-599: f64 mean of squares, out = (f32)(x * rstd * w) in f64.
+    __shared__ double sh[32];
+    const float *xr = x + (size_t)blockIdx.x * d;
+    double s = 0.0;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) s += (double)xr[j] * (double)xr[j];
+    s = warp_sum_d(s);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) sh[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += sh[i];
+        sh[0] = 1.0 / sqrt(t / (double)d + (double)eps);
+    }
+    __syncthreads();
+    const double rstd = sh[0];
+    for (int j = threadIdx.x; j < d; j += blockDim.x)
+        out[(size_t)blockIdx.x * d + j] = (float)(__dmul_rn(__dmul_rn((double)xr[j], rstd), (double)w[j]));
+}
+
+int rmsnorm_launch(const float *x, const float *w, int rows, int d, float eps, float *out, cudaStream_t st) {
+    if (rows <= 0) return SB_OK;
+    rmsnorm_kernel<<<rows, 256, 0, st>>>(x, w, d, eps, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+__global__ void rope_kernel(const float *__restrict__ x, int seq, int n_heads, int hd, int start_pos,
+                            const float *__restrict__ freqs, float scale, float *__restrict__ out) {
+    // cpu.rs:635-664, then the trait-default scale (backend/mod.rs:219-230).
+    const int half = hd / 2;
+    const size_t total = (size_t)seq * n_heads * half;
+    for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
+        const int i = (int)(t % half);
+        const size_t sh = t / half;  // (s, h)
+        const int s = (int)(sh / n_heads);
+        const double angle = __dmul_rn((double)(start_pos + s), (double)freqs[i]);
+        const float cs = (float)cos(angle), sn = (float)sin(angle);
+        const size_t base = sh * hd + 2 * i;
+        const float x0 = x[base], x1 = x[base + 1];
+        const float o0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float o1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        out[base] = __fmul_rn(o0, scale);
+        out[base + 1] = __fmul_rn(o1, scale);
+    }
+}
+
+int rope_launch(const float *x, int seq, int n_heads, int hd, int start_pos, const float *freqs, float scale,
+                float *out, cudaStream_t st) {
+    const size_t total = (size_t)seq * n_heads * (hd / 2);
+    if (total == 0) return SB_OK;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, 65535);
+    rope_kernel<<<blocks, 256, 0, st>>>(x, seq, n_heads, hd, start_pos, freqs, scale, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+__global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, size_t n,
+                              float *__restrict__ out) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __fmul_rn(silu_f64(g[i]), u[i]);  // cpu.rs:666-678
+}
+
+int swiglu_launch(const float *g, const float *u, size_t n, float *out, cudaStream_t st) {
+    if (n == 0) return SB_OK;
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 65535);
+    swiglu_kernel<<<blocks, 256, 0, st>>>(g, u, n, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+__global__ void argmax_rows_kernel(const float *__restrict__ x, int n, int *out) {
+    float v = -INFINITY;
+    int idx = -1;
+    const float *xr = x + (size_t)blockIdx.x * n;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) amax_merge(v, idx, xr[j], j);
+    block_amax(v, idx);
+    if (threadIdx.x == 0) out[blockIdx.x] = idx < 0 ? 0 : idx;
+}
+
+int argmax_rows_launch(const float *x, int rows, int n, int *out, cudaStream_t st) {
+    if (rows <= 0) return SB_OK;
+    argmax_rows_kernel<<<rows, 1024, 0, st>>>(x, n, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// quantize_symmetric on device (quantize.rs:16-32)
+
+__device__ __forceinline__ int8_t quant_one(float w, float inv) {
+    float r = roundf(__fmul_rn(w, inv));  // f32::round: half away from zero
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int8_t)r;
+}
+
+__global__ void absmax_kernel(const float *__restrict__ w, size_t n, unsigned *amax) {
+    float m = 0.0f;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(w[i]));
+    m = warp_max_f(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(m));  // non-negative floats order as uints
+}
+
+__global__ void quantize_kernel(const float *__restrict__ w, size_t n, const unsigned *amax, int8_t *q,
+                                float *scale_out) {
+    const float am = __uint_as_float(*amax);
+    const float scale = am / 127.0f;   // f32 division (IEEE, no fast-math)
+    const float inv = 1.0f / scale;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = am == 0.0f ? 0.0f : scale;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        q[i] = am == 0.0f ? (int8_t)0 : quant_one(w[i], inv);
+}
+
+int quantize_device(const float *w, size_t n, int8_t *q, float *scale_dev, unsigned *amax, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(unsigned), st));
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)device_props().sm_count * 8);
+    if (n > 0) absmax_kernel<<<std::max(blocks, 1), 256, 0, st>>>(w, n, amax);
+    quantize_kernel<<<std::max(blocks, 1), 256, 0, st>>>(w, n, amax, q, scale_dev);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// seeded weights: fastrand 2.3.0 wyrand + Box-Muller (nn/init.rs:2-14)
+//
+// The generator's state after d draws is seed + d*C0 (mod 2^64), so normal
+// sample i (draws 2i+1 and 2i+2 of the stream) is computed independently.
+
+constexpr uint64_t WY0 = 0x2d358dccaa6c78a5ULL;
+constexpr uint64_t WY1 = 0x8bb84b93962eacc9ULL;
+
+__device__ __forceinline__ uint64_t wy_mix(uint64_t s) {
+    const uint64_t t = s ^ WY1;
+    return (s * t) ^ __umul64hi(s, t);
+}
+
+__device__ __forceinline__ double unit_f64(uint64_t r) {
+    return __longlong_as_double((long long)(0x3FF0000000000000ULL + (r >> 12))) - 1.0;
+}
+
+__device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i) {
+    const uint64_t s1 = seed + (2 * i + 1) * WY0;
+    const uint64_t s2 = s1 + WY0;
+    double u1 = unit_f64(wy_mix(s1));
+    const double u2 = unit_f64(wy_mix(s2));
+    if (u1 < 1e-30) u1 = 1e-30;
+    const double z = __dmul_rn(sqrt(__dmul_rn(-2.0, log(u1))), cos(__dmul_rn(2.0 * 3.14159265358979323846, u2)));
+    return (float)__dadd_rn(0.0, __dmul_rn((double)0.02f, z));  // mean 0, std 0.02 (llama.rs:599)
+}
+
+__device__ __forceinline__ float gen_value(const GenSpec &g, uint64_t seed, int r, int c) {
+    if (g.src) return g.transposed ? g.src[(size_t)c * g.K + r] : g.src[(size_t)r * g.N + c];
+    int i = 0;
+    if (g.nseg > 1 && c >= g.c0[1]) i = 1;
+    if (g.nseg > 2 && c >= g.c0[2]) i = 2;
+    const int cc = c - g.c0[i];
+    const uint64_t idx = g.transposed ? g.base[i] + (uint64_t)cc * g.K + r : g.base[i] + (uint64_t)r * g.width[i] + cc;
+    return normal_at(seed, idx);
+}
+
+__global__ void gen_absmax_kernel(GenSpec g, uint64_t seed, unsigned *amax) {
+    const size_t n = (size_t)g.K * g.N;
+    float m = 0.0f;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(gen_value(g, seed, (int)(e / g.N), (int)(e % g.N))));
+    m = warp_max_f(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(m));
+}
+
+__global__ void gen_quantize_kernel(GenSpec g, uint64_t seed, const unsigned *amax, int8_t *q, float *scale_out) {
+    const float am = __uint_as_float(*amax);
+    const float scale = am / 127.0f;
+    const float inv = 1.0f / scale;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = am == 0.0f ? 0.0f : scale;
+    const size_t n = (size_t)g.K * g.N;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        q[e] = am == 0.0f ? (int8_t)0 : quant_one(gen_value(g, seed, (int)(e / g.N), (int)(e % g.N)), inv);
+}
+
+static int gen_blocks(size_t n) {
+    return (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, (size_t)device_props().sm_count * 16));
+}
+
+int gen_absmax(const GenSpec &g, uint64_t seed, unsigned *amax, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(unsigned), st));
+    gen_absmax_kernel<<<gen_blocks((size_t)g.K * g.N), 256, 0, st>>>(g, seed, amax);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+int gen_quantize(const GenSpec &g, uint64_t seed, const unsigned *amax, int8_t *q, float *scale_out,
+                 cudaStream_t st) {
+    gen_quantize_kernel<<<gen_blocks((size_t)g.K * g.N), 256, 0, st>>>(g, seed, amax, q, scale_out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+__global__ void gen_normal_kernel(uint64_t seed, uint64_t first, size_t n, float *out) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = normal_at(seed, first + i);
+}
+
+int gen_normal_f32(uint64_t seed, uint64_t first_sample, size_t n, float *out, cudaStream_t st) {
+    gen_normal_kernel<<<gen_blocks(n), 256, 0, st>>>(seed, first_sample, n, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+}  // namespace sb

@@ -1,0 +1,383 @@
+"""Host-side mirror of scry-llm's Llama decode API over the B200 engine.
+
+Names and argument meanings follow the reference crate:
+
+* ``LlamaConfig`` / ``RopeScaling``           -- nn/llama.rs:10-139
+* ``QuantLlamaB200`` implements ``CausalLM``   -- generate.rs:5-21 (the
+  quantized counterpart of ``LlamaModel``, llama.rs:583-1004)
+* ``SamplingConfig``, ``generate``, ``sample_token`` -- generate.rs:24-185
+* ``quantize_symmetric``                        -- quantize.rs:16-32
+* ``QWeight`` + ``matmul_i8_f32``               -- backend/mod.rs:521-557
+
+Every numeric call goes through libscryb200.so (include/sb_api.h).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _native as N
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+# ---------------------------------------------------------------------------
+# configuration (llama.rs:10-139)
+
+@dataclass
+class RopeScaling:
+    factor: float = 32.0
+    low_freq_factor: float = 1.0
+    high_freq_factor: float = 4.0
+    original_max_position_embeddings: int = 8192
+
+
+@dataclass
+class LlamaConfig:
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    max_seq_len: int = 4096
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    tie_word_embeddings: bool = False
+    rope_scaling: Optional[RopeScaling] = None
+
+    def head_dim(self) -> int:  # llama.rs:97-99
+        return self.hidden_size // self.n_heads
+
+    # Reference presets (llama.rs:46-95).
+    @staticmethod
+    def llama_1b() -> "LlamaConfig":
+        return LlamaConfig(128256, 2048, 8192, 16, 32, 8, 131072, 1e-5, 500000.0, True, RopeScaling())
+
+    @staticmethod
+    def llama_3b() -> "LlamaConfig":
+        return LlamaConfig(128256, 3072, 8192, 28, 24, 8, 131072, 1e-5, 500000.0, True, RopeScaling())
+
+    @staticmethod
+    def llama_8b() -> "LlamaConfig":
+        return LlamaConfig(128256, 4096, 14336, 32, 32, 8, 131072, 1e-5, 500000.0, False, RopeScaling())
+
+    # The benchmark shapes (random-init, untied lm_head).
+    @staticmethod
+    def tiny() -> "LlamaConfig":
+        return LlamaConfig(32000, 512, 1376, 8, 8, 8, 4096, 1e-5, 10000.0, False, None)
+
+    @staticmethod
+    def llama2_7b_shape() -> "LlamaConfig":
+        return LlamaConfig(32000, 4096, 11008, 32, 32, 32, 4096, 1e-5, 10000.0, False, None)
+
+    @staticmethod
+    def llama3_8b_shape() -> "LlamaConfig":
+        return LlamaConfig(128256, 4096, 14336, 32, 32, 8, 8192, 1e-5, 500000.0, False, None)
+
+    @staticmethod
+    def llama3_70b_shape() -> "LlamaConfig":
+        return LlamaConfig(128256, 8192, 28672, 80, 64, 8, 8192, 1e-5, 500000.0, False, None)
+
+    def to_c(self, max_seq: int, max_batch: int, page_size: int, kv_dtype: int) -> N.LlamaConfigC:
+        c = N.LlamaConfigC()
+        c.vocab_size, c.hidden_size, c.intermediate_size = self.vocab_size, self.hidden_size, self.intermediate_size
+        c.n_layers, c.n_heads, c.n_kv_heads = self.n_layers, self.n_heads, self.n_kv_heads
+        c.max_seq_len = max_seq
+        c.rms_norm_eps, c.rope_theta = self.rms_norm_eps, self.rope_theta
+        c.tie_word_embeddings = int(self.tie_word_embeddings)
+        if self.rope_scaling is not None:
+            c.has_rope_scaling = 1
+            rs = self.rope_scaling
+            for i, v in enumerate((rs.factor, rs.low_freq_factor, rs.high_freq_factor,
+                                   float(rs.original_max_position_embeddings))):
+                c.rope_scaling[i] = v
+        c.max_batch, c.page_size, c.kv_dtype = max_batch, page_size, kv_dtype
+        return c
+
+
+# ---------------------------------------------------------------------------
+# quantization and the op-level int8 matmul
+
+def quantize_symmetric(weights: np.ndarray):
+    """quantize.rs:16-32 -> (int8 array, scale).  Bit-exact with the reference."""
+    w = np.ascontiguousarray(weights, np.float32).ravel()
+    q = np.empty(w.size, np.int8)
+    s = C.c_float()
+    N.check(N.lib().sb_quantize_symmetric_host(_ptr(w), w.size, _ptr(q), C.byref(s)))
+    return q.reshape(np.shape(weights)), np.float32(s.value)
+
+
+class QWeight:
+    """An int8 [K,N] weight packed on the device (the I8Storage of this backend)."""
+
+    def __init__(self, q: np.ndarray, scales, group: int = 0):
+        q = np.ascontiguousarray(q, np.int8)
+        self.K, self.N = q.shape
+        self.group = group
+        h = C.c_void_p()
+        N.check(N.lib().sb_qweight_create(self.K, self.N, group, C.byref(h)))
+        self._h = h
+        sc = np.ascontiguousarray(np.atleast_1d(np.asarray(scales, np.float32)))
+        N.check(N.lib().sb_qweight_load(self._h, _ptr(q), _ptr(sc)))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and N._lib is not None:
+            N._lib.sb_qweight_destroy(self._h)
+            self._h = None
+
+
+def matmul_i8_f32(a, w: QWeight, out=None, bias=None, stream: int = 0):
+    """backend/mod.rs:521-557 on torch CUDA tensors: a [M,K] f32/bf16 -> [M,N] f32."""
+    import torch
+
+    assert a.is_cuda and a.is_contiguous() and a.shape[-1] == w.K
+    M = a.numel() // w.K
+    if out is None:
+        out = torch.empty((M, w.N), dtype=torch.float32, device=a.device)
+    dt = N.SB_DTYPE_BF16 if a.dtype == torch.bfloat16 else N.SB_DTYPE_F32
+    if dt == N.SB_DTYPE_F32:
+        assert a.dtype == torch.float32
+    st = C.c_void_p(stream or torch.cuda.current_stream(a.device).cuda_stream)
+    if bias is None:
+        N.check(N.lib().sb_matmul_i8_f32(w._h, C.c_void_p(a.data_ptr()), dt, M, C.c_void_p(out.data_ptr()), st))
+    else:
+        N.check(N.lib().sb_matmul_i8_f32_bias(w._h, C.c_void_p(a.data_ptr()), dt, M, C.c_void_p(bias.data_ptr()),
+                                              C.c_void_p(out.data_ptr()), st))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# the model (CausalLM, generate.rs:5-21)
+
+class LlamaKvCacheHandle:
+    """Caller-owned cache handle (LlamaKvCache, kv_cache.rs:134-145).
+
+    The pages live inside the engine; the handle records the sequence slot and
+    the number of cached positions, like LlamaLayerKvCache::seq_len."""
+
+    def __init__(self, model: "QuantLlamaB200", max_seq: int, slot: int = 0):
+        self.model, self.max_seq, self.slot, self.seq_len = model, max_seq, slot, 0
+
+
+class QuantLlamaB200:
+    """Int8 Llama decode on one B200 (the quantized LlamaModel)."""
+
+    def __init__(self, config: LlamaConfig, *, max_seq: Optional[int] = None, max_batch: int = 1,
+                 page_size: int = 64, kv_dtype: str = "bf16"):
+        self.config = config
+        self.max_seq = max_seq or config.max_seq_len
+        self.max_batch = max_batch
+        kvd = {"bf16": N.SB_KV_BF16, "f32": N.SB_KV_F32}[kv_dtype]
+        self.kv_dtype = kv_dtype
+        cfg = config.to_c(self.max_seq, max_batch, page_size, kvd)
+        h = C.c_void_p()
+        N.check(N.lib().sb_llama_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None) and N._lib is not None:
+            N._lib.sb_llama_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    # -- weights --------------------------------------------------------
+    @classmethod
+    def new_random(cls, config: LlamaConfig, seed: int, **kw) -> "QuantLlamaB200":
+        """LlamaModel::new (llama.rs:593-680) + quantize_symmetric, on the device."""
+        m = cls(config, **kw)
+        N.check(N.lib().sb_llama_init_random(m._h, seed))
+        return m
+
+    def load_qweight(self, layer: int, slot: int, q: np.ndarray, scale: float):
+        q = np.ascontiguousarray(q, np.int8)
+        N.check(N.lib().sb_llama_load_qweight(self._h, layer, slot, _ptr(q), float(scale)))
+
+    def get_qweight(self, layer: int, slot: int):
+        """(int8 [K,N] in the reference layout, scale); layer -1 = lm_head [V,h]."""
+        c = self.config
+        hd = c.head_dim()
+        qkv = c.n_heads * hd + 2 * c.n_kv_heads * hd
+        shapes = {N.SB_W_QKV: (c.hidden_size, qkv), N.SB_W_O: (c.n_heads * hd, c.hidden_size),
+                  N.SB_W_GATE: (c.hidden_size, c.intermediate_size), N.SB_W_UP: (c.hidden_size, c.intermediate_size),
+                  N.SB_W_DOWN: (c.intermediate_size, c.hidden_size)}
+        shape = (c.vocab_size, c.hidden_size) if layer < 0 else shapes[slot]
+        q = np.empty(shape, np.int8)
+        s = C.c_float()
+        N.check(N.lib().sb_llama_get_qweight(self._h, layer, slot, _ptr(q), C.byref(s)))
+        return q, np.float32(s.value)
+
+    def load_f32(self, which: int, layer: int, data: np.ndarray):
+        d = np.ascontiguousarray(data, np.float32)
+        N.check(N.lib().sb_llama_load_f32(self._h, which, layer, _ptr(d)))
+
+    # -- CausalLM ------------------------------------------------------
+    def vocab_size(self) -> int:
+        return self.config.vocab_size
+
+    def new_kv_cache(self, max_seq: int) -> LlamaKvCacheHandle:
+        if max_seq > self.max_seq:
+            raise N.SbError(4, f"cache of {max_seq} positions exceeds the engine's {self.max_seq}")
+        N.check(N.lib().sb_llama_reset(self._h))
+        return LlamaKvCacheHandle(self, max_seq)
+
+    def forward_with_cache(self, token_id: int, pos: int, cache: LlamaKvCacheHandle) -> np.ndarray:
+        """forward_with_llama_cache (llama.rs:744-763): logits [vocab] of one token."""
+        logits, _ = self.forward_batch([token_id], [pos], slots=[cache.slot])
+        cache.seq_len = pos + 1
+        return logits[0]
+
+    def forward_batch(self, tokens: Sequence[int], positions: Sequence[int], slots=None, want_logits=True):
+        """One decode step of len(tokens) sequences (slot b = row b)."""
+        B = len(tokens)
+        if slots is not None and list(slots) != list(range(B)):
+            raise N.SbError(6, "sequences occupy slots 0..B-1 in order")
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        am = np.empty(B, np.int32)
+        lg = np.empty((B, self.config.vocab_size), np.float32) if want_logits else None
+        N.check(N.lib().sb_llama_forward(self._h, B, _ptr(t), _ptr(p), _ptr(lg) if want_logits else None, _ptr(am)))
+        return lg, am
+
+    def set_trace(self, on: bool):
+        N.check(N.lib().sb_llama_set_trace(self._h, int(on)))
+
+    def get_trace(self, batch: int = 1) -> np.ndarray:
+        out = np.empty((self.config.n_layers, batch, self.config.hidden_size), np.float32)
+        N.check(N.lib().sb_llama_get_trace(self._h, _ptr(out)))
+        return out
+
+    def generate_greedy(self, prompts, max_tokens: int) -> np.ndarray:
+        """generate (generate.rs:51-89) at temperature 0 for equal-length prompts."""
+        pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        out = np.empty((pr.shape[0], max_tokens), np.int32)
+        N.check(N.lib().sb_llama_generate_greedy(self._h, pr.shape[0], _ptr(pr), pr.shape[1], max_tokens, _ptr(out)))
+        return out
+
+    # -- benchmark helpers --------------------------------------------------
+    def begin(self, prompts):
+        pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        N.check(N.lib().sb_llama_begin(self._h, pr.shape[0], _ptr(pr), pr.shape[1]))
+
+    def step(self, n: int = 1):
+        N.check(N.lib().sb_llama_step(self._h, n))
+
+    def tokens(self, batch: int, max_tokens: int) -> np.ndarray:
+        out = np.zeros((batch, max_tokens), np.int32)
+        n = C.c_int32()
+        N.check(N.lib().sb_llama_tokens(self._h, _ptr(out), max_tokens, C.byref(n)))
+        return out[:, : n.value]
+
+    def stream(self) -> int:
+        return N.lib().sb_llama_stream(self._h) or 0
+
+    def profile_step(self):
+        """One eager step timed per kernel class: (gemv_ms, attn_ms, other_ms, launches)."""
+        g, a, o = C.c_float(), C.c_float(), C.c_float()
+        n = C.c_int32()
+        N.check(N.lib().sb_llama_profile_step(self._h, C.byref(g), C.byref(a), C.byref(o), C.byref(n)))
+        return g.value, a.value, o.value, n.value
+
+    def step_bytes(self):
+        w, kv = C.c_double(), C.c_double()
+        N.check(N.lib().sb_llama_step_bytes(self._h, C.byref(w), C.byref(kv)))
+        return w.value, kv.value
+
+
+# ---------------------------------------------------------------------------
+# generation (generate.rs:24-185)
+
+@dataclass
+class SamplingConfig:
+    temperature: float = 1.0
+    top_k: int = 0
+    top_p: float = 1.0
+    max_tokens: int = 128
+
+
+class Rng:
+    """fastrand::Rng (wyrand), used by the sampler's weighted_sample."""
+
+    C0 = 0x2D358DCCAA6C78A5
+    C1 = 0x8BB84B93962EACC9
+    MASK = (1 << 64) - 1
+
+    def __init__(self, seed: int):
+        self.state = seed & self.MASK
+
+    def u64(self) -> int:
+        self.state = (self.state + self.C0) & self.MASK
+        s = self.state
+        t = s * (s ^ self.C1)
+        return (t & self.MASK) ^ (t >> 64)
+
+    def f64(self) -> float:
+        bits = ((1 << 62) - (1 << 52)) + (self.u64() >> 12)
+        return float(np.array([bits], np.uint64).view(np.float64)[0]) - 1.0
+
+
+def argmax_last(logits: np.ndarray) -> int:
+    """generate.rs:167-173: the last index among equal maxima."""
+    lg = np.asarray(logits)
+    return int(len(lg) - 1 - np.argmax(lg[::-1]))
+
+
+def sample_token(logits: np.ndarray, config: SamplingConfig, rng: Rng) -> int:
+    """generate.rs:92-165."""
+    n = len(logits)
+    if config.temperature < 1e-8:
+        return argmax_last(logits)
+    scaled = np.asarray(logits, np.float64) / float(np.float32(config.temperature))
+    if 0 < config.top_k < n:
+        thr = np.sort(scaled)[::-1][config.top_k - 1]
+        scaled = np.where(scaled < thr, -np.inf, scaled)
+    mx = scaled.max()
+    probs = np.exp(scaled - mx)
+    s = probs.sum()
+    probs = probs / s if s > 0 else np.full(n, 1.0 / n)
+    if 0.0 < config.top_p < 1.0:
+        order = np.argsort(-probs, kind="stable")
+        cum = np.cumsum(probs[order])
+        hit = np.nonzero(cum >= float(np.float32(config.top_p)))[0]
+        cut = int(hit[0]) + 1 if hit.size else n
+        keep = np.zeros(n, bool)
+        keep[order[:cut]] = True
+        probs = np.where(keep, probs, 0.0)
+        s2 = probs.sum()
+        if s2 > 0:
+            probs = probs / s2
+    r = rng.f64()
+    cum = 0.0
+    for i, p in enumerate(probs):
+        cum += p
+        if r < cum:
+            return i
+    return n - 1
+
+
+def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: SamplingConfig, rng: Rng) -> list:
+    """generate.rs:51-89.  Greedy runs entirely on the device."""
+    if len(prompt_tokens) == 0:
+        raise ValueError("generate: prompt_tokens must not be empty")
+    if config.temperature < 1e-8:
+        return model.generate_greedy([list(prompt_tokens)], config.max_tokens)[0].tolist()
+    max_seq = len(prompt_tokens) + config.max_tokens
+    cache = model.new_kv_cache(max_seq)
+    V = model.vocab_size()
+    out = []
+    for pos, tok in enumerate(prompt_tokens):
+        logits = model.forward_with_cache(int(tok), pos, cache)
+        if pos == len(prompt_tokens) - 1:
+            out.append(sample_token(logits[:V], config, rng))
+    for i in range(1, config.max_tokens):
+        logits = model.forward_with_cache(out[-1], len(prompt_tokens) + i - 1, cache)
+        out.append(sample_token(logits[:V], config, rng))
+    return out

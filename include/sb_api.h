@@ -1,0 +1,185 @@
+/*
+ * sb_api.h -- C ABI of libscryb200.so, the B200-native engine for
+ * scry-llm's int8 (W8A32) Llama decode path.
+ *
+ * Plain C types only (pointers, sizes, ints, floats): a Rust FFI crate
+ * (`scry-b200-sys`), ctypes or any other FFI binds it directly.  Every entry
+ * point returns an sb_status; on failure sb_last_error() gives the message.
+ * Each declaration names the reference interface it replaces (paths are
+ * inside the reference project, crate scry-llm).
+ *
+ * Threading: like the reference CUDA backend (backend/cuda.rs:26-79, one
+ * thread-local GpuCtx), one host thread drives one device at a time.
+ * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default).
+ */
+#ifndef SB_API_H
+#define SB_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int sb_status;
+enum {
+    SB_OK = 0,
+    SB_ERR_CUDA = 1,        /* a CUDA runtime call failed */
+    SB_ERR_NCCL = 2,        /* a collective failed */
+    SB_ERR_TIMEOUT = 3,     /* a bounded device wait gave up */
+    SB_ERR_SHAPE = 4,       /* shapes inconsistent or unsupported */
+    SB_ERR_OOM = 5,         /* device allocation failed */
+    SB_ERR_ARG = 6,         /* bad argument (null pointer, range) */
+    SB_ERR_STATE = 7,       /* call out of order (not initialised, no weights) */
+    SB_ERR_UNSUPPORTED = 8, /* configuration not built into this library */
+};
+
+enum { SB_DTYPE_F32 = 0, SB_DTYPE_BF16 = 1 };
+enum { SB_KV_BF16 = 0, SB_KV_F32 = 1 };
+
+/* Message of the last failure on this thread; returns its status code. */
+int sb_last_error(char *buf, size_t len);
+/* ABI revision of this header (bumped on any signature change). */
+int sb_abi_version(void);
+
+/* ---- device (replaces backend/cuda.rs:39-59 init_gpu / GpuCtx) --------- */
+/* Select and initialise `device` for the calling thread. */
+sb_status sb_init(int device);
+sb_status sb_device_info(int *sm_count, int *cc_major, int *cc_minor, size_t *hbm_bytes);
+
+/* ---- DeviceBackend storage (backend/mod.rs:12-45) ----------------------- */
+/* zeros(): zero-filled device buffer. */
+sb_status sb_alloc(void **dptr, size_t bytes);
+sb_status sb_free(void *dptr);
+/* from_vec() / to_vec(): host<->device copies on `stream` (synchronous
+ * when stream is NULL). */
+sb_status sb_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream);
+sb_status sb_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream);
+sb_status sb_stream_sync(void *stream);
+
+/* ---- quantize.rs ------------------------------------------------------- */
+/* quantize_symmetric (quantize.rs:16-32) on the host; bit-exact. */
+sb_status sb_quantize_symmetric_host(const float *w, size_t n, int8_t *q, float *scale);
+/* Same on device buffers (w, q, scale all device pointers); bit-exact. */
+sb_status sb_quantize_symmetric(const float *w, size_t n, int8_t *q, float *scale, void *stream);
+
+/* ---- I8Storage: packed int8 weights (backend/mod.rs:15-21) -------------
+ * A [K,N] int8 matrix in the reference layout (linear.rs:17, row-major
+ * [in,out]) is re-packed once into column tiles streamed by the GEMV.
+ * Re-packing only permutes the int8 values.  group = 0 is the reference's
+ * per-tensor scale; group = 32 or 64 keeps f32 scales[ceil(K/g), N]. */
+typedef struct sb_qweight sb_qweight;
+sb_status sb_qweight_create(int K, int N, int group, sb_qweight **out);
+/* q: host [K,N] int8; scales: host, 1 value (group 0) or [ceil(K/g), N]. */
+sb_status sb_qweight_load(sb_qweight *w, const int8_t *q, const float *scales);
+sb_status sb_qweight_destroy(sb_qweight *w);
+
+/* matmul_i8_f32 (backend/mod.rs:521-533; CPU cpu.rs:1129-1160):
+ * c[M,N] = a[M,K] . dequant(q)[K,N], f32 accumulate.  a, c are device
+ * pointers; a_dtype is SB_DTYPE_F32 or SB_DTYPE_BF16.  Uses a library-owned
+ * workspace on the current device. */
+sb_status sb_matmul_i8_f32(const sb_qweight *w, const void *a, int a_dtype, int M, float *c,
+                           void *stream);
+/* matmul_i8_f32_bias (backend/mod.rs:537-557): c = a . dequant(q) + bias. */
+sb_status sb_matmul_i8_f32_bias(const sb_qweight *w, const void *a, int a_dtype, int M,
+                                const float *bias, float *c, void *stream);
+
+/* ---- Llama ops of MathBackend (device pointers) ------------------------ */
+/* rmsnorm (backend/mod.rs rmsnorm; cpu.rs:574-599). */
+sb_status sb_rmsnorm(const float *x, const float *w, int rows, int d, float eps, float *out,
+                     void *stream);
+/* rope_with_freqs_preloaded (cpu.rs:635-664) when scale == 1, and
+ * rope_with_freqs_scaled_preloaded (backend/mod.rs:219-230) otherwise. */
+sb_status sb_rope_with_freqs(const float *x, int seq, int n_heads, int head_dim, int start_pos,
+                             const float *freqs, float scale, float *out, void *stream);
+/* swiglu (cpu.rs:666-678). */
+sb_status sb_swiglu(const float *gate, const float *up, size_t n, float *out, void *stream);
+/* argmax over each row, ties -> last index (generate.rs:167-173). */
+sb_status sb_argmax_rows(const float *x, int rows, int n, int32_t *out, void *stream);
+
+/* ---- paged GQA decode attention ----------------------------------------
+ * Replaces llama.rs:414-456 (gather_reshape_repeat_kv + strided-batched
+ * QK^T + softmax + AV).  q: [B, n_heads*hd] f32, already RoPE'd and
+ * scaled by 1/sqrt(hd).  K/V caches: [pages][n_kv][page_size][hd] in
+ * kv_dtype.  page_table: [B, max_pages] int32.  ctx_len: [B] int32 device.
+ * out: [B, n_heads*hd] f32.  Uses a library-owned workspace. */
+sb_status sb_attn_decode_paged(const float *q, const void *k_cache, const void *v_cache,
+                               int kv_dtype, const int32_t *page_table, int max_pages,
+                               const int32_t *ctx_len, int B, int n_heads, int n_kv, int head_dim,
+                               int page_size, int max_ctx, float *out, void *stream);
+
+/* ---- the quantized Llama engine ----------------------------------------
+ * Replaces LlamaModel (llama.rs:583-964) + LlamaKvCache (kv_cache.rs:134-145)
+ * behind CausalLM (generate.rs:5-21).  Every projection is an int8 weight
+ * with the reference per-tensor scale; embeddings and norm weights stay f32.
+ * One decode step of every active sequence is one CUDA-graph replay. */
+typedef struct sb_llama_config {
+    int32_t vocab_size, hidden_size, intermediate_size, n_layers, n_heads, n_kv_heads;
+    int32_t max_seq_len; /* KV capacity per sequence, in positions */
+    float rms_norm_eps, rope_theta;
+    int32_t tie_word_embeddings;
+    int32_t has_rope_scaling;
+    double rope_scaling[4]; /* factor, low_freq_factor, high_freq_factor, original_max_pos */
+    int32_t max_batch;      /* sequences decoded together (rows of every GEMV) */
+    int32_t page_size;      /* KV positions per page */
+    int32_t kv_dtype;       /* SB_KV_BF16 or SB_KV_F32 */
+} sb_llama_config;
+
+typedef struct sb_llama sb_llama;
+enum { SB_W_QKV = 0, SB_W_O = 1, SB_W_GATE = 2, SB_W_UP = 3, SB_W_DOWN = 4 };
+enum { SB_F_EMBED = 0, SB_F_NORM_IN = 1, SB_F_NORM_POST = 2, SB_F_NORM_FINAL = 3 };
+
+/* LlamaModel construction; allocates weights, KV pages and scratch. */
+sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out);
+sb_status sb_llama_destroy(sb_llama *m);
+/* LlamaModel::new (llama.rs:593-680) generated on the device with the
+ * fastrand stream and draw order of the reference, then quantized per
+ * tensor (quantize.rs:16-32) and packed.  No host copy of the weights. */
+sb_status sb_llama_init_random(sb_llama *m, uint64_t seed);
+/* Load one quantized projection, reference layout [K,N] (layer -1 = lm_head,
+ * given as [V,h] like llama.rs:943-948). */
+sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *q, float scale);
+/* Read back one quantized projection in the reference layout (inverse of
+ * sb_llama_load_qweight; the lm_head comes back as [V,h]).  q: host buffer
+ * of K*N bytes; scale: host float. */
+sb_status sb_llama_get_qweight(sb_llama *m, int layer, int slot, int8_t *q, float *scale);
+/* Load an f32 tensor: embed [V,h] or a norm weight [h]. */
+sb_status sb_llama_load_f32(sb_llama *m, int which, int layer, const float *data);
+/* Forget all cached positions (LlamaKvCache::new). */
+sb_status sb_llama_reset(sb_llama *m);
+/* forward_with_llama_cache (llama.rs:744-763) for `batch` sequences:
+ * token[b] at position pos[b] of sequence b.  Optional outputs (host):
+ * logits [batch, V] f32, argmax [batch] (ties -> last). */
+sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const int32_t *pos,
+                           float *logits, int32_t *argmax);
+/* generate (generate.rs:51-89) with temperature 0, for `batch` prompts of
+ * equal length: prompts [batch, n_prompt], out [batch, max_tokens]. */
+sb_status sb_llama_generate_greedy(sb_llama *m, int batch, const int32_t *prompts, int n_prompt,
+                                   int max_tokens, int32_t *out);
+/* Residual stream after every layer of the last sb_llama_forward call,
+ * [n_layers, batch, h] (host), when tracing was enabled at that call. */
+sb_status sb_llama_set_trace(sb_llama *m, int enabled);
+sb_status sb_llama_get_trace(sb_llama *m, float *out);
+
+/* Benchmark helpers: queue n decode steps of the current batch on the
+ * engine stream (device-driven tokens and positions; no host sync). */
+sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt);
+sb_status sb_llama_step(sb_llama *m, int n_steps);
+sb_status sb_llama_tokens(sb_llama *m, int32_t *out, int max_tokens, int *n_out);
+void *sb_llama_stream(sb_llama *m);
+/* One eager (non-graph) decode step of the current batch with a CUDA event
+ * pair around every kernel on the engine stream: per-class device time in
+ * ms (GEMV = all int8 projections, attention, other = embed + argmax) and
+ * the int8 weight bytes those GEMVs read.  Advances the sequences like
+ * sb_llama_step(m, 1). */
+sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, float *other_ms,
+                                int *launches);
+/* Bytes the engine streams per decode step at the current context (int8
+ * weights + scales + KV read), for roofline accounting. */
+sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_bytes_per_pos);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SB_API_H */

@@ -1,0 +1,223 @@
+"""GPU parity of the op-level C ABI against the CPU oracle.
+
+Tolerances: f32-accumulate results within 1e-3 max
+relative error (max|gpu - ref| / max|ref|); integer work bit-exact.  The int8
+GEMV is additionally held to 2e-5, its measured accuracy, so that a
+regression in the fixed-point path shows up long before the contract bound.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from esolearn_b200 import QWeight, matmul_i8_f32
+from esolearn_b200 import _native as N
+from tests.gpu_util import rel_err
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-3
+TOL_GEMV = 2e-5
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def vp(t):
+    return C.c_void_p(t.data_ptr())
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    N.check(N.lib().sb_init(0))
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 7])
+@pytest.mark.parametrize("K,N_", [(512, 1536), (4096, 4096), (1376, 512), (100, 45), (16, 16), (4096, 32000)])
+def test_matmul_i8_f32_per_tensor(M, K, N_):
+    rng = np.random.default_rng(M * 1000 + K + N_)
+    w = (rng.standard_normal((K, N_)) * 0.02).astype(np.float32)
+    q, s = O.quantize_symmetric(w)
+    q = q.reshape(K, N_)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    ref = O.matmul_i8_f32(a, q, s, M, K, N_)
+    qw = QWeight(q, [s])
+    out = matmul_i8_f32(dev(a), qw).cpu().numpy()
+    torch.cuda.synchronize()
+    e = rel_err(out, ref)
+    assert e < TOL_F32 and e < TOL_GEMV, e
+
+
+@pytest.mark.parametrize("group", [32, 64])
+@pytest.mark.parametrize("M", [1, 4, 8])
+@pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008)])
+def test_matmul_grouped_bf16_sweep_shapes(group, M, K, N_):
+    # Quantized-linear sweep inputs: int8 uniform in [-127,127], f32 group
+    # scales = absmax/127 of N(0,0.02) groups, bf16 activations ~ N(0,1).
+    rng = np.random.default_rng(K + N_ + group + M)
+    q = rng.integers(-127, 128, (K, N_), dtype=np.int8)
+    src = (rng.standard_normal((K // group, group, N_)) * 0.02).astype(np.float32)
+    scales = (np.abs(src).max(axis=1) / np.float32(127.0)).astype(np.float32)
+    a16 = torch.randn(M, K, generator=torch.Generator().manual_seed(M + K)).to(torch.bfloat16)
+    a32 = a16.float().numpy()
+    ref = O.matmul_i8_f32_grouped(a32, q, scales, group, M, K, N_)
+    qw = QWeight(q, scales, group=group)
+    out = matmul_i8_f32(a16.cuda(), qw).cpu().numpy()
+    assert rel_err(out, ref) < TOL_GEMV
+
+
+def test_matmul_bias_and_zero_weights():
+    rng = np.random.default_rng(7)
+    K, N_, M = 256, 96, 3
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    bias = rng.standard_normal(N_).astype(np.float32)
+    q = np.zeros((K, N_), np.int8)
+    qw = QWeight(q, [0.0])
+    out = matmul_i8_f32(dev(a), qw, bias=dev(bias)).cpu().numpy()
+    assert np.array_equal(out, np.broadcast_to(bias, (M, N_)))
+    w = (rng.standard_normal((K, N_)) * 0.02).astype(np.float32)
+    q, s = O.quantize_symmetric(w)
+    q = q.reshape(K, N_)
+    qw = QWeight(q, [s])
+    ref = O.matmul_i8_f32(a, q, s, M, K, N_) + bias  # cpu.rs:554-570
+    out = matmul_i8_f32(dev(a), qw, bias=dev(bias)).cpu().numpy()
+    assert rel_err(out, ref) < TOL_GEMV
+
+
+def test_matmul_zero_and_tiny_activations():
+    rng = np.random.default_rng(8)
+    K, N_ = 512, 64
+    q = rng.integers(-127, 128, (K, N_), dtype=np.int8)
+    qw = QWeight(q, [0.01])
+    a = np.zeros((2, K), np.float32)
+    a[1, 3] = 1e-30  # a single denormal-range value must not break the exponent choice
+    out = matmul_i8_f32(dev(a), qw).cpu().numpy()
+    ref = O.matmul_i8_f32(a, q, 0.01, 2, K, N_)
+    assert np.array_equal(out[0], np.zeros(N_, np.float32))
+    assert rel_err(out[1], ref[1]) < TOL_GEMV
+
+
+def test_rmsnorm_matches_reference():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, 4096)).astype(np.float32)
+    w = rng.standard_normal(4096).astype(np.float32)
+    ref = O.rmsnorm(x, w, 1e-5)
+    xd, wd = dev(x), dev(w)
+    out = torch.empty_like(xd)
+    N.check(N.lib().sb_rmsnorm(vp(xd), vp(wd), 5, 4096, 1e-5, vp(out), None))
+    torch.cuda.synchronize()
+    d = np.abs(out.cpu().numpy().view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert d.max() <= 1  # f64 row sum in a different order: at most 1 ulp in f32
+
+
+@pytest.mark.parametrize("scale", [1.0, 0.125])
+def test_rope_matches_reference(scale):
+    rng = np.random.default_rng(4)
+    seq, heads, hd, start = 3, 8, 64, 37
+    x = rng.standard_normal(seq * heads * hd).astype(np.float32)
+    fr = O.compute_rope_freqs(hd, 10000.0).astype(np.float32)
+    ref = O.scale(O.rope(x, seq, heads, hd, start, fr), scale)
+    xd, fd = dev(x), dev(fr)
+    out = torch.empty_like(xd)
+    N.check(N.lib().sb_rope_with_freqs(vp(xd), seq, heads, hd, start, vp(fd), scale, vp(out), None))
+    torch.cuda.synchronize()
+    d = np.abs(out.cpu().numpy().view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert d.max() <= 1
+
+
+def test_swiglu_matches_reference():
+    rng = np.random.default_rng(5)
+    g = rng.standard_normal(11008).astype(np.float32) * 3
+    u = rng.standard_normal(11008).astype(np.float32)
+    ref = O.swiglu(g, u)
+    gd, ud = dev(g), dev(u)
+    out = torch.empty_like(gd)
+    N.check(N.lib().sb_swiglu(vp(gd), vp(ud), g.size, vp(out), None))
+    torch.cuda.synchronize()
+    d = np.abs(out.cpu().numpy().view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert d.max() <= 1
+
+
+def test_argmax_rows_ties_to_last():
+    x = np.zeros((3, 32000), np.float32)
+    x[0, [5, 77, 31999]] = 2.0
+    x[1, 0] = 1.0
+    x[2, [100, 200]] = -1.0
+    x[2] -= 5.0
+    xd = dev(x)
+    out = torch.empty(3, dtype=torch.int32, device="cuda")
+    N.check(N.lib().sb_argmax_rows(vp(xd), 3, 32000, vp(out), None))
+    got = out.cpu().numpy().tolist()
+    assert got == [O.argmax(x[i]) for i in range(3)] == [31999, 0, 31999]
+
+
+def test_device_quantizer_bit_exact():
+    rng = np.random.default_rng(6)
+    w = (rng.standard_normal(1 << 20) * 0.02).astype(np.float32)
+    w[1234] = 0.5  # exact .5 products exercise round-half-away-from-zero
+    qo, so = O.quantize_symmetric(w)
+    wd = dev(w)
+    q = torch.empty(w.size, dtype=torch.int8, device="cuda")
+    s = torch.empty(1, dtype=torch.float32, device="cuda")
+    N.check(N.lib().sb_quantize_symmetric(vp(wd), w.size, vp(q), vp(s), None))
+    torch.cuda.synchronize()
+    assert s.item() == so
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
+def _paged(cache_rows, page_size, n_kv, hd, perm):
+    """Scatter contiguous [S, n_kv*hd] rows into pages [P][n_kv][page][hd] via a page table."""
+    S = cache_rows.shape[0]
+    npages = (S + page_size - 1) // page_size
+    pages = np.zeros((len(perm), n_kv, page_size, hd), np.float32)
+    table = np.zeros(npages, np.int32)
+    for i in range(npages):
+        table[i] = perm[i]
+        rows = cache_rows[i * page_size:(i + 1) * page_size].reshape(-1, n_kv, hd)
+        pages[perm[i], :, :rows.shape[0], :] = rows.transpose(1, 0, 2)
+    return pages, table
+
+
+@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("n_q,n_kv,hd", [(8, 8, 64), (32, 8, 128), (64, 8, 128), (4, 2, 64), (32, 32, 128)])
+def test_paged_gqa_decode_attention(kv_dtype, n_q, n_kv, hd):
+    rng = np.random.default_rng(n_q * 7 + hd)
+    B, page = 3, 16
+    lens = [1, 37, 300]  # ragged contexts, including a single position and partial pages
+    max_pages = (max(lens) + page - 1) // page
+    q = (rng.standard_normal((B, n_q * hd)) / np.sqrt(hd)).astype(np.float32)
+    all_pages, tables, refs = [], [], []
+    perm = rng.permutation(B * max_pages)
+    kps, vps = np.zeros((B * max_pages, n_kv, page, hd), np.float32), np.zeros((B * max_pages, n_kv, page, hd), np.float32)
+    for b, S in enumerate(lens):
+        k = rng.standard_normal((S, n_kv * hd)).astype(np.float32)
+        v = rng.standard_normal((S, n_kv * hd)).astype(np.float32)
+        if kv_dtype == "bf16":
+            k, v = O.round_bf16(k), O.round_bf16(v)
+        myperm = perm[b * max_pages:(b + 1) * max_pages]
+        kp, tab = _paged(k, page, n_kv, hd, myperm)
+        vp_, _ = _paged(v, page, n_kv, hd, myperm)
+        kps += kp
+        vps += vp_
+        t = np.zeros(max_pages, np.int32)
+        t[:len(tab)] = tab
+        tables.append(t)
+        refs.append(O.attention_decode(q[b], k, v, n_q, n_kv, hd))
+    if kv_dtype == "bf16":
+        kd, vd = dev(kps).to(torch.bfloat16), dev(vps).to(torch.bfloat16)
+        kvt = N.SB_KV_BF16
+    else:
+        kd, vd = dev(kps), dev(vps)
+        kvt = N.SB_KV_F32
+    qd = dev(q)
+    td = dev(np.stack(tables))
+    ld = dev(np.array(lens, np.int32))
+    out = torch.empty_like(qd)
+    N.check(N.lib().sb_attn_decode_paged(vp(qd), vp(kd), vp(vd), kvt, vp(td), max_pages, vp(ld), B, n_q, n_kv, hd,
+                                         page, max_pages * page, vp(out), None))
+    got = out.cpu().numpy()
+    for b in range(B):
+        assert rel_err(got[b], refs[b]) < 1e-5, b
