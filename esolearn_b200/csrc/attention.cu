@@ -226,9 +226,13 @@ static int attn_inst(const AttnArgs &a, cudaStream_t st, bool pdl) {
     constexpr int NPG = ATT_THREADS / (HD / EPL);
     const size_t smem = sizeof(float) * ((size_t)REP * HD + (size_t)REP * a.max_chunk + (size_t)NPG * REP * HD);
     auto kern = attn_decode_kernel<HD, REP, KV>;
-    SB_CHECK(smem <= (size_t)device_props().max_smem_optin, SB_ERR_SHAPE,
-             "attention: split of %d positions needs %zu B shared memory", a.max_chunk, smem);
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    static int limit[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!limit[dev & 63]) SB_TRY(allow_max_dynamic_smem(kern, &limit[dev & 63]));  // once, before any capture
+    SB_CHECK(smem <= (size_t)limit[dev & 63], SB_ERR_SHAPE,
+             "attention: split of %d positions needs %zu B shared memory (limit %d)", a.max_chunk, smem,
+             limit[dev & 63]);
     SB_CUDA_TRY(launch(kern, dim3(a.n_kv, a.n_splits, a.B), dim3(ATT_THREADS), smem, st, pdl, a));
     return SB_OK;
 }

@@ -406,17 +406,12 @@ template <int M, int EPI, bool GROUPED>
 static int launch_inst(const QGemvArgs &a, cudaStream_t st, bool pdl) {
     const size_t smem = qgemv_smem_bytes(M, a.w.KS, a.w.TN);
     auto kern = qgemv_kernel<M, EPI, GROUPED>;
-    static bool attr_set[64] = {};
+    static int limit[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         device_props().max_smem_optin));
-        attr_set[dev & 63] = true;
-    }
-    SB_CHECK(smem <= (size_t)device_props().max_smem_optin, SB_ERR_SHAPE,
-             "qgemv: K=%d with M=%d needs %zu B of shared memory (max %d)", a.w.K, M, smem,
-             device_props().max_smem_optin);
+    if (!limit[dev & 63]) SB_TRY(allow_max_dynamic_smem(kern, &limit[dev & 63]));
+    SB_CHECK(smem <= (size_t)limit[dev & 63], SB_ERR_SHAPE,
+             "qgemv: K=%d with M=%d needs %zu B of shared memory (max %d)", a.w.K, M, smem, limit[dev & 63]);
     SB_CUDA_TRY(launch(kern, dim3(a.w.ntiles), dim3(QG_THREADS), smem, st, pdl, a));
     return SB_OK;
 }

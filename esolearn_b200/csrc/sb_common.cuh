@@ -17,6 +17,14 @@ namespace sb {
 // Records the failure message for sb_last_error() on this thread.
 int set_error(int code, const char *fmt, ...);
 
+// Device properties cached per device.
+struct DeviceProps {
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    int cc_major = 0, cc_minor = 0;
+};
+const DeviceProps &device_props();
+
 #define SB_CUDA_TRY(expr)                                                                   \
     do {                                                                                    \
         cudaError_t _e = (expr);                                                            \
@@ -105,15 +113,21 @@ __device__ __forceinline__ float silu_f64(float x) {
     return (float)(x64 / (1.0 + exp(-x64)));
 }
 
-// Device properties cached per device.
-struct DeviceProps {
-    int sm_count = 0;
-    int max_smem_optin = 0;
-    int cc_major = 0, cc_minor = 0;
-};
-const DeviceProps &device_props();
-
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Raise a kernel's dynamic shared-memory limit to what the device allows
+// next to the kernel's static shared memory (once per device and kernel).
+template <typename K>
+inline int allow_max_dynamic_smem(K kern, int *limit_out) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return set_error(SB_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    const int limit = device_props().max_smem_optin - (int)fa.sharedSizeBytes;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+    if (e != cudaSuccess) return set_error(SB_ERR_CUDA, "cudaFuncSetAttribute(%d): %s", limit, cudaGetErrorString(e));
+    if (limit_out) *limit_out = limit;
+    return SB_OK;
+}
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 }  // namespace sb

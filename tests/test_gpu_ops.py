@@ -168,11 +168,11 @@ def test_device_quantizer_bit_exact():
     assert np.array_equal(q.cpu().numpy(), qo)
 
 
-def _paged(cache_rows, page_size, n_kv, hd, perm):
+def _paged(cache_rows, page_size, n_kv, hd, perm, total_pages):
     """Scatter contiguous [S, n_kv*hd] rows into pages [P][n_kv][page][hd] via a page table."""
     S = cache_rows.shape[0]
     npages = (S + page_size - 1) // page_size
-    pages = np.zeros((len(perm), n_kv, page_size, hd), np.float32)
+    pages = np.zeros((total_pages, n_kv, page_size, hd), np.float32)
     table = np.zeros(npages, np.int32)
     for i in range(npages):
         table[i] = perm[i]
@@ -198,8 +198,8 @@ def test_paged_gqa_decode_attention(kv_dtype, n_q, n_kv, hd):
         if kv_dtype == "bf16":
             k, v = O.round_bf16(k), O.round_bf16(v)
         myperm = perm[b * max_pages:(b + 1) * max_pages]
-        kp, tab = _paged(k, page, n_kv, hd, myperm)
-        vp_, _ = _paged(v, page, n_kv, hd, myperm)
+        kp, tab = _paged(k, page, n_kv, hd, myperm, B * max_pages)
+        vp_, _ = _paged(v, page, n_kv, hd, myperm, B * max_pages)
         kps += kp
         vps += vp_
         t = np.zeros(max_pages, np.int32)
