@@ -175,12 +175,12 @@ def run_ours(args, rank: int, world: int, dist):
     cfg = LlamaConfig.llama2_7b_shape()
     B = args.batch
     K, W = args.steps, args.warmup
-    max_seq = PROMPT_LEN + W + K + 8
+    max_seq = args.prompt + W + K + 8
     model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=B, kv_dtype="bf16")
     rng = np.random.default_rng(1000 + rank)
-    prompts = rng.integers(0, cfg.vocab_size, (B, PROMPT_LEN), dtype=np.int64).astype(np.int32)
+    prompts = rng.integers(0, cfg.vocab_size, (B, args.prompt), dtype=np.int64).astype(np.int32)
     model.begin(prompts)
-    model.step(PROMPT_LEN - 1 + W)  # prefill (token by token, as generate() does) + warm-up
+    model.step(args.prompt - 1 + W)  # prefill (token by token, as generate() does) + warm-up
     st = torch.cuda.ExternalStream(model.stream())
     torch.cuda.synchronize()
 
@@ -207,7 +207,7 @@ def run_ours(args, rank: int, world: int, dist):
         ms = float(t.item())
     clk = clocks.summary(t_wall0, t_wall1)
     clocks.stop()
-    ctx_mid = PROMPT_LEN + W + K / 2
+    ctx_mid = args.prompt + W + K / 2
     wbytes, kv_per_pos = model.step_bytes()
     value = world * B * K / (ms / 1000.0)
 
@@ -228,7 +228,7 @@ def run_ours(args, rank: int, world: int, dist):
         # context length as the matching timed step.
         toks = model.tokens(B, max_seq)
         last = int(toks[0, -1]) if toks.shape[1] else 0
-        p0 = PROMPT_LEN + W
+        p0 = args.prompt + W
         n_e2e = K
         pinned_tok = torch.empty(1, dtype=torch.int32).pin_memory()
         for i in range(3):
@@ -251,7 +251,7 @@ def run_ours(args, rank: int, world: int, dist):
         "dtype": "int8 weights x f32 activations (exact int32 dp4a products), f32 accumulate; bf16 KV",
         "data": "synthetic: seeded random-init weights (fastrand/Box-Muller N(0,0.02), LlamaModel::new order), "
                 "seeded uniform prompt ids",
-        "config": {"workload": "llama2-7b-shape int8 decode (BASELINE configs[2])", "batch": B, "prompt": PROMPT_LEN,
+        "config": {"workload": "llama2-7b-shape int8 decode (BASELINE configs[2])", "batch": B, "prompt": args.prompt,
                    "context_mid": ctx_mid, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "weights 6.6 GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
                    "graph": "CUDA graph per step, programmatic dependent launch"},
@@ -280,6 +280,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (the workload uses 512)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -168,7 +168,7 @@ sb_status sb_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream) 
 
 sb_status sb_stream_sync(void *stream) {
     SB_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
-    return SB_OK;
+    return qgemv_check_error();
 }
 
 sb_status sb_quantize_symmetric_host(const float *w, size_t n, int8_t *q, float *scale) {
@@ -339,7 +339,6 @@ sb_status sb_attn_decode_paged(const float *q, const void *k_cache, const void *
     a.hd = head_dim;
     a.page_size = page_size;
     a.n_splits = attn_pick_splits(B, n_kv, max_ctx);
-    a.max_chunk = ceil_div(max_ctx, a.n_splits);
     a.out = out;
     if (a.n_splits > 1) {
         SB_CHECK((size_t)B * n_kv * sizeof(unsigned) <= WS_ATTN_COUNTER_BYTES, SB_ERR_SHAPE,

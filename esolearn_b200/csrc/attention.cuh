@@ -16,7 +16,6 @@ struct AttnArgs {
     int len_is_pos = 0;        // context = len[b] + 1 (the position just written)
     int B = 1, n_heads = 0, n_kv = 0, hd = 0, page_size = 0;
     int n_splits = 1;   // context splits per (sequence, kv head)
-    int max_chunk = 0;  // upper bound of positions per split (shared-memory sizing)
     float *out = nullptr;           // [B, n_heads*hd]
     float *part = nullptr;          // scratch [B][n_heads][n_splits][hd+2]
     unsigned *counters = nullptr;   // scratch [B][n_kv], zero between launches

@@ -71,7 +71,7 @@ struct sb_llama {
     int *cand_idx = nullptr;
     float *att_part = nullptr;
     unsigned *att_cnt = nullptr;
-    int att_splits = 1, att_chunk = 1;
+    int att_splits = 1;
 
     // sequence state
     SeqState seq;
@@ -236,7 +236,6 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.hd = m->hd;
             a.page_size = m->P;
             a.n_splits = m->att_splits;
-            a.max_chunk = m->att_chunk;
             a.out = m->attn;
             a.part = m->att_part;
             a.counters = m->att_cnt;
@@ -431,7 +430,6 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
     if ((rc = dalloc_t(m, &m->cand_val, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->cand_idx, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
     m->att_splits = attn_pick_splits(B, m->nkv, c.max_seq_len);
-    m->att_chunk = ceil_div(c.max_seq_len, m->att_splits);
     if ((rc = dalloc_t(m, &m->att_part, attn_scratch_floats(B, m->nh, m->att_splits, hd))) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->att_cnt, (size_t)B * m->nkv)) != SB_OK) return fail(rc);
     // sequence state
@@ -710,7 +708,7 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
                                     m->st));
     if (argmax) SB_CUDA_TRY(cudaMemcpyAsync(argmax, m->d_last, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
-    return SB_OK;
+    return qgemv_check_error();
 }
 
 sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt) {
@@ -747,6 +745,7 @@ sb_status sb_llama_step(sb_llama *m, int n_steps) {
 sb_status sb_llama_tokens(sb_llama *m, int32_t *out, int max_tokens, int *n_out) {
     SB_CHECK(m && out && n_out && m->active > 0, SB_ERR_STATE, "sb_llama_tokens: no active batch");
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    SB_TRY(qgemv_check_error());
     std::vector<int> ngen(m->active);
     SB_CUDA_TRY(cudaMemcpy(ngen.data(), m->d_ngen, sizeof(int) * m->active, cudaMemcpyDeviceToHost));
     int n = max_tokens;
@@ -782,6 +781,7 @@ sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, flo
     p.st = m->st;
     SB_TRY(enqueue_step(m, m->active, m->st, false, false, &p));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    SB_TRY(qgemv_check_error());
     float t[3] = {0, 0, 0};
     for (size_t i = 0; i < p.cls.size(); i++) {
         float ms = 0;

@@ -18,11 +18,17 @@ __global__ void embed_kernel(const float *__restrict__ embed, int h, int V, SeqS
     tok = min(max(tok, 0), V - 1);  // the reference asserts idx < vocab (cpu.rs:486-491)
     const float *src = embed + (size_t)tok * h;
     float *dst = x + (size_t)b * h;
-    for (int i = threadIdx.x; i < h; i += blockDim.x) dst[i] = src[i];
+    if ((h & 3) == 0) {  // rows are 16-byte aligned when h % 4 == 0
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int i = threadIdx.x; i < h / 4; i += blockDim.x) d4[i] = __ldg(s4 + i);
+    } else {
+        for (int i = threadIdx.x; i < h; i += blockDim.x) dst[i] = src[i];
+    }
 }
 
 int embed_launch(const float *embed, int h, int V, SeqState s, int B, float *x, cudaStream_t st, bool pdl) {
-    SB_CUDA_TRY(launch(embed_kernel, dim3(B), dim3(256), 0, st, pdl, embed, h, V, s, x));
+    SB_CUDA_TRY(launch(embed_kernel, dim3(B), dim3(1024), 0, st, pdl, embed, h, V, s, x));
     return SB_OK;
 }
 

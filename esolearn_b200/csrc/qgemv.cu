@@ -13,42 +13,101 @@
 // integer dot product once, in f64, in the epilogue.  Grouped scales (32 or
 // 64 rows) are applied per group, in f64.
 //
-// Bandwidth.  One CTA owns one TN-column tile over all of K.  Tile widths
-// are chosen so that every tile is resident in a single wave with equal
-// work, each thread keeps QG_DEPTH 16-byte weight loads in flight (the first
-// batch is issued before the grid-dependency wait, overlapping the previous
-// kernel's tail), and weight loads bypass L1.
+// Bandwidth.  One CTA owns one TN-column tile over all of K; its weights are
+// one contiguous slab (the packed layout), streamed by a producer warp with
+// 1-D TMA bulk copies (cp.async.bulk, no multicast) through a ring of
+// QG_NST x 16 KB shared-memory stages guarded by mbarriers.  The first
+// QG_NST stages are requested before the grid-dependency wait, so under
+// programmatic dependent launch the weight stream starts while the previous
+// kernel is still running.  Tile widths are chosen so that every tile is
+// resident in one wave with equal work.  Eight consumer warps read the
+// stage from shared memory: each thread owns 4 columns of one k-step per
+// stage, so the three activation-plane loads serve 4 weight vectors.
 //
 // RMSNorm fusion (rmsnorm, cpu.rs:574-599): with norm_w set, the planes
 // encode x[k]*w[k] and each CTA computes rstd = 1/sqrt(mean(x^2)+eps) of the
-// whole row in f64; y is multiplied by rstd in the epilogue.
+// whole row; y is multiplied by rstd in the epilogue.
+//
+// Every mbarrier wait is bounded (2 s of %globaltimer); a wait that runs out
+// sets qg_error_flag and the kernel returns instead of hanging.
 #include "qgemv.cuh"
 
 #include <algorithm>
 
 namespace sb {
 
-constexpr int QG_DEPTH = 8;
+constexpr int QG_CONSUMERS = 256;            // 8 consumer warps
+constexpr int QG_STAGE = 16384;              // bytes per ring stage
+constexpr int QG_NST = 4;                    // ring stages
+constexpr int QG_CPT = 4;                    // columns per consumer thread
+constexpr unsigned long long QG_WAIT_NS = 2000000000ull;
+
+__device__ unsigned qg_error_flag = 0;       // 1: a bounded wait ran out
 
 struct QGSmem {
     // Offsets inside the dynamic shared memory block.
-    size_t planes, red, ys, rowinfo, total;
+    size_t ring, planes, red, ys, rowinfo, bars, total;
 };
 
 __host__ __device__ inline QGSmem qg_layout(int M, int KS, int TN) {
     QGSmem L;
-    L.planes = 0;
-    L.red = (size_t)M * 3 * KS * 16;
-    L.ys = L.red + (size_t)M * QG_THREADS * 8;
-    L.rowinfo = L.ys + (size_t)M * TN * 4;
-    L.rowinfo = (L.rowinfo + 15) & ~(size_t)15;
-    // rowinfo: rstd[M] (double), shift[M] (int, stored as double), prologue
-    // reduction scratch [8 warps][M][2] doubles.
-    L.total = L.rowinfo + (size_t)M * 16 + (size_t)8 * M * 2 * 8;
+    L.ring = 0;
+    L.planes = (size_t)QG_NST * QG_STAGE;
+    L.red = L.planes + (size_t)M * 3 * KS * 16;
+    L.ys = L.red + (size_t)M * QG_CONSUMERS * QG_CPT * 8;
+    L.rowinfo = (L.ys + (size_t)M * TN * 4 + 15) & ~(size_t)15;
+    // rowinfo: rstd[M] (double), shift[M] (int), reduction scratch [8][M][2] doubles
+    L.bars = L.rowinfo + (size_t)M * 16 + (size_t)8 * M * 2 * 8;
+    L.total = L.bars + 2 * QG_NST * 8;
     return L;
 }
 
 size_t qgemv_smem_bytes(int M, int KS, int TN) { return qg_layout(M, KS, TN).total; }
+
+// ---- mbarrier / TMA helpers --------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase with the given parity; false when it timed out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; it++) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((it & 63) == 0) {
+            const uint64_t t = global_ns();
+            if (it == 0) t0 = t;
+            else if (t - t0 > QG_WAIT_NS) return false;
+        }
+    }
+}
+// 1-D bulk copy global -> shared, completion counted on an mbarrier.
+__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(QG_CONSUMERS) : "memory"); }
 
 template <int M>
 __device__ __forceinline__ void load_quad(const QGemvArgs &a, int m, int q, float v[4]) {
@@ -65,17 +124,32 @@ __device__ __forceinline__ void load_quad(const QGemvArgs &a, int m, int q, floa
     } else {
         const float *xr = reinterpret_cast<const float *>(a.x) + (size_t)m * a.ldx;
         if (k0 + 4 <= K && ((reinterpret_cast<uintptr_t>(xr + k0) & 15) == 0)) {
-            float4 t = *reinterpret_cast<const float4 *>(xr + k0);
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(xr + k0));
             v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = (k0 + i < K) ? xr[k0 + i] : 0.0f;
+            for (int i = 0; i < 4; i++) v[i] = (k0 + i < K) ? __ldg(xr + k0 + i) : 0.0f;
         }
     }
 }
 
+__device__ __forceinline__ void load_norm_quad(const QGemvArgs &a, int q, float nw[4]) {
+    const int K = a.w.K, k0 = q * 4;
+    if (!a.norm_w) {
+        nw[0] = nw[1] = nw[2] = nw[3] = 1.0f;
+        return;
+    }
+    if (k0 + 4 <= K && ((reinterpret_cast<uintptr_t>(a.norm_w + k0) & 15) == 0)) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0));
+        nw[0] = t.x, nw[1] = t.y, nw[2] = t.z, nw[3] = t.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) nw[i] = (k0 + i < K) ? __ldg(a.norm_w + k0 + i) : 0.0f;
+    }
+}
+
 // Builds the fixed-point byte planes of the M activation rows in shared
-// memory and the per-row rstd / exponent.
+// memory and the per-row rstd / exponent.  Consumer threads only.
 template <int M>
 __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) {
     const int KS = a.w.KS, K = a.w.K;
@@ -89,12 +163,10 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) 
     float ssq[M], amx[M];
 #pragma unroll
     for (int m = 0; m < M; m++) ssq[m] = 0.0f, amx[m] = 0.0f;
-    for (int q = tid; q < nq; q += QG_THREADS) {
-        float nw[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-        if (a.norm_w) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) nw[i] = (q * 4 + i < K) ? __ldg(a.norm_w + q * 4 + i) : 0.0f;
-        }
+#pragma unroll 8
+    for (int q = tid; q < nq; q += QG_CONSUMERS) {
+        float nw[4];
+        load_norm_quad(a, q, nw);
 #pragma unroll
         for (int m = 0; m < M; m++) {
             float v[4];
@@ -115,28 +187,26 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) 
             scratch[(warp * M + m) * 2 + 1] = (double)x;
         }
     }
-    __syncthreads();
+    consumer_sync();
     if (tid < M) {
         const int m = tid;
         double s = 0.0, x = 0.0;
-        for (int w = 0; w < QG_THREADS / 32; w++) {
+        for (int w = 0; w < QG_CONSUMERS / 32; w++) {
             s += scratch[(w * M + m) * 2 + 0];
             x = fmax(x, scratch[(w * M + m) * 2 + 1]);
         }
         // rmsnorm (cpu.rs:582-588): mean of squares, rstd = 1/sqrt(mean+eps), f64.
         rstd[m] = a.norm_w ? 1.0 / sqrt(s / (double)K + (double)a.eps) : 1.0;
         int e = 0;
-        if (x > 0.0) frexp(x, &e);  // x = f * 2^e, f in [0.5, 1)
+        if (x > 0.0) frexp(x, &e);        // x = f * 2^e, f in [0.5, 1)
         int sh = (x > 0.0) ? 22 - e : 0;  // |a * 2^sh| < 2^22
         shift[m] = sh < -126 ? -126 : (sh > 126 ? 126 : sh);
     }
-    __syncthreads();
-    for (int q = tid; q < nq; q += QG_THREADS) {
-        float nw[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-        if (a.norm_w) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) nw[i] = (q * 4 + i < K) ? __ldg(a.norm_w + q * 4 + i) : 0.0f;
-        }
+    consumer_sync();
+#pragma unroll 4
+    for (int q = tid; q < nq; q += QG_CONSUMERS) {
+        float nw[4];
+        load_norm_quad(a, q, nw);
 #pragma unroll
         for (int m = 0; m < M; m++) {
             float v[4];
@@ -160,37 +230,31 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) 
     }
 }
 
-template <int M>
-__device__ __forceinline__ void qg_mac(const uint4 &wv, const uint4 *planes4, int KS, int ks,
-                                       int (&acc0)[M], int (&acc1)[M], int (&acc2)[M]) {
-#pragma unroll
-    for (int m = 0; m < M; m++) {
-        const uint4 p0 = planes4[(size_t)(m * 3 + 0) * KS + ks];
-        const uint4 p1 = planes4[(size_t)(m * 3 + 1) * KS + ks];
-        const uint4 p2 = planes4[(size_t)(m * 3 + 2) * KS + ks];
-        acc0[m] = dp4a_su(wv.x, p0.x, acc0[m]);
-        acc0[m] = dp4a_su(wv.y, p0.y, acc0[m]);
-        acc0[m] = dp4a_su(wv.z, p0.z, acc0[m]);
-        acc0[m] = dp4a_su(wv.w, p0.w, acc0[m]);
-        acc1[m] = dp4a_su(wv.x, p1.x, acc1[m]);
-        acc1[m] = dp4a_su(wv.y, p1.y, acc1[m]);
-        acc1[m] = dp4a_su(wv.z, p1.z, acc1[m]);
-        acc1[m] = dp4a_su(wv.w, p1.w, acc1[m]);
-        acc2[m] = dp4a_ss(wv.x, p2.x, acc2[m]);
-        acc2[m] = dp4a_ss(wv.y, p2.y, acc2[m]);
-        acc2[m] = dp4a_ss(wv.z, p2.z, acc2[m]);
-        acc2[m] = dp4a_ss(wv.w, p2.w, acc2[m]);
-    }
-}
-
 __device__ __forceinline__ long long combine_planes(int a0, int a1, int a2) {
     return (long long)a0 + ((long long)a1 << 8) + ((long long)a2 << 16);
 }
 
+__device__ __forceinline__ void dot16(const uint4 &w, const uint4 &p0, const uint4 &p1, const uint4 &p2, int &a0,
+                                      int &a1, int &a2) {
+    a0 = dp4a_su(w.x, p0.x, a0);
+    a0 = dp4a_su(w.y, p0.y, a0);
+    a0 = dp4a_su(w.z, p0.z, a0);
+    a0 = dp4a_su(w.w, p0.w, a0);
+    a1 = dp4a_su(w.x, p1.x, a1);
+    a1 = dp4a_su(w.y, p1.y, a1);
+    a1 = dp4a_su(w.z, p1.z, a1);
+    a1 = dp4a_su(w.w, p1.w, a1);
+    a2 = dp4a_ss(w.x, p2.x, a2);
+    a2 = dp4a_ss(w.y, p2.y, a2);
+    a2 = dp4a_ss(w.z, p2.z, a2);
+    a2 = dp4a_ss(w.w, p2.w, a2);
+}
+
+
 template <int M, int EPI>
 __device__ void qg_epilogue(const QGemvArgs &a, const float *ys) {
     const int TN = a.w.TN, tile = blockIdx.x, tid = threadIdx.x;
-    for (int it = tid; it < M * TN; it += QG_THREADS) {
+    for (int it = tid; it < M * TN; it += QG_CONSUMERS) {
         const int m = it / TN, c = it - m * TN;
         if (m >= a.M) continue;
         const int n = tile * TN + c;
@@ -276,95 +340,165 @@ __device__ void qg_epilogue(const QGemvArgs &a, const float *ys) {
     }
 }
 
+
 template <int M, int EPI, bool GROUPED>
-__global__ void __launch_bounds__(QG_THREADS, 2) qgemv_kernel(const QGemvArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
     const int KS = a.w.KS, TN = a.w.TN;
     const QGSmem L = qg_layout(M, KS, TN);
     const int tid = threadIdx.x;
-    const int nkg = QG_THREADS / TN;
-    const int col = tid % TN, kg = tid / TN;
-    const int R = GROUPED ? a.w.group / 16 : 1;  // k-steps per scale group
-    const int nruns = KS / R;
-    const int myruns = nruns > kg ? (nruns - kg + nkg - 1) / nkg : 0;
-    const int nsteps = myruns * R;
-    const uint4 *wp = a.w.w + (size_t)blockIdx.x * KS * TN + col;
-    auto step_ks = [&](int i) { return GROUPED ? (kg + (i / R) * nkg) * R + (i % R) : kg + i * nkg; };
+    const int TPK = TN / QG_CPT;              // threads per k-step
+    const int KPS = QG_STAGE / (TN * 16);     // k-steps per stage (= QG_CONSUMERS / TPK)
+    const int nstages = (KS + KPS - 1) / KPS;
+    const size_t slab_bytes = (size_t)KS * TN * 16;
+    const uint8_t *slab = reinterpret_cast<const uint8_t *>(a.w.w + (size_t)blockIdx.x * KS * TN);
+    const uint32_t bars = smem_u32(smem + L.bars);  // full[QG_NST], then empty[QG_NST]
+    const uint32_t ring = smem_u32(smem + L.ring);
 
-    // Weight loads do not depend on earlier kernels: start them before the
-    // grid-dependency wait.
-    uint4 wb[QG_DEPTH];
-#pragma unroll
-    for (int d = 0; d < QG_DEPTH; d++)
-        if (d < nsteps) wb[d] = ldg_stream(wp + (size_t)step_ks(d) * TN);
-    pdl_launch_dependents();
-    pdl_wait();
-
-    qg_prologue<M>(a, smem, L);
+    if (tid == 0) {
+        for (int i = 0; i < QG_NST; i++) {
+            mbar_init(bars + 8 * i, 1);                              // full: producer arrival + tx bytes
+            mbar_init(bars + 8 * (QG_NST + i), QG_CONSUMERS / 32);   // empty: one arrival per consumer warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     __syncthreads();
+    pdl_launch_dependents();
+
+    if (tid >= QG_CONSUMERS) {
+        // ---- producer warp: stream the slab through the ring
+        if (tid == QG_CONSUMERS) {
+            bool ok = true;
+            for (int s = 0; s < nstages && ok; s++) {
+                const int slot = s % QG_NST;
+                if (s == QG_NST) pdl_wait();  // first ring fill precedes the dependency wait
+                if (s >= QG_NST && !mbar_wait(bars + 8 * (QG_NST + slot), ((s / QG_NST) - 1) & 1)) {
+                    atomicOr(&qg_error_flag, 1u);
+                    ok = false;
+                    break;
+                }
+                const size_t off = (size_t)s * QG_STAGE;
+                const uint32_t bytes = (uint32_t)std::min<size_t>(QG_STAGE, slab_bytes - off);
+                mbar_expect_tx(bars + 8 * slot, bytes);
+                tma_load_1d(ring + slot * QG_STAGE, slab + off, bytes, bars + 8 * slot);
+            }
+            if (nstages <= QG_NST) pdl_wait();
+        }
+        return;
+    }
+
+    // ---- consumer warps
+    pdl_wait();
+    qg_prologue<M>(a, smem, L);
+    consumer_sync();
 
     const uint4 *planes4 = reinterpret_cast<const uint4 *>(smem + L.planes);
-    int acc0[M], acc1[M], acc2[M];
-    double accd[M];
+    const uint4 *ring4 = reinterpret_cast<const uint4 *>(smem + L.ring);
+    const int ksl = tid / TPK, c0 = tid % TPK;
+    const int lane = tid & 31;
+    int acc[M][QG_CPT][3];
+    double accd[M][QG_CPT];
 #pragma unroll
-    for (int m = 0; m < M; m++) acc0[m] = acc1[m] = acc2[m] = 0, accd[m] = 0.0;
+    for (int m = 0; m < M; m++)
+#pragma unroll
+        for (int j = 0; j < QG_CPT; j++) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = 0, accd[m][j] = 0.0;
+    const int R = GROUPED ? a.w.group / 16 : 1;
     const int NG = GROUPED ? KS / R : 0;
-    const float *gs = GROUPED ? a.w.gscale + (size_t)blockIdx.x * NG * TN + col : nullptr;
+    const float *gs = GROUPED ? a.w.gscale + (size_t)blockIdx.x * NG * TN + c0 : nullptr;
 
-    for (int base = 0; base < nsteps; base += QG_DEPTH) {
+    // A timed-out wait leaves the stage loop early, but the thread still
+    // passes every consumer barrier below so that no warp blocks forever.
+    __shared__ int s_failed;
+    if (tid == 0) s_failed = 0;
+    consumer_sync();
+    for (int s = 0; s < nstages; s++) {
+        const int slot = s % QG_NST;
+        if (!mbar_wait(bars + 8 * slot, (s / QG_NST) & 1)) {
+            atomicOr(&qg_error_flag, 1u);
+            s_failed = 1;
+            break;
+        }
+        const int ks = s * KPS + ksl;
+        if (ks < KS) {
+            const uint4 *wst = ring4 + (size_t)slot * (QG_STAGE / 16) + ksl * TN + c0;
+            uint4 w[QG_CPT];
 #pragma unroll
-        for (int d = 0; d < QG_DEPTH; d++) {
-            const int i = base + d;
-            if (i < nsteps) {
-                const int ks = step_ks(i);
-                const uint4 wv = wb[d];
-                if (i + QG_DEPTH < nsteps) wb[d] = ldg_stream(wp + (size_t)step_ks(i + QG_DEPTH) * TN);
-                qg_mac<M>(wv, planes4, KS, ks, acc0, acc1, acc2);
-                if (GROUPED && (i % R) == R - 1) {
-                    const double g = (double)__ldg(gs + (size_t)(ks / R) * TN);
+            for (int j = 0; j < QG_CPT; j++) w[j] = wst[j * TPK];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                const uint4 p0 = planes4[(size_t)(m * 3 + 0) * KS + ks];
+                const uint4 p1 = planes4[(size_t)(m * 3 + 1) * KS + ks];
+                const uint4 p2 = planes4[(size_t)(m * 3 + 2) * KS + ks];
+#pragma unroll
+                for (int j = 0; j < QG_CPT; j++) dot16(w[j], p0, p1, p2, acc[m][j][0], acc[m][j][1], acc[m][j][2]);
+            }
+            if (GROUPED) {
+#pragma unroll
+                for (int j = 0; j < QG_CPT; j++) {
+                    const double g = (double)__ldg(gs + (size_t)(ks / R) * TN + j * TPK);
 #pragma unroll
                     for (int m = 0; m < M; m++) {
-                        accd[m] += (double)combine_planes(acc0[m], acc1[m], acc2[m]) * g;
-                        acc0[m] = acc1[m] = acc2[m] = 0;
+                        accd[m][j] += (double)combine_planes(acc[m][j][0], acc[m][j][1], acc[m][j][2]) * g;
+                        acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = 0;
                     }
                 }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars + 8 * (QG_NST + slot));
     }
-
-    // Reduce the nkg partial sums of every column in a fixed order.
+    // Reduce the KPS partial sums of every column in a fixed order: first
+    // across the lanes of a warp that share columns (shuffles), then across
+    // warps through shared memory.
     const double *rstd = reinterpret_cast<const double *>(smem + L.rowinfo);
     const int *shift = reinterpret_cast<const int *>(smem + L.rowinfo + (size_t)M * 8);
     float *ys = reinterpret_cast<float *>(smem + L.ys);
+    const int warp = tid >> 5;
+    const int wpk = TPK >= 32 ? TPK / 32 : 1;      // warps spanning one k-step
+    const int ngroups = (QG_CONSUMERS / 32) / wpk;  // warp groups holding the same columns
+    const int wgrp = warp / wpk;
     if (GROUPED) {
         double *red = reinterpret_cast<double *>(smem + L.red);
 #pragma unroll
-        for (int m = 0; m < M; m++) red[m * QG_THREADS + tid] = accd[m];
-        __syncthreads();
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int j = 0; j < QG_CPT; j++) {
+                double v = accd[m][j];
+                for (int o = TPK; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane < TPK || TPK >= 32) red[((size_t)m * ngroups + wgrp) * TN + c0 + j * TPK] = v;
+            }
+        consumer_sync();
         if (tid < TN) {
 #pragma unroll
             for (int m = 0; m < M; m++) {
                 double s = 0.0;
-                for (int g = 0; g < nkg; g++) s += red[m * QG_THREADS + g * TN + tid];
+                for (int g = 0; g < ngroups; g++) s += red[((size_t)m * ngroups + g) * TN + tid];
                 ys[m * TN + tid] = (float)(ldexp(s, -shift[m]) * rstd[m]);
             }
         }
     } else {
         long long *red = reinterpret_cast<long long *>(smem + L.red);
 #pragma unroll
-        for (int m = 0; m < M; m++) red[m * QG_THREADS + tid] = combine_planes(acc0[m], acc1[m], acc2[m]);
-        __syncthreads();
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int j = 0; j < QG_CPT; j++) {
+                long long v = combine_planes(acc[m][j][0], acc[m][j][1], acc[m][j][2]);
+                for (int o = TPK; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane < TPK || TPK >= 32) red[((size_t)m * ngroups + wgrp) * TN + c0 + j * TPK] = v;
+            }
+        consumer_sync();
         if (tid < TN) {
 #pragma unroll
             for (int m = 0; m < M; m++) {
                 long long s = 0;
-                for (int g = 0; g < nkg; g++) s += red[m * QG_THREADS + g * TN + tid];
+                for (int g = 0; g < ngroups; g++) s += red[((size_t)m * ngroups + g) * TN + tid];
                 const float sc = (EPI == QEPI_SWIGLU && (tid & 31) >= 16) ? a.w.scale_up : a.w.scale;
                 ys[m * TN + tid] = (float)(ldexp((double)s, -shift[m]) * (double)sc * rstd[m]);
             }
         }
     }
-    __syncthreads();
+    consumer_sync();
+    if (s_failed) return;  // a bounded wait ran out: qg_error_flag is set, nothing is written
     qg_epilogue<M, EPI>(a, ys);
 }
 
@@ -389,9 +523,9 @@ int qgemv_pick_tn(int N, int K, int min_tn) {
     // tile width whose tile count fits in (#SMs x CTAs per SM).
     const DeviceProps &dp = device_props();
     const int KS = ceil_div(K, 16);
-    int per_sm = 2;
-    const size_t smem = qgemv_smem_bytes(1, KS, 64);
-    if (smem * 3 <= 200 * 1024) per_sm = 3;
+    const size_t smem = qgemv_smem_bytes(1, KS, 64) + 1024;
+    int per_sm = (int)std::min<size_t>(2, (size_t)233472 / smem);
+    per_sm = std::max(per_sm, 1);
     const int slots = dp.sm_count * per_sm;
     const int cands[5] = {16, 32, 64, 128, 256};
     for (int i = 0; i < 5; i++) {
@@ -400,6 +534,17 @@ int qgemv_pick_tn(int N, int K, int min_tn) {
         if (ceil_div(N, tn) <= slots) return tn;
     }
     return 256;
+}
+
+int qgemv_check_error() {
+    unsigned f = 0;
+    SB_CUDA_TRY(cudaMemcpyFromSymbol(&f, qg_error_flag, sizeof f));
+    if (f) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(qg_error_flag, &zero, sizeof zero);
+        return set_error(SB_ERR_TIMEOUT, "qgemv: a bounded shared-memory pipeline wait timed out");
+    }
+    return SB_OK;
 }
 
 template <int M, int EPI, bool GROUPED>
@@ -429,7 +574,7 @@ static int dispatch_m(const QGemvArgs &a, cudaStream_t st, bool pdl) {
 
 int qgemv_launch(int epi, const QGemvArgs &a, cudaStream_t st, bool pdl) {
     SB_CHECK(a.w.w != nullptr && a.x != nullptr, SB_ERR_ARG, "qgemv: null weight or input");
-    SB_CHECK(a.w.TN >= 16 && a.w.TN <= 256 && (QG_THREADS % a.w.TN) == 0, SB_ERR_SHAPE,
+    SB_CHECK(a.w.TN >= 16 && a.w.TN <= 256 && (a.w.TN & (a.w.TN - 1)) == 0, SB_ERR_SHAPE,
              "qgemv: bad tile width %d", a.w.TN);
     const bool grouped = a.w.group > 0;
     if (grouped) {

@@ -61,7 +61,7 @@ struct QGemvArgs {
     int *cand_idx = nullptr;
 };
 
-constexpr int QG_THREADS = 256;
+constexpr int QG_THREADS = 288;  // 8 consumer warps + 1 TMA producer warp
 constexpr int QG_MAX_M = 4;
 
 // Tile width for an N-column weight read by M-row GEMVs on this device.
@@ -71,6 +71,8 @@ size_t qweight_scale_count(int K, int N, int TN, int group);
 size_t qgemv_smem_bytes(int M, int KS, int TN);
 
 // Launch one GEMV.  pdl enables programmatic dependent launch.
+// qgemv_check_error() reports (and clears) a timed-out pipeline wait.
+int qgemv_check_error();
 int qgemv_launch(int epi, const QGemvArgs &a, cudaStream_t st, bool pdl);
 
 // Permute a device [K,N] int8 matrix into the packed layout.  With
