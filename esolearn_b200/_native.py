@@ -65,6 +65,8 @@ SIGNATURES = {
     "sb_argmax_rows": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
     "sb_attn_decode_paged": (C.c_int, [vp, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
                                        C.c_int, C.c_int, C.c_int, vp, vp]),
+    "sb_attn_decode_paged_noalloc": (C.c_int, [vp, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, C.c_int, vp, vp]),
     "sb_llama_create": (C.c_int, [C.POINTER(LlamaConfigC), C.POINTER(vp)]),
     "sb_llama_destroy": (C.c_int, [vp]),
     "sb_llama_init_random": (C.c_int, [vp, C.c_uint64]),

@@ -109,6 +109,24 @@ sb_status sb_attn_decode_paged(const float *q, const void *k_cache, const void *
                                const int32_t *ctx_len, int B, int n_heads, int n_kv, int head_dim,
                                int page_size, int max_ctx, float *out, void *stream);
 
+/* Same computation as sb_attn_decode_paged, but it never allocates device
+ * memory.  No counterpart in the reference: it exists for callers that
+ * cannot let the library cudaMalloc a workspace -- hosts whose device
+ * memory is owned by their own pool, and decode loops that cannot take the
+ * synchronisation of an allocation mid-step.  Its split scratch is a fixed
+ * array inside the library (16 KiB of counters, 1 MiB of partials, held on
+ * every GPU that loads the library until exit); shapes needing more
+ * (B*n_kv > 4096, or B*n_heads*splits*(head_dim+2)*4 bytes > 1 MiB, with
+ * the split count sb_attn_decode_paged would choose) fail with SB_ERR_SHAPE.
+ * The first call on a device resolves the array's address (make it before
+ * any stream capture).  Calls share the array: calls that overlap on the
+ * GPU race and must be ordered by the caller. */
+sb_status sb_attn_decode_paged_noalloc(const float *q, const void *k_cache, const void *v_cache,
+                                       int kv_dtype, const int32_t *page_table, int max_pages,
+                                       const int32_t *ctx_len, int B, int n_heads, int n_kv,
+                                       int head_dim, int page_size, int max_ctx, float *out,
+                                       void *stream);
+
 /* ---- the quantized Llama engine ----------------------------------------
  * Replaces LlamaModel (llama.rs:583-964) + LlamaKvCache (kv_cache.rs:134-145)
  * behind CausalLM (generate.rs:5-21).  Every projection is an int8 weight
