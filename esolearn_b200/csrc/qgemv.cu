@@ -13,56 +13,78 @@
 // integer dot product once, in f64, in the epilogue.  Grouped scales (32 or
 // 64 rows) are applied per group, in f64.
 //
-// Bandwidth.  One CTA owns one TN-column tile over all of K; its weights are
-// one contiguous slab (the packed layout), streamed by a producer warp with
-// 1-D TMA bulk copies (cp.async.bulk, no multicast) through a ring of
-// QG_NST x 16 KB shared-memory stages guarded by mbarriers.  The first
-// QG_NST stages are requested before the grid-dependency wait, so under
+// Data movement.  One CTA owns one TN-column tile over all of K; its weights
+// are one contiguous slab of the packed layout.  A producer warp streams the
+// slab with 1-D TMA bulk copies (cp.async.bulk, no multicast) through a ring
+// of QG_NST x 16 KB shared-memory stages guarded by mbarriers; the first
+// ring fill is requested before the grid-dependency wait, so under
 // programmatic dependent launch the weight stream starts while the previous
-// kernel is still running.  Tile widths are chosen so that every tile is
+// kernel drains.  Right after the wait the same warp fetches the activation
+// rows with one bulk copy each, so the consumers never issue scattered
+// global loads for them.  Tile widths are chosen so that every tile is
 // resident in one wave with equal work.  Eight consumer warps read the
 // stage from shared memory: each thread owns 4 columns of one k-step per
 // stage, so the three activation-plane loads serve 4 weight vectors.
 //
 // RMSNorm fusion (rmsnorm, cpu.rs:574-599): with norm_w set, the planes
 // encode x[k]*w[k] and each CTA computes rstd = 1/sqrt(mean(x^2)+eps) of the
-// whole row; y is multiplied by rstd in the epilogue.
+// whole row; y is multiplied by rstd in the epilogue.  The norm weights are
+// read before the dependency wait (they never change).
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); a wait that runs out
-// sets qg_error_flag and the kernel returns instead of hanging.
+// sets qg_error_flag and the kernel writes nothing instead of hanging.
 #include "qgemv.cuh"
 
 #include <algorithm>
 
 namespace sb {
 
-constexpr int QG_CONSUMERS = 256;            // 8 consumer warps
-constexpr int QG_STAGE = 16384;              // bytes per ring stage
-constexpr int QG_NST = 4;                    // ring stages
-constexpr int QG_CPT = 4;                    // columns per consumer thread
+constexpr int QG_CONSUMERS = 256;  // 8 consumer warps
+constexpr int QG_STAGE = 16384;    // bytes per ring stage
+constexpr int QG_NST = 4;          // ring stages
+constexpr int QG_CPT = 4;          // columns per consumer thread
 constexpr unsigned long long QG_WAIT_NS = 2000000000ull;
 
-__device__ unsigned qg_error_flag = 0;       // 1: a bounded wait ran out
+__device__ unsigned qg_error_flag = 0;  // 1: a bounded wait ran out
+
+// Epilogues whose input is RMSNorm-fused (QKV, SwiGLU, logits).
+__host__ __device__ constexpr bool epi_has_norm(int epi) {
+    return epi == QEPI_QKV || epi == QEPI_SWIGLU || epi == QEPI_LOGITS;
+}
+
+// Activation quads each consumer thread holds per prologue batch (fewer with
+// a fused norm, whose weights take registers too).
+__host__ __device__ constexpr int qg_quads_per_thread(int M, bool norm) {
+    return (M == 1 ? 6 : (M == 2 ? 4 : (M == 3 ? 2 : 1))) * (norm ? 1 : 2);
+}
+// Whole rows fit one register batch: the only case in which the producer
+// copies the f32 rows into shared memory (the planes then overwrite them).
+__host__ __device__ constexpr bool qg_row_in_smem(int M, int KS, bool norm) {
+    return KS * 4 <= qg_quads_per_thread(M, norm) * QG_CONSUMERS;
+}
 
 struct QGSmem {
-    // Offsets inside the dynamic shared memory block.
-    size_t ring, planes, red, ys, rowinfo, bars, total;
+    // Offsets inside the dynamic shared memory block.  `xp` holds the byte
+    // planes (plane (m,p) at (3m+p)*16*KS bytes); when the rows come in by
+    // bulk copy it first receives them (row m at m*64*KS bytes).  The column
+    // partial sums reuse the ring once its last stage is consumed.
+    size_t ring, xp, ys, pre, rowinfo, bars, total;
 };
 
-__host__ __device__ inline QGSmem qg_layout(int M, int KS, int TN) {
+__host__ __device__ inline QGSmem qg_layout(int M, int KS, int TN, bool norm) {
     QGSmem L;
     L.ring = 0;
-    L.planes = (size_t)QG_NST * QG_STAGE;
-    L.red = L.planes + (size_t)M * 3 * KS * 16;
-    L.ys = L.red + (size_t)M * QG_CONSUMERS * QG_CPT * 8;
-    L.rowinfo = (L.ys + (size_t)M * TN * 4 + 15) & ~(size_t)15;
+    L.xp = (size_t)QG_NST * QG_STAGE;
+    L.ys = L.xp + (size_t)M * (qg_row_in_smem(M, KS, norm) ? 64 : 48) * KS;
+    L.pre = L.ys + (size_t)M * TN * 4;  // residual tile preloaded for the RESID epilogue
+    L.rowinfo = (L.pre + (size_t)M * TN * 4 + 15) & ~(size_t)15;
     // rowinfo: rstd[M] (double), shift[M] (int), reduction scratch [8][M][2] doubles
     L.bars = L.rowinfo + (size_t)M * 16 + (size_t)8 * M * 2 * 8;
-    L.total = L.bars + 2 * QG_NST * 8;
+    L.total = L.bars + (2 * QG_NST + 1) * 8;  // full[], empty[], x
     return L;
 }
 
-size_t qgemv_smem_bytes(int M, int KS, int TN) { return qg_layout(M, KS, TN).total; }
+size_t qgemv_smem_bytes(int M, int KS, int TN, bool norm) { return qg_layout(M, KS, TN, norm).total; }
 
 // ---- mbarrier / TMA helpers --------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -148,35 +170,90 @@ __device__ __forceinline__ void load_norm_quad(const QGemvArgs &a, int q, float 
     }
 }
 
+
+// Quads (4 elements) of one activation row that each consumer thread keeps
+// in registers.  Without a fused norm the norm-weight registers hold
+// activations instead.
+template <int M, bool NORM>
+struct QgPro {
+    static constexpr int QB = qg_quads_per_thread(M, NORM);
+    float4 nv[NORM ? QB : 1];  // norm weights (loaded before the dependency wait)
+    float4 xv[M][QB];          // activations of the current batch
+};
+
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.0f, 0.0f, 0.0f, 0.0f); }
+
+template <int M, bool NORM>
+__device__ __forceinline__ void pro_load_norm(const QGemvArgs &a, int q0, QgPro<M, NORM> &P) {
+    if (!NORM) return;
+    const int K = a.w.K, nq = a.w.KS * 4;
+#pragma unroll
+    for (int j = 0; j < QgPro<M, NORM>::QB; j++) {
+        const int q = q0 + j * QG_CONSUMERS;
+        float nw[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+        if (q < nq) load_norm_quad(a, q, nw);
+        P.nv[NORM ? j : 0] = (q < nq && q * 4 < K) ? make_float4(nw[0], nw[1], nw[2], nw[3]) : f4_zero();
+    }
+}
+
+// Activations from global memory (general path) or from the rows the
+// producer copied into shared memory (xs != nullptr, one batch only).
+template <int M, bool NORM>
+__device__ __forceinline__ void pro_load_x(const QGemvArgs &a, int q0, QgPro<M, NORM> &P, const float *xs, int KS) {
+    const int nq = KS * 4, K = a.w.K;
+#pragma unroll
+    for (int j = 0; j < QgPro<M, NORM>::QB; j++) {
+        const int q = q0 + j * QG_CONSUMERS;
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (q < nq) {
+                if (xs) {
+                    if (m < a.M && q * 4 < K) {  // rows are K floats (K % 4 == 0 on this path)
+                        const float4 t = reinterpret_cast<const float4 *>(xs + (size_t)m * 16 * KS)[q];
+                        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+                    }
+                } else {
+                    load_quad<M>(a, m, q, v);
+                }
+            }
+            P.xv[m][j] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
 // Builds the fixed-point byte planes of the M activation rows in shared
-// memory and the per-row rstd / exponent.  Consumer threads only.
-template <int M>
-__device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) {
+// memory and the per-row rstd / exponent.  Consumer threads only.  P holds
+// the norm weights of the first batch, loaded before the dependency wait.
+template <int M, bool NORM>
+__device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L, QgPro<M, NORM> &P, const float *xs) {
+    constexpr int QB = QgPro<M, NORM>::QB;
     const int KS = a.w.KS, K = a.w.K;
     const int nq = KS * 4;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    uint32_t *planes = reinterpret_cast<uint32_t *>(smem + L.planes);
+    const bool one_batch = nq <= QB * QG_CONSUMERS;
+    uint32_t *planes = reinterpret_cast<uint32_t *>(smem + L.xp);
     double *rstd = reinterpret_cast<double *>(smem + L.rowinfo);
     int *shift = reinterpret_cast<int *>(smem + L.rowinfo + (size_t)M * 8);
     double *scratch = reinterpret_cast<double *>(smem + L.rowinfo + (size_t)M * 16);
 
+    // pass 1: sum of squares and max |x*w| per row, QB quads per load batch
     float ssq[M], amx[M];
 #pragma unroll
     for (int m = 0; m < M; m++) ssq[m] = 0.0f, amx[m] = 0.0f;
-#pragma unroll 8
-    for (int q = tid; q < nq; q += QG_CONSUMERS) {
-        float nw[4];
-        load_norm_quad(a, q, nw);
+    for (int q0 = tid; q0 < nq; q0 += QB * QG_CONSUMERS) {
+        if (q0 != tid) pro_load_norm<M, NORM>(a, q0, P);
+        pro_load_x<M, NORM>(a, q0, P, xs, KS);
 #pragma unroll
-        for (int m = 0; m < M; m++) {
-            float v[4];
-            load_quad<M>(a, m, q, v);
+        for (int j = 0; j < QB; j++)
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                ssq[m] = fmaf(v[i], v[i], ssq[m]);
-                amx[m] = fmaxf(amx[m], fabsf(__fmul_rn(v[i], nw[i])));
+            for (int m = 0; m < M; m++) {
+                const float4 x = P.xv[m][j];
+                const float4 w = NORM ? P.nv[NORM ? j : 0] : make_float4(1.f, 1.f, 1.f, 1.f);
+                ssq[m] = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ssq[m]))));
+                amx[m] = fmaxf(amx[m], fmaxf(fmaxf(fabsf(__fmul_rn(x.x, w.x)), fabsf(__fmul_rn(x.y, w.y))),
+                                             fmaxf(fabsf(__fmul_rn(x.z, w.z)), fabsf(__fmul_rn(x.w, w.w)))));
             }
-        }
     }
 #pragma unroll
     for (int m = 0; m < M; m++) {
@@ -187,7 +264,7 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) 
             scratch[(warp * M + m) * 2 + 1] = (double)x;
         }
     }
-    consumer_sync();
+    consumer_sync();  // also: every thread has read its x from shared memory
     if (tid < M) {
         const int m = tid;
         double s = 0.0, x = 0.0;
@@ -196,36 +273,44 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L) 
             x = fmax(x, scratch[(w * M + m) * 2 + 1]);
         }
         // rmsnorm (cpu.rs:582-588): mean of squares, rstd = 1/sqrt(mean+eps), f64.
-        rstd[m] = a.norm_w ? 1.0 / sqrt(s / (double)K + (double)a.eps) : 1.0;
+        rstd[m] = NORM ? 1.0 / sqrt(s / (double)K + (double)a.eps) : 1.0;
         int e = 0;
         if (x > 0.0) frexp(x, &e);        // x = f * 2^e, f in [0.5, 1)
         int sh = (x > 0.0) ? 22 - e : 0;  // |a * 2^sh| < 2^22
         shift[m] = sh < -126 ? -126 : (sh > 126 ? 126 : sh);
     }
     consumer_sync();
-#pragma unroll 4
-    for (int q = tid; q < nq; q += QG_CONSUMERS) {
-        float nw[4];
-        load_norm_quad(a, q, nw);
+    // pass 2: quantize to three byte planes (registers still hold a single batch)
+    for (int q0 = tid; q0 < nq; q0 += QB * QG_CONSUMERS) {
+        if (!one_batch) {
+            pro_load_norm<M, NORM>(a, q0, P);
+            pro_load_x<M, NORM>(a, q0, P, nullptr, KS);
+        }
 #pragma unroll
-        for (int m = 0; m < M; m++) {
-            float v[4];
-            load_quad<M>(a, m, q, v);
-            const float sc = __int_as_float((shift[m] + 127) << 23);  // 2^shift, exact
-            uint32_t w0 = 0, w1 = 0, w2 = 0;
+        for (int j = 0; j < QB; j++) {
+            const int q = q0 + j * QG_CONSUMERS;
+            if (q >= nq) continue;
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                // round-to-nearest-even to an integer: |t| < 2^22, so t + 1.5*2^23
-                // lands in [2^23, 2^24) where the float ulp is 1.
-                const float t = __fmul_rn(__fmul_rn(v[i], nw[i]), sc);
-                const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
-                w0 |= (uint32_t)(A & 0xff) << (8 * i);
-                w1 |= (uint32_t)((A >> 8) & 0xff) << (8 * i);
-                w2 |= (uint32_t)((A >> 16) & 0xff) << (8 * i);
+            for (int m = 0; m < M; m++) {
+                const float sc = __int_as_float((shift[m] + 127) << 23);  // 2^shift, exact
+                const float xs4[4] = {P.xv[m][j].x, P.xv[m][j].y, P.xv[m][j].z, P.xv[m][j].w};
+                const float4 wv = NORM ? P.nv[NORM ? j : 0] : make_float4(1.f, 1.f, 1.f, 1.f);
+                const float ws[4] = {wv.x, wv.y, wv.z, wv.w};
+                uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    // round-to-nearest-even to an integer: |t| < 2^22, so t + 1.5*2^23
+                    // lands in [2^23, 2^24) where the float ulp is 1.
+                    const float t = __fmul_rn(__fmul_rn(xs4[i], ws[i]), sc);
+                    const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+                    w0 |= (uint32_t)(A & 0xff) << (8 * i);
+                    w1 |= (uint32_t)((A >> 8) & 0xff) << (8 * i);
+                    w2 |= (uint32_t)((A >> 16) & 0xff) << (8 * i);
+                }
+                planes[(size_t)(m * 3 + 0) * nq + q] = w0;
+                planes[(size_t)(m * 3 + 1) * nq + q] = w1;
+                planes[(size_t)(m * 3 + 2) * nq + q] = w2;
             }
-            planes[(size_t)(m * 3 + 0) * nq + q] = w0;
-            planes[(size_t)(m * 3 + 1) * nq + q] = w1;
-            planes[(size_t)(m * 3 + 2) * nq + q] = w2;
         }
     }
 }
@@ -250,10 +335,9 @@ __device__ __forceinline__ void dot16(const uint4 &w, const uint4 &p0, const uin
     a2 = dp4a_ss(w.w, p2.w, a2);
 }
 
-
 template <int M, int EPI>
-__device__ void qg_epilogue(const QGemvArgs &a, const float *ys) {
-    const int TN = a.w.TN, tile = blockIdx.x, tid = threadIdx.x;
+__device__ void qg_epilogue(const QGemvArgs &a, const float *ys, int tile, const float *pre) {
+    const int TN = a.w.TN, tid = threadIdx.x;
     for (int it = tid; it < M * TN; it += QG_CONSUMERS) {
         const int m = it / TN, c = it - m * TN;
         if (m >= a.M) continue;
@@ -266,7 +350,7 @@ __device__ void qg_epilogue(const QGemvArgs &a, const float *ys) {
         } else if (EPI == QEPI_RESID) {
             if (n < a.w.N) {
                 float *o = a.out + (size_t)m * a.ldo + n;
-                *o = __fadd_rn(*o, y);
+                *o = __fadd_rn(pre ? pre[m * TN + c] : *o, y);
             }
         } else if (EPI == QEPI_SWIGLU) {
             const int within = n & 31;
@@ -341,61 +425,106 @@ __device__ void qg_epilogue(const QGemvArgs &a, const float *ys) {
 }
 
 
+// Reduce the CTA's partial sums of one tile (stages [first, first+n) of it),
+// then either finish the tile (epilogue) or, when other CTAs hold the rest of
+// its K range, add the exact int64 partial to the tile accumulator; the CTA
+// that completes the tile's stage count runs the epilogue.  Every consumer
+// thread calls this at the same points (it contains consumer barriers).
+
 template <int M, int EPI, bool GROUPED>
-__global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a) {
+__global__ void __launch_bounds__(QG_THREADS, M <= 2 ? 2 : 1) qgemv_kernel(const QGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int KS = a.w.KS, TN = a.w.TN;
-    const QGSmem L = qg_layout(M, KS, TN);
+    const int KS = a.w.KS, TN = a.w.TN, K = a.w.K;
+    constexpr bool NORM = epi_has_norm(EPI);
+    const QGSmem L = qg_layout(M, KS, TN, NORM);
     const int tid = threadIdx.x;
+    const int tile = blockIdx.x;
     const int TPK = TN / QG_CPT;              // threads per k-step
     const int KPS = QG_STAGE / (TN * 16);     // k-steps per stage (= QG_CONSUMERS / TPK)
     const int nstages = (KS + KPS - 1) / KPS;
     const size_t slab_bytes = (size_t)KS * TN * 16;
-    const uint8_t *slab = reinterpret_cast<const uint8_t *>(a.w.w + (size_t)blockIdx.x * KS * TN);
-    const uint32_t bars = smem_u32(smem + L.bars);  // full[QG_NST], then empty[QG_NST]
+    const uint8_t *slab = reinterpret_cast<const uint8_t *>(a.w.w + (size_t)tile * KS * TN);
+    const uint32_t bars = smem_u32(smem + L.bars);  // full[QG_NST], empty[QG_NST], x
+    const uint32_t xbar = bars + 8 * (2 * QG_NST);
     const uint32_t ring = smem_u32(smem + L.ring);
+    // The activation rows come in by TMA when they are f32 rows of a whole
+    // number of 16-byte chunks and fit one register batch of the prologue.
+    const bool xtma = !a.x_bf16 && (K & 3) == 0 && (a.ldx & 3) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0) &&
+                      qg_row_in_smem(M, KS, NORM);
+    __shared__ int s_failed;
 
     if (tid == 0) {
         for (int i = 0; i < QG_NST; i++) {
-            mbar_init(bars + 8 * i, 1);                              // full: producer arrival + tx bytes
-            mbar_init(bars + 8 * (QG_NST + i), QG_CONSUMERS / 32);   // empty: one arrival per consumer warp
+            mbar_init(bars + 8 * i, 1);                            // full: producer arrival + tx bytes
+            mbar_init(bars + 8 * (QG_NST + i), QG_CONSUMERS / 32);  // empty: one arrival per consumer warp
         }
+        mbar_init(xbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_failed = 0;
     }
     __syncthreads();
     pdl_launch_dependents();
 
     if (tid >= QG_CONSUMERS) {
-        // ---- producer warp: stream the slab through the ring
+        // ---- producer warp
         if (tid == QG_CONSUMERS) {
-            bool ok = true;
-            for (int s = 0; s < nstages && ok; s++) {
+            const int first = min(nstages, QG_NST);
+            for (int s = 0; s < first; s++) {  // weights never change: before the dependency wait
+                const uint32_t bytes = (uint32_t)min((size_t)QG_STAGE, slab_bytes - (size_t)s * QG_STAGE);
+                mbar_expect_tx(bars + 8 * s, bytes);
+                tma_load_1d(ring + s * QG_STAGE, slab + (size_t)s * QG_STAGE, bytes, bars + 8 * s);
+            }
+            pdl_wait();
+            if (xtma) {
+                const uint32_t row = (uint32_t)K * 4;
+                mbar_expect_tx(xbar, row * (uint32_t)a.M);
+                for (int m = 0; m < a.M; m++)
+                    tma_load_1d(smem_u32(smem + L.xp + (size_t)m * 64 * KS),
+                                reinterpret_cast<const float *>(a.x) + (size_t)m * a.ldx, row, xbar);
+            }
+            for (int s = QG_NST; s < nstages; s++) {
                 const int slot = s % QG_NST;
-                if (s == QG_NST) pdl_wait();  // first ring fill precedes the dependency wait
-                if (s >= QG_NST && !mbar_wait(bars + 8 * (QG_NST + slot), ((s / QG_NST) - 1) & 1)) {
+                if (!mbar_wait(bars + 8 * (QG_NST + slot), ((s / QG_NST) - 1) & 1)) {
                     atomicOr(&qg_error_flag, 1u);
-                    ok = false;
                     break;
                 }
-                const size_t off = (size_t)s * QG_STAGE;
-                const uint32_t bytes = (uint32_t)std::min<size_t>(QG_STAGE, slab_bytes - off);
+                const uint32_t bytes = (uint32_t)min((size_t)QG_STAGE, slab_bytes - (size_t)s * QG_STAGE);
                 mbar_expect_tx(bars + 8 * slot, bytes);
-                tma_load_1d(ring + slot * QG_STAGE, slab + off, bytes, bars + 8 * slot);
+                tma_load_1d(ring + slot * QG_STAGE, slab + (size_t)s * QG_STAGE, bytes, bars + 8 * slot);
             }
-            if (nstages <= QG_NST) pdl_wait();
         }
         return;
     }
 
     // ---- consumer warps
+    QgPro<M, NORM> pro;
+    pro_load_norm<M, NORM>(a, tid, pro);  // norm weights never change: load before the wait
     pdl_wait();
-    qg_prologue<M>(a, smem, L);
+    // RESID: read the residual tile now, so the epilogue does not wait for it.
+    float *pre = nullptr;
+    if (EPI == QEPI_RESID) {
+        pre = reinterpret_cast<float *>(smem + L.pre);
+        for (int it = tid; it < M * TN; it += QG_CONSUMERS) {
+            const int m = it / TN, n = tile * TN + (it - m * TN);
+            pre[it] = (m < a.M && n < a.w.N) ? a.out[(size_t)m * a.ldo + n] : 0.0f;
+        }
+    }
+    // A timed-out wait stops all further waiting and computing, but every
+    // thread still makes the same consumer-barrier calls so none blocks.
+    bool failed = false;
+    if (xtma && !mbar_wait(xbar, 0)) {
+        atomicOr(&qg_error_flag, 1u);
+        s_failed = 1;
+        failed = true;
+    }
+    qg_prologue<M, NORM>(a, smem, L, pro, xtma ? reinterpret_cast<const float *>(smem + L.xp) : nullptr);
     consumer_sync();
 
-    const uint4 *planes4 = reinterpret_cast<const uint4 *>(smem + L.planes);
+    const uint4 *planes4 = reinterpret_cast<const uint4 *>(smem + L.xp);
     const uint4 *ring4 = reinterpret_cast<const uint4 *>(smem + L.ring);
     const int ksl = tid / TPK, c0 = tid % TPK;
-    const int lane = tid & 31;
+    const int lane = tid & 31, warp = tid >> 5;
     int acc[M][QG_CPT][3];
     double accd[M][QG_CPT];
 #pragma unroll
@@ -404,22 +533,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a)
         for (int j = 0; j < QG_CPT; j++) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = 0, accd[m][j] = 0.0;
     const int R = GROUPED ? a.w.group / 16 : 1;
     const int NG = GROUPED ? KS / R : 0;
-    const float *gs = GROUPED ? a.w.gscale + (size_t)blockIdx.x * NG * TN + c0 : nullptr;
+    const float *gs = GROUPED ? a.w.gscale + (size_t)tile * NG * TN + c0 : nullptr;
 
-    // A timed-out wait leaves the stage loop early, but the thread still
-    // passes every consumer barrier below so that no warp blocks forever.
-    __shared__ int s_failed;
-    if (tid == 0) s_failed = 0;
-    consumer_sync();
+    int slot = 0, phase = 0;
     for (int s = 0; s < nstages; s++) {
-        const int slot = s % QG_NST;
-        if (!mbar_wait(bars + 8 * slot, (s / QG_NST) & 1)) {
+        if (!failed && !mbar_wait(bars + 8 * slot, phase)) {
             atomicOr(&qg_error_flag, 1u);
             s_failed = 1;
-            break;
+            failed = true;
         }
         const int ks = s * KPS + ksl;
-        if (ks < KS) {
+        if (!failed && ks < KS) {
             const uint4 *wst = ring4 + (size_t)slot * (QG_STAGE / 16) + ksl * TN + c0;
             uint4 w[QG_CPT];
 #pragma unroll
@@ -445,20 +569,22 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a)
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(bars + 8 * (QG_NST + slot));
+        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (QG_NST + slot));
+        if (++slot == QG_NST) slot = 0, phase ^= 1;
     }
-    // Reduce the KPS partial sums of every column in a fixed order: first
-    // across the lanes of a warp that share columns (shuffles), then across
-    // warps through shared memory.
+
+    // Reduce the partial sums of every column in a fixed order: across the
+    // lanes of a warp that share columns (shuffles), then across warps
+    // through shared memory (the ring, whose last stage has been consumed).
+    consumer_sync();
     const double *rstd = reinterpret_cast<const double *>(smem + L.rowinfo);
     const int *shift = reinterpret_cast<const int *>(smem + L.rowinfo + (size_t)M * 8);
     float *ys = reinterpret_cast<float *>(smem + L.ys);
-    const int warp = tid >> 5;
-    const int wpk = TPK >= 32 ? TPK / 32 : 1;      // warps spanning one k-step
-    const int ngroups = (QG_CONSUMERS / 32) / wpk;  // warp groups holding the same columns
+    const int wpk = TPK >= 32 ? TPK / 32 : 1;       // warps spanning one k-step
+    const int ngroups = (QG_CONSUMERS / 32) / wpk;   // warp groups holding the same columns
     const int wgrp = warp / wpk;
     if (GROUPED) {
-        double *red = reinterpret_cast<double *>(smem + L.red);
+        double *red = reinterpret_cast<double *>(smem + L.ring);
 #pragma unroll
         for (int m = 0; m < M; m++)
 #pragma unroll
@@ -471,13 +597,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a)
         if (tid < TN) {
 #pragma unroll
             for (int m = 0; m < M; m++) {
-                double s = 0.0;
-                for (int g = 0; g < ngroups; g++) s += red[((size_t)m * ngroups + g) * TN + tid];
-                ys[m * TN + tid] = (float)(ldexp(s, -shift[m]) * rstd[m]);
+                double t = 0.0;
+                for (int g = 0; g < ngroups; g++) t += red[((size_t)m * ngroups + g) * TN + tid];
+                ys[m * TN + tid] = (float)(ldexp(t, -shift[m]) * rstd[m]);
             }
         }
     } else {
-        long long *red = reinterpret_cast<long long *>(smem + L.red);
+        long long *red = reinterpret_cast<long long *>(smem + L.ring);
 #pragma unroll
         for (int m = 0; m < M; m++)
 #pragma unroll
@@ -490,16 +616,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QGemvArgs a)
         if (tid < TN) {
 #pragma unroll
             for (int m = 0; m < M; m++) {
-                long long s = 0;
-                for (int g = 0; g < ngroups; g++) s += red[((size_t)m * ngroups + g) * TN + tid];
+                long long t = 0;
+                for (int g = 0; g < ngroups; g++) t += red[((size_t)m * ngroups + g) * TN + tid];
                 const float sc = (EPI == QEPI_SWIGLU && (tid & 31) >= 16) ? a.w.scale_up : a.w.scale;
-                ys[m * TN + tid] = (float)(ldexp((double)s, -shift[m]) * (double)sc * rstd[m]);
+                ys[m * TN + tid] = (float)(ldexp((double)t, -shift[m]) * (double)sc * rstd[m]);
             }
         }
     }
     consumer_sync();
     if (s_failed) return;  // a bounded wait ran out: qg_error_flag is set, nothing is written
-    qg_epilogue<M, EPI>(a, ys);
+    qg_epilogue<M, EPI>(a, ys, tile, pre);
 }
 
 // ---------------------------------------------------------------------------
@@ -523,8 +649,8 @@ int qgemv_pick_tn(int N, int K, int min_tn) {
     // tile width whose tile count fits in (#SMs x CTAs per SM).
     const DeviceProps &dp = device_props();
     const int KS = ceil_div(K, 16);
-    const size_t smem = qgemv_smem_bytes(1, KS, 64) + 1024;
-    int per_sm = (int)std::min<size_t>(2, (size_t)233472 / smem);
+    const size_t smem = qgemv_smem_bytes(1, KS, 64, false) + 1024;
+    int per_sm = (int)std::min<size_t>(2, (size_t)dp.max_smem_optin / smem);
     per_sm = std::max(per_sm, 1);
     const int slots = dp.sm_count * per_sm;
     const int cands[5] = {16, 32, 64, 128, 256};
@@ -549,7 +675,7 @@ int qgemv_check_error() {
 
 template <int M, int EPI, bool GROUPED>
 static int launch_inst(const QGemvArgs &a, cudaStream_t st, bool pdl) {
-    const size_t smem = qgemv_smem_bytes(M, a.w.KS, a.w.TN);
+    const size_t smem = qgemv_smem_bytes(M, a.w.KS, a.w.TN, epi_has_norm(EPI));
     auto kern = qgemv_kernel<M, EPI, GROUPED>;
     static int limit[64] = {};
     int dev = 0;
@@ -576,6 +702,7 @@ int qgemv_launch(int epi, const QGemvArgs &a, cudaStream_t st, bool pdl) {
     SB_CHECK(a.w.w != nullptr && a.x != nullptr, SB_ERR_ARG, "qgemv: null weight or input");
     SB_CHECK(a.w.TN >= 16 && a.w.TN <= 256 && (a.w.TN & (a.w.TN - 1)) == 0, SB_ERR_SHAPE,
              "qgemv: bad tile width %d", a.w.TN);
+    SB_CHECK(a.norm_w == nullptr || epi_has_norm(epi), SB_ERR_ARG, "qgemv: epilogue %d takes no fused RMSNorm", epi);
     const bool grouped = a.w.group > 0;
     if (grouped) {
         SB_CHECK(a.w.group == 32 || a.w.group == 64, SB_ERR_SHAPE, "qgemv: group %d not 32/64", a.w.group);

@@ -68,7 +68,7 @@ constexpr int QG_MAX_M = 4;
 int qgemv_pick_tn(int N, int K, int min_tn);
 size_t qweight_bytes(int K, int N, int TN);
 size_t qweight_scale_count(int K, int N, int TN, int group);
-size_t qgemv_smem_bytes(int M, int KS, int TN);
+size_t qgemv_smem_bytes(int M, int KS, int TN, bool norm);
 
 // Launch one GEMV.  pdl enables programmatic dependent launch.
 // qgemv_check_error() reports (and clears) a timed-out pipeline wait.
