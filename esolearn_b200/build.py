@@ -9,6 +9,7 @@ import glob
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -33,7 +34,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     os.makedirs(OBJ, exist_ok=True)
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     headers = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(ROOT, "include", "sb_api.h")]
-    objs = []
+    objs, cmds = [], []
     for src in sources:
         obj = os.path.join(OBJ, os.path.basename(src) + ".o")
         objs.append(obj)
@@ -41,9 +42,21 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
             cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
             if ptxas_info:
                 cmd.insert(1, "-Xptxas=-v")
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append(cmd)
+    # Translation units compile independently; the persistent decode step's
+    # instantiation units dominate, so they run side by side.
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        return subprocess.run(cmd, capture_output=True, text=True)
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(run, cmds))
+    for cmd, r in zip(cmds, results):
+        if r.stdout or r.stderr:
+            sys.stdout.write(r.stdout)
+            sys.stderr.write(r.stderr)
+        if r.returncode != 0:
+            raise subprocess.CalledProcessError(r.returncode, cmd)
     if force or _needs(LIB, objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
         if verbose:

@@ -16,11 +16,17 @@
 // CUDA graph and replayed; consecutive kernels use programmatic dependent
 // launch so the next GEMV starts streaming its weights while the previous
 // kernel drains.
+//
+// A single sequence (batch 1) runs instead as one persistent cooperative
+// kernel per step (decode_step.cu) whenever the shape allows it; every
+// packed weight then uses the 128-column tiles that kernel streams.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_step.cuh"
 #include "misc.cuh"
 #include "qgemv.cuh"
 
@@ -85,6 +91,17 @@ struct sb_llama {
     bool trace = false;
     float *trace_buf = nullptr;
     int trace_batch = 0;
+
+    // persistent batch-1 step
+    bool ds_ok = false;
+    int ds_chunk = 0, ds_nst = 0;
+    DsLayer *ds_layers = nullptr;  // device copy of the per-layer weight table
+    float *ds_x = nullptr;
+    long long *ds_acc = nullptr;
+    int ds_acc_n = 0;
+    float *ds_part = nullptr, *ds_cand_val = nullptr;
+    int *ds_cand_idx = nullptr;
+    unsigned *ds_sync = nullptr;
 };
 
 namespace {
@@ -110,7 +127,7 @@ int make_qweight(sb_llama *m, QWeightDesc &d, int K, int N, int min_tn) {
     d.K = K;
     d.N = N;
     d.KS = ceil_div(K, 16);
-    d.TN = qgemv_pick_tn(N, K, min_tn);
+    d.TN = m->ds_ok ? DS_TN : qgemv_pick_tn(N, K, min_tn);
     d.ntiles = ceil_div(N, d.TN);
     d.group = 0;
     void *p = nullptr;
@@ -290,6 +307,80 @@ int check_ready(sb_llama *m) {
 
 int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const int32_t *plen);
 
+// One batch-1 step as the persistent kernel (m->ds_ok).
+int ds_step(sb_llama *m) {
+    std::vector<DsLayer> tab(m->L);
+    for (int l = 0; l < m->L; l++) {
+        const sb_llama::Layer &ly = m->layers[l];
+        const QWeightDesc *w[4] = {&ly.qkv, &ly.o, &ly.gu, &ly.down};
+        for (int i = 0; i < 4; i++) {
+            tab[l].w[i] = w[i]->w;
+            tab[l].scale[i] = w[i]->scale;
+        }
+        tab[l].scale_up = ly.gu.scale_up;
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(m->ds_layers, tab.data(), sizeof(DsLayer) * tab.size(), cudaMemcpyHostToDevice, m->st));
+    DsArgs a;
+    a.L = m->L;
+    a.h = m->h;
+    a.F = m->F;
+    a.V = m->V;
+    a.nh = m->nh;
+    a.nkv = m->nkv;
+    a.hd = m->hd;
+    a.q_dim = m->q_dim;
+    a.kv_dim = m->kv_dim;
+    a.ks_h = ceil_div(m->h, 16);
+    a.ks_q = ceil_div(m->q_dim, 16);
+    a.ks_f = ceil_div(m->F, 16);
+    const sb_llama::Layer &l0 = m->layers[0];
+    a.nt_qkv = l0.qkv.ntiles;
+    a.nt_o = l0.o.ntiles;
+    a.nt_gu = l0.gu.ntiles;
+    a.nt_down = l0.down.ntiles;
+    a.nt_lm = m->lm.ntiles;
+    a.layers = m->ds_layers;
+    a.lm_w = m->lm.w;
+    a.lm_scale = m->lm.scale;
+    a.embed = m->embed;
+    a.norm_in = m->norm_in;
+    a.norm_post = m->norm_post;
+    a.norm_final = m->norm_final;
+    a.eps = m->cfg.rms_norm_eps;
+    a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.layer_kv_bytes = m->layer_kv_elems * (m->kv_f32 ? 4 : 2);
+    a.kv_f32 = m->kv_f32;
+    a.page_size = m->P;
+    a.max_pages = m->pps;
+    a.max_pos = m->cfg.max_seq_len;
+    a.chunk = m->ds_chunk;
+    a.page_table = m->page_table;
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    a.seq = m->seq;
+    a.x = m->ds_x;
+    a.acc = m->ds_acc;
+    a.acc_n = m->ds_acc_n;
+    a.part = m->ds_part;
+    a.act = m->act;
+    a.logits = m->logits;
+    a.cand_val = m->ds_cand_val;
+    a.cand_idx = m->ds_cand_idx;
+    a.sync = m->ds_sync;
+    a.trace = m->trace ? m->trace_buf : nullptr;
+    a.nst = m->ds_nst;
+    a.mtab_bytes = ds_mtab_bytes(m->nh, m->nkv);
+    return ds_launch(a, m->nh / m->nkv, m->st);
+}
+
+// Errors a bounded device wait may have left behind.
+int check_device_errors(sb_llama *m) {
+    if (m->ds_ok) SB_TRY(ds_check_error(m->ds_sync, m->st));
+    return qgemv_check_error();
+}
+
 int get_graph(sb_llama *m, int M, cudaGraphExec_t *out) {
     if (m->graphs[M]) {
         *out = m->graphs[M];
@@ -371,6 +462,22 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         return fail(set_error(SB_ERR_CUDA, "cudaStreamCreate failed"));
 
     int rc = SB_OK;
+    {
+        int chunk = 0;
+        if (ds_supported(m->h, m->F, m->q_dim, hd, m->nh / m->nkv, m->kv_f32, m->P, &chunk)) {
+            const int ksmax = ceil_div(std::max(std::max(m->h, m->F), m->q_dim), 16);
+            int nst = 0;
+            size_t smem = 0;
+            int coop = 0;
+            cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->dev);
+            if (coop && ds_plan(ksmax, m->nh / m->nkv, hd, chunk, m->kv_f32, ds_mtab_bytes(m->nh, m->nkv), &nst, &smem) == SB_OK &&
+                nst >= 3) {
+                m->ds_ok = true;
+                m->ds_chunk = chunk;
+                m->ds_nst = nst;
+            }
+        }
+    }
     m->layers.resize(m->L);
     const int gu_cols = ceil_div(m->F, 16) * 32;  // gate/up interleaved in blocks of 16
     for (int l = 0; l < m->L && rc == SB_OK; l++) {
@@ -449,6 +556,19 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
     m->seq.ngen = m->d_ngen;
     m->seq.max_gen = c.max_seq_len;
     m->seq.last = m->d_last;
+    if (m->ds_ok) {
+        const int G = ds_grid();
+        int nt = m->lm.ntiles;
+        for (const auto &ly : m->layers) nt = std::max({nt, ly.qkv.ntiles, ly.o.ntiles, ly.gu.ntiles, ly.down.ntiles});
+        m->ds_acc_n = nt * DS_TN;
+        if ((rc = dalloc_t(m, &m->ds_layers, (size_t)m->L)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_x, (size_t)2 * m->h)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_acc, (size_t)3 * m->ds_acc_n)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_part, ds_part_floats(m->nkv, m->nh / m->nkv, m->hd))) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_cand_val, (size_t)G)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_cand_idx, (size_t)G)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_sync, 4)) != SB_OK) return fail(rc);
+    }
     if ((rc = dalloc_t(m, &m->trace_buf, (size_t)m->L * B * m->h)) != SB_OK) return fail(rc);
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     *out = m;
@@ -692,7 +812,10 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
     SB_TRY(check_ready(m));
     std::vector<int32_t> zero(batch, 0);
     SB_TRY(set_state(m, batch, tokens, pos, zero.data()));
-    if (m->trace) {
+    if (batch == 1 && m->ds_ok) {
+        SB_TRY(ds_step(m));
+        if (m->trace) m->trace_batch = 1;
+    } else if (m->trace) {
         SB_TRY(enqueue_step(m, batch, m->st, false, true));
         m->trace_batch = batch;
     } else {
@@ -708,7 +831,7 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
                                     m->st));
     if (argmax) SB_CUDA_TRY(cudaMemcpyAsync(argmax, m->d_last, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
-    return qgemv_check_error();
+    return check_device_errors(m);
 }
 
 sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt) {
@@ -718,8 +841,10 @@ sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_p
     for (size_t i = 0; i < (size_t)batch * n_prompt; i++)
         SB_CHECK(prompts[i] >= 0 && prompts[i] < m->V, SB_ERR_ARG, "prompt token %d outside vocab", prompts[i]);
     SB_TRY(check_ready(m));
-    cudaGraphExec_t g = nullptr;
-    SB_TRY(get_graph(m, batch, &g));
+    if (!(batch == 1 && m->ds_ok)) {
+        cudaGraphExec_t g = nullptr;
+        SB_TRY(get_graph(m, batch, &g));
+    }
     for (int b = 0; b < batch; b++)
         SB_CUDA_TRY(cudaMemcpyAsync(m->d_prompt + (size_t)b * m->cfg.max_seq_len, prompts + (size_t)b * n_prompt,
                                     sizeof(int) * n_prompt, cudaMemcpyHostToDevice, m->st));
@@ -736,8 +861,12 @@ sb_status sb_llama_step(sb_llama *m, int n_steps) {
     cudaGraphExec_t g = nullptr;
     SB_CHECK(n_steps >= 0 && (long long)m->steps + n_steps <= m->cfg.max_seq_len, SB_ERR_SHAPE,
              "sb_llama_step: %d + %d steps exceed the cache (%d positions)", m->steps, n_steps, m->cfg.max_seq_len);
-    SB_TRY(get_graph(m, m->active, &g));
-    for (int i = 0; i < n_steps; i++) SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
+    if (m->active == 1 && m->ds_ok) {
+        for (int i = 0; i < n_steps; i++) SB_TRY(ds_step(m));
+    } else {
+        SB_TRY(get_graph(m, m->active, &g));
+        for (int i = 0; i < n_steps; i++) SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
+    }
     m->steps += n_steps;
     return SB_OK;
 }
@@ -745,7 +874,7 @@ sb_status sb_llama_step(sb_llama *m, int n_steps) {
 sb_status sb_llama_tokens(sb_llama *m, int32_t *out, int max_tokens, int *n_out) {
     SB_CHECK(m && out && n_out && m->active > 0, SB_ERR_STATE, "sb_llama_tokens: no active batch");
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
-    SB_TRY(qgemv_check_error());
+    SB_TRY(check_device_errors(m));
     std::vector<int> ngen(m->active);
     SB_CUDA_TRY(cudaMemcpy(ngen.data(), m->d_ngen, sizeof(int) * m->active, cudaMemcpyDeviceToHost));
     int n = max_tokens;

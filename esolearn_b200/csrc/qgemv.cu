@@ -34,6 +34,7 @@
 // Every mbarrier wait is bounded (2 s of %globaltimer); a wait that runs out
 // sets qg_error_flag and the kernel writes nothing instead of hanging.
 #include "qgemv.cuh"
+#include "pipeline.cuh"
 
 #include <algorithm>
 
@@ -43,9 +44,10 @@ constexpr int QG_CONSUMERS = 256;  // 8 consumer warps
 constexpr int QG_STAGE = 16384;    // bytes per ring stage
 constexpr int QG_NST = 4;          // ring stages
 constexpr int QG_CPT = 4;          // columns per consumer thread
-constexpr unsigned long long QG_WAIT_NS = 2000000000ull;
 
-__device__ unsigned qg_error_flag = 0;  // 1: a bounded wait ran out
+__device__ unsigned qg_error_flag = 0;
+
+__device__ __forceinline__ void consumer_sync() { named_sync<QG_CONSUMERS>(); }  // 1: a bounded wait ran out
 
 // Epilogues whose input is RMSNorm-fused (QKV, SwiGLU, logits).
 __host__ __device__ constexpr bool epi_has_norm(int epi) {
@@ -85,51 +87,6 @@ __host__ __device__ inline QGSmem qg_layout(int M, int KS, int TN, bool norm) {
 }
 
 size_t qgemv_smem_bytes(int M, int KS, int TN, bool norm) { return qg_layout(M, KS, TN, norm).total; }
-
-// ---- mbarrier / TMA helpers --------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait for the phase with the given parity; false when it timed out.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    uint64_t t0 = 0;
-    for (uint32_t it = 0;; it++) {
-        uint32_t done;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if ((it & 63) == 0) {
-            const uint64_t t = global_ns();
-            if (it == 0) t0 = t;
-            else if (t - t0 > QG_WAIT_NS) return false;
-        }
-    }
-}
-// 1-D bulk copy global -> shared, completion counted on an mbarrier.
-__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(QG_CONSUMERS) : "memory"); }
 
 template <int M>
 __device__ __forceinline__ void load_quad(const QGemvArgs &a, int m, int q, float v[4]) {
@@ -313,26 +270,6 @@ __device__ void qg_prologue(const QGemvArgs &a, uint8_t *smem, const QGSmem &L, 
             }
         }
     }
-}
-
-__device__ __forceinline__ long long combine_planes(int a0, int a1, int a2) {
-    return (long long)a0 + ((long long)a1 << 8) + ((long long)a2 << 16);
-}
-
-__device__ __forceinline__ void dot16(const uint4 &w, const uint4 &p0, const uint4 &p1, const uint4 &p2, int &a0,
-                                      int &a1, int &a2) {
-    a0 = dp4a_su(w.x, p0.x, a0);
-    a0 = dp4a_su(w.y, p0.y, a0);
-    a0 = dp4a_su(w.z, p0.z, a0);
-    a0 = dp4a_su(w.w, p0.w, a0);
-    a1 = dp4a_su(w.x, p1.x, a1);
-    a1 = dp4a_su(w.y, p1.y, a1);
-    a1 = dp4a_su(w.z, p1.z, a1);
-    a1 = dp4a_su(w.w, p1.w, a1);
-    a2 = dp4a_ss(w.x, p2.x, a2);
-    a2 = dp4a_ss(w.y, p2.y, a2);
-    a2 = dp4a_ss(w.z, p2.z, a2);
-    a2 = dp4a_ss(w.w, p2.w, a2);
 }
 
 template <int M, int EPI>
@@ -599,7 +536,7 @@ __global__ void __launch_bounds__(QG_THREADS, M <= 2 ? 2 : 1) qgemv_kernel(const
             for (int m = 0; m < M; m++) {
                 double t = 0.0;
                 for (int g = 0; g < ngroups; g++) t += red[((size_t)m * ngroups + g) * TN + tid];
-                ys[m * TN + tid] = (float)(ldexp(t, -shift[m]) * rstd[m]);
+                ys[m * TN + tid] = (float)(t * pow2_neg(shift[m]) * rstd[m]);
             }
         }
     } else {
@@ -619,7 +556,7 @@ __global__ void __launch_bounds__(QG_THREADS, M <= 2 ? 2 : 1) qgemv_kernel(const
                 long long t = 0;
                 for (int g = 0; g < ngroups; g++) t += red[((size_t)m * ngroups + g) * TN + tid];
                 const float sc = (EPI == QEPI_SWIGLU && (tid & 31) >= 16) ? a.w.scale_up : a.w.scale;
-                ys[m * TN + tid] = (float)(ldexp((double)t, -shift[m]) * (double)sc * rstd[m]);
+                ys[m * TN + tid] = gemv_out(t, gemv_factor(shift[m], sc, rstd[m]));
             }
         }
     }
