@@ -6,13 +6,19 @@ Workload: Llama-2-7B-shape random-init int8 model (dim
 of every sequence: K timed steps follow the prompt and W warm-up steps.
 
 * value      -- decode tokens/s with weights and KV resident in HBM (CUDA
-                events on the engine stream around K graph replays).
+                events on the engine stream around K steps; at batch 1 each
+                step is one launch of the persistent decode-step kernel).
 * e2e        -- the same metric through the reference-facing C-ABI call
                 sb_llama_forward (token id from pinned host memory in, argmax
                 token id back to the host, every step).
-* roofline   -- HBM bound: int8 weight bytes streamed by the GEMV launches of
-                a step divided by their CUDA-event duration (eager profile
-                pass of the same step), against MEASURED_PEAKS.json.
+* roofline   -- HBM bound.  Batch 1: the algorithmic bytes of one launch of
+                the persistent step kernel (all int8 weights + the K/V rows
+                of the context) divided by its average launch duration (the
+                timed region above), against MEASURED_PEAKS.json.  Larger
+                batches run per-operation kernels: int8 weight bytes of the
+                GEMV launches over their eager per-kernel event time.
+                traffic -- DRAM bytes of one launch from an ncu capture
+                (profiles/decode_step_7b_bs1_traffic.json).
 * cpu_baseline -- the reference's CPU path (the oracle restatement of
                 cpu.rs) timed on this host on a bounded sample, scaled to a
                 full 7B token.
@@ -51,7 +57,7 @@ def read_peaks():
 
 
 def read_traffic():
-    p = os.path.join(ROOT, "profiles", "qgemv_7b_bs1_traffic.json")
+    p = os.path.join(ROOT, "profiles", "decode_step_7b_bs1_traffic.json")
     if os.path.exists(p):
         with open(p) as f:
             return json.load(f)
@@ -210,15 +216,27 @@ def run_ours(args, rank: int, world: int, dist):
     ctx_mid = args.prompt + W + K / 2
     wbytes, kv_per_pos = model.step_bytes()
     value = world * B * K / (ms / 1000.0)
-
-    # kernel profile pass: the same steps eagerly, one CUDA event pair per kernel
-    prof = [model.profile_step() for _ in range(4)]
-    gemv_ms = float(np.median([p[0] for p in prof]))
-    attn_ms = float(np.median([p[1] for p in prof]))
-    launches_per_step = prof[0][3]
-    achieved = wbytes / (gemv_ms / 1000.0) / 1e9
+    launches_per_step = model.step_launches(B)
     peak, peak_kind = read_peaks()
-    traffic = read_traffic()
+    step_alg_bytes = wbytes + kv_per_pos * ctx_mid * B
+    if launches_per_step == 1:
+        # one persistent kernel per step: its average launch duration is the step time
+        traffic = read_traffic()
+        achieved = step_alg_bytes / (ms / K / 1000.0) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": peak_kind, "kernel": "decode_step_kernel (persistent: every projection + attention)",
+                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                "traffic_context": traffic.get("context") if traffic else None,
+                "algorithmic_bytes_per_launch": step_alg_bytes, "launch_ms": ms / K}
+    else:
+        # per-operation kernels: eager pass, one CUDA event pair per kernel
+        prof = [model.profile_step() for _ in range(4)]
+        gemv_ms = float(np.median([p[0] for p in prof]))
+        achieved = wbytes / (gemv_ms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": peak_kind, "kernel": "qgemv_kernel (all int8 projections of a step)", "traffic": None,
+                "algorithmic_bytes_per_step": wbytes, "gemv_ms_per_step": gemv_ms,
+                "attn_ms_per_step": float(np.median([p[1] for p in prof]))}
 
     # e2e: reference-facing call with host buffers every step (token in, argmax out)
     e2e = None
@@ -254,15 +272,10 @@ def run_ours(args, rank: int, world: int, dist):
         "config": {"workload": "llama2-7b-shape int8 decode (BASELINE configs[2])", "batch": B, "prompt": args.prompt,
                    "context_mid": ctx_mid, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "weights 6.6 GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
-                   "graph": "CUDA graph per step, programmatic dependent launch"},
+                   "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else
+                              "CUDA graph of per-operation kernels per step, programmatic dependent launch")},
         "gpu_launches": launches_per_step * K,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "kernel": "qgemv_kernel (all int8 projections of a step)",
-                     "traffic": traffic.get("bytes_per_step") if traffic else None,
-                     "algorithmic_bytes_per_step": wbytes, "gemv_ms_per_step": gemv_ms, "attn_ms_per_step": attn_ms},
-        "whole_step_hbm": {"bytes": wbytes + kv_per_pos * ctx_mid,
-                           "achieved_gbs": (wbytes + kv_per_pos * ctx_mid) / (ms / K / 1000.0) / 1e9,
-                           "frac": (wbytes + kv_per_pos * ctx_mid) / (ms / K / 1000.0) / 1e9 / peak},
+        "roofline": roof,
         "clocks": clk,
     }
     if e2e:

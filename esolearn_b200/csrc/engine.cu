@@ -925,6 +925,13 @@ sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, flo
     return SB_OK;
 }
 
+sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
+    SB_CHECK(m && launches, SB_ERR_ARG, "sb_llama_step_launches: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    *launches = (batch == 1 && m->ds_ok) ? 1 : 3 + 5 * m->L;  // embed, 5 per layer, lm_head, argmax
+    return SB_OK;
+}
+
 sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_bytes_per_pos) {
     SB_CHECK(m, SB_ERR_ARG, "null model");
     const double h = m->h, F = m->F, V = m->V;

@@ -286,6 +286,12 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_profile_step(self._h, C.byref(g), C.byref(a), C.byref(o), C.byref(n)))
         return g.value, a.value, o.value, n.value
 
+    def step_launches(self, batch: int = 1) -> int:
+        """Kernel launches per decode step (1 = the persistent single-kernel step)."""
+        n = C.c_int32()
+        N.check(N.lib().sb_llama_step_launches(self._h, batch, C.byref(n)))
+        return n.value
+
     def step_bytes(self):
         w, kv = C.c_double(), C.c_double()
         N.check(N.lib().sb_llama_step_bytes(self._h, C.byref(w), C.byref(kv)))

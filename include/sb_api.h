@@ -196,6 +196,11 @@ sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, flo
 /* Bytes the engine streams per decode step at the current context (int8
  * weights + scales + KV read), for roofline accounting. */
 sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_bytes_per_pos);
+/* Kernel launches one decode step of `batch` sequences makes: 1 when the
+ * step runs as the persistent single-kernel step (batch 1 on supported
+ * shapes), else the per-operation kernel count.  No reference counterpart
+ * (the reference runs on the CPU); it documents which device path runs. */
+sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches);
 
 #ifdef __cplusplus
 }

@@ -160,6 +160,25 @@ def test_batched_decode_equals_independent_sequences(B):
         assert got[b].tolist() == om.generate_greedy(prompts[b], 33, kv_bf16=True).tolist(), b
 
 
+def test_batch1_runs_the_persistent_step_and_agrees_with_per_op_path():
+    # Batch 1 is one persistent-kernel launch per step; batches of 2-4 run the
+    # per-operation kernels.  The same sequence decoded in both must give the
+    # same tokens and logits within the f32 bar (attention splits differ).
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 128), 5)
+    e = engine_from_oracle(om, c, max_seq=128, max_batch=2, kv_dtype="bf16")
+    assert e.step_launches(1) == 1
+    assert e.step_launches(2) == 3 + 5 * c.n_layers
+    toks = O.prompt_ids(7, 20, c.vocab_size)
+    cache = e.new_kv_cache(128)
+    one = [e.forward_with_cache(int(t), p, cache) for p, t in enumerate(toks)]
+    e.new_kv_cache(128)
+    for p, t in enumerate(toks):
+        lg, _ = e.forward_batch([int(t), int(t)], [p, p])
+        assert rel_err(lg[0], one[p]) < TOL_F32, p
+        assert np.array_equal(lg[0], lg[1]), p
+
+
 def test_seven_b_shape_two_layers():
     # Llama-2-7B layer shapes (h 4096, ffn 11008, 32 heads, vocab 32000), 2 layers.
     c = LlamaConfig(32000, 4096, 11008, 2, 32, 32, 4096, 1e-5, 10000.0, False, None)
