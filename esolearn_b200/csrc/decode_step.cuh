@@ -23,7 +23,7 @@ constexpr int DS_QMAX_F = 16;  // ... for the SwiGLU row of width F (<= 16384)
 constexpr int DS_MAX_NST = 16;
 
 struct DsSmem {
-    size_t ring, pa, red, qs, sc, kvnew, bars, total;
+    size_t ring, pa, red, qs, kvnew, bars, total;
 };
 
 // pa: the fixed-point planes of a GEMV input; during attention, the
@@ -34,13 +34,12 @@ __host__ __device__ inline DsSmem ds_layout(int nst, int ksmax, int rep, int hd,
     L.ring = 0;
     L.pa = (size_t)nst * DS_STAGE;
     size_t pa = (size_t)48 * ksmax;
-    const size_t att_red = (size_t)8 * rep * hd * 4;
+    const size_t att_red = (size_t)8 * rep * (hd + 2) * 4;
     if (att_red > pa) pa = att_red;
     if ((size_t)mtab > pa) pa = (size_t)mtab;
     L.red = L.pa + ((pa + 127) & ~(size_t)127);
     L.qs = L.red + (size_t)8 * DS_TN * 8;
-    L.sc = L.qs + (size_t)rep * hd * 4;
-    L.kvnew = L.sc + (((size_t)rep * chunk * 4 + 15) & ~(size_t)15);
+    L.kvnew = L.qs + (size_t)rep * hd * 4;
     L.bars = L.kvnew + (size_t)2 * hd * 4;
     L.total = L.bars + (size_t)2 * nst * 8;
     return L;

@@ -22,7 +22,6 @@ extern __shared__ __align__(1024) uint8_t ds_smem[];
 // Per-CTA state shared by the consumer warps.
 struct DsShared {
     double red_d[8][2];
-    float soft_m[8], soft_l[8], soft_alpha[8];
     float cand_v[8];
     int cand_i[8];
     double rstd;  // of the last GEMV input stage
@@ -75,6 +74,18 @@ struct DsKv<__nv_bfloat16> {
     }
     __device__ static __nv_bfloat16 from(float f) { return __float2bfloat16_rn(f); }
     __device__ static float to(__nv_bfloat16 b) { return __bfloat162float(b); }
+    // N consecutive elements (N = 2 or 4, 4- or 8-byte aligned) as floats.
+    template <int N>
+    __device__ static void load_n(const __nv_bfloat16 *p, float (&v)[N]) {
+        if (N == 4) {
+            const uint2 u = *reinterpret_cast<const uint2 *>(p);
+            v[0] = __uint_as_float(u.x << 16), v[1] = __uint_as_float(u.x & 0xffff0000u);
+            v[N > 2 ? 2 : 0] = __uint_as_float(u.y << 16), v[N > 3 ? 3 : 0] = __uint_as_float(u.y & 0xffff0000u);
+        } else {
+            const uint32_t u = *reinterpret_cast<const uint32_t *>(p);
+            v[0] = __uint_as_float(u << 16), v[N > 1 ? 1 : 0] = __uint_as_float(u & 0xffff0000u);
+        }
+    }
 };
 template <>
 struct DsKv<float> {
@@ -85,6 +96,16 @@ struct DsKv<float> {
     }
     __device__ static float from(float f) { return f; }
     __device__ static float to(float f) { return f; }
+    template <int N>
+    __device__ static void load_n(const float *p, float (&v)[N]) {
+        if (N == 4) {
+            const float4 u = *reinterpret_cast<const float4 *>(p);
+            v[0] = u.x, v[1] = u.y, v[N > 2 ? 2 : 0] = u.z, v[N > 3 ? 3 : 0] = u.w;
+        } else {
+            const float2 u = *reinterpret_cast<const float2 *>(p);
+            v[0] = u.x, v[N > 1 ? 1 : 0] = u.y;
+        }
+    }
 };
 
 // ---- input stage -----------------------------------------------------------
@@ -420,15 +441,198 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, int nst, uint32_t bars, in
     return it;
 }
 
+// ---- attention consumer -------------------------------------------------------
+// Attention over this CTA's (kv head, chunk) units [u0, u1) of one layer, in
+// the flash-decoding form: each warp owns rows w, w+8, ... of every chunk and
+// keeps its own online-softmax state (m, l, o) per q head of the group, so
+// scores, the running maximum and the weighted V sum need only warp
+// shuffles (four rows per shuffle round); the eight warp states are merged
+// once per head into the head's record.  Lane x holds dims
+// [DPL*x, DPL*x + DPL) of q and o.  Out of line, so its state stays in
+// registers.  Returns the updated count of consumed ring stages.
+template <int HD, int REP, typename KV>
+__device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bars, long long u0, long long u1, int nch,
+                                              int ctx, int pos, bool has_new, const long long *accq, double fq,
+                                              const float *cos_row, const float *sin_row, KV *kcl, KV *vcl,
+                                              const int *page_table, float *part, int nkv, int q_dim, int kv_dim,
+                                              int page_size, int chunk, float q_scale, int G, int cta,
+                                              uint32_t qs_off, uint32_t kvnew_off, uint32_t pa_off) {
+    using KL = DsKv<KV>;
+    constexpr int DPL = HD / 32;  // dims per lane
+    constexpr int BR = 4;         // rows per warp per shuffle round
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t *smem = ds_smem;
+    float *qs = reinterpret_cast<float *>(smem + qs_off);
+    float *knew = reinterpret_cast<float *>(smem + kvnew_off);
+    float *vnew = knew + HD;
+    float *ared = reinterpret_cast<float *>(smem + pa_off);  // [8 warps][REP][HD + 2]
+    bool failed = ds_sh.abort != 0;
+    uint32_t slot = it % nst, par = (it / nst) & 1;
+    float q[REP][DPL], o[REP][DPL], m[REP], ls[REP];
+    int cur = -1;
+    // RoPE of the element pair (d, d^1) of a head whose columns start at
+    // col (rope_with_freqs_preloaded, cpu.rs:650-661).
+    auto roped = [&](int col, int d) {
+        const float y = gemv_out(__ldcg(accq + col + d), fq);
+        const float partner = gemv_out(__ldcg(accq + col + (d ^ 1)), fq);
+        const int i = d >> 1;
+        const float cs = __ldg(cos_row + i), sn = __ldg(sin_row + i);
+        return (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
+                       : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
+    };
+    // q of head group g (pre-scaled, llama.rs:394) and, when this CTA owns
+    // the chunk holding the decoded position, the new K/V row (rounded to
+    // the cache type, also stored in the cache) -- one pass of loads.
+    auto begin = [&](int g) {
+        const long long ulast = (long long)g * nch + nch - 1;
+        const bool own_new = has_new && ulast >= u0 && ulast < u1;
+        const int nq_el = REP * HD;
+        for (int i = tid; i < nq_el + (own_new ? HD : 0); i += DS_CONSUMERS) {
+            if (i < nq_el) {
+                const int r = i / HD, d = i - r * HD;
+                qs[i] = __fmul_rn(roped((g * REP + r) * HD, d), q_scale);
+            } else {
+                const int d = i - nq_el;
+                const size_t row =
+                    (((size_t)page_table[pos / page_size] * nkv + g) * page_size + pos % page_size) * HD;
+                const KV kq = KL::from(roped(q_dim + g * HD, d));
+                const KV vq = KL::from(gemv_out(__ldcg(accq + q_dim + kv_dim + g * HD + d), fq));
+                knew[d] = KL::to(kq);
+                vnew[d] = KL::to(vq);
+                kcl[row + d] = kq;
+                vcl[row + d] = vq;
+            }
+        }
+        ds_sync();
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
+            m[r] = -INFINITY;
+            ls[r] = 0.f;
+#pragma unroll
+            for (int e = 0; e < DPL; e++) q[r][e] = qs[r * HD + lane * DPL + e], o[r][e] = 0.f;
+        }
+    };
+    // Merge the warp states: M = max_w m_w, o = sum_w e^(m_w - M) o_w,
+    // l likewise; write the head's record.
+    auto finish = [&](int g) {
+#pragma unroll
+        for (int r = 0; r < REP; r++) {
+            float *aw = ared + ((size_t)warp * REP + r) * (HD + 2);
+#pragma unroll
+            for (int e = 0; e < DPL; e++) aw[lane * DPL + e] = o[r][e];
+            if (lane == 0) aw[HD] = m[r], aw[HD + 1] = ls[r];
+        }
+        ds_sync();
+        float *rec = part + ((size_t)g * G + cta) * REP * DS_REC(HD);
+        for (int i = tid; i < REP * HD; i += DS_CONSUMERS) {
+            const int r = i / HD, d = i - r * HD;
+            float M = -INFINITY;
+            for (int w = 0; w < 8; w++) M = fmaxf(M, ared[((size_t)w * REP + r) * (HD + 2) + HD]);
+            float O = 0.f, Lz = 0.f;
+            for (int w = 0; w < 8; w++) {
+                const float *aw = ared + ((size_t)w * REP + r) * (HD + 2);
+                if (aw[HD] == -INFINITY) continue;
+                const float sw = expf(aw[HD] - M);
+                O = fmaf(aw[d], sw, O);
+                Lz = fmaf(aw[HD + 1], sw, Lz);
+            }
+            rec[(size_t)r * DS_REC(HD) + d] = O;
+            if (d == 0) {
+                rec[(size_t)r * DS_REC(HD) + HD] = M;
+                rec[(size_t)r * DS_REC(HD) + HD + 1] = Lz;
+            }
+        }
+        ds_sync();
+    };
+    for (long long u = u0; u < u1; u++) {
+        const int g = (int)(u / nch), j = (int)(u - (long long)g * nch);
+        if (g != cur) {
+            if (cur >= 0) finish(cur);
+            cur = g;
+            begin(g);
+        }
+        const int p0 = j * chunk, np = min(chunk, ctx - p0);
+        // one stage: K rows in the first half, V rows in the second
+        if (!failed && !mbar_wait(bars + 8 * slot, par)) {
+            failed = true;
+            ds_sh.abort = 1;
+        }
+        KV *kst = reinterpret_cast<KV *>(smem + (size_t)slot * DS_STAGE);
+        KV *vst = reinterpret_cast<KV *>(smem + (size_t)slot * DS_STAGE + DS_KV_HALF);
+        if (has_new && j == nch - 1) {
+            for (int d = tid; d < HD; d += DS_CONSUMERS) {
+                kst[(size_t)(pos - p0) * HD + d] = KL::from(knew[d]);
+                vst[(size_t)(pos - p0) * HD + d] = KL::from(vnew[d]);
+            }
+            ds_sync();
+        }
+        if (!failed) {
+            for (int i0 = warp; i0 < np; i0 += 8 * BR) {
+                float sc[BR][REP];
+#pragma unroll
+                for (int b = 0; b < BR; b++) {
+                    const int i = i0 + 8 * b;
+                    float kx[DPL];
+                    if (i < np) KL::template load_n<DPL>(kst + (size_t)i * HD + lane * DPL, kx);
+#pragma unroll
+                    for (int r = 0; r < REP; r++) {
+                        float t = 0.f;
+                        if (i < np) {
+#pragma unroll
+                            for (int e = 0; e < DPL; e++) t = fmaf(q[r][e], kx[e], t);
+                        }
+                        sc[b][r] = t;
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int b = 0; b < BR; b++)
+#pragma unroll
+                        for (int r = 0; r < REP; r++) sc[b][r] += __shfl_xor_sync(0xffffffffu, sc[b][r], off);
+#pragma unroll
+                for (int r = 0; r < REP; r++) {
+                    float mn = m[r];
+#pragma unroll
+                    for (int b = 0; b < BR; b++)
+                        if (i0 + 8 * b < np) mn = fmaxf(mn, sc[b][r]);
+                    const float al = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
+                    ls[r] *= al;
+#pragma unroll
+                    for (int e = 0; e < DPL; e++) o[r][e] *= al;
+                    m[r] = mn;
+#pragma unroll
+                    for (int b = 0; b < BR; b++) sc[b][r] = (i0 + 8 * b < np) ? expf(sc[b][r] - mn) : 0.f;
+                }
+#pragma unroll
+                for (int b = 0; b < BR; b++) {
+                    const int i = i0 + 8 * b;
+                    if (i >= np) continue;
+                    float vx[DPL];
+                    KL::template load_n<DPL>(vst + (size_t)i * HD + lane * DPL, vx);
+#pragma unroll
+                    for (int r = 0; r < REP; r++) {
+                        ls[r] += sc[b][r];
+#pragma unroll
+                        for (int e = 0; e < DPL; e++) o[r][e] = fmaf(sc[b][r], vx[e], o[r][e]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+        it++;
+    }
+    if (cur >= 0) finish(cur);
+    return it;
+}
+
 // ---- the kernel ----------------------------------------------------------------
 template <int HD, int REP, typename KV>
 __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs a) {
     using KL = DsKv<KV>;
-    constexpr int EPL = KL::EPL;             // elements per 16-byte chunk of a K/V row
-    constexpr int LPP = HD / EPL;            // lanes per row
-    constexpr int PPW = 32 / LPP;            // rows per warp pass
-    constexpr int NPG = DS_CONSUMERS / LPP;  // row groups of the AV pass
-    static_assert(LPP <= 32 && 32 % LPP == 0, "head_dim / lanes mismatch");
+    static_assert(HD % 64 == 0, "head_dim must give each lane 2 or 4 dims");
 
     uint8_t *smem = ds_smem;
     DsShared &sh = ds_sh;
@@ -468,6 +672,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (tid != DS_CONSUMERS) return;
         uint32_t it = 0, slot = 0, par = 0;
         bool ok = true;
+        // Every streamed byte is read once per step: keep it from evicting
+        // the step's code, activations and column sums from L2.
+        const uint64_t stream_policy = l2_evict_first_policy();
         // One stage: a copy of bytes0 at src0 into the slot, and optionally
         // a second copy of bytes1 at src1 into its second half.
         auto issue = [&](const void *src0, uint32_t bytes0, const void *src1 = nullptr, uint32_t bytes1 = 0) {
@@ -478,8 +685,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 }
             }
             mbar_expect_tx(bars + 8 * slot, bytes0 + bytes1);
-            tma_load_1d(ring + slot * DS_STAGE, src0, bytes0, bars + 8 * slot);
-            if (src1) tma_load_1d(ring + slot * DS_STAGE + DS_KV_HALF, src1, bytes1, bars + 8 * slot);
+            tma_load_1d_hint(ring + slot * DS_STAGE, src0, bytes0, bars + 8 * slot, stream_policy);
+            if (src1) tma_load_1d_hint(ring + slot * DS_STAGE + DS_KV_HALF, src1, bytes1, bars + 8 * slot, stream_policy);
             it++;
             if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
         };
@@ -570,193 +777,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
 
     // Attention over this CTA's (kv head, chunk) units of layer l.
     auto attention = [&](int l) {
-        const long long U = att_U;
-        const long long u0 = U * cta / G, u1 = U * (cta + 1) / G;
-        float *qs = reinterpret_cast<float *>(smem + L.qs);
-        float *sc = reinterpret_cast<float *>(smem + L.sc);
-        float *knew = reinterpret_cast<float *>(smem + L.kvnew);
-        float *vnew = knew + HD;
-        float *ared = reinterpret_cast<float *>(smem + L.pa);
-        const long long *accq = a.acc + (size_t)((4 * l) % 3) * a.acc_n;
-        const double fq = gemv_factor(sh.shift, a.layers[l].scale[0], sh.rstd);
+        const long long u0 = att_U * cta / G, u1 = att_U * (cta + 1) / G;
         const int rp = min(max(pos, 0), a.max_pos - 1);  // rope table row
-        KV *kcl = reinterpret_cast<KV *>(static_cast<char *>(a.kc) + (size_t)l * a.layer_kv_bytes);
-        KV *vcl = reinterpret_cast<KV *>(static_cast<char *>(a.vc) + (size_t)l * a.layer_kv_bytes);
-        const int sub = lane % LPP;
-        const int pg = tid / LPP, asub = tid % LPP;
-        bool failed = sh.abort != 0;
-        uint32_t slot = it % nst, par = (it / nst) & 1;
-        float o[REP][EPL];
-        int cur = -1;
-        // RoPE'd value of element d of a head whose columns start at col
-        // (rope_with_freqs_preloaded, cpu.rs:650-661).
-        auto roped = [&](int col, int d) {
-            const float y = gemv_out(__ldcg(accq + col + d), fq);
-            const float partner = gemv_out(__ldcg(accq + col + (d ^ 1)), fq);
-            const int i = d >> 1;
-            const float cs = __ldg(a.rope_cos + (size_t)rp * (HD / 2) + i);
-            const float sn = __ldg(a.rope_sin + (size_t)rp * (HD / 2) + i);
-            return (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
-                           : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
-        };
-        auto wait_stage = [&]() {
-            if (!failed && !mbar_wait(bars + 8 * slot, par)) {
-                failed = true;
-                sh.abort = 1;
-            }
-        };
-        auto release_stage = [&]() {
-            __syncwarp();
-            if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
-            if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
-            it++;
-        };
-        auto begin = [&](int g) {
-            for (int i = tid; i < REP * HD; i += DS_CONSUMERS) {
-                const int r = i / HD, d = i - r * HD;
-                qs[i] = __fmul_rn(roped((g * REP + r) * HD, d), a.q_scale);  // llama.rs:394
-            }
-            const long long ulast = (long long)g * nch + nch - 1;
-            if (has_new && ulast >= u0 && ulast < u1) {
-                // This CTA owns the chunk holding the new position: build its
-                // K/V row (rounded to the cache type) and store it in the cache.
-                const size_t row =
-                    (((size_t)a.page_table[pos / a.page_size] * a.nkv + g) * a.page_size + pos % a.page_size) * HD;
-                for (int d = tid; d < HD; d += DS_CONSUMERS) {
-                    const KV kq = KL::from(roped(a.q_dim + g * HD, d));
-                    const KV vq = KL::from(gemv_out(__ldcg(accq + a.q_dim + a.kv_dim + g * HD + d), fq));
-                    knew[d] = KL::to(kq);
-                    vnew[d] = KL::to(vq);
-                    kcl[row + d] = kq;
-                    vcl[row + d] = vq;
-                }
-            }
-            if (tid < REP) sh.soft_m[tid] = -INFINITY, sh.soft_l[tid] = 0.f;
-#pragma unroll
-            for (int r = 0; r < REP; r++)
-#pragma unroll
-                for (int e = 0; e < EPL; e++) o[r][e] = 0.f;
-            ds_sync();
-        };
-        auto finish = [&](int g) {
-#pragma unroll
-            for (int r = 0; r < REP; r++)
-#pragma unroll
-                for (int e = 0; e < EPL; e++) {
-                    float t = o[r][e];
-                    for (int off = LPP; off < 32; off <<= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-                    o[r][e] = t;
-                }
-            if (lane < LPP) {
-#pragma unroll
-                for (int r = 0; r < REP; r++)
-#pragma unroll
-                    for (int e = 0; e < EPL; e++) ared[((size_t)warp * REP + r) * HD + asub * EPL + e] = o[r][e];
-            }
-            ds_sync();
-            float *rec = a.part + ((size_t)g * G + cta) * REP * DS_REC(HD);
-            for (int i = tid; i < REP * HD; i += DS_CONSUMERS) {
-                const int r = i / HD, d = i - r * HD;
-                float t = 0.f;
-                for (int w = 0; w < 8; w++) t += ared[((size_t)w * REP + r) * HD + d];
-                rec[(size_t)r * DS_REC(HD) + d] = t;
-            }
-            if (tid < REP) {
-                rec[(size_t)tid * DS_REC(HD) + HD] = sh.soft_m[tid];
-                rec[(size_t)tid * DS_REC(HD) + HD + 1] = sh.soft_l[tid];
-            }
-            ds_sync();
-        };
-        for (long long u = u0; u < u1; u++) {
-            const int g = (int)(u / nch), j = (int)(u - (long long)g * nch);
-            if (g != cur) {
-                if (cur >= 0) finish(cur);
-                cur = g;
-                begin(g);
-            }
-            const int p0 = j * a.chunk, np = min(a.chunk, ctx - p0);
-            const bool patch = has_new && j == nch - 1;
-            // one stage: K rows in the first half, V rows in the second
-            wait_stage();
-            KV *kst = reinterpret_cast<KV *>(smem + L.ring + (size_t)slot * DS_STAGE);
-            KV *vst = reinterpret_cast<KV *>(smem + L.ring + (size_t)slot * DS_STAGE + DS_KV_HALF);
-            if (patch) {
-                for (int d = tid; d < HD; d += DS_CONSUMERS) {
-                    kst[(size_t)(pos - p0) * HD + d] = KL::from(knew[d]);
-                    vst[(size_t)(pos - p0) * HD + d] = KL::from(vnew[d]);
-                }
-                ds_sync();
-            }
-            for (int pb = warp * PPW; pb < np; pb += 8 * PPW) {
-                const int pi = pb + lane / LPP;
-                float dots[REP];
-#pragma unroll
-                for (int r = 0; r < REP; r++) dots[r] = 0.f;
-                if (pi < np && !failed) {
-                    float kv[EPL];
-                    KL::load(kst + (size_t)pi * HD + sub * EPL, kv);
-#pragma unroll
-                    for (int r = 0; r < REP; r++) {
-                        const float *qr = qs + r * HD + sub * EPL;
-#pragma unroll
-                        for (int e = 0; e < EPL; e++) dots[r] = fmaf(qr[e], kv[e], dots[r]);
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < REP; r++)
-#pragma unroll
-                    for (int off = LPP / 2; off > 0; off >>= 1) dots[r] += __shfl_xor_sync(0xffffffffu, dots[r], off);
-                if (sub == 0 && pi < np) {
-#pragma unroll
-                    for (int r = 0; r < REP; r++) sc[r * a.chunk + pi] = dots[r];
-                }
-            }
-            ds_sync();
-            // online softmax update (softmax, cpu.rs:336-366, over the chunk)
-            for (int r = warp; r < REP; r += 8) {
-                float mx = -INFINITY;
-                for (int i = lane; i < np; i += 32) mx = fmaxf(mx, sc[r * a.chunk + i]);
-                mx = warp_max_f(mx);
-                const float m_old = sh.soft_m[r];
-                const float m_new = fmaxf(m_old, mx);
-                float sum = 0.f;
-                for (int i = lane; i < np; i += 32) {
-                    const float e = expf(sc[r * a.chunk + i] - m_new);
-                    sc[r * a.chunk + i] = e;
-                    sum += e;
-                }
-                sum = warp_sum_f(sum);
-                if (lane == 0) {
-                    const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-                    sh.soft_alpha[r] = alpha;
-                    sh.soft_l[r] = fmaf(sh.soft_l[r], alpha, sum);
-                    sh.soft_m[r] = m_new;
-                }
-            }
-            ds_sync();
-            // o = alpha * o + sum_i p_i v_i
-#pragma unroll
-            for (int r = 0; r < REP; r++) {
-                const float al = sh.soft_alpha[r];
-#pragma unroll
-                for (int e = 0; e < EPL; e++) o[r][e] *= al;
-            }
-            if (!failed) {
-                for (int pi = pg; pi < np; pi += NPG) {
-                    float vv[EPL];
-                    KL::load(vst + (size_t)pi * HD + asub * EPL, vv);
-#pragma unroll
-                    for (int r = 0; r < REP; r++) {
-                        const float w = sc[r * a.chunk + pi];
-#pragma unroll
-                        for (int e = 0; e < EPL; e++) o[r][e] = fmaf(w, vv[e], o[r][e]);
-                    }
-                }
-            }
-            release_stage();
-            ds_sync();
-        }
-        if (cur >= 0) finish(cur);
+        it = ds_attention<HD, REP, KV>(
+            it, nst, bars, u0, u1, nch, ctx, pos, has_new, a.acc + (size_t)((4 * l) % 3) * a.acc_n,
+            gemv_factor(sh.shift, a.layers[l].scale[0], sh.rstd), a.rope_cos + (size_t)rp * (HD / 2),
+            a.rope_sin + (size_t)rp * (HD / 2),
+            reinterpret_cast<KV *>(static_cast<char *>(a.kc) + (size_t)l * a.layer_kv_bytes),
+            reinterpret_cast<KV *>(static_cast<char *>(a.vc) + (size_t)l * a.layer_kv_bytes), a.page_table, a.part,
+            a.nkv, a.q_dim, a.kv_dim, a.page_size, a.chunk, a.q_scale, G, cta, (uint32_t)L.qs, (uint32_t)L.kvnew,
+            (uint32_t)L.pa);
     };
 
     auto accbuf = [&](int j) { return a.acc + (size_t)(j % 3) * a.acc_n; };

@@ -52,6 +52,23 @@ __device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *src, uint3
                  : "memory");
 }
 
+// L2 policy for data read once per pass (weights, KV rows): evict first, so
+// the stream does not push out what is reused (code, activations, sums).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// tma_load_1d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_1d_hint(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
 // Named barrier over the first N threads of the block (the consumer warps).
 template <int N>
 __device__ __forceinline__ void named_sync() {
