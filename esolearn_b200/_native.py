@@ -55,6 +55,7 @@ SIGNATURES = {
     "sb_quantize_symmetric_host": (C.c_int, [vp, C.c_size_t, vp, f32p]),
     "sb_quantize_symmetric": (C.c_int, [vp, C.c_size_t, vp, vp, vp]),
     "sb_qweight_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(vp)]),
+    "sb_qweight_create_tn": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]),
     "sb_qweight_load": (C.c_int, [vp, vp, vp]),
     "sb_qweight_destroy": (C.c_int, [vp]),
     "sb_matmul_i8_f32": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp]),

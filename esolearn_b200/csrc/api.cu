@@ -9,6 +9,7 @@
 
 #include "attention.cuh"
 #include "misc.cuh"
+#include "qgemm.cuh"
 #include "qgemv.cuh"
 
 namespace sb {
@@ -64,7 +65,10 @@ struct Workspace {
 // split partials).  Each kind has its own buffer per device so that one op
 // never sees another op's leftovers; counters return to zero after every
 // launch, so a buffer only needs zeroing when it is (re)allocated.
-enum { WS_QUANT = 0, WS_ATTN = 1, WS_KINDS = 2 };
+// WS_GEMM_SUMS only ever holds the tensor-core GEMM's int64 column sums,
+// which must read zero before every call: a grown buffer is zero-filled and
+// every call clears what it used.
+enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_KINDS = 4 };
 constexpr size_t WS_ATTN_COUNTER_BYTES = 64 * 1024;
 
 static int workspace_get(int kind, size_t bytes, void **out, cudaStream_t st) {
@@ -202,15 +206,19 @@ sb_status sb_quantize_symmetric(const float *w, size_t n, int8_t *q, float *scal
     return SB_OK;
 }
 
-sb_status sb_qweight_create(int K, int N, int group, sb_qweight **out) {
+sb_status sb_qweight_create(int K, int N, int group, sb_qweight **out) { return sb_qweight_create_tn(K, N, group, 0, out); }
+
+sb_status sb_qweight_create_tn(int K, int N, int group, int tile_n, sb_qweight **out) {
     SB_CHECK(out && K > 0 && N > 0, SB_ERR_ARG, "sb_qweight_create: bad argument");
+    SB_CHECK(tile_n == 0 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256, SB_ERR_ARG,
+             "sb_qweight_create_tn: tile width %d not in {0,16,32,64,128,256}", tile_n);
     SB_CHECK(group == 0 || group == 32 || group == 64, SB_ERR_UNSUPPORTED, "group %d not in {0,32,64}", group);
     SB_CHECK(group == 0 || K % group == 0, SB_ERR_SHAPE, "K=%d not a multiple of group %d", K, group);
     sb_qweight *w = new sb_qweight();
     w->d.K = K;
     w->d.N = N;
     w->d.KS = ceil_div(K, 16);
-    w->d.TN = qgemv_pick_tn(N, K, 16);
+    w->d.TN = tile_n ? tile_n : qgemv_pick_tn(N, K, 16);
     w->d.ntiles = ceil_div(N, w->d.TN);
     w->d.group = group;
     cudaError_t e = cudaMalloc(&w->buf, qweight_bytes(K, N, w->d.TN));
@@ -269,6 +277,30 @@ static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, in
     SB_CHECK(a_dtype == SB_DTYPE_F32 || a_dtype == SB_DTYPE_BF16, SB_ERR_ARG, "bad activation dtype %d", a_dtype);
     SB_CHECK(M >= 0, SB_ERR_ARG, "M < 0");
     const size_t esz = a_dtype == SB_DTYPE_BF16 ? 2 : 4;
+    if (qgemm_supported(w->d, M)) {
+        // 5-32 rows on the tensor cores: scratch = planes, column sums, row exponents
+        QGemmWs ws;
+        ws.ld_acc = w->d.ntiles * 128;
+        const size_t pb = align_up(qgemm_planes_bytes(w->d.K, M), 256);
+        void *base = nullptr, *sums = nullptr;
+        SB_TRY(workspace_get(WS_GEMM, pb + 256 + 512, &base, (cudaStream_t)stream));
+        SB_TRY(workspace_get(WS_GEMM_SUMS, sizeof(long long) * (size_t)M * ws.ld_acc, &sums, (cudaStream_t)stream));
+        char *b = static_cast<char *>(base);
+        ws.planes = reinterpret_cast<uint8_t *>(b);
+        ws.acc = reinterpret_cast<long long *>(sums);
+        ws.rstd = reinterpret_cast<double *>(b + pb);
+        ws.shift = reinterpret_cast<int *>(b + pb + 256);
+        QGemvArgs g;
+        g.w = w->d;
+        g.M = M;
+        g.x = a;
+        g.ldx = w->d.K;
+        g.x_bf16 = a_dtype == SB_DTYPE_BF16;
+        g.out = c;
+        g.ldo = w->d.N;
+        g.bias = bias;
+        return qgemm_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, (cudaStream_t)stream, false);
+    }
     for (int r0 = 0; r0 < M; r0 += QG_MAX_M) {
         QGemvArgs g;
         g.w = w->d;

@@ -1,0 +1,494 @@
+// Batched int8 linear on tcgen05 tensor cores: the batched-decode form of
+// matmul_i8_f32 (backend/mod.rs:521-533, CPU cpu.rs:1129-1160) for 5-32 rows.
+//
+// Arithmetic.  Exactly the fixed point of the GEMV (qgemv.cu): each row is
+// scaled by a power of two so |a * 2^s| < 2^22 and rounded to an integer A;
+// here it is offset to U = A + 2^23 in [0, 2^24) and split into three
+// UNSIGNED byte planes.  The tensor cores multiply the signed int8 weights
+// (A operand, 128 output columns x K) with the unsigned planes plus one
+// all-ones row (B operand, 3M+1 rows x K) into int32 accumulators in TMEM
+// (tcgen05.mma kind::i8); |each accumulator| <= K * 127 * 255 < 2^31 for
+// K <= 16384.  Per output column and row:
+//   sum_k w a 2^s = D[plane0] + 2^8 D[plane1] + 2^16 D[plane2] - 2^23 D[ones]
+// exactly, so results equal the GEMV path bit for bit whenever the row
+// exponents agree.
+//
+// Data movement.  A producer thread streams 32 KB stages of the packed weight
+// (the same tile-major 16 KB units as the persistent decode step, split evenly
+// over the CTAs) together with the matching 16-k-chunk slice of the planes
+// through a ring of shared-memory slots with 1-D TMA bulk copies.  The packed
+// tile layout [k/16][128 columns][16 bytes] already is the K-major
+// no-swizzle core-matrix layout the MMA reads (8 rows x 16 bytes per core
+// matrix, 128 B between row groups, 2 KB between k chunks).  One thread
+// issues the MMAs of a stage and commits them to the slot's "empty" barrier,
+// so the tensor core releases the slot.  At the end of a tile segment four
+// warps drain TMEM (tcgen05.ld, one output column per lane), recombine the
+// planes and add the exact int64 column sums into global memory; a finish
+// kernel applies the scale, rstd and epilogue and clears the sums.
+//
+// Every wait is bounded (2 s); a wait that runs out sets qgm_error_flag and
+// the CTA stops issuing, waits for its tensor-core work and frees TMEM.
+#include "qgemm.cuh"
+
+#include <algorithm>
+
+#include "pipeline.cuh"
+
+namespace sb {
+
+namespace {
+
+constexpr int QGM_TN = 128;
+constexpr int QGM_UNIT_KS = 8;      // k-steps per 16 KB work unit (split granularity)
+constexpr int QGM_STAGE_KS = 16;    // k-steps per stage (two units)
+constexpr int QGM_WBYTES = QGM_STAGE_KS * QGM_TN * 16;  // 32 KB of weights per stage
+constexpr int QGM_THREADS = 192;    // warps 0-3 TMEM drain, 4 MMA, 5 producer
+constexpr int QGM_MAX_NST = 6;
+
+__device__ unsigned qgm_error_flag = 0;
+
+__host__ __device__ inline int qgm_slot_bytes(int np) { return QGM_WBYTES + QGM_STAGE_KS * np * 16; }
+
+// ---- tcgen05 helpers (cta_group::1) ------------------------------------------------
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    // K-major, no swizzle: LBO = byte distance between 16-byte k chunks,
+    // SBO = byte distance between 8-row groups; descriptor version 1.
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// kind::i8, signed A (weights), unsigned B (planes), s32 accumulate, both K-major.
+__device__ __forceinline__ uint32_t umma_idesc_i8(int n) {
+    return (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(QGM_TN >> 4) << 24);
+}
+__device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }" ::"r"(
+                     tmem),
+                 "l"(da), "l"(db), "r"(idesc), "r"(acc)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// One 32-bit column of this warp's 32 TMEM lanes (and three consecutive ones).
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return r;
+}
+__device__ __forceinline__ void tmem_ld3(uint32_t taddr, uint32_t &a, uint32_t &b, uint32_t &c) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(a) : "r"(taddr));
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(b) : "r"(taddr + 1));
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(c) : "r"(taddr + 2));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The CTA's stages: units of 8 k-steps of a 128-column tile, tile-major,
+// CTA c takes [c*U/G, (c+1)*U/G), two units of one tile per stage.
+struct QgmWalk {
+    int tile, ut, u, u1, upt, KS;
+    __device__ QgmWalk(int KS_, int ntiles, int G, int cta) : KS(KS_) {
+        upt = (KS + QGM_UNIT_KS - 1) / QGM_UNIT_KS;
+        const int U = ntiles * upt;
+        u = (int)((long long)U * cta / G);
+        u1 = (int)((long long)U * (cta + 1) / G);
+        tile = u / upt;
+        ut = u - tile * upt;
+    }
+    __device__ bool more() const { return u < u1; }
+    // Next stage: tile, first k-step, k-steps, and whether it ends the CTA's
+    // segment of that tile.
+    __device__ void next(int &t, int &k0, int &nks, bool &seg_end) {
+        const int n = (ut + 1 < upt && u + 1 < u1) ? 2 : 1;
+        t = tile;
+        k0 = ut * QGM_UNIT_KS;
+        nks = min(n * QGM_UNIT_KS, KS - k0);
+        u += n;
+        ut += n;
+        if (ut >= upt) ut = 0, tile++;
+        seg_end = (u >= u1) || (tile != t);
+    }
+};
+
+// ---- kernel 0: activation rows -> fixed-point planes ----------------------------
+// Block m < M: row m (RMSNorm-weighted when norm_w is set).  Block M: the
+// all-ones row and the zero padding rows.
+__global__ void __launch_bounds__(256) qgm_planes_kernel(const QGemvArgs a, QGemmWs ws, int np) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int K = a.w.K, KS = a.w.KS, M = a.M;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m = blockIdx.x;
+    if (m == M) {
+        for (int i = tid; i < KS * np; i += blockDim.x) {
+            const int kc = i / np, r = i - kc * np;
+            if (r < 3 * M) continue;
+            uint4 v = r == 3 * M ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+            reinterpret_cast<uint4 *>(ws.planes)[(size_t)kc * np + r] = v;
+        }
+        return;
+    }
+    auto xval = [&](int k) -> float {
+        if (a.x_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.x)[(size_t)m * a.ldx + k]);
+        return reinterpret_cast<const float *>(a.x)[(size_t)m * a.ldx + k];
+    };
+    __shared__ double red_s[8];
+    __shared__ float red_m[8];
+    __shared__ int s_shift;
+    float ssq = 0.f, amx = 0.f;
+    for (int k = tid; k < K; k += blockDim.x) {
+        const float x = xval(k);
+        ssq = fmaf(x, x, ssq);
+        const float v = a.norm_w ? __fmul_rn(x, __ldg(a.norm_w + k)) : x;
+        amx = fmaxf(amx, fabsf(v));
+    }
+    const double s = warp_sum_d((double)ssq);
+    const float mx = warp_max_f(amx);
+    if (lane == 0) red_s[warp] = s, red_m[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        double st = 0.0, mt = 0.0;
+        for (int w = 0; w < (int)blockDim.x / 32; w++) st += red_s[w], mt = fmax(mt, (double)red_m[w]);
+        // rmsnorm (cpu.rs:582-588): rstd = 1/sqrt(mean(x^2) + eps) in f64
+        ws.rstd[m] = a.norm_w ? 1.0 / sqrt(st / (double)K + (double)a.eps) : 1.0;
+        int e = 0;
+        if (mt > 0.0) frexp(mt, &e);
+        const int sh = (mt > 0.0) ? 22 - e : 0;  // |a * 2^sh| < 2^22
+        s_shift = sh < -126 ? -126 : (sh > 126 ? 126 : sh);
+        ws.shift[m] = s_shift;
+    }
+    __syncthreads();
+    const float sc = __int_as_float((s_shift + 127) << 23);
+    // one thread per 16-k chunk: U = A + 2^23, three unsigned byte planes
+    for (int kc = tid; kc < KS; kc += blockDim.x) {
+        uint32_t w[3][4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int k = kc * 16 + q * 4 + i;
+                float v = 0.f;
+                if (k < K) {
+                    const float x = xval(k);
+                    v = a.norm_w ? __fmul_rn(x, __ldg(a.norm_w + k)) : x;
+                }
+                const float t = __fmul_rn(v, sc);
+                const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;  // round to nearest even
+                const uint32_t U = (uint32_t)(A + (1 << 23));
+                b0 |= (U & 0xffu) << (8 * i);
+                b1 |= ((U >> 8) & 0xffu) << (8 * i);
+                b2 |= ((U >> 16) & 0xffu) << (8 * i);
+            }
+            w[0][q] = b0, w[1][q] = b1, w[2][q] = b2;
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(ws.planes) + (size_t)kc * np + 3 * m;
+#pragma unroll
+        for (int p = 0; p < 3; p++) dst[p] = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
+    }
+}
+
+// ---- kernel 1: weights x planes on the tensor cores -> int64 column sums -------
+__global__ void __launch_bounds__(QGM_THREADS, 1)
+    qgm_gemm_kernel(const QWeightDesc w, const QGemmWs ws, int M, int np, int nst) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long bars[2 * QGM_MAX_NST + 2];  // full, empty, tmem full, tmem empty
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int slot_bytes = qgm_slot_bytes(np);
+    const uint32_t b_full = smem_u32(&bars[0]), b_empty = smem_u32(&bars[QGM_MAX_NST]);
+    const uint32_t b_tfull = smem_u32(&bars[2 * QGM_MAX_NST]), b_tempty = smem_u32(&bars[2 * QGM_MAX_NST + 1]);
+    const int ncols = np <= 32 ? 32 : (np <= 64 ? 64 : 128);
+    if (tid == 0) {
+        for (int i = 0; i < nst; i++) {
+            mbar_init(b_full + 8 * i, 1);
+            mbar_init(b_empty + 8 * i, 1);  // arrived by tcgen05.commit
+        }
+        mbar_init(b_tfull, 1);
+        mbar_init(b_tempty, 4);  // one arrival per draining warp
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_abort = 0;
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    pdl_launch_dependents();
+    const uint32_t tmem = s_tmem;
+    const uint32_t ring = smem_u32(smem);
+
+    if (warp == 5) {
+        // ---- producer: weights (immutable) may stream before the planes exist
+        if (lane == 0) {
+            QgmWalk wk(w.KS, w.ntiles, G, cta);
+            uint32_t it = 0, slot = 0, par = 0;
+            bool waited = false;
+            while (wk.more()) {
+                int t, k0, nks;
+                bool se;
+                wk.next(t, k0, nks, se);
+                if (it >= (uint32_t)nst) {
+                    if (!waited) pdl_wait(), waited = true;
+                    if (*(volatile int *)&s_abort || !mbar_wait(b_empty + 8 * slot, par ^ 1)) {
+                        atomicOr(&qgm_error_flag, 1u);
+                        s_abort = 1;
+                        break;
+                    }
+                }
+                const uint32_t wbytes = (uint32_t)nks * QGM_TN * 16, pbytes = (uint32_t)nks * np * 16;
+                const uint32_t dst = ring + slot * slot_bytes;
+                mbar_expect_tx(b_full + 8 * slot, wbytes + pbytes);
+                tma_load_1d(dst, reinterpret_cast<const uint8_t *>(w.w) + ((size_t)t * w.KS + k0) * QGM_TN * 16, wbytes,
+                            b_full + 8 * slot);
+                if (!waited) pdl_wait(), waited = true;  // the planes come from the previous kernel
+                tma_load_1d(dst + QGM_WBYTES, ws.planes + (size_t)k0 * np * 16, pbytes, b_full + 8 * slot);
+                it++;
+                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+            }
+        }
+    } else if (warp == 4) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            QgmWalk wk(w.KS, w.ntiles, G, cta);
+            const uint32_t idesc = umma_idesc_i8(np);
+            uint32_t slot = 0, par = 0, seg = 0;
+            bool seg_start = true, ok = true;
+            while (wk.more() && ok) {
+                int t, k0, nks;
+                bool se;
+                wk.next(t, k0, nks, se);
+                if (seg_start && seg > 0 && !mbar_wait(b_tempty, (seg - 1) & 1)) ok = false;  // TMEM drained
+                if (ok && !mbar_wait(b_full + 8 * slot, par)) ok = false;
+                if (!ok) {
+                    atomicOr(&qgm_error_flag, 1u);
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = ring + slot * slot_bytes, p0 = a0 + QGM_WBYTES;
+                for (int kk = 0; kk < nks / 2; kk++) {
+                    const uint64_t da = umma_sdesc(a0 + kk * 2 * QGM_TN * 16, QGM_TN * 16, 128);
+                    const uint64_t db = umma_sdesc(p0 + kk * 2 * np * 16, np * 16, 128);
+                    umma_i8(tmem, da, db, idesc, (seg_start && kk == 0) ? 0u : 1u);
+                }
+                umma_commit(b_empty + 8 * slot);  // the slot is free once these MMAs complete
+                seg_start = false;
+                if (se) {
+                    umma_commit(b_tfull);  // this tile's sums are complete in TMEM
+                    seg++;
+                    seg_start = true;
+                }
+                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+            }
+            // leave no tensor-core work running: the last commit covers every MMA issued
+            if (seg > 0 && !mbar_wait(b_tempty, (seg - 1) & 1)) atomicOr(&qgm_error_flag, 1u);
+        }
+    } else {
+        // ---- warps 0-3: drain TMEM per tile segment into exact int64 column sums
+        pdl_wait();  // the previous finish kernel has cleared the sums
+        QgmWalk wk(w.KS, w.ntiles, G, cta);
+        uint32_t seg = 0;
+        const int col = warp * 32 + lane;  // output column within the tile (= TMEM lane)
+        while (wk.more()) {
+            int t, k0, nks;
+            bool se;
+            wk.next(t, k0, nks, se);
+            if (!se) continue;
+            const bool ok = !s_abort && mbar_wait(b_tfull, seg & 1);
+            if (!ok) {
+                atomicOr(&qgm_error_flag, 1u);
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+            // D[3M] = sum_k w over this segment's k range (the ones row)
+            const long long ones = (long long)(int)tmem_ld1(lane_base + (uint32_t)(3 * M));
+            long long *out = ws.acc + (size_t)t * QGM_TN + col;
+            for (int m = 0; m < M; m++) {
+                uint32_t d0, d1, d2;
+                tmem_ld3(lane_base + (uint32_t)(3 * m), d0, d1, d2);
+                const long long s = (long long)(int)d0 + ((long long)(int)d1 << 8) + ((long long)(int)d2 << 16) -
+                                    (ones << 23);
+                if (s != 0)
+                    atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)m * ws.ld_acc), (unsigned long long)s);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_tempty);
+            seg++;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+}
+
+// ---- kernel 2: scale, epilogue, clear the sums ------------------------------------
+// One CTA per 128-column tile, all rows.  The epilogues are those of
+// qgemv.cu for any row count.
+template <int EPI>
+__global__ void __launch_bounds__(256) qgm_finish_kernel(const QGemvArgs a, const QGemmWs ws) {
+    __shared__ float ys[QGM_MAX_M * QGM_TN];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tile = blockIdx.x, tid = threadIdx.x, M = a.M;
+    for (int it = tid; it < M * QGM_TN; it += blockDim.x) {
+        const int m = it / QGM_TN, c = it - m * QGM_TN;
+        long long *p = ws.acc + (size_t)m * ws.ld_acc + (size_t)tile * QGM_TN + c;
+        const long long t = __ldcg(p);
+        *p = 0;
+        const float sc = (EPI == QEPI_SWIGLU && (c & 31) >= 16) ? a.w.scale_up : a.w.scale;
+        ys[it] = gemv_out(t, gemv_factor(ws.shift[m], sc, ws.rstd[m]));
+    }
+    __syncthreads();
+    for (int it = tid; it < M * QGM_TN; it += blockDim.x) {
+        const int m = it / QGM_TN, c = it - m * QGM_TN;
+        const int n = tile * QGM_TN + c;
+        const float y = ys[it];
+        if (EPI == QEPI_STORE || EPI == QEPI_LOGITS) {
+            if (n < a.w.N) a.out[(size_t)m * a.ldo + n] = y;
+        } else if (EPI == QEPI_BIAS) {
+            if (n < a.w.N) a.out[(size_t)m * a.ldo + n] = __fadd_rn(y, a.bias[n]);
+        } else if (EPI == QEPI_RESID) {
+            if (n < a.w.N) {
+                float *o = a.out + (size_t)m * a.ldo + n;
+                *o = __fadd_rn(*o, y);  // x = x + proj (llama.rs:564,568)
+            }
+        } else if (EPI == QEPI_SWIGLU) {
+            const int within = n & 31;
+            if (within < 16) {
+                const int j = (n >> 5) * 16 + within;
+                if (j < a.F) a.out[(size_t)m * a.ldo + j] = __fmul_rn(silu_f64(y), ys[it + 16]);
+            }
+        } else if (EPI == QEPI_QKV) {
+            if (n >= a.w.N) continue;
+            const int pos = a.pos[m];
+            if (pos < 0 || pos >= a.max_pos) continue;
+            const int qk = a.q_dim + a.kv_dim;
+            float val = y;
+            if (n < qk) {
+                // rope_with_freqs_preloaded (cpu.rs:650-661)
+                const int nn = n < a.q_dim ? n : n - a.q_dim;
+                const int d = nn % a.hd, i = d >> 1;
+                const float partner = ys[it ^ 1];
+                const float cs = a.rope_cos[(size_t)pos * (a.hd / 2) + i];
+                const float sn = a.rope_sin[(size_t)pos * (a.hd / 2) + i];
+                val = (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
+                              : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
+            }
+            if (n < a.q_dim) {
+                a.q_out[(size_t)m * a.q_dim + n] = __fmul_rn(val, a.q_scale);
+            } else {
+                const bool is_k = n < qk;
+                const int nn = is_k ? n - a.q_dim : n - qk;
+                const int kh = nn / a.hd, d = nn - kh * a.hd;
+                const int page = a.page_table[(size_t)m * a.max_pages + pos / a.page_size];
+                const size_t idx = (((size_t)page * a.n_kv + kh) * a.page_size + pos % a.page_size) * a.hd + d;
+                void *cache = is_k ? a.kcache : a.vcache;
+                if (a.kv_f32)
+                    reinterpret_cast<float *>(cache)[idx] = val;
+                else
+                    reinterpret_cast<__nv_bfloat16 *>(cache)[idx] = __float2bfloat16_rn(val);
+            }
+        }
+    }
+    if (EPI == QEPI_LOGITS) {
+        // per-tile argmax candidate of every row; ties resolve to the larger index
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int m = warp; m < M; m += blockDim.x / 32) {
+            float best = -INFINITY;
+            int bi = -1;
+            for (int c = lane; c < QGM_TN; c += 32) {
+                const int n = tile * QGM_TN + c;
+                if (n < a.w.N) {
+                    const float v = ys[m * QGM_TN + c];
+                    if (bi < 0 || v >= best) best = v, bi = n;
+                }
+            }
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
+            }
+            if (lane == 0) {
+                a.cand_val[(size_t)m * a.w.ntiles + tile] = best;
+                a.cand_idx[(size_t)m * a.w.ntiles + tile] = bi;
+            }
+        }
+    }
+}
+
+int qgm_nst(int np, int *limit_out) {
+    static int lim[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!lim[dev & 63]) SB_TRY(allow_max_dynamic_smem(qgm_gemm_kernel, &lim[dev & 63]));
+    *limit_out = lim[dev & 63];
+    return std::min(QGM_MAX_NST, lim[dev & 63] / qgm_slot_bytes(np));
+}
+
+template <int EPI>
+int finish_launch(const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
+    SB_CUDA_TRY(launch(qgm_finish_kernel<EPI>, dim3(a.w.ntiles), dim3(256), 0, st, pdl, a, ws));
+    return SB_OK;
+}
+
+}  // namespace
+
+size_t qgemm_planes_bytes(int K, int M) { return (size_t)ceil_div(K, 16) * qgemm_np(M) * 16; }
+
+bool qgemm_supported(const QWeightDesc &w, int M) {
+    return w.TN == QGM_TN && w.group == 0 && (w.KS % 2) == 0 && M > QG_MAX_M && M <= QGM_MAX_M && w.K <= 16384;
+}
+
+int qgemm_check_error() {
+    unsigned f = 0;
+    SB_CUDA_TRY(cudaMemcpyFromSymbol(&f, qgm_error_flag, sizeof f));
+    if (f) {
+        const unsigned zero = 0;
+        cudaMemcpyToSymbol(qgm_error_flag, &zero, sizeof zero);
+        return set_error(SB_ERR_TIMEOUT, "qgemm: a bounded pipeline wait timed out");
+    }
+    return SB_OK;
+}
+
+int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
+    SB_CHECK(qgemm_supported(a.w, a.M), SB_ERR_UNSUPPORTED, "qgemm: weight/rows not supported (TN %d, group %d, M %d)",
+             a.w.TN, a.w.group, a.M);
+    SB_CHECK(ws.planes && ws.acc && ws.shift && ws.rstd && ws.ld_acc >= a.w.ntiles * QGM_TN, SB_ERR_ARG,
+             "qgemm: missing scratch");
+    SB_CHECK(a.norm_w == nullptr || epi == QEPI_QKV || epi == QEPI_SWIGLU || epi == QEPI_LOGITS, SB_ERR_ARG,
+             "qgemm: epilogue %d takes no fused RMSNorm", epi);
+    const int np = qgemm_np(a.M);
+    int limit = 0;
+    const int nst = qgm_nst(np, &limit);
+    SB_CHECK(nst >= 2, SB_ERR_SHAPE, "qgemm: %d rows need %d B per stage (limit %d)", a.M, qgm_slot_bytes(np), limit);
+    SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + 1), dim3(256), 0, st, pdl, a, ws, np));
+    const int upt = ceil_div(a.w.KS, QGM_UNIT_KS);
+    const int G = std::max(1, std::min(device_props().sm_count, a.w.ntiles * upt / 2));
+    SB_CUDA_TRY(launch(qgm_gemm_kernel, dim3(G), dim3(QGM_THREADS), (size_t)nst * qgm_slot_bytes(np), st, pdl, a.w, ws,
+                       a.M, np, nst));
+    switch (epi) {
+    case QEPI_STORE: return finish_launch<QEPI_STORE>(a, ws, st, pdl);
+    case QEPI_BIAS: return finish_launch<QEPI_BIAS>(a, ws, st, pdl);
+    case QEPI_RESID: return finish_launch<QEPI_RESID>(a, ws, st, pdl);
+    case QEPI_SWIGLU: return finish_launch<QEPI_SWIGLU>(a, ws, st, pdl);
+    case QEPI_QKV: return finish_launch<QEPI_QKV>(a, ws, st, pdl);
+    case QEPI_LOGITS: return finish_launch<QEPI_LOGITS>(a, ws, st, pdl);
+    default: return set_error(SB_ERR_ARG, "qgemm: unknown epilogue %d", epi);
+    }
+}
+
+}  // namespace sb

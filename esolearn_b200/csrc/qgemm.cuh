@@ -1,0 +1,37 @@
+// Batched int8 linear on the 5th-generation tensor cores (tcgen05 + TMEM),
+// for 5 to 32 activation rows (batched decode, the quantized-linear sweep).
+#pragma once
+
+#include "qgemv.cuh"
+
+namespace sb {
+
+constexpr int QGM_MAX_M = 32;
+
+// Plane rows of the MMA's B operand for M activation rows: three byte planes
+// per row plus one all-ones row, padded to a multiple of 16.
+inline int qgemm_np(int M) { return (3 * M + 1 + 15) / 16 * 16; }
+
+// Scratch of one batched linear (device memory, owned by the caller).
+struct QGemmWs {
+    uint8_t *planes = nullptr;  // [KS][np][16] fixed-point planes of the M input rows
+    long long *acc = nullptr;   // [M][ld_acc] exact column sums (all zero between calls)
+    int *shift = nullptr;       // [M] per-row exponent
+    double *rstd = nullptr;     // [M] per-row RMSNorm factor (1 without norm)
+    int ld_acc = 0;             // >= ntiles * 128
+};
+size_t qgemm_planes_bytes(int K, int M);
+
+// Whether the tensor-core path takes this weight and row count: 128-column
+// tiles, per-tensor scale, K a multiple of 32, 5 <= M <= 32.
+bool qgemm_supported(const QWeightDesc &w, int M);
+
+// y = epilogue(x W) for M rows, as qgemv_launch (same QGemvArgs and epilogues)
+// in three launches: quantize the rows into planes, stream the weights
+// through the tensor cores into exact int64 column sums, finish (scale +
+// epilogue; clears the sums).  pdl enables programmatic dependent launch.
+int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl);
+// Reports (and clears) a timed-out pipeline wait of the GEMM kernel.
+int qgemm_check_error();
+
+}  // namespace sb

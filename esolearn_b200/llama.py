@@ -117,12 +117,14 @@ def quantize_symmetric(weights: np.ndarray):
 class QWeight:
     """An int8 [K,N] weight packed on the device (the I8Storage of this backend)."""
 
-    def __init__(self, q: np.ndarray, scales, group: int = 0):
+    def __init__(self, q: np.ndarray, scales, group: int = 0, tile_n: int = 0):
+        """tile_n: on-device column tile width (0 = the GEMV's choice; 128
+        lets 5-32-row products run on the tensor cores)."""
         q = np.ascontiguousarray(q, np.int8)
         self.K, self.N = q.shape
         self.group = group
         h = C.c_void_p()
-        N.check(N.lib().sb_qweight_create(self.K, self.N, group, C.byref(h)))
+        N.check(N.lib().sb_qweight_create_tn(self.K, self.N, group, tile_n, C.byref(h)))
         self._h = h
         sc = np.ascontiguousarray(np.atleast_1d(np.asarray(scales, np.float32)))
         N.check(N.lib().sb_qweight_load(self._h, _ptr(q), _ptr(sc)))

@@ -71,13 +71,21 @@ sb_status sb_quantize_symmetric(const float *w, size_t n, int8_t *q, float *scal
  * per-tensor scale; group = 32 or 64 keeps f32 scales[ceil(K/g), N]. */
 typedef struct sb_qweight sb_qweight;
 sb_status sb_qweight_create(int K, int N, int group, sb_qweight **out);
+/* Same with an explicit tile width tile_n in {16, 32, 64, 128, 256} (0 =
+ * the GEMV's choice).  128-column tiles let 5-32-row products run on the
+ * tensor cores (see sb_matmul_i8_f32).  No reference counterpart: the
+ * reference keeps [K,N] as is; this only picks the on-device packing. */
+sb_status sb_qweight_create_tn(int K, int N, int group, int tile_n, sb_qweight **out);
 /* q: host [K,N] int8; scales: host, 1 value (group 0) or [ceil(K/g), N]. */
 sb_status sb_qweight_load(sb_qweight *w, const int8_t *q, const float *scales);
 sb_status sb_qweight_destroy(sb_qweight *w);
 
 /* matmul_i8_f32 (backend/mod.rs:521-533; CPU cpu.rs:1129-1160):
  * c[M,N] = a[M,K] . dequant(q)[K,N], f32 accumulate.  a, c are device
- * pointers; a_dtype is SB_DTYPE_F32 or SB_DTYPE_BF16.  Uses a library-owned
+ * pointers; a_dtype is SB_DTYPE_F32 or SB_DTYPE_BF16.  1-4 rows run the
+ * GEMV; 5-32 rows of a per-tensor-scaled weight with 128-column tiles run
+ * on the tcgen05 tensor cores (same fixed-point arithmetic, same results
+ * as row-by-row GEMVs); other shapes run the GEMV 4 rows at a time.  Uses a library-owned
  * workspace on the current device. */
 sb_status sb_matmul_i8_f32(const sb_qweight *w, const void *a, int a_dtype, int M, float *c,
                            void *stream);

@@ -51,6 +51,32 @@ def test_matmul_i8_f32_per_tensor(M, K, N_):
     assert e < TOL_F32 and e < TOL_GEMV, e
 
 
+@pytest.mark.parametrize("M", [5, 8, 17, 32])
+@pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008), (512, 1536), (96, 384), (100, 45)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_batched_tensor_core_matmul_equals_rowwise_gemv(M, K, N_, bf16):
+    # 5-32 rows of a 128-column-tile weight run on the tcgen05 tensor cores
+    # with the GEMV's fixed-point arithmetic: every row must equal the GEMV of
+    # that row alone bit for bit, and the reference within the f32 bar.
+    # (K=100 is not a multiple of 32: that case runs the GEMV 4 rows at a time.)
+    rng = np.random.default_rng(M * 7919 + K + N_ + bf16)
+    w = (rng.standard_normal((K, N_)) * 0.02).astype(np.float32)
+    q, s = O.quantize_symmetric(w)
+    q = q.reshape(K, N_)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    qw = QWeight(q, [s], tile_n=128)
+    at = torch.from_numpy(a).cuda()
+    if bf16:
+        at = at.to(torch.bfloat16)
+        a = at.float().cpu().numpy()
+    out = matmul_i8_f32(at, qw).cpu().numpy()
+    rows = np.vstack([matmul_i8_f32(at[i:i + 1].contiguous(), qw).cpu().numpy() for i in range(M)])
+    torch.cuda.synchronize()
+    assert np.array_equal(out, rows)
+    ref = O.matmul_i8_f32(a, q, s, M, K, N_)
+    assert rel_err(out, ref) < TOL_F32
+
+
 @pytest.mark.parametrize("group", [32, 64])
 @pytest.mark.parametrize("M", [1, 4, 8])
 @pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008)])
