@@ -1,9 +1,12 @@
 """Decode throughput of the B200 int8 Llama engine (one JSON line on rank 0).
 
-Workload: Llama-2-7B-shape random-init int8 model (dim
-4096, 32 layers, 32 heads, ffn 11008, vocab 32000, RoPE theta 1e4), seeded
-512-token prompt, then greedy decode at batch 1.  A step is one decode token
-of every sequence: K timed steps follow the prompt and W warm-up steps.
+Default workload: Llama-2-7B-shape random-init int8
+model (dim 4096, 32 layers, 32 heads, ffn 11008, vocab 32000, RoPE theta 1e4),
+seeded 512-token prompt, then greedy decode at batch 1.  --workload
+llama3-8b-bs32: Llama-3-8B shape with GQA (32 query /
+8 KV heads, ffn 14336, vocab 128256, theta 5e5), 32 sequences with seeded
+2048-token prompts.  A step is one decode token of every sequence: K timed
+steps follow the prompt and W warm-up steps.
 
 * value      -- decode tokens/s with weights and KV resident in HBM (CUDA
                 events on the engine stream around K steps; at batch 1 each
@@ -15,8 +18,10 @@ of every sequence: K timed steps follow the prompt and W warm-up steps.
                 the persistent step kernel (all int8 weights + the K/V rows
                 of the context) divided by its average launch duration (the
                 timed region above), against MEASURED_PEAKS.json.  Larger
-                batches run per-operation kernels: int8 weight bytes of the
-                GEMV launches over their eager per-kernel event time.
+                batches run a CUDA graph of per-operation kernels (GEMV up to
+                4 rows, the tcgen05 GEMM for 5-32): the same step bytes over
+                the step time, with the eager per-kernel-class split (linears,
+                attention) beside it.
                 traffic -- DRAM bytes of one launch from an ncu capture
                 (profiles/decode_step_7b_bs1_traffic.json).
 * cpu_baseline -- the reference's CPU path (the oracle restatement of
@@ -43,8 +48,15 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "decode tok/s, 7B-shape int8, bs1"
 PROMPT_LEN = 512
+
+WORKLOADS = {
+    "llama2-7b-bs1": {"metric": "decode tok/s, 7B-shape int8, bs1", "shape": "llama2_7b_shape", "batch": 1,
+                      "prompt": 512, "desc": "llama2-7b-shape int8 decode (BASELINE configs[2])"},
+    "llama3-8b-bs32": {"metric": "decode tok/s, 8B-shape GQA int8, bs32", "shape": "llama3_8b_shape", "batch": 32,
+                       "prompt": 2048,
+                       "desc": "llama3-8b-shape GQA int8 decode, 2048-token bf16 KV context (BASELINE configs[3])"},
+}
 
 
 def read_peaks():
@@ -116,21 +128,24 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside)}
 
 
-def cpu_reference_tok_s(budget_s: float = 20.0):
+def cpu_reference_tok_s(shape, budget_s: float = 20.0):
     """The reference CPU decode (oracle restatement of cpu.rs) on a bounded sample.
 
-    Sample: a 7B-shape model with 2 decoder layers + the 32000x4096 lm_head,
+    Sample: the workload's model shape with 2 decoder layers + its lm_head,
     seeded weights; 4 decode steps after a 4-token prefix are timed and the
-    per-layer time is scaled to 32 layers.  Returns (tok/s, cores, sample)."""
+    per-layer time is scaled to the full depth.  The reference decodes one
+    sequence at a time, so its tok/s is the same at any batch.  Returns
+    (tok/s, cores, sample)."""
     import oracle as O
 
     cores = os.cpu_count() or 1
     O.set_threads(cores)
     L = 2
-    cfg = O.make_config(32000, 4096, 11008, L, 32, 32, 64, 1e-5, 10000.0, False)
+    V, h, F = shape.vocab_size, shape.hidden_size, shape.intermediate_size
+    cfg = O.make_config(V, h, F, L, shape.n_heads, shape.n_kv_heads, 64, 1e-5, shape.rope_theta, False)
     m = O.OracleLlama(cfg, 0)
     cache = m.new_cache(64)
-    toks = O.prompt_ids(0, 8, 32000)
+    toks = O.prompt_ids(0, 8, V)
     for pos in range(4):
         m.forward_with_cache(cache, int(toks[pos]), pos)
     times = []
@@ -142,28 +157,32 @@ def cpu_reference_tok_s(budget_s: float = 20.0):
         if time.perf_counter() - t_start > budget_s:
             break
     t_step = float(np.median(times))
-    # lm_head share: time the [1,4096]x[4096,32000] int8 matmul alone
-    q = np.zeros((32000, 4096), np.int8)
-    x = np.ones(4096, np.float32)
+    # lm_head share: time the [1,h]x[h,V] int8 matmul alone
+    q = np.zeros((V, h), np.int8)
+    x = np.ones(h, np.float32)
     t0 = time.perf_counter()
-    O.matmul_i8_f32_tb(x, q, 0.01, 1, 4096, 32000)
+    O.matmul_i8_f32_tb(x, q, 0.01, 1, h, V)
     t_head = time.perf_counter() - t0
     t_layer = max(t_step - t_head, 1e-9) / L
-    t_token = 32 * t_layer + t_head
-    return 1.0 / t_token, cores, (f"7B-shape, {L} of 32 layers + lm_head, {len(times)} decode steps at context 5-8, "
-                                  f"per-layer time x32 + lm_head; {cores} OpenMP threads")
+    t_token = shape.n_layers * t_layer + t_head
+    return 1.0 / t_token, cores, (f"h{h}/ffn{F}/vocab{V}, {L} of {shape.n_layers} layers + lm_head, {len(times)} "
+                                  f"decode steps at context 5-8, per-layer time x{shape.n_layers} + lm_head; "
+                                  f"{cores} OpenMP threads")
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    tok_s, cores, sample = cpu_reference_tok_s()
+    from esolearn_b200 import LlamaConfig
+
+    wl = WORKLOADS[args.workload]
+    tok_s, cores, sample = cpu_reference_tok_s(getattr(LlamaConfig, wl["shape"])())
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": wl["metric"], "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / tok_s, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 activations", "data": "synthetic",
-        "config": {"workload": "llama2-7b-shape int8 decode bs1 (reference CPU path, sampled)", "batch": 1,
-                   "prompt": PROMPT_LEN},
+        "config": {"workload": wl["desc"] + " (reference CPU path, sampled; one sequence at a time)",
+                   "batch": args.batch, "prompt": args.prompt},
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -178,7 +197,8 @@ def run_ours(args, rank: int, world: int, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     N.check(N.lib().sb_init(local))
-    cfg = LlamaConfig.llama2_7b_shape()
+    wl = WORKLOADS[args.workload]
+    cfg = getattr(LlamaConfig, wl["shape"])()
     B = args.batch
     K, W = args.steps, args.warmup
     max_seq = args.prompt + W + K + 8
@@ -229,49 +249,54 @@ def run_ours(args, rank: int, world: int, dist):
                 "traffic_context": traffic.get("context") if traffic else None,
                 "algorithmic_bytes_per_launch": step_alg_bytes, "launch_ms": ms / K}
     else:
-        # per-operation kernels: eager pass, one CUDA event pair per kernel
+        # CUDA graph of per-operation kernels: the step bytes over the step
+        # time, and an eager pass with one CUDA event pair per kernel class
         prof = [model.profile_step() for _ in range(4)]
-        gemv_ms = float(np.median([p[0] for p in prof]))
-        achieved = wbytes / (gemv_ms / 1000.0) / 1e9
+        lin_ms = float(np.median([p[0] for p in prof]))
+        att_ms = float(np.median([p[1] for p in prof]))
+        achieved = step_alg_bytes / (ms / K / 1000.0) / 1e9
+        lin_kernel = "qgm_gemm_kernel (tcgen05)" if B > 4 else "qgemv_kernel"
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_source": peak_kind, "kernel": "qgemv_kernel (all int8 projections of a step)", "traffic": None,
-                "algorithmic_bytes_per_step": wbytes, "gemv_ms_per_step": gemv_ms,
-                "attn_ms_per_step": float(np.median([p[1] for p in prof]))}
+                "peak_source": peak_kind, "kernel": f"whole step: {lin_kernel} linears + attn_decode_kernel",
+                "traffic": None, "algorithmic_bytes_per_step": step_alg_bytes, "step_ms": ms / K,
+                "linears": {"bytes": wbytes, "eager_ms": lin_ms, "gbs": wbytes / (lin_ms / 1000.0) / 1e9},
+                "attention": {"bytes": kv_per_pos * ctx_mid * B, "eager_ms": att_ms,
+                              "gbs": kv_per_pos * ctx_mid * B / (att_ms / 1000.0) / 1e9}}
 
-    # e2e: reference-facing call with host buffers every step (token in, argmax out)
+    # e2e: reference-facing call with host buffers every step (tokens in, argmax out)
     e2e = None
-    if not args.no_e2e and B == 1:
+    if not args.no_e2e:
         # Re-decode the timed positions (each step rewrites its own KV row
         # before reading the context), so every e2e step sees the same
         # context length as the matching timed step.
         toks = model.tokens(B, max_seq)
-        last = int(toks[0, -1]) if toks.shape[1] else 0
+        last = toks[:, -1].copy() if toks.shape[1] else np.zeros(B, np.int32)
         p0 = args.prompt + W
         n_e2e = K
-        pinned_tok = torch.empty(1, dtype=torch.int32).pin_memory()
+        pinned_tok = torch.empty(B, dtype=torch.int32).pin_memory()
         for i in range(3):
-            model.forward_batch([last], [p0 - 3 + i], want_logits=False)
+            model.forward_batch(last.tolist(), [p0 - 3 + i] * B, want_logits=False)
         t0 = time.perf_counter()
         for i in range(n_e2e):
-            pinned_tok[0] = last
-            _, am = model.forward_batch(pinned_tok.numpy(), [p0 + i], want_logits=False)
-            last = int(am[0])
+            pinned_tok.numpy()[:] = last
+            _, am = model.forward_batch(pinned_tok.numpy(), [p0 + i] * B, want_logits=False)
+            last = am
         t1 = time.perf_counter()
-        e2e = {"value": world * n_e2e / (t1 - t0), "unit": "tok/s", "h2d_bytes_per_step": 12,
-               "d2h_bytes_per_step": 4, "steps": n_e2e,
+        e2e = {"value": world * B * n_e2e / (t1 - t0), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+               "d2h_bytes_per_step": 4 * B, "steps": n_e2e,
                "api": "sb_llama_forward (token, position in; argmax out; stream-synchronous)"}
 
     if rank != 0:
         return
     res = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "metric": wl["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 weights x f32 activations (exact int32 dp4a products), f32 accumulate; bf16 KV",
         "data": "synthetic: seeded random-init weights (fastrand/Box-Muller N(0,0.02), LlamaModel::new order), "
                 "seeded uniform prompt ids",
-        "config": {"workload": "llama2-7b-shape int8 decode (BASELINE configs[2])", "batch": B, "prompt": args.prompt,
+        "config": {"workload": wl["desc"], "batch": B, "prompt": args.prompt,
                    "context_mid": ctx_mid, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "weights 6.6 GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
+                   "l2": f"weights {wbytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
                    "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else
                               "CUDA graph of per-operation kernels per step, programmatic dependent launch")},
         "gpu_launches": launches_per_step * K,
@@ -281,7 +306,7 @@ def run_ours(args, rank: int, world: int, dist):
     if e2e:
         res["e2e"] = e2e
     if not args.no_cpu:
-        tok_s, cores, sample = cpu_reference_tok_s()
+        tok_s, cores, sample = cpu_reference_tok_s(cfg)
         res["cpu_baseline"] = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
     print(json.dumps(res), flush=True)
 
@@ -292,11 +317,15 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (the workload uses 512)")
+    ap.add_argument("--workload", default="llama2-7b-bs1", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=None, help="sequences (default: the workload's)")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt length (default: the workload's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    args.batch = wl["batch"] if args.batch is None else args.batch
+    args.prompt = wl["prompt"] if args.prompt is None else args.prompt
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     dist = None

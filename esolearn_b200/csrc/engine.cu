@@ -28,6 +28,7 @@
 #include "attention.cuh"
 #include "decode_step.cuh"
 #include "misc.cuh"
+#include "qgemm.cuh"
 #include "qgemv.cuh"
 
 namespace sb {
@@ -102,6 +103,9 @@ struct sb_llama {
     float *ds_part = nullptr, *ds_cand_val = nullptr;
     int *ds_cand_idx = nullptr;
     unsigned *ds_sync = nullptr;
+
+    // batched steps of 5-32 sequences: tensor-core linears and their scratch
+    QGemmWs gws;
 };
 
 namespace {
@@ -127,7 +131,7 @@ int make_qweight(sb_llama *m, QWeightDesc &d, int K, int N, int min_tn) {
     d.K = K;
     d.N = N;
     d.KS = ceil_div(K, 16);
-    d.TN = m->ds_ok ? DS_TN : qgemv_pick_tn(N, K, min_tn);
+    d.TN = (m->ds_ok || m->B > QG_MAX_M) ? DS_TN : qgemv_pick_tn(N, K, min_tn);
     d.ntiles = ceil_div(N, d.TN);
     d.group = 0;
     void *p = nullptr;
@@ -202,6 +206,13 @@ struct StepProfiler {
     }
 };
 
+// One linear of a step: the GEMV for up to 4 rows, the tensor-core GEMM for
+// 5-32 (every weight then has 128-column tiles).
+int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, bool pdl) {
+    if (a.M > QG_MAX_M) return qgemm_launch(epi, a, m->gws, st, pdl);
+    return qgemv_launch(epi, a, st, pdl);
+}
+
 #define SB_PROF(p, c, expr)                \
     do {                                   \
         if (p) SB_TRY((p)->begin(c));      \
@@ -235,7 +246,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.rope_cos = m->rope_cos;
             a.rope_sin = m->rope_sin;
             a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
-            SB_PROF(prof, 0, qgemv_launch(QEPI_QKV, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, QEPI_QKV, a, st, pdl));
         }
         {
             AttnArgs a;
@@ -262,7 +273,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             QGemvArgs a = gemv_common(ly.o, M, m->attn, m->q_dim);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, qgemv_launch(QEPI_RESID, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, QEPI_RESID, a, st, pdl));
         }
         {
             QGemvArgs a = gemv_common(ly.gu, M, m->x, m->h);
@@ -271,13 +282,13 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.out = m->act;
             a.ldo = m->F;
             a.F = m->F;
-            SB_PROF(prof, 0, qgemv_launch(QEPI_SWIGLU, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, QEPI_SWIGLU, a, st, pdl));
         }
         {
             QGemvArgs a = gemv_common(ly.down, M, m->act, m->F);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, qgemv_launch(QEPI_RESID, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, QEPI_RESID, a, st, pdl));
         }
         if (trace)
             SB_CUDA_TRY(cudaMemcpyAsync(m->trace_buf + (size_t)l * M * m->h, m->x, sizeof(float) * M * m->h,
@@ -291,7 +302,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
         a.ldo = m->V;
         a.cand_val = m->cand_val;
         a.cand_idx = m->cand_idx;
-        SB_PROF(prof, 0, qgemv_launch(QEPI_LOGITS, a, st, pdl));
+        SB_PROF(prof, 0, engine_linear(m, QEPI_LOGITS, a, st, pdl));
     }
     SB_PROF(prof, 2, argmax_step_launch(m->cand_val, m->cand_idx, m->lm.ntiles, m->seq, M, st, pdl));
     return SB_OK;
@@ -378,6 +389,7 @@ int ds_step(sb_llama *m) {
 // Errors a bounded device wait may have left behind.
 int check_device_errors(sb_llama *m) {
     if (m->ds_ok) SB_TRY(ds_check_error(m->ds_sync, m->st));
+    SB_TRY(qgemm_check_error());
     return qgemv_check_error();
 }
 
@@ -431,8 +443,14 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
              SB_ERR_SHAPE, "sb_llama_create: non-positive dimension");
     SB_CHECK(c.hidden_size % c.n_heads == 0 && c.n_heads % c.n_kv_heads == 0, SB_ERR_SHAPE,
              "sb_llama_create: hidden %% heads or heads %% kv_heads != 0");
-    SB_CHECK(c.max_batch >= 1 && c.max_batch <= QG_MAX_M, SB_ERR_UNSUPPORTED,
-             "sb_llama_create: max_batch %d outside 1..%d", c.max_batch, QG_MAX_M);
+    SB_CHECK(c.max_batch >= 1 && c.max_batch <= QGM_MAX_M, SB_ERR_UNSUPPORTED,
+             "sb_llama_create: max_batch %d outside 1..%d", c.max_batch, QGM_MAX_M);
+    if (c.max_batch > QG_MAX_M) {
+        // the tensor-core path reads the input in 32-element k steps
+        const int qd = c.hidden_size / c.n_heads * c.n_heads;
+        SB_CHECK(c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 && qd % 32 == 0, SB_ERR_UNSUPPORTED,
+                 "sb_llama_create: batches above %d need hidden, q and ffn sizes that are multiples of 32", QG_MAX_M);
+    }
     const int hd = c.hidden_size / c.n_heads;
     SB_CHECK(hd == 64 || hd == 128, SB_ERR_UNSUPPORTED, "sb_llama_create: head_dim %d not in {64,128}", hd);
 
@@ -568,6 +586,16 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         if ((rc = dalloc_t(m, &m->ds_cand_val, (size_t)G)) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_cand_idx, (size_t)G)) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_sync, 4)) != SB_OK) return fail(rc);
+    }
+    if (B > QG_MAX_M) {
+        int nt = m->lm.ntiles;
+        for (const auto &ly : m->layers) nt = std::max({nt, ly.qkv.ntiles, ly.o.ntiles, ly.gu.ntiles, ly.down.ntiles});
+        const int kmax = std::max(std::max(m->h, m->F), m->q_dim);
+        m->gws.ld_acc = nt * DS_TN;
+        if ((rc = dalloc(m, (void **)&m->gws.planes, qgemm_planes_bytes(kmax, B))) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->gws.acc, (size_t)B * m->gws.ld_acc)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->gws.shift, (size_t)B)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->gws.rstd, (size_t)B)) != SB_OK) return fail(rc);
     }
     if ((rc = dalloc_t(m, &m->trace_buf, (size_t)m->L * B * m->h)) != SB_OK) return fail(rc);
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
@@ -928,7 +956,12 @@ sb_status sb_llama_profile_step(sb_llama *m, float *gemv_ms, float *attn_ms, flo
 sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
     SB_CHECK(m && launches, SB_ERR_ARG, "sb_llama_step_launches: null argument");
     SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
-    *launches = (batch == 1 && m->ds_ok) ? 1 : 3 + 5 * m->L;  // embed, 5 per layer, lm_head, argmax
+    if (batch == 1 && m->ds_ok)
+        *launches = 1;  // the persistent step kernel
+    else if (batch > QG_MAX_M)
+        *launches = 5 + 13 * m->L;  // embed, 4 linears x 3 + attention per layer, lm_head x 3, argmax
+    else
+        *launches = 3 + 5 * m->L;  // embed, 5 per layer, lm_head, argmax
     return SB_OK;
 }
 

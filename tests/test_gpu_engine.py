@@ -160,6 +160,42 @@ def test_batched_decode_equals_independent_sequences(B):
         assert got[b].tolist() == om.generate_greedy(prompts[b], 33, kv_bf16=True).tolist(), b
 
 
+@pytest.mark.parametrize("B", [5, 8, 32])
+def test_tensor_core_batched_decode_equals_independent_sequences(B):
+    # Batches of 5-32 run every projection through the tcgen05 GEMM (three
+    # launches per linear); greedy streams must equal the per-sequence oracle.
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 128), 9)
+    e = engine_from_oracle(om, c, max_seq=128, max_batch=32, kv_dtype="bf16")
+    assert e.step_launches(B) == 5 + 13 * c.n_layers
+    assert e.step_launches(4) == 3 + 5 * c.n_layers
+    prompts = np.stack([O.prompt_ids(200 + b, 12, c.vocab_size) for b in range(B)])
+    got = e.generate_greedy(prompts, 33)
+    for b in range(B):
+        assert got[b].tolist() == om.generate_greedy(prompts[b], 33, kv_bf16=True).tolist(), b
+
+
+@pytest.mark.parametrize("desc,cfg,B", [
+    ("small_gqa4", small_config(layers=2, heads=8, kv=2), 8),
+    ("llama3_8b_shape_1layer", LlamaConfig(128256, 4096, 14336, 1, 32, 8, 8192, 1e-5, 500000.0, False,
+                                           RopeScaling()), 8),
+])
+def test_tensor_core_batch_logits_match_oracle(desc, cfg, B):
+    # Every row of a batched step (distinct tokens and histories) against the
+    # oracle's forward_with_cache of that sequence alone, f32 cache.
+    om = O.OracleLlama(orc_config(cfg, 64), 3)
+    e = engine_from_oracle(om, cfg, max_seq=64, max_batch=B, kv_dtype="f32")
+    seqs = np.stack([O.prompt_ids(50 + b, 4, cfg.vocab_size) for b in range(B)])
+    caches = [om.new_cache(64) for _ in range(B)]
+    e.new_kv_cache(64)
+    for p in range(seqs.shape[1]):
+        lg, am = e.forward_batch(seqs[:, p].tolist(), [p] * B)
+        for b in range(B):
+            ref = om.forward_with_cache(caches[b], int(seqs[b, p]), p)
+            assert rel_err(lg[b], ref) < TOL_F32, (p, b)
+            assert int(am[b]) == argmax_last(lg[b]), (p, b)
+
+
 def test_batch1_runs_the_persistent_step_and_agrees_with_per_op_path():
     # Batch 1 is one persistent-kernel launch per step; batches of 2-4 run the
     # per-operation kernels.  The same sequence decoded in both must give the
@@ -191,6 +227,11 @@ def test_seven_b_shape_two_layers():
 
 def test_capacity_and_argument_errors():
     c = small_config(layers=1)
+    with pytest.raises(N.SbError):
+        QuantLlamaB200.new_random(c, seed=0, max_seq=32, max_batch=33)  # above the tensor-core path's 32 rows
+    with pytest.raises(N.SbError):  # batches above 4 need 32-aligned hidden / ffn sizes
+        QuantLlamaB200.new_random(small_config(h=256, heads=4, kv=4, layers=1, ffn=200), seed=0, max_seq=32,
+                                  max_batch=8)
     om, e = _pair(c, 1, 32, kv_dtype="f32")
     with pytest.raises(N.SbError):
         e.generate_greedy(np.zeros(20, np.int32), 20)  # 20 + 20 - 1 > 32 positions
