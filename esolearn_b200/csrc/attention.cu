@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 
 int attn_pick_splits(int B, int n_kv, int max_ctx) {
     const int sms = device_props().sm_count;
-    int splits = ceil_div(2 * sms, std::max(1, B * n_kv));
+    int splits = std::max(ceil_div(2 * sms, std::max(1, B * n_kv)), ceil_div(std::max(max_ctx, 1), 256));
     splits = std::min(splits, ceil_div(std::max(max_ctx, 1), 16));
     return std::max(1, std::min(splits, 64));
 }
@@ -318,6 +318,7 @@ static int attn_rep(const AttnArgs &a, cudaStream_t st, bool pdl) {
 int attn_launch(const AttnArgs &a, cudaStream_t st, bool pdl) {
     SB_CHECK(a.n_kv > 0 && a.n_heads % a.n_kv == 0, SB_ERR_SHAPE, "attention: n_heads %% n_kv != 0");
     SB_CHECK(a.n_splits == 1 || (a.part && a.counters), SB_ERR_ARG, "attention: split without scratch");
+    if (attn_tc_supported(a)) return attn_tc_launch(a, st, pdl);
     if (a.hd == 128) return a.kv_f32 ? attn_rep<128, float>(a, st, pdl) : attn_rep<128, __nv_bfloat16>(a, st, pdl);
     if (a.hd == 64) return a.kv_f32 ? attn_rep<64, float>(a, st, pdl) : attn_rep<64, __nv_bfloat16>(a, st, pdl);
     return set_error(SB_ERR_UNSUPPORTED, "attention: head_dim %d not in {64,128}", a.hd);

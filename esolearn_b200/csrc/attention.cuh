@@ -21,9 +21,14 @@ struct AttnArgs {
     unsigned *counters = nullptr;   // scratch [B][n_kv], zero between launches
 };
 
-// Splits per (sequence, kv head) for a given max context on this device.
+// Splits per (sequence, kv head) for a given max context on this device:
+// enough CTAs for two waves, and at most about 256 positions per split.
 int attn_pick_splits(int B, int n_kv, int max_ctx);
 size_t attn_scratch_floats(int B, int n_heads, int n_splits, int hd);
+// Runs the tensor-core kernel (attention_tc.cu) for bf16 caches with 2, 4 or
+// 8 query heads per kv head, the SIMT kernel (attention.cu) otherwise.
 int attn_launch(const AttnArgs &a, cudaStream_t st, bool pdl);
+bool attn_tc_supported(const AttnArgs &a);
+int attn_tc_launch(const AttnArgs &a, cudaStream_t st, bool pdl);
 
 }  // namespace sb

@@ -10,6 +10,7 @@
 // (tcgen05.mma kind::i8); |each accumulator| <= K * 127 * 255 < 2^31 for
 // K <= 16384.  Per output column and row:
 //   sum_k w a 2^s = D[plane0] + 2^8 D[plane1] + 2^16 D[plane2] - 2^23 D[ones]
+// (B rows: the ones row first, then the three planes of each activation row)
 // exactly, so results equal the GEMV path bit for bit whenever the row
 // exponents agree.
 //
@@ -22,9 +23,10 @@
 // matrix, 128 B between row groups, 2 KB between k chunks).  One thread
 // issues the MMAs of a stage and commits them to the slot's "empty" barrier,
 // so the tensor core releases the slot.  At the end of a tile segment four
-// warps drain TMEM (tcgen05.ld, one output column per lane), recombine the
-// planes and add the exact int64 column sums into global memory; a finish
-// kernel applies the scale, rstd and epilogue and clears the sums.
+// warps drain TMEM (tcgen05.ld, one output column per lane; two accumulator
+// buffers, so the next segment's MMAs run meanwhile), recombine the planes
+// and add the exact int64 column sums into global memory; a finish kernel
+// applies the scale, rstd and epilogue and clears the sums.
 //
 // Every wait is bounded (2 s); a wait that runs out sets qgm_error_flag and
 // the CTA stops issuing, waits for its tensor-core work and frees TMEM.
@@ -71,20 +73,6 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-// One 32-bit column of this warp's 32 TMEM lanes (and three consecutive ones).
-__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
-    uint32_t r;
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    return r;
-}
-__device__ __forceinline__ void tmem_ld3(uint32_t taddr, uint32_t &a, uint32_t &b, uint32_t &c) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(a) : "r"(taddr));
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(b) : "r"(taddr + 1));
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(c) : "r"(taddr + 2));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // The CTA's stages: units of 8 k-steps of a 128-column tile, tile-major,
 // CTA c takes [c*U/G, (c+1)*U/G), two units of one tile per stage.
 struct QgmWalk {
@@ -113,37 +101,96 @@ struct QgmWalk {
 };
 
 // ---- kernel 0: activation rows -> fixed-point planes ----------------------------
-// Block m < M: row m (RMSNorm-weighted when norm_w is set).  Block M: the
-// all-ones row and the zero padding rows.
-__global__ void __launch_bounds__(256) qgm_planes_kernel(const QGemvArgs a, QGemmWs ws, int np) {
+// Plane rows of one 16-k chunk: row 0 is all ones, rows 1+3m .. 3+3m the three
+// byte planes of activation row m, the rest zero padding.  Block m < M builds
+// row m (RMSNorm-weighted when norm_w is set): every thread keeps up to
+// QGM_PL_CHUNKS chunks of 16 values in registers, so the row is read once with
+// independent 16-byte loads.  Blocks M.. write the ones row and the padding
+// rows of 16 chunks each.
+constexpr int QGM_PL_THREADS = 256;
+constexpr int QGM_PL_CHUNKS = 4;  // 16-k chunks per thread: K <= 256 * 4 * 16 = 16384
+static_assert(QGM_PL_THREADS == 256, "the padding blocks map 16 chunks x 16 rows onto the threads");
+
+__device__ __forceinline__ void qgm_load16(const QGemvArgs &a, int m, int kc, bool vec, float v[16]) {
+    const int K = a.w.K, k0 = kc * 16;
+    if (a.x_bf16) {
+        const __nv_bfloat16 *x = reinterpret_cast<const __nv_bfloat16 *>(a.x) + (size_t)m * a.ldx + k0;
+        if (vec && k0 + 16 <= K) {
+            const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(x)), u1 = __ldg(reinterpret_cast<const uint4 *>(x) + 1);
+            const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                v[2 * i] = __uint_as_float(w[i] << 16);
+                v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = k0 + i < K ? __bfloat162float(x[i]) : 0.f;
+        }
+    } else {
+        const float *x = reinterpret_cast<const float *>(a.x) + (size_t)m * a.ldx + k0;
+        if (vec && k0 + 16 <= K) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 f = __ldg(reinterpret_cast<const float4 *>(x) + i);
+                v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = k0 + i < K ? x[i] : 0.f;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(QGM_PL_THREADS) qgm_planes_kernel(const QGemvArgs a, QGemmWs ws, int np) {
     pdl_launch_dependents();
     pdl_wait();
     const int K = a.w.K, KS = a.w.KS, M = a.M;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int m = blockIdx.x;
-    if (m == M) {
-        for (int i = tid; i < KS * np; i += blockDim.x) {
-            const int kc = i / np, r = i - kc * np;
-            if (r < 3 * M) continue;
-            uint4 v = r == 3 * M ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u)
-                                 : make_uint4(0u, 0u, 0u, 0u);
-            reinterpret_cast<uint4 *>(ws.planes)[(size_t)kc * np + r] = v;
+    if (m >= M) {
+        // ones row and padding rows of 16 chunks per block: thread -> (chunk, padding row)
+        const int npad = np - 3 * M;  // 1 ones row + 0..15 zero rows
+        const int kc = (m - M) * 16 + (tid >> 4), j = tid & 15;
+        if (kc < KS && j < npad) {
+            const int r = j == 0 ? 0 : 3 * M + j;
+            const uint32_t one = j == 0 ? 0x01010101u : 0u;
+            reinterpret_cast<uint4 *>(ws.planes)[(size_t)kc * np + r] = make_uint4(one, one, one, one);
         }
         return;
     }
-    auto xval = [&](int k) -> float {
-        if (a.x_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.x)[(size_t)m * a.ldx + k]);
-        return reinterpret_cast<const float *>(a.x)[(size_t)m * a.ldx + k];
-    };
-    __shared__ double red_s[8];
-    __shared__ float red_m[8];
+    const size_t esz = a.x_bf16 ? 2 : 4;
+    const bool vec = ((reinterpret_cast<uintptr_t>(a.x) | ((size_t)a.ldx * esz)) & 15) == 0;
+    const bool vecw = a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+    __shared__ double red_s[QGM_PL_THREADS / 32];
+    __shared__ float red_m[QGM_PL_THREADS / 32];
     __shared__ int s_shift;
+    float v[QGM_PL_CHUNKS][16];
     float ssq = 0.f, amx = 0.f;
-    for (int k = tid; k < K; k += blockDim.x) {
-        const float x = xval(k);
-        ssq = fmaf(x, x, ssq);
-        const float v = a.norm_w ? __fmul_rn(x, __ldg(a.norm_w + k)) : x;
-        amx = fmaxf(amx, fabsf(v));
+#pragma unroll
+    for (int j = 0; j < QGM_PL_CHUNKS; j++) {
+        const int kc = tid + QGM_PL_THREADS * j;
+        if (kc >= KS) continue;
+        qgm_load16(a, m, kc, vec, v[j]);
+#pragma unroll
+        for (int i = 0; i < 16; i++) ssq = fmaf(v[j][i], v[j][i], ssq);
+        if (a.norm_w) {
+            float w[16];
+            if (vecw && kc * 16 + 16 <= K) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(a.norm_w + kc * 16) + i);
+                    w[4 * i] = f.x, w[4 * i + 1] = f.y, w[4 * i + 2] = f.z, w[4 * i + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; i++) w[i] = kc * 16 + i < K ? __ldg(a.norm_w + kc * 16 + i) : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[j][i] = __fmul_rn(v[j][i], w[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) amx = fmaxf(amx, fabsf(v[j][i]));
     }
     const double s = warp_sum_d((double)ssq);
     const float mx = warp_max_f(amx);
@@ -151,7 +198,7 @@ __global__ void __launch_bounds__(256) qgm_planes_kernel(const QGemvArgs a, QGem
     __syncthreads();
     if (tid == 0) {
         double st = 0.0, mt = 0.0;
-        for (int w = 0; w < (int)blockDim.x / 32; w++) st += red_s[w], mt = fmax(mt, (double)red_m[w]);
+        for (int w = 0; w < QGM_PL_THREADS / 32; w++) st += red_s[w], mt = fmax(mt, (double)red_m[w]);
         // rmsnorm (cpu.rs:582-588): rstd = 1/sqrt(mean(x^2) + eps) in f64
         ws.rstd[m] = a.norm_w ? 1.0 / sqrt(st / (double)K + (double)a.eps) : 1.0;
         int e = 0;
@@ -162,21 +209,18 @@ __global__ void __launch_bounds__(256) qgm_planes_kernel(const QGemvArgs a, QGem
     }
     __syncthreads();
     const float sc = __int_as_float((s_shift + 127) << 23);
-    // one thread per 16-k chunk: U = A + 2^23, three unsigned byte planes
-    for (int kc = tid; kc < KS; kc += blockDim.x) {
+    // U = A + 2^23 in [0, 2^24): three unsigned byte planes per 16-k chunk
+#pragma unroll
+    for (int j = 0; j < QGM_PL_CHUNKS; j++) {
+        const int kc = tid + QGM_PL_THREADS * j;
+        if (kc >= KS) continue;
         uint32_t w[3][4];
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             uint32_t b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const int k = kc * 16 + q * 4 + i;
-                float v = 0.f;
-                if (k < K) {
-                    const float x = xval(k);
-                    v = a.norm_w ? __fmul_rn(x, __ldg(a.norm_w + k)) : x;
-                }
-                const float t = __fmul_rn(v, sc);
+                const float t = __fmul_rn(v[j][q * 4 + i], sc);
                 const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;  // round to nearest even
                 const uint32_t U = (uint32_t)(A + (1 << 23));
                 b0 |= (U & 0xffu) << (8 * i);
@@ -185,38 +229,57 @@ __global__ void __launch_bounds__(256) qgm_planes_kernel(const QGemvArgs a, QGem
             }
             w[0][q] = b0, w[1][q] = b1, w[2][q] = b2;
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(ws.planes) + (size_t)kc * np + 3 * m;
+        uint4 *dst = reinterpret_cast<uint4 *>(ws.planes) + (size_t)kc * np + 1 + 3 * m;
 #pragma unroll
         for (int p = 0; p < 3; p++) dst[p] = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
     }
 }
 
 // ---- kernel 1: weights x planes on the tensor cores -> int64 column sums -------
+// TMEM holds two accumulator buffers of ncols columns each: the MMAs of tile
+// segment s go to buffer s & 1, so the drain of one segment overlaps the MMAs
+// of the next.  A drain warp reads its 32 lanes' plane columns with 16-column
+// tcgen05.ld loads and one wait, then recombines every row in registers.
+constexpr int QGM_DRAIN_LD = (QGM_MAX_M * 3 + 1 + 15) / 16;  // 16-column loads covering every plane row
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
 __global__ void __launch_bounds__(QGM_THREADS, 1)
     qgm_gemm_kernel(const QWeightDesc w, const QGemmWs ws, int M, int np, int nst) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[2 * QGM_MAX_NST + 2];  // full, empty, tmem full, tmem empty
+    // full[nst], empty[nst], tmem full[2], tmem empty[2], mma done
+    __shared__ __align__(8) unsigned long long bars[2 * QGM_MAX_NST + 5];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int slot_bytes = qgm_slot_bytes(np);
     const uint32_t b_full = smem_u32(&bars[0]), b_empty = smem_u32(&bars[QGM_MAX_NST]);
-    const uint32_t b_tfull = smem_u32(&bars[2 * QGM_MAX_NST]), b_tempty = smem_u32(&bars[2 * QGM_MAX_NST + 1]);
-    const int ncols = np <= 32 ? 32 : (np <= 64 ? 64 : 128);
+    const uint32_t b_tfull = smem_u32(&bars[2 * QGM_MAX_NST]), b_tempty = smem_u32(&bars[2 * QGM_MAX_NST + 2]);
+    const uint32_t b_done = smem_u32(&bars[2 * QGM_MAX_NST + 4]);
+    const int ncols = np <= 32 ? 32 : (np <= 64 ? 64 : 128);  // one buffer; two are allocated
     if (tid == 0) {
         for (int i = 0; i < nst; i++) {
             mbar_init(b_full + 8 * i, 1);
             mbar_init(b_empty + 8 * i, 1);  // arrived by tcgen05.commit
         }
-        mbar_init(b_tfull, 1);
-        mbar_init(b_tempty, 4);  // one arrival per draining warp
+        for (int i = 0; i < 2; i++) {
+            mbar_init(b_tfull + 8 * i, 1);
+            mbar_init(b_tempty + 8 * i, 4);  // one arrival per draining warp
+        }
+        mbar_init(b_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_abort = 0;
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(ncols)
+                     "r"(2 * ncols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -267,7 +330,9 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
                 int t, k0, nks;
                 bool se;
                 wk.next(t, k0, nks, se);
-                if (seg_start && seg > 0 && !mbar_wait(b_tempty, (seg - 1) & 1)) ok = false;  // TMEM drained
+                const uint32_t buf = seg & 1;
+                // the buffer's previous segment (seg - 2) has been drained
+                if (seg_start && seg >= 2 && !mbar_wait(b_tempty + 8 * buf, ((seg >> 1) - 1) & 1)) ok = false;
                 if (ok && !mbar_wait(b_full + 8 * slot, par)) ok = false;
                 if (!ok) {
                     atomicOr(&qgm_error_flag, 1u);
@@ -276,22 +341,24 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t a0 = ring + slot * slot_bytes, p0 = a0 + QGM_WBYTES;
+                const uint32_t acc = tmem + buf * (uint32_t)ncols;
                 for (int kk = 0; kk < nks / 2; kk++) {
                     const uint64_t da = umma_sdesc(a0 + kk * 2 * QGM_TN * 16, QGM_TN * 16, 128);
                     const uint64_t db = umma_sdesc(p0 + kk * 2 * np * 16, np * 16, 128);
-                    umma_i8(tmem, da, db, idesc, (seg_start && kk == 0) ? 0u : 1u);
+                    umma_i8(acc, da, db, idesc, (seg_start && kk == 0) ? 0u : 1u);
                 }
                 umma_commit(b_empty + 8 * slot);  // the slot is free once these MMAs complete
                 seg_start = false;
                 if (se) {
-                    umma_commit(b_tfull);  // this tile's sums are complete in TMEM
+                    umma_commit(b_tfull + 8 * buf);  // this tile segment's sums are complete in TMEM
                     seg++;
                     seg_start = true;
                 }
                 if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
             }
-            // leave no tensor-core work running: the last commit covers every MMA issued
-            if (seg > 0 && !mbar_wait(b_tempty, (seg - 1) & 1)) atomicOr(&qgm_error_flag, 1u);
+            // leave no tensor-core work running: this commit tracks every MMA issued
+            umma_commit(b_done);
+            if (!mbar_wait(b_done, 0)) atomicOr(&qgm_error_flag, 1u);
         }
     } else {
         // ---- warps 0-3: drain TMEM per tile segment into exact int64 column sums
@@ -299,64 +366,80 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
         QgmWalk wk(w.KS, w.ntiles, G, cta);
         uint32_t seg = 0;
         const int col = warp * 32 + lane;  // output column within the tile (= TMEM lane)
+        const int nld = (3 * M + 1 + 15) >> 4;
         while (wk.more()) {
             int t, k0, nks;
             bool se;
             wk.next(t, k0, nks, se);
             if (!se) continue;
-            const bool ok = !s_abort && mbar_wait(b_tfull, seg & 1);
+            const uint32_t buf = seg & 1;
+            const bool ok = !s_abort && mbar_wait(b_tfull + 8 * buf, (seg >> 1) & 1);
             if (!ok) {
                 atomicOr(&qgm_error_flag, 1u);
                 s_abort = 1;
                 break;
             }
             tc_fence_after();
-            const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-            // D[3M] = sum_k w over this segment's k range (the ones row)
-            const long long ones = (long long)(int)tmem_ld1(lane_base + (uint32_t)(3 * M));
-            long long *out = ws.acc + (size_t)t * QGM_TN + col;
-            for (int m = 0; m < M; m++) {
-                uint32_t d0, d1, d2;
-                tmem_ld3(lane_base + (uint32_t)(3 * m), d0, d1, d2);
-                const long long s = (long long)(int)d0 + ((long long)(int)d1 << 8) + ((long long)(int)d2 << 16) -
-                                    (ones << 23);
-                if (s != 0)
-                    atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)m * ws.ld_acc), (unsigned long long)s);
-            }
+            const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16) + buf * (uint32_t)ncols;
+            uint32_t d[QGM_DRAIN_LD * 16];
+#pragma unroll
+            for (int j = 0; j < QGM_DRAIN_LD; j++)
+                if (j < nld) tmem_ld16(lane_base + 16 * j, d + 16 * j);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(b_tempty);
+            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the registers hold the segment now
+            // D[0] = sum_k w over this segment's k range (the ones row)
+            const long long ones = (long long)(int)d[0];
+            long long *out = ws.acc + (size_t)t * QGM_TN + col;
+#pragma unroll
+            for (int m = 0; m < QGM_MAX_M; m++) {
+                if (m < M) {
+                    const long long s = (long long)(int)d[1 + 3 * m] + ((long long)(int)d[2 + 3 * m] << 8) +
+                                        ((long long)(int)d[3 + 3 * m] << 16) - (ones << 23);
+                    if (s != 0)
+                        atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)m * ws.ld_acc),
+                                  (unsigned long long)s);
+                }
+            }
             seg++;
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * ncols) : "memory");
 }
 
 // ---- kernel 2: scale, epilogue, clear the sums ------------------------------------
-// One CTA per 128-column tile, all rows.  The epilogues are those of
+// One CTA per (128-column tile, pair of rows), one element per thread, so no
+// thread waits on a chain of dependent loads.  The epilogues are those of
 // qgemv.cu for any row count.
+constexpr int QGM_FIN_ROWS = 2;
+
 template <int EPI>
-__global__ void __launch_bounds__(256) qgm_finish_kernel(const QGemvArgs a, const QGemmWs ws) {
-    __shared__ float ys[QGM_MAX_M * QGM_TN];
+__global__ void __launch_bounds__(QGM_FIN_ROWS * QGM_TN) qgm_finish_kernel(const QGemvArgs a, const QGemmWs ws) {
+    __shared__ float ys[QGM_FIN_ROWS * QGM_TN];
+    __shared__ float s_bv[QGM_FIN_ROWS * QGM_TN / 32];
+    __shared__ int s_bi[QGM_FIN_ROWS * QGM_TN / 32];
     pdl_launch_dependents();
     pdl_wait();
     const int tile = blockIdx.x, tid = threadIdx.x, M = a.M;
-    for (int it = tid; it < M * QGM_TN; it += blockDim.x) {
-        const int m = it / QGM_TN, c = it - m * QGM_TN;
-        long long *p = ws.acc + (size_t)m * ws.ld_acc + (size_t)tile * QGM_TN + c;
+    const int c = tid & (QGM_TN - 1);
+    const int m = blockIdx.y * QGM_FIN_ROWS + tid / QGM_TN;
+    const int n = tile * QGM_TN + c;
+    const bool row = m < M;
+    float y = 0.f;
+    if (row) {
+        long long *p = ws.acc + (size_t)m * ws.ld_acc + n;
         const long long t = __ldcg(p);
         *p = 0;
         const float sc = (EPI == QEPI_SWIGLU && (c & 31) >= 16) ? a.w.scale_up : a.w.scale;
-        ys[it] = gemv_out(t, gemv_factor(ws.shift[m], sc, ws.rstd[m]));
+        y = gemv_out(t, gemv_factor(ws.shift[m], sc, ws.rstd[m]));
     }
+    ys[tid] = y;
     __syncthreads();
-    for (int it = tid; it < M * QGM_TN; it += blockDim.x) {
-        const int m = it / QGM_TN, c = it - m * QGM_TN;
-        const int n = tile * QGM_TN + c;
-        const float y = ys[it];
+    if (row) {
         if (EPI == QEPI_STORE || EPI == QEPI_LOGITS) {
             if (n < a.w.N) a.out[(size_t)m * a.ldo + n] = y;
         } else if (EPI == QEPI_BIAS) {
@@ -370,61 +453,65 @@ __global__ void __launch_bounds__(256) qgm_finish_kernel(const QGemvArgs a, cons
             const int within = n & 31;
             if (within < 16) {
                 const int j = (n >> 5) * 16 + within;
-                if (j < a.F) a.out[(size_t)m * a.ldo + j] = __fmul_rn(silu_f64(y), ys[it + 16]);
+                if (j < a.F) a.out[(size_t)m * a.ldo + j] = __fmul_rn(silu_f64(y), ys[tid + 16]);
             }
         } else if (EPI == QEPI_QKV) {
-            if (n >= a.w.N) continue;
             const int pos = a.pos[m];
-            if (pos < 0 || pos >= a.max_pos) continue;
-            const int qk = a.q_dim + a.kv_dim;
-            float val = y;
-            if (n < qk) {
-                // rope_with_freqs_preloaded (cpu.rs:650-661)
-                const int nn = n < a.q_dim ? n : n - a.q_dim;
-                const int d = nn % a.hd, i = d >> 1;
-                const float partner = ys[it ^ 1];
-                const float cs = a.rope_cos[(size_t)pos * (a.hd / 2) + i];
-                const float sn = a.rope_sin[(size_t)pos * (a.hd / 2) + i];
-                val = (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
-                              : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
-            }
-            if (n < a.q_dim) {
-                a.q_out[(size_t)m * a.q_dim + n] = __fmul_rn(val, a.q_scale);
-            } else {
-                const bool is_k = n < qk;
-                const int nn = is_k ? n - a.q_dim : n - qk;
-                const int kh = nn / a.hd, d = nn - kh * a.hd;
-                const int page = a.page_table[(size_t)m * a.max_pages + pos / a.page_size];
-                const size_t idx = (((size_t)page * a.n_kv + kh) * a.page_size + pos % a.page_size) * a.hd + d;
-                void *cache = is_k ? a.kcache : a.vcache;
-                if (a.kv_f32)
-                    reinterpret_cast<float *>(cache)[idx] = val;
-                else
-                    reinterpret_cast<__nv_bfloat16 *>(cache)[idx] = __float2bfloat16_rn(val);
+            if (n < a.w.N && pos >= 0 && pos < a.max_pos) {
+                const int qk = a.q_dim + a.kv_dim;
+                float val = y;
+                if (n < qk) {
+                    // rope_with_freqs_preloaded (cpu.rs:650-661)
+                    const int nn = n < a.q_dim ? n : n - a.q_dim;
+                    const int d = nn % a.hd, i = d >> 1;
+                    const float partner = ys[tid ^ 1];
+                    const float cs = a.rope_cos[(size_t)pos * (a.hd / 2) + i];
+                    const float sn = a.rope_sin[(size_t)pos * (a.hd / 2) + i];
+                    val = (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
+                                  : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
+                }
+                if (n < a.q_dim) {
+                    a.q_out[(size_t)m * a.q_dim + n] = __fmul_rn(val, a.q_scale);
+                } else {
+                    const bool is_k = n < qk;
+                    const int nn = is_k ? n - a.q_dim : n - qk;
+                    const int kh = nn / a.hd, d = nn - kh * a.hd;
+                    const int page = a.page_table[(size_t)m * a.max_pages + pos / a.page_size];
+                    const size_t idx = (((size_t)page * a.n_kv + kh) * a.page_size + pos % a.page_size) * a.hd + d;
+                    void *cache = is_k ? a.kcache : a.vcache;
+                    if (a.kv_f32)
+                        reinterpret_cast<float *>(cache)[idx] = val;
+                    else
+                        reinterpret_cast<__nv_bfloat16 *>(cache)[idx] = __float2bfloat16_rn(val);
+                }
             }
         }
     }
     if (EPI == QEPI_LOGITS) {
         // per-tile argmax candidate of every row; ties resolve to the larger index
         const int warp = tid >> 5, lane = tid & 31;
-        for (int m = warp; m < M; m += blockDim.x / 32) {
-            float best = -INFINITY;
-            int bi = -1;
-            for (int c = lane; c < QGM_TN; c += 32) {
-                const int n = tile * QGM_TN + c;
-                if (n < a.w.N) {
-                    const float v = ys[m * QGM_TN + c];
-                    if (bi < 0 || v >= best) best = v, bi = n;
-                }
+        float best = y;
+        int bi = (row && n < a.w.N) ? n : -1;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
+        }
+        if (lane == 0) s_bv[warp] = best, s_bi[warp] = bi;
+        __syncthreads();
+        constexpr int WPR = QGM_TN / 32;  // warps per row
+        if (tid < QGM_FIN_ROWS) {
+            const int mm = blockIdx.y * QGM_FIN_ROWS + tid;
+            float bv = s_bv[tid * WPR];
+            int bj = s_bi[tid * WPR];
+            for (int k = 1; k < WPR; k++) {
+                const float ov = s_bv[tid * WPR + k];
+                const int oi = s_bi[tid * WPR + k];
+                if (oi >= 0 && (bj < 0 || ov > bv || (ov == bv && oi > bj))) bv = ov, bj = oi;
             }
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
-            }
-            if (lane == 0) {
-                a.cand_val[(size_t)m * a.w.ntiles + tile] = best;
-                a.cand_idx[(size_t)m * a.w.ntiles + tile] = bi;
+            if (mm < M) {
+                a.cand_val[(size_t)mm * a.w.ntiles + tile] = bv;
+                a.cand_idx[(size_t)mm * a.w.ntiles + tile] = bj;
             }
         }
     }
@@ -441,7 +528,8 @@ int qgm_nst(int np, int *limit_out) {
 
 template <int EPI>
 int finish_launch(const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
-    SB_CUDA_TRY(launch(qgm_finish_kernel<EPI>, dim3(a.w.ntiles), dim3(256), 0, st, pdl, a, ws));
+    SB_CUDA_TRY(launch(qgm_finish_kernel<EPI>, dim3(a.w.ntiles, ceil_div(a.M, QGM_FIN_ROWS)), dim3(QGM_FIN_ROWS * QGM_TN),
+                       0, st, pdl, a, ws));
     return SB_OK;
 }
 
@@ -475,7 +563,8 @@ int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st
     int limit = 0;
     const int nst = qgm_nst(np, &limit);
     SB_CHECK(nst >= 2, SB_ERR_SHAPE, "qgemm: %d rows need %d B per stage (limit %d)", a.M, qgm_slot_bytes(np), limit);
-    SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + 1), dim3(256), 0, st, pdl, a, ws, np));
+    SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + ceil_div(a.w.KS, 16)), dim3(QGM_PL_THREADS), 0, st, pdl, a, ws,
+                       np));
     const int upt = ceil_div(a.w.KS, QGM_UNIT_KS);
     const int G = std::max(1, std::min(device_props().sm_count, a.w.ntiles * upt / 2));
     SB_CUDA_TRY(launch(qgm_gemm_kernel, dim3(G), dim3(QGM_THREADS), (size_t)nst * qgm_slot_bytes(np), st, pdl, a.w, ws,
