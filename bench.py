@@ -30,8 +30,13 @@ steps follow the prompt and W warm-up steps.
 
 --impl reference times that CPU path alone (the reference is Rust and cannot
 be built here; the oracle restates it operation by operation).
-Multi-GPU (torchrun): every rank runs an independent replica (the path is
-replicated; tensor parallelism is not built yet), value sums over ranks.
+Multi-GPU (torchrun, N ranks): tensor parallelism over the N GPUs -- every
+rank holds 1/N of every projection and of the KV heads, the partial o and
+down products are summed with an NCCL all-reduce over NVLink, and the greedy
+token is the argmax over all ranks' vocabulary slices.  The workload (model,
+batch, prompt) is the same at every N ("scaling": "strong"); value is the
+job's tokens/s from the slowest rank's CUDA-event time.  --replicas runs N
+independent single-GPU replicas instead (weak scaling).
 """
 from __future__ import annotations
 
@@ -202,8 +207,17 @@ def run_ours(args, rank: int, world: int, dist):
     B = args.batch
     K, W = args.steps, args.warmup
     max_seq = args.prompt + W + K + 8
-    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=B, kv_dtype="bf16")
-    rng = np.random.default_rng(1000 + rank)
+    tp = world if (world > 1 and not args.replicas) else 1
+    tp_kw = {}
+    if tp > 1:
+        from esolearn_b200 import tp_unique_id
+
+        obj = [tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp_kw = {"tp_rank": rank, "tp_size": tp, "tp_id": obj[0]}
+    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=B, kv_dtype="bf16", **tp_kw)
+    # tensor-parallel ranks decode the same sequences; replicas decode their own
+    rng = np.random.default_rng(1000 + (0 if tp > 1 else rank))
     prompts = rng.integers(0, cfg.vocab_size, (B, args.prompt), dtype=np.int64).astype(np.int32)
     model.begin(prompts)
     model.step(args.prompt - 1 + W)  # prefill (token by token, as generate() does) + warm-up
@@ -235,7 +249,8 @@ def run_ours(args, rank: int, world: int, dist):
     clocks.stop()
     ctx_mid = args.prompt + W + K / 2
     wbytes, kv_per_pos = model.step_bytes()
-    value = world * B * K / (ms / 1000.0)
+    n_jobs = 1 if tp > 1 else world  # independent decode jobs in the run
+    value = n_jobs * B * K / (ms / 1000.0)
     launches_per_step = model.step_launches(B)
     peak, peak_kind = read_peaks()
     step_alg_bytes = wbytes + kv_per_pos * ctx_mid * B
@@ -282,7 +297,12 @@ def run_ours(args, rank: int, world: int, dist):
             _, am = model.forward_batch(pinned_tok.numpy(), [p0 + i] * B, want_logits=False)
             last = am
         t1 = time.perf_counter()
-        e2e = {"value": world * B * n_e2e / (t1 - t0), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+        e2e_s = t1 - t0
+        if dist is not None:
+            tt = torch.tensor([e2e_s], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = float(tt.item())
+        e2e = {"value": n_jobs * B * n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
                "d2h_bytes_per_step": 4 * B, "steps": n_e2e,
                "api": "sb_llama_forward (token, position in; argmax out; stream-synchronous)"}
 
@@ -290,12 +310,15 @@ def run_ours(args, rank: int, world: int, dist):
         return
     res = {
         "metric": wl["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
+        "vs_baseline": None,
         "dtype": "int8 weights x f32 activations (exact int32 dp4a products), f32 accumulate; bf16 KV",
         "data": "synthetic: seeded random-init weights (fastrand/Box-Muller N(0,0.02), LlamaModel::new order), "
                 "seeded uniform prompt ids",
         "config": {"workload": wl["desc"], "batch": B, "prompt": args.prompt,
-                   "context_mid": ctx_mid, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "context_mid": ctx_mid,
+                   "parallelism": (f"tp{tp} (NCCL all-reduce after o and down, NVLink)" if tp > 1 else
+                                   f"replicas x{world}" if world > 1 else "single GPU"),
                    "l2": f"weights {wbytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
                    "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else
                               "CUDA graph of per-operation kernels per step, programmatic dependent launch")},
@@ -322,6 +345,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=None, help="prompt length (default: the workload's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     args.batch = wl["batch"] if args.batch is None else args.batch

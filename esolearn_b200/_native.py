@@ -16,7 +16,8 @@ STATUS_NAMES = {0: "SB_OK", 1: "SB_ERR_CUDA", 2: "SB_ERR_NCCL", 3: "SB_ERR_TIMEO
                 5: "SB_ERR_OOM", 6: "SB_ERR_ARG", 7: "SB_ERR_STATE", 8: "SB_ERR_UNSUPPORTED"}
 SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
 SB_KV_BF16, SB_KV_F32 = 0, 1
-SB_W_QKV, SB_W_O, SB_W_GATE, SB_W_UP, SB_W_DOWN = range(5)
+SB_W_QKV, SB_W_O, SB_W_GATE, SB_W_UP, SB_W_DOWN, SB_W_LM_HEAD = range(6)
+SB_TP_ID_BYTES = 128
 SB_F_EMBED, SB_F_NORM_IN, SB_F_NORM_POST, SB_F_NORM_FINAL = range(4)
 
 
@@ -69,6 +70,9 @@ SIGNATURES = {
     "sb_attn_decode_paged_noalloc": (C.c_int, [vp, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
                                                C.c_int, C.c_int, C.c_int, vp, vp]),
     "sb_llama_create": (C.c_int, [C.POINTER(LlamaConfigC), C.POINTER(vp)]),
+    "sb_tp_unique_id": (C.c_int, [vp]),
+    "sb_llama_create_tp": (C.c_int, [C.POINTER(LlamaConfigC), C.c_int, C.c_int, vp, C.POINTER(vp)]),
+    "sb_tp_shard_qweight": (C.c_int, [C.POINTER(LlamaConfigC), C.c_int, C.c_int, C.c_int, vp, vp, i32p, i32p]),
     "sb_llama_destroy": (C.c_int, [vp]),
     "sb_llama_init_random": (C.c_int, [vp, C.c_uint64]),
     "sb_llama_load_qweight": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_float]),

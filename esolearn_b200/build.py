@@ -58,7 +58,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
         if r.returncode != 0:
             raise subprocess.CalledProcessError(r.returncode, cmd)
     if force or _needs(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -30,6 +30,7 @@
 #include "misc.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
+#include "tp_comm.cuh"
 
 namespace sb {
 
@@ -45,7 +46,14 @@ using namespace sb;
 struct sb_llama {
     sb_llama_config cfg{};
     int dev = 0;
+    // h, V: full hidden size and vocabulary; F, nh, nkv, q/kv dims and Vl:
+    // this rank's share under tensor parallelism (the full values at tp = 1)
     int h = 0, F = 0, V = 0, L = 0, nh = 0, nkv = 0, hd = 0, q_dim = 0, kv_dim = 0, qkv_dim = 0;
+    int Vl = 0;
+    int tp = 1, tp_rank = 0;
+    TpComm comm;
+    float *cand_all_val = nullptr, *logits_all = nullptr;  // all ranks' candidates / logits
+    int *cand_all_idx = nullptr;
     int B = 1, P = 64, pps = 0;
     cudaStream_t st = nullptr;
     std::vector<void *> allocs;
@@ -206,6 +214,17 @@ struct StepProfiler {
     }
 };
 
+// O and down projections add into the residual stream x.  Under tensor
+// parallelism each rank holds a row slice of the weight, so rank 0 adds its
+// partial product to x and the other ranks store theirs; the sum over ranks
+// (NCCL all-reduce over NVLink, in place) is then x + sum of partials
+// (llama.rs:564,568).
+int resid_epi(const sb_llama *m) { return (m->tp > 1 && m->tp_rank != 0) ? QEPI_STORE : QEPI_RESID; }
+int tp_reduce_residual(sb_llama *m, int M, cudaStream_t st) {
+    if (m->tp == 1) return SB_OK;
+    return tp_allreduce_f32(m->comm, m->x, (size_t)M * m->h, st);
+}
+
 // One linear of a step: the GEMV for up to 4 rows, the tensor-core GEMM for
 // 5-32 (every weight then has 128-column tiles).
 int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, bool pdl) {
@@ -273,7 +292,8 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             QGemvArgs a = gemv_common(ly.o, M, m->attn, m->q_dim);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, engine_linear(m, QEPI_RESID, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, resid_epi(m), a, st, pdl));
+            SB_TRY(tp_reduce_residual(m, M, st));
         }
         {
             QGemvArgs a = gemv_common(ly.gu, M, m->x, m->h);
@@ -288,7 +308,8 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             QGemvArgs a = gemv_common(ly.down, M, m->act, m->F);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, engine_linear(m, QEPI_RESID, a, st, pdl));
+            SB_PROF(prof, 0, engine_linear(m, resid_epi(m), a, st, pdl));
+            SB_TRY(tp_reduce_residual(m, M, st));
         }
         if (trace)
             SB_CUDA_TRY(cudaMemcpyAsync(m->trace_buf + (size_t)l * M * m->h, m->x, sizeof(float) * M * m->h,
@@ -299,12 +320,21 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
         a.norm_w = m->norm_final;
         a.eps = m->cfg.rms_norm_eps;
         a.out = m->logits;
-        a.ldo = m->V;
+        a.ldo = m->Vl;
         a.cand_val = m->cand_val;
         a.cand_idx = m->cand_idx;
         SB_PROF(prof, 0, engine_linear(m, QEPI_LOGITS, a, st, pdl));
     }
-    SB_PROF(prof, 2, argmax_step_launch(m->cand_val, m->cand_idx, m->lm.ntiles, m->seq, M, st, pdl));
+    if (m->tp > 1) {
+        // every rank's per-tile candidates [rank][row][tile]; rank r's columns start at r * Vl
+        const size_t n = (size_t)M * m->lm.ntiles;
+        SB_TRY(tp_allgather32(m->comm, m->cand_val, m->cand_all_val, n, st));
+        SB_TRY(tp_allgather32(m->comm, m->cand_idx, m->cand_all_idx, n, st));
+        SB_PROF(prof, 2, argmax_step_launch(m->cand_all_val, m->cand_all_idx, m->lm.ntiles, m->seq, M, st, pdl,
+                                            m->tp, (int)n, m->Vl));
+    } else {
+        SB_PROF(prof, 2, argmax_step_launch(m->cand_val, m->cand_idx, m->lm.ntiles, m->seq, M, st, pdl));
+    }
     return SB_OK;
 }
 
@@ -435,9 +465,65 @@ int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const 
 
 extern "C" {
 
-sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
+}  // extern "C"
+
+namespace {
+
+// Rank r's slice of a full reference tensor under tensor parallelism
+// (Megatron-style): column slices of q|k|v (by heads), gate and up (by ffn
+// columns); row slices of o (by heads), down (by ffn rows) and the [V,h]
+// lm_head (by vocabulary rows).  Shapes in rows x cols of the reference
+// layout; with src == nullptr only the shapes are returned.
+int tp_shard(const sb_llama_config &c, int slot, int r, int T, const int8_t *src, int8_t *dst, int *rows,
+             int *cols) {
+    SB_CHECK(T >= 1 && r >= 0 && r < T, SB_ERR_ARG, "tensor parallel rank %d of %d", r, T);
+    SB_CHECK(c.n_heads > 0 && c.n_kv_heads > 0 && c.hidden_size % c.n_heads == 0, SB_ERR_SHAPE, "bad head counts");
+    SB_CHECK(c.n_heads % T == 0 && c.n_kv_heads % T == 0 && c.intermediate_size % T == 0 && c.vocab_size % T == 0,
+             SB_ERR_SHAPE, "tensor parallel %d must divide heads, kv heads, ffn and vocab", T);
+    const int h = c.hidden_size, hd = h / c.n_heads;
+    const int Qf = c.n_heads * hd, KVf = c.n_kv_heads * hd, q = Qf / T, kv = KVf / T;
+    const int F = c.intermediate_size, Fl = F / T, V = c.vocab_size, Vl = V / T;
+    // full cols (row stride), row offset, row count, then up to three column runs (src col, count)
+    int fc = 0, r0 = 0, nr = 0, nrun = 1, c0[3] = {0, 0, 0}, cn[3] = {0, 0, 0};
+    switch (slot) {
+    case SB_W_QKV:
+        fc = Qf + 2 * KVf, nr = h, nrun = 3;
+        c0[0] = r * q, cn[0] = q, c0[1] = Qf + r * kv, cn[1] = kv, c0[2] = Qf + KVf + r * kv, cn[2] = kv;
+        break;
+    case SB_W_O: fc = h, r0 = r * q, nr = q, cn[0] = h; break;
+    case SB_W_GATE:
+    case SB_W_UP: fc = F, nr = h, c0[0] = r * Fl, cn[0] = Fl; break;
+    case SB_W_DOWN: fc = h, r0 = r * Fl, nr = Fl, cn[0] = h; break;
+    case SB_W_LM_HEAD: fc = h, r0 = r * Vl, nr = Vl, cn[0] = h; break;
+    default: return set_error(SB_ERR_ARG, "tp_shard: unknown weight slot %d", slot);
+    }
+    int nc = 0;
+    for (int i = 0; i < nrun; i++) nc += cn[i];
+    if (rows) *rows = nr;
+    if (cols) *cols = nc;
+    if (!src) return SB_OK;
+    SB_CHECK(dst, SB_ERR_ARG, "tp_shard: null destination");
+    for (int i = 0; i < nr; i++) {
+        const int8_t *srow = src + (size_t)(r0 + i) * fc;
+        int8_t *drow = dst + (size_t)i * nc;
+        for (int k = 0; k < nrun; k++) {
+            std::memcpy(drow, srow + c0[k], (size_t)cn[k]);
+            drow += cn[k];
+        }
+    }
+    return SB_OK;
+}
+
+int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uint8_t *tp_id, sb_llama **out) {
     SB_CHECK(cfg && out, SB_ERR_ARG, "sb_llama_create: null argument");
     const sb_llama_config &c = *cfg;
+    SB_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, SB_ERR_ARG, "tensor parallel rank %d of %d", tp_rank,
+             tp_size);
+    SB_CHECK(tp_size == 1 || tp_id, SB_ERR_ARG, "sb_llama_create_tp: null communicator id");
+    SB_CHECK(c.n_heads % tp_size == 0 && c.n_kv_heads % tp_size == 0 && c.intermediate_size % tp_size == 0 &&
+                 c.vocab_size % tp_size == 0,
+             SB_ERR_SHAPE, "tensor parallel %d must divide heads %d, kv heads %d, ffn %d and vocab %d", tp_size,
+             c.n_heads, c.n_kv_heads, c.intermediate_size, c.vocab_size);
     SB_CHECK(c.hidden_size > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.n_layers > 0 && c.vocab_size > 0 &&
                  c.intermediate_size > 0 && c.max_seq_len > 0,
              SB_ERR_SHAPE, "sb_llama_create: non-positive dimension");
@@ -447,9 +533,11 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
              "sb_llama_create: max_batch %d outside 1..%d", c.max_batch, QGM_MAX_M);
     if (c.max_batch > QG_MAX_M) {
         // the tensor-core path reads the input in 32-element k steps
-        const int qd = c.hidden_size / c.n_heads * c.n_heads;
-        SB_CHECK(c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 && qd % 32 == 0, SB_ERR_UNSUPPORTED,
-                 "sb_llama_create: batches above %d need hidden, q and ffn sizes that are multiples of 32", QG_MAX_M);
+        const int qd = c.hidden_size / c.n_heads * (c.n_heads / tp_size);
+        SB_CHECK(c.hidden_size % 32 == 0 && (c.intermediate_size / tp_size) % 32 == 0 && qd % 32 == 0,
+                 SB_ERR_UNSUPPORTED,
+                 "sb_llama_create: batches above %d need hidden, q and ffn sizes (per rank) that are multiples of 32",
+                 QG_MAX_M);
     }
     const int hd = c.hidden_size / c.n_heads;
     SB_CHECK(hd == 64 || hd == 128, SB_ERR_UNSUPPORTED, "sb_llama_create: head_dim %d not in {64,128}", hd);
@@ -457,12 +545,15 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
     sb_llama *m = new sb_llama();
     m->cfg = c;
     cudaGetDevice(&m->dev);
+    m->tp = tp_size;
+    m->tp_rank = tp_rank;
     m->h = c.hidden_size;
-    m->F = c.intermediate_size;
+    m->F = c.intermediate_size / tp_size;
     m->V = c.vocab_size;
+    m->Vl = c.vocab_size / tp_size;
     m->L = c.n_layers;
-    m->nh = c.n_heads;
-    m->nkv = c.n_kv_heads;
+    m->nh = c.n_heads / tp_size;
+    m->nkv = c.n_kv_heads / tp_size;
     m->hd = hd;
     m->q_dim = m->nh * hd;
     m->kv_dim = m->nkv * hd;
@@ -480,7 +571,8 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         return fail(set_error(SB_ERR_CUDA, "cudaStreamCreate failed"));
 
     int rc = SB_OK;
-    {
+    if (tp_size > 1 && (rc = tp_init(m->comm, tp_id, tp_rank, tp_size, 120.0)) != SB_OK) return fail(rc);
+    if (tp_size == 1) {
         int chunk = 0;
         if (ds_supported(m->h, m->F, m->q_dim, hd, m->nh / m->nkv, m->kv_f32, m->P, &chunk)) {
             const int ksmax = ceil_div(std::max(std::max(m->h, m->F), m->q_dim), 16);
@@ -505,7 +597,7 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         if ((rc = make_qweight(m, ly.gu, m->h, gu_cols, 32)) != SB_OK) break;
         if ((rc = make_qweight(m, ly.down, m->F, m->h, 16)) != SB_OK) break;
     }
-    if (rc == SB_OK) rc = make_qweight(m, m->lm, m->h, m->V, 16);
+    if (rc == SB_OK) rc = make_qweight(m, m->lm, m->h, m->Vl, 16);
     if (rc == SB_OK) rc = dalloc_t(m, &m->embed, (size_t)m->V * m->h);
     if (rc == SB_OK) rc = dalloc_t(m, &m->norm_in, (size_t)m->L * m->h);
     if (rc == SB_OK) rc = dalloc_t(m, &m->norm_post, (size_t)m->L * m->h);
@@ -520,7 +612,7 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         cudaStreamSynchronize(m->st);
     }
     // staging for gate/up pairing and for on-device generation
-    m->stage_bytes = std::max<size_t>((size_t)2 * m->h * m->F, (size_t)m->V * m->h);
+    m->stage_bytes = std::max<size_t>((size_t)2 * m->h * m->F, (size_t)m->Vl * m->h);
     m->stage_bytes = std::max<size_t>(m->stage_bytes, (size_t)m->h * m->qkv_dim);
     if ((rc = dalloc(m, (void **)&m->stage, m->stage_bytes)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->amax, 4)) != SB_OK) return fail(rc);
@@ -551,7 +643,7 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
     if ((rc = dalloc_t(m, &m->q, (size_t)B * m->q_dim)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->attn, (size_t)B * m->q_dim)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->act, (size_t)B * m->F)) != SB_OK) return fail(rc);
-    if ((rc = dalloc_t(m, &m->logits, (size_t)B * m->V)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->logits, (size_t)B * m->Vl)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->cand_val, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->cand_idx, (size_t)B * m->lm.ntiles)) != SB_OK) return fail(rc);
     m->att_splits = attn_pick_splits(B, m->nkv, c.max_seq_len);
@@ -598,16 +690,45 @@ sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) {
         if ((rc = dalloc_t(m, &m->gws.rstd, (size_t)B)) != SB_OK) return fail(rc);
     }
     if ((rc = dalloc_t(m, &m->trace_buf, (size_t)m->L * B * m->h)) != SB_OK) return fail(rc);
+    if (tp_size > 1) {
+        const size_t nc = (size_t)tp_size * B * m->lm.ntiles;
+        if ((rc = dalloc_t(m, &m->cand_all_val, nc)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->cand_all_idx, nc)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->logits_all, (size_t)B * m->V)) != SB_OK) return fail(rc);
+    }
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     *out = m;
     return SB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out) { return llama_create(cfg, 0, 1, nullptr, out); }
+
+sb_status sb_llama_create_tp(const sb_llama_config *cfg, int tp_rank, int tp_size, const uint8_t *tp_id,
+                             sb_llama **out) {
+    return llama_create(cfg, tp_rank, tp_size, tp_id, out);
+}
+
+sb_status sb_tp_shard_qweight(const sb_llama_config *cfg, int slot, int tp_rank, int tp_size, const int8_t *full,
+                              int8_t *shard, int *rows, int *cols) {
+    SB_CHECK(cfg, SB_ERR_ARG, "sb_tp_shard_qweight: null config");
+    return tp_shard(*cfg, slot, tp_rank, tp_size, full, shard, rows, cols);
+}
+
+sb_status sb_tp_unique_id(uint8_t *id) {
+    SB_CHECK(id, SB_ERR_ARG, "sb_tp_unique_id: null argument");
+    return tp_unique_id(id);
 }
 
 sb_status sb_llama_destroy(sb_llama *m) {
     if (!m) return SB_OK;
     if (m->st) cudaStreamSynchronize(m->st);
     for (auto g : m->graphs)
-        if (g) cudaGraphExecDestroy(g);
+        if (g) cudaGraphExecDestroy(g);  // graphs hold NCCL calls: release them before the communicator
+    tp_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
@@ -638,9 +759,20 @@ sb_status sb_llama_load_f32(sb_llama *m, int which, int layer, const float *data
 
 sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *q, float scale) {
     SB_CHECK(m && q, SB_ERR_ARG, "sb_llama_load_qweight: null argument");
+    std::vector<int8_t> shard;
+    if (m->tp > 1) {  // keep this rank's slice of the full tensor (the scale is the full tensor's)
+        SB_CHECK(layer < m->L && (layer < 0 || (slot >= 0 && slot < 5)), SB_ERR_ARG, "bad layer %d / slot %d", layer,
+                 slot);
+        const int sl = layer < 0 ? SB_W_LM_HEAD : slot;
+        int rows = 0, cols = 0;
+        SB_TRY(tp_shard(m->cfg, sl, m->tp_rank, m->tp, nullptr, nullptr, &rows, &cols));
+        shard.resize((size_t)rows * cols);
+        SB_TRY(tp_shard(m->cfg, sl, m->tp_rank, m->tp, q, shard.data(), nullptr, nullptr));
+        q = shard.data();
+    }
     if (layer < 0) {  // lm_head, [V,h] like llama.rs:943-948
-        SB_CUDA_TRY(cudaMemcpyAsync(m->stage, q, (size_t)m->V * m->h, cudaMemcpyHostToDevice, m->st));
-        SB_TRY(qweight_pack(m->stage, m->h, m->V, m->lm.TN, 0, 1, const_cast<uint4 *>(m->lm.w), m->st));
+        SB_CUDA_TRY(cudaMemcpyAsync(m->stage, q, (size_t)m->Vl * m->h, cudaMemcpyHostToDevice, m->st));
+        SB_TRY(qweight_pack(m->stage, m->h, m->Vl, m->lm.TN, 0, 1, const_cast<uint4 *>(m->lm.w), m->st));
         m->lm.scale = scale;
         m->has_lm = true;
         SB_CUDA_TRY(cudaStreamSynchronize(m->st));
@@ -685,12 +817,12 @@ sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *
 sb_status sb_llama_get_qweight(sb_llama *m, int layer, int slot, int8_t *q, float *scale) {
     SB_CHECK(m && q && scale, SB_ERR_ARG, "sb_llama_get_qweight: null argument");
     if (layer < 0) {
-        SB_TRY(qweight_unpack(m->lm.w, m->h, m->V, m->lm.TN, 0, m->stage, m->st));
-        std::vector<int8_t> hv((size_t)m->h * m->V);
+        SB_TRY(qweight_unpack(m->lm.w, m->h, m->Vl, m->lm.TN, 0, m->stage, m->st));
+        std::vector<int8_t> hv((size_t)m->h * m->Vl);
         SB_CUDA_TRY(cudaMemcpyAsync(hv.data(), m->stage, hv.size(), cudaMemcpyDeviceToHost, m->st));
         SB_CUDA_TRY(cudaStreamSynchronize(m->st));
         for (int k = 0; k < m->h; k++)
-            for (int n = 0; n < m->V; n++) q[(size_t)n * m->h + k] = hv[(size_t)k * m->V + n];
+            for (int n = 0; n < m->Vl; n++) q[(size_t)n * m->h + k] = hv[(size_t)k * m->Vl + n];
         *scale = m->lm.scale;
         return SB_OK;
     }
@@ -725,81 +857,89 @@ sb_status sb_llama_get_qweight(sb_llama *m, int layer, int slot, int8_t *q, floa
 
 sb_status sb_llama_init_random(sb_llama *m, uint64_t seed) {
     // LlamaModel::new (llama.rs:593-680) draw order: embed [V*h]; per layer
-    // q, k, v, o, gate, up, down; lm_head [V*h] when untied.
+    // q, k, v, o, gate, up, down; lm_head [V*h] when untied.  Under tensor
+    // parallelism every rank walks the same full stream: the scale comes from
+    // the full tensor's absmax (spec `full`), the quantized values only for
+    // this rank's slice (spec `part`, same sample indices).
     SB_CHECK(m, SB_ERR_ARG, "sb_llama_init_random: null model");
-    const int h = m->h, F = m->F, V = m->V;
+    const int h = m->h, V = m->V, T = m->tp, r = m->tp_rank;
+    const int F = m->F, Ff = F * T;                       // local / full ffn
+    const int q = m->q_dim, kv = m->kv_dim, Qf = q * T, KVf = kv * T;
+    const int Vl = m->Vl;
     uint64_t sample = 0;
     SB_TRY(gen_normal_f32(seed, sample, (size_t)V * h, m->embed, m->st));
     sample += (uint64_t)V * h;
-    float scale = 0.0f;
-    auto quant_pack = [&](GenSpec &g, QWeightDesc &d, int pair_F, int8_t *dst_stage, bool pack, float *sc) -> int {
-        SB_TRY(gen_absmax(g, seed, m->amax, m->st));
-        SB_TRY(gen_quantize(g, seed, m->amax, dst_stage, m->scale_dev, m->st));
+    auto quant = [&](const GenSpec &full, const GenSpec &part, int8_t *dst_stage, float *sc) -> int {
+        SB_TRY(gen_absmax(full, seed, m->amax, m->st));
+        SB_TRY(gen_quantize(part, seed, m->amax, dst_stage, m->scale_dev, m->st));
         SB_CUDA_TRY(cudaMemcpyAsync(sc, m->scale_dev, 4, cudaMemcpyDeviceToHost, m->st));
         SB_CUDA_TRY(cudaStreamSynchronize(m->st));
-        if (pack) SB_TRY(qweight_pack(m->stage, d.K, d.N, d.TN, pair_F, 0, const_cast<uint4 *>(d.w), m->st));
         return SB_OK;
+    };
+    // [K, N] matrix of the stream at `base` (row stride N): rows [r0, r0+k), cols [c0, c0+n)
+    auto block = [&](uint64_t base, int N, int r0, int k, int c0, int n) {
+        GenSpec g;
+        g.K = k;
+        g.N = n;
+        g.width[0] = N;
+        g.base[0] = base + (uint64_t)r0 * N + c0;
+        return g;
     };
     for (int l = 0; l < m->L; l++) {
         sb_llama::Layer &ly = m->layers[l];
-        GenSpec g;
-        g.K = h;
-        g.N = m->qkv_dim;
-        g.nseg = 3;
-        g.c0[0] = 0, g.c0[1] = m->q_dim, g.c0[2] = m->q_dim + m->kv_dim;
-        g.width[0] = m->q_dim, g.width[1] = m->kv_dim, g.width[2] = m->kv_dim;
-        g.base[0] = sample;
-        g.base[1] = sample + (uint64_t)h * m->q_dim;
-        g.base[2] = g.base[1] + (uint64_t)h * m->kv_dim;
-        sample = g.base[2] + (uint64_t)h * m->kv_dim;
-        SB_TRY(quant_pack(g, ly.qkv, 0, m->stage, true, &scale));
-        ly.qkv.scale = scale;
-        GenSpec go;
-        go.K = m->q_dim;
-        go.N = h;
-        go.width[0] = h;
-        go.base[0] = sample;
-        sample += (uint64_t)m->q_dim * h;
-        SB_TRY(quant_pack(go, ly.o, 0, m->stage, true, &scale));
-        ly.o.scale = scale;
-        GenSpec gg;
-        gg.K = h;
-        gg.N = F;
-        gg.width[0] = F;
-        gg.base[0] = sample;
-        sample += (uint64_t)h * F;
+        const uint64_t bq = sample, bk = bq + (uint64_t)h * Qf, bv = bk + (uint64_t)h * KVf;
+        GenSpec full;
+        full.K = h;
+        full.N = Qf + 2 * KVf;
+        full.nseg = 3;
+        full.c0[0] = 0, full.c0[1] = Qf, full.c0[2] = Qf + KVf;
+        full.width[0] = Qf, full.width[1] = KVf, full.width[2] = KVf;
+        full.base[0] = bq, full.base[1] = bk, full.base[2] = bv;
+        GenSpec part = full;
+        part.N = q + 2 * kv;
+        part.c0[1] = q, part.c0[2] = q + kv;
+        part.base[0] = bq + (uint64_t)r * q, part.base[1] = bk + (uint64_t)r * kv, part.base[2] = bv + (uint64_t)r * kv;
+        sample = bv + (uint64_t)h * KVf;
+        SB_TRY(quant(full, part, m->stage, &ly.qkv.scale));
+        SB_TRY(qweight_pack(m->stage, h, ly.qkv.N, ly.qkv.TN, 0, 0, const_cast<uint4 *>(ly.qkv.w), m->st));
+        SB_TRY(quant(block(sample, h, 0, Qf, 0, h), block(sample, h, r * q, q, 0, h), m->stage, &ly.o.scale));
+        SB_TRY(qweight_pack(m->stage, q, h, ly.o.TN, 0, 0, const_cast<uint4 *>(ly.o.w), m->st));
+        sample += (uint64_t)Qf * h;
         float sg = 0.0f, su = 0.0f;
-        SB_TRY(quant_pack(gg, ly.gu, 0, m->stage, false, &sg));
-        GenSpec gu = gg;
-        gu.base[0] = sample;
-        sample += (uint64_t)h * F;
-        SB_TRY(quant_pack(gu, ly.gu, 0, m->stage + (size_t)h * F, false, &su));
+        SB_TRY(quant(block(sample, Ff, 0, h, 0, Ff), block(sample, Ff, 0, h, r * F, F), m->stage, &sg));
+        sample += (uint64_t)h * Ff;
+        SB_TRY(quant(block(sample, Ff, 0, h, 0, Ff), block(sample, Ff, 0, h, r * F, F), m->stage + (size_t)h * F,
+                     &su));
+        sample += (uint64_t)h * Ff;
         SB_TRY(qweight_pack(m->stage, h, ly.gu.N, ly.gu.TN, F, 0, const_cast<uint4 *>(ly.gu.w), m->st));
         ly.gu.scale = sg;
         ly.gu.scale_up = su;
-        GenSpec gd;
-        gd.K = F;
-        gd.N = h;
-        gd.width[0] = h;
-        gd.base[0] = sample;
-        sample += (uint64_t)F * h;
-        SB_TRY(quant_pack(gd, ly.down, 0, m->stage, true, &scale));
-        ly.down.scale = scale;
+        SB_TRY(quant(block(sample, h, 0, Ff, 0, h), block(sample, h, r * F, F, 0, h), m->stage, &ly.down.scale));
+        SB_TRY(qweight_pack(m->stage, F, h, ly.down.TN, 0, 0, const_cast<uint4 *>(ly.down.w), m->st));
+        sample += (uint64_t)Ff * h;
         for (int s = 0; s < 5; s++) ly.has[s] = true;
     }
+    // lm_head: target [h, V] from the [V,h] stream order (transposed)
     GenSpec gl;
     gl.K = h;
     gl.N = V;
-    gl.transposed = 1;  // target [h,V] from the [V,h] stream order
+    gl.transposed = 1;
     if (m->cfg.tie_word_embeddings) {
         gl.src = m->embed;
     } else {
         gl.base[0] = sample;
         sample += (uint64_t)V * h;
     }
-    SB_TRY(quant_pack(gl, m->lm, 0, m->stage, false, &scale));
-    // gen_quantize wrote [h,V] row-major (K x N) into stage: pack as untransposed.
-    SB_TRY(qweight_pack(m->stage, h, V, m->lm.TN, 0, 0, const_cast<uint4 *>(m->lm.w), m->st));
+    GenSpec gp = gl;
+    gp.N = Vl;
+    if (gl.src)
+        gp.src = m->embed + (size_t)r * Vl * h;
+    else
+        gp.base[0] = gl.base[0] + (uint64_t)r * Vl * h;
+    float scale = 0.0f;
+    SB_TRY(quant(gl, gp, m->stage, &scale));
+    // gen_quantize wrote [h,Vl] row-major (K x N) into stage: pack as untransposed.
+    SB_TRY(qweight_pack(m->stage, h, Vl, m->lm.TN, 0, 0, const_cast<uint4 *>(m->lm.w), m->st));
     m->lm.scale = scale;
     m->has_lm = true;
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
@@ -854,11 +994,24 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
         SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
     }
     m->active = 0;
-    if (logits)
+    if (logits && m->tp == 1)
         SB_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * (size_t)batch * m->V, cudaMemcpyDeviceToHost,
                                     m->st));
+    std::vector<float> lg_all;
+    if (logits && m->tp > 1) {
+        // every rank's vocabulary slice: [rank][row][Vl] -> host [row][V]
+        SB_TRY(tp_allgather32(m->comm, m->logits, m->logits_all, (size_t)batch * m->Vl, m->st));
+        lg_all.resize((size_t)batch * m->V);
+        SB_CUDA_TRY(cudaMemcpyAsync(lg_all.data(), m->logits_all, sizeof(float) * lg_all.size(), cudaMemcpyDeviceToHost,
+                                    m->st));
+    }
     if (argmax) SB_CUDA_TRY(cudaMemcpyAsync(argmax, m->d_last, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    if (!lg_all.empty())
+        for (int t = 0; t < m->tp; t++)
+            for (int b = 0; b < batch; b++)
+                std::memcpy(logits + (size_t)b * m->V + (size_t)t * m->Vl,
+                            lg_all.data() + ((size_t)t * batch + b) * m->Vl, sizeof(float) * m->Vl);
     return check_device_errors(m);
 }
 

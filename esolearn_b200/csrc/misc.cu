@@ -62,14 +62,18 @@ __device__ void block_amax(float &v, int &i) {
 }
 
 __global__ void argmax_step_kernel(const float *__restrict__ cv, const int *__restrict__ ci, int ntiles,
-                                   SeqState s) {
+                                   SeqState s, int tp, int rank_stride, int idx_stride) {
     pdl_launch_dependents();
     pdl_wait();
     const int b = blockIdx.x;
     float v = -INFINITY;
     int idx = -1;
-    for (int t = threadIdx.x; t < ntiles; t += blockDim.x)
-        amax_merge(v, idx, cv[(size_t)b * ntiles + t], ci[(size_t)b * ntiles + t]);
+    for (int j = threadIdx.x; j < tp * ntiles; j += blockDim.x) {
+        const int r = j / ntiles, t = j - r * ntiles;
+        const size_t o = (size_t)r * rank_stride + (size_t)b * ntiles + t;
+        const int i = ci[o];
+        amax_merge(v, idx, cv[o], i < 0 ? i : i + r * idx_stride);
+    }
     block_amax(v, idx);
     if (threadIdx.x == 0) {
         const int next = idx < 0 ? 0 : idx;
@@ -87,8 +91,9 @@ __global__ void argmax_step_kernel(const float *__restrict__ cv, const int *__re
 }
 
 int argmax_step_launch(const float *cand_val, const int *cand_idx, int ntiles, SeqState s, int B,
-                       cudaStream_t st, bool pdl) {
-    SB_CUDA_TRY(launch(argmax_step_kernel, dim3(B), dim3(256), 0, st, pdl, cand_val, cand_idx, ntiles, s));
+                       cudaStream_t st, bool pdl, int tp, int rank_stride, int idx_stride) {
+    SB_CUDA_TRY(launch(argmax_step_kernel, dim3(B), dim3(256), 0, st, pdl, cand_val, cand_idx, ntiles, s, tp,
+                       rank_stride, idx_stride));
     return SB_OK;
 }
 

@@ -24,8 +24,11 @@ int embed_launch(const float *embed, int h, int V, SeqState s, int B, float *x, 
 // Reduce per-tile (value, index) candidates to the argmax of each row (ties ->
 // last index, generate.rs:167-173), record it, feed it to the next step and
 // advance the position.
+// With tp > 1 the candidates of tp ranks are concatenated, rank t's at
+// offset t * rank_stride, and rank t's indices are local to its vocabulary
+// slice starting at t * idx_stride.
 int argmax_step_launch(const float *cand_val, const int *cand_idx, int ntiles, SeqState s, int B,
-                       cudaStream_t st, bool pdl);
+                       cudaStream_t st, bool pdl, int tp = 1, int rank_stride = 0, int idx_stride = 0);
 
 int rmsnorm_launch(const float *x, const float *w, int rows, int d, float eps, float *out, cudaStream_t st);
 int rope_launch(const float *x, int seq, int n_heads, int hd, int start_pos, const float *freqs, float scale,

@@ -156,6 +156,37 @@ def matmul_i8_f32(a, w: QWeight, out=None, bias=None, stream: int = 0):
 
 
 # ---------------------------------------------------------------------------
+# tensor parallelism (no reference counterpart)
+
+def tp_unique_id() -> bytes:
+    """A fresh communicator id for a tensor-parallel model (make it on one rank, send it to the others)."""
+    buf = (C.c_uint8 * N.SB_TP_ID_BYTES)()
+    N.check(N.lib().sb_tp_unique_id(buf))
+    return bytes(buf)
+
+
+def _cfg_c(config: LlamaConfig):
+    return config.to_c(config.max_seq_len, 1, 64, N.SB_KV_BF16)
+
+
+def tp_shard_shape(config: LlamaConfig, slot: int, rank: int, size: int):
+    """(rows, cols) of rank's slice of weight `slot` (SB_W_*, SB_W_LM_HEAD = [V,h]); host only."""
+    r, c = C.c_int32(), C.c_int32()
+    cfg = _cfg_c(config)
+    N.check(N.lib().sb_tp_shard_qweight(C.byref(cfg), slot, rank, size, None, None, C.byref(r), C.byref(c)))
+    return r.value, c.value
+
+
+def tp_shard_qweight(config: LlamaConfig, slot: int, rank: int, size: int, full: np.ndarray) -> np.ndarray:
+    """Rank's slice of a full reference int8 tensor, as the engine keeps it (host only, no GPU)."""
+    full = np.ascontiguousarray(full, np.int8)
+    out = np.empty(tp_shard_shape(config, slot, rank, size), np.int8)
+    cfg = _cfg_c(config)
+    N.check(N.lib().sb_tp_shard_qweight(C.byref(cfg), slot, rank, size, _ptr(full), _ptr(out), None, None))
+    return out
+
+
+# ---------------------------------------------------------------------------
 # the model (CausalLM, generate.rs:5-21)
 
 class LlamaKvCacheHandle:
@@ -172,15 +203,27 @@ class QuantLlamaB200:
     """Int8 Llama decode on one B200 (the quantized LlamaModel)."""
 
     def __init__(self, config: LlamaConfig, *, max_seq: Optional[int] = None, max_batch: int = 1,
-                 page_size: int = 64, kv_dtype: str = "bf16"):
+                 page_size: int = 64, kv_dtype: str = "bf16", tp_rank: int = 0, tp_size: int = 1,
+                 tp_id: Optional[bytes] = None):
+        """tp_size > 1: this process is rank tp_rank of a tensor-parallel model
+        (one GPU per rank, the current device); every rank passes the same
+        tp_id (from tp_unique_id() on one rank) and makes the same calls."""
         self.config = config
         self.max_seq = max_seq or config.max_seq_len
         self.max_batch = max_batch
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         kvd = {"bf16": N.SB_KV_BF16, "f32": N.SB_KV_F32}[kv_dtype]
         self.kv_dtype = kv_dtype
         cfg = config.to_c(self.max_seq, max_batch, page_size, kvd)
+        self._cfg_c = cfg
         h = C.c_void_p()
-        N.check(N.lib().sb_llama_create(C.byref(cfg), C.byref(h)))
+        if tp_size > 1:
+            if tp_id is None or len(tp_id) != N.SB_TP_ID_BYTES:
+                raise N.SbError(6, "tensor parallelism needs the communicator id of tp_unique_id()")
+            idb = (C.c_uint8 * N.SB_TP_ID_BYTES).from_buffer_copy(tp_id)
+            N.check(N.lib().sb_llama_create_tp(C.byref(cfg), tp_rank, tp_size, idb, C.byref(h)))
+        else:
+            N.check(N.lib().sb_llama_create(C.byref(cfg), C.byref(h)))
         self._h = h
 
     def close(self):
@@ -204,14 +247,10 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_load_qweight(self._h, layer, slot, _ptr(q), float(scale)))
 
     def get_qweight(self, layer: int, slot: int):
-        """(int8 [K,N] in the reference layout, scale); layer -1 = lm_head [V,h]."""
-        c = self.config
-        hd = c.head_dim()
-        qkv = c.n_heads * hd + 2 * c.n_kv_heads * hd
-        shapes = {N.SB_W_QKV: (c.hidden_size, qkv), N.SB_W_O: (c.n_heads * hd, c.hidden_size),
-                  N.SB_W_GATE: (c.hidden_size, c.intermediate_size), N.SB_W_UP: (c.hidden_size, c.intermediate_size),
-                  N.SB_W_DOWN: (c.intermediate_size, c.hidden_size)}
-        shape = (c.vocab_size, c.hidden_size) if layer < 0 else shapes[slot]
+        """(int8 [K,N] in the reference layout, scale); layer -1 = lm_head [V,h].
+        Under tensor parallelism: this rank's slice (tp_shard_qweight)."""
+        sl = N.SB_W_LM_HEAD if layer < 0 else slot
+        shape = tp_shard_shape(self.config, sl, self.tp_rank, self.tp_size)
         q = np.empty(shape, np.int8)
         s = C.c_float()
         N.check(N.lib().sb_llama_get_qweight(self._h, layer, slot, _ptr(q), C.byref(s)))

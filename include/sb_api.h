@@ -153,11 +153,40 @@ typedef struct sb_llama_config {
 } sb_llama_config;
 
 typedef struct sb_llama sb_llama;
-enum { SB_W_QKV = 0, SB_W_O = 1, SB_W_GATE = 2, SB_W_UP = 3, SB_W_DOWN = 4 };
+enum { SB_W_QKV = 0, SB_W_O = 1, SB_W_GATE = 2, SB_W_UP = 3, SB_W_DOWN = 4, SB_W_LM_HEAD = 5 };
 enum { SB_F_EMBED = 0, SB_F_NORM_IN = 1, SB_F_NORM_POST = 2, SB_F_NORM_FINAL = 3 };
 
 /* LlamaModel construction; allocates weights, KV pages and scratch. */
 sb_status sb_llama_create(const sb_llama_config *cfg, sb_llama **out);
+
+/* ---- tensor parallelism over the GPUs of one node ----------------------
+ * No reference counterpart (the reference decodes on one device).  A model
+ * of tp_size ranks, one process (or thread) and one GPU per rank: column
+ * slices of q|k|v (by heads), gate and up (by ffn columns) and of the
+ * lm_head (by vocabulary rows), row slices of o and down; the KV cache holds
+ * the rank's kv heads.  After o and down the partial residual updates are
+ * summed over the ranks with an NCCL all-reduce over NVLink (libnccl.so.2,
+ * loaded at the first call); the greedy token is the argmax over every
+ * rank's vocabulary slice (ties -> last index), identical on all ranks.
+ * Every rank makes the same calls in the same order (they are collective),
+ * with the same arguments; outputs (tokens, argmax, logits) are the full
+ * ones on every rank.  Weights: sb_llama_init_random and
+ * sb_llama_load_qweight take the FULL tensors (same seed / same data on every
+ * rank) and keep the rank's slice; per-tensor scales are those of the full
+ * tensors, so every shard holds the reference's int8 values bit for bit.
+ * sb_llama_get_qweight returns the rank's slice. */
+#define SB_TP_ID_BYTES 128
+/* A fresh communicator id (rank 0 makes it and sends it to the others). */
+sb_status sb_tp_unique_id(uint8_t *id);
+/* Rank tp_rank of tp_size joins the communicator `id` (waits at most 120 s
+ * for the others: SB_ERR_TIMEOUT) and allocates its shard of the model. */
+sb_status sb_llama_create_tp(const sb_llama_config *cfg, int tp_rank, int tp_size, const uint8_t *id,
+                             sb_llama **out);
+/* Host-only: rank tp_rank's slice of the full reference tensor of `slot`
+ * (SB_W_*; SB_W_LM_HEAD is [V,h]) in the reference layout, and its shape.
+ * With full == NULL only rows/cols are returned. */
+sb_status sb_tp_shard_qweight(const sb_llama_config *cfg, int slot, int tp_rank, int tp_size, const int8_t *full,
+                              int8_t *shard, int *rows, int *cols);
 sb_status sb_llama_destroy(sb_llama *m);
 /* LlamaModel::new (llama.rs:593-680) generated on the device with the
  * fastrand stream and draw order of the reference, then quantized per
