@@ -420,6 +420,7 @@ int ds_step(sb_llama *m) {
 int check_device_errors(sb_llama *m) {
     if (m->ds_ok) SB_TRY(ds_check_error(m->ds_sync, m->st));
     SB_TRY(qgemm_check_error());
+    if (m->tp > 1) SB_TRY(tp_check_error(m->comm));
     return qgemv_check_error();
 }
 
@@ -572,6 +573,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
 
     int rc = SB_OK;
     if (tp_size > 1 && (rc = tp_init(m->comm, tp_id, tp_rank, tp_size, 120.0)) != SB_OK) return fail(rc);
+    if (tp_size > 1 && (rc = tp_setup_p2p(m->comm, m->B * m->h, m->st)) != SB_OK) return fail(rc);
     if (tp_size == 1) {
         int chunk = 0;
         if (ds_supported(m->h, m->F, m->q_dim, hd, m->nh / m->nkv, m->kv_f32, m->P, &chunk)) {

@@ -412,107 +412,166 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
 }
 
 // ---- kernel 2: scale, epilogue, clear the sums ------------------------------------
-// One CTA per (128-column tile, pair of rows), one element per thread, so no
-// thread waits on a chain of dependent loads.  The epilogues are those of
-// qgemv.cu for any row count.
-constexpr int QGM_FIN_ROWS = 2;
+// CTA (tile, g) handles rows [g*R, g*R + R) of one 128-column tile; thread
+// (c, h) owns column c of rows g*R + h, + 2, + 4, ...  R is picked on the
+// host so the grid stays near one wave: these CTAs are short, so many small
+// ones are bound by the CTA launch rate and few large ones leave SMs idle.
+// Every global value a thread needs is loaded in one batch before the
+// dependent work.  The epilogues are those of qgemv.cu for any row count.
+constexpr int QGM_FIN_THREADS = 256;
 
-template <int EPI>
-__global__ void __launch_bounds__(QGM_FIN_ROWS * QGM_TN) qgm_finish_kernel(const QGemvArgs a, const QGemmWs ws) {
-    __shared__ float ys[QGM_FIN_ROWS * QGM_TN];
-    __shared__ float s_bv[QGM_FIN_ROWS * QGM_TN / 32];
-    __shared__ int s_bi[QGM_FIN_ROWS * QGM_TN / 32];
+// J = rows per thread (R = 2J rows per CTA); sized arrays keep registers low.
+template <int EPI, int J>
+__global__ void __launch_bounds__(QGM_FIN_THREADS) qgm_finish_kernel(const QGemvArgs a, const QGemmWs ws) {
+    constexpr int QGM_FIN_MAXJ = J;
+    constexpr int R = 2 * J;
+    __shared__ float ys[R * QGM_TN];  // rows of this CTA, local index
+    __shared__ float s_bv[R][QGM_TN / 32];
+    __shared__ int s_bi[R][QGM_TN / 32];
     pdl_launch_dependents();
     pdl_wait();
-    const int tile = blockIdx.x, tid = threadIdx.x, M = a.M;
-    const int c = tid & (QGM_TN - 1);
-    const int m = blockIdx.y * QGM_FIN_ROWS + tid / QGM_TN;
+    const int tile = blockIdx.x, tid = threadIdx.x;
+    const int m0 = blockIdx.y * R, nr = min(R, a.M - m0);  // rows of this CTA
+    const int c = tid & (QGM_TN - 1), h = tid >> 7;        // column, first local row
     const int n = tile * QGM_TN + c;
-    const bool row = m < M;
-    float y = 0.f;
-    if (row) {
-        long long *p = ws.acc + (size_t)m * ws.ld_acc + n;
-        const long long t = __ldcg(p);
-        *p = 0;
-        const float sc = (EPI == QEPI_SWIGLU && (c & 31) >= 16) ? a.w.scale_up : a.w.scale;
-        y = gemv_out(t, gemv_factor(ws.shift[m], sc, ws.rstd[m]));
+    const int lane = tid & 31, wic = c >> 5;               // warp index within the row
+    // 1. the exact sums and the row factors, all loads in flight together
+    long long t[QGM_FIN_MAXJ];
+    int sh[QGM_FIN_MAXJ];
+    double rs[QGM_FIN_MAXJ];
+#pragma unroll
+    for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+        const int r = h + 2 * j;
+        if (r < nr) {
+            t[j] = __ldcg(ws.acc + (size_t)(m0 + r) * ws.ld_acc + n);
+            sh[j] = ws.shift[m0 + r];
+            rs[j] = ws.rstd[m0 + r];
+        }
     }
-    ys[tid] = y;
+#pragma unroll
+    for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+        const int r = h + 2 * j;
+        if (r < nr) ws.acc[(size_t)(m0 + r) * ws.ld_acc + n] = 0;
+    }
+    const float sc = (EPI == QEPI_SWIGLU && (c & 31) >= 16) ? a.w.scale_up : a.w.scale;
+#pragma unroll
+    for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+        const int r = h + 2 * j;
+        if (r < nr) ys[r * QGM_TN + c] = gemv_out(t[j], gemv_factor(sh[j], sc, rs[j]));
+    }
     __syncthreads();
-    if (row) {
-        if (EPI == QEPI_STORE || EPI == QEPI_LOGITS) {
-            if (n < a.w.N) a.out[(size_t)m * a.ldo + n] = y;
-        } else if (EPI == QEPI_BIAS) {
-            if (n < a.w.N) a.out[(size_t)m * a.ldo + n] = __fadd_rn(y, a.bias[n]);
-        } else if (EPI == QEPI_RESID) {
-            if (n < a.w.N) {
-                float *o = a.out + (size_t)m * a.ldo + n;
-                *o = __fadd_rn(*o, y);  // x = x + proj (llama.rs:564,568)
+    // 2. epilogue
+    if (EPI == QEPI_STORE || EPI == QEPI_LOGITS || EPI == QEPI_BIAS) {
+        const float bias = (EPI == QEPI_BIAS && n < a.w.N) ? a.bias[n] : 0.f;
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            if (r < nr && n < a.w.N) {
+                const float y = ys[r * QGM_TN + c];
+                a.out[(size_t)(m0 + r) * a.ldo + n] = EPI == QEPI_BIAS ? __fadd_rn(y, bias) : y;
             }
-        } else if (EPI == QEPI_SWIGLU) {
-            const int within = n & 31;
-            if (within < 16) {
-                const int j = (n >> 5) * 16 + within;
-                if (j < a.F) a.out[(size_t)m * a.ldo + j] = __fmul_rn(silu_f64(y), ys[tid + 16]);
+        }
+    } else if (EPI == QEPI_RESID) {
+        float o[QGM_FIN_MAXJ];
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            if (r < nr && n < a.w.N) o[j] = a.out[(size_t)(m0 + r) * a.ldo + n];
+        }
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            if (r < nr && n < a.w.N)  // x = x + proj (llama.rs:564,568)
+                a.out[(size_t)(m0 + r) * a.ldo + n] = __fadd_rn(o[j], ys[r * QGM_TN + c]);
+        }
+    } else if (EPI == QEPI_SWIGLU) {
+        const int within = n & 31;
+        if (within < 16) {
+            const int jf = (n >> 5) * 16 + within;
+#pragma unroll
+            for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+                const int r = h + 2 * j;
+                if (r < nr && jf < a.F)
+                    a.out[(size_t)(m0 + r) * a.ldo + jf] =
+                        __fmul_rn(silu_f64(ys[r * QGM_TN + c]), ys[r * QGM_TN + c + 16]);
             }
-        } else if (EPI == QEPI_QKV) {
-            const int pos = a.pos[m];
-            if (n < a.w.N && pos >= 0 && pos < a.max_pos) {
-                const int qk = a.q_dim + a.kv_dim;
-                float val = y;
-                if (n < qk) {
-                    // rope_with_freqs_preloaded (cpu.rs:650-661)
-                    const int nn = n < a.q_dim ? n : n - a.q_dim;
-                    const int d = nn % a.hd, i = d >> 1;
-                    const float partner = ys[tid ^ 1];
-                    const float cs = a.rope_cos[(size_t)pos * (a.hd / 2) + i];
-                    const float sn = a.rope_sin[(size_t)pos * (a.hd / 2) + i];
-                    val = (d & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(y, cs))
-                                  : __fsub_rn(__fmul_rn(y, cs), __fmul_rn(partner, sn));
-                }
-                if (n < a.q_dim) {
-                    a.q_out[(size_t)m * a.q_dim + n] = __fmul_rn(val, a.q_scale);
-                } else {
-                    const bool is_k = n < qk;
-                    const int nn = is_k ? n - a.q_dim : n - qk;
-                    const int kh = nn / a.hd, d = nn - kh * a.hd;
-                    const int page = a.page_table[(size_t)m * a.max_pages + pos / a.page_size];
-                    const size_t idx = (((size_t)page * a.n_kv + kh) * a.page_size + pos % a.page_size) * a.hd + d;
-                    void *cache = is_k ? a.kcache : a.vcache;
-                    if (a.kv_f32)
-                        reinterpret_cast<float *>(cache)[idx] = val;
-                    else
-                        reinterpret_cast<__nv_bfloat16 *>(cache)[idx] = __float2bfloat16_rn(val);
-                }
+        }
+    } else if (EPI == QEPI_QKV) {
+        const int qk = a.q_dim + a.kv_dim;
+        int pos[QGM_FIN_MAXJ];
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            pos[j] = r < nr ? a.pos[m0 + r] : -1;
+        }
+        const bool rope = n < qk;
+        const int nn = n < a.q_dim ? n : n - a.q_dim;
+        const int d = nn % a.hd, i = d >> 1;
+        float cs[QGM_FIN_MAXJ], sn[QGM_FIN_MAXJ];
+        int page[QGM_FIN_MAXJ];
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            const bool live = r < nr && pos[j] >= 0 && pos[j] < a.max_pos && n < a.w.N;
+            cs[j] = (live && rope) ? a.rope_cos[(size_t)pos[j] * (a.hd / 2) + i] : 0.f;
+            sn[j] = (live && rope) ? a.rope_sin[(size_t)pos[j] * (a.hd / 2) + i] : 0.f;
+            page[j] = (live && n >= a.q_dim) ? a.page_table[(size_t)(m0 + r) * a.max_pages + pos[j] / a.page_size] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            if (!(r < nr && pos[j] >= 0 && pos[j] < a.max_pos && n < a.w.N)) continue;
+            const int m = m0 + r;
+            const float y = ys[r * QGM_TN + c];
+            float val = y;
+            if (rope) {
+                // rope_with_freqs_preloaded (cpu.rs:650-661)
+                const float partner = ys[r * QGM_TN + (c ^ 1)];
+                val = (d & 1) ? __fadd_rn(__fmul_rn(partner, sn[j]), __fmul_rn(y, cs[j]))
+                              : __fsub_rn(__fmul_rn(y, cs[j]), __fmul_rn(partner, sn[j]));
+            }
+            if (n < a.q_dim) {
+                a.q_out[(size_t)m * a.q_dim + n] = __fmul_rn(val, a.q_scale);
+            } else {
+                const bool is_k = n < qk;
+                const int kn = is_k ? n - a.q_dim : n - qk;
+                const int kh = kn / a.hd, dd = kn - kh * a.hd;
+                const size_t idx =
+                    (((size_t)page[j] * a.n_kv + kh) * a.page_size + pos[j] % a.page_size) * a.hd + dd;
+                void *cache = is_k ? a.kcache : a.vcache;
+                if (a.kv_f32)
+                    reinterpret_cast<float *>(cache)[idx] = val;
+                else
+                    reinterpret_cast<__nv_bfloat16 *>(cache)[idx] = __float2bfloat16_rn(val);
             }
         }
     }
     if (EPI == QEPI_LOGITS) {
         // per-tile argmax candidate of every row; ties resolve to the larger index
-        const int warp = tid >> 5, lane = tid & 31;
-        float best = y;
-        int bi = (row && n < a.w.N) ? n : -1;
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
+#pragma unroll
+        for (int j = 0; j < QGM_FIN_MAXJ; j++) {
+            const int r = h + 2 * j;
+            if (r >= nr) break;  // uniform over each warp (a warp holds one row parity)
+            float best = ys[r * QGM_TN + c];
+            int bi = n < a.w.N ? n : -1;
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
+            }
+            if (lane == 0) s_bv[r][wic] = best, s_bi[r][wic] = bi;
         }
-        if (lane == 0) s_bv[warp] = best, s_bi[warp] = bi;
         __syncthreads();
-        constexpr int WPR = QGM_TN / 32;  // warps per row
-        if (tid < QGM_FIN_ROWS) {
-            const int mm = blockIdx.y * QGM_FIN_ROWS + tid;
-            float bv = s_bv[tid * WPR];
-            int bj = s_bi[tid * WPR];
-            for (int k = 1; k < WPR; k++) {
-                const float ov = s_bv[tid * WPR + k];
-                const int oi = s_bi[tid * WPR + k];
+        if (tid < nr) {
+            float bv = s_bv[tid][0];
+            int bj = s_bi[tid][0];
+            for (int k = 1; k < QGM_TN / 32; k++) {
+                const float ov = s_bv[tid][k];
+                const int oi = s_bi[tid][k];
                 if (oi >= 0 && (bj < 0 || ov > bv || (ov == bv && oi > bj))) bv = ov, bj = oi;
             }
-            if (mm < M) {
-                a.cand_val[(size_t)mm * a.w.ntiles + tile] = bv;
-                a.cand_idx[(size_t)mm * a.w.ntiles + tile] = bj;
-            }
+            a.cand_val[(size_t)(m0 + tid) * a.w.ntiles + tile] = bv;
+            a.cand_idx[(size_t)(m0 + tid) * a.w.ntiles + tile] = bj;
         }
     }
 }
@@ -528,8 +587,19 @@ int qgm_nst(int np, int *limit_out) {
 
 template <int EPI>
 int finish_launch(const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
-    SB_CUDA_TRY(launch(qgm_finish_kernel<EPI>, dim3(a.w.ntiles, ceil_div(a.M, QGM_FIN_ROWS)), dim3(QGM_FIN_ROWS * QGM_TN),
-                       0, st, pdl, a, ws));
+    // rows per CTA: the smallest power of two (>= 2) that keeps the grid
+    // within two CTAs per SM
+    const int cap = 2 * device_props().sm_count;
+    int R = 2;
+    while (R < QGM_MAX_M && a.w.ntiles * ceil_div(a.M, R) > cap) R *= 2;
+    const dim3 grid(a.w.ntiles, ceil_div(a.M, R));
+    switch (R) {
+    case 2: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 1>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
+    case 4: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 2>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
+    case 8: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 4>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
+    case 16: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 8>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
+    default: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 16>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
+    }
     return SB_OK;
 }
 

@@ -1,11 +1,28 @@
-// NCCL communicator of the tensor-parallel engine, resolved with dlopen.
+// Communication of the tensor-parallel engine: an NCCL communicator resolved
+// with dlopen, and a one-shot all-reduce over NVLink peer memory for the
+// small per-layer residual sums.
+//
+// Peer all-reduce (tp_ar_kernel).  CTA c of every rank owns slice c of the
+// vector.  It writes each value of its slice, paired with the call's epoch in
+// one 8-byte store, into slot [parity][rank] of every other rank's cells over
+// NVLink; then it reads the other ranks' cells of slice c from its own HBM,
+// waiting (bounded: 2 s of %globaltimer, then an error word) until each
+// cell carries the epoch, and sums the ranks' values in rank order -- so all
+// ranks get the same bits.  The value and its epoch travel in one store, so
+// no fence or separate flag is needed.  Slots alternate by epoch parity: a
+// rank can write call e+2 only after every rank wrote call e+1, i.e. after
+// every rank finished reading call e.
 #include "tp_comm.cuh"
 
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <vector>
+
+#include "pipeline.cuh"
 #include <mutex>
 #include <thread>
 
@@ -81,7 +98,139 @@ int enqueued(const TpComm &c, ncclResult_t r, const char *what) {
     return nccl_fail(what, r);
 }
 
+// A cell is one aligned 64-bit word (epoch << 32 | value bits): scalar 64-bit
+// accesses are single-copy atomic, so a reader sees a value only together
+// with the epoch it was written for.
+__device__ __forceinline__ void st_cell(uint2 *p, float v, unsigned e) {
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint2 ld_cell(const uint2 *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return make_uint2((unsigned)w, (unsigned)(w >> 32));
+}
+
+__global__ void __launch_bounds__(256) tp_ar_kernel(float *x, int n, TpPeers P, int rank, int T) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int c = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
+    const int per = (n + G - 1) / G;
+    const int i0 = min(n, c * per), i1 = min(n, i0 + per);
+    __shared__ unsigned s_epoch;
+    if (tid == 0) s_epoch = P.epoch[c] + 1;
+    __syncthreads();
+    const unsigned e = s_epoch;
+    const size_t par = e & 1u;
+    // 1. this rank's values, with the epoch, into slot [par][rank] of every other rank
+    for (int r = 0; r < T; r++) {
+        if (r == rank) continue;
+        uint2 *dst = P.recv[r] + (par * T + rank) * (size_t)P.cap;
+        for (int i = i0 + tid; i < i1; i += blockDim.x) st_cell(dst + i, x[i], e);
+    }
+    // 2. every rank's value of each element, summed in rank order
+    const uint2 *mine = P.recv[rank] + par * T * (size_t)P.cap;
+    bool bad = false;
+    for (int i = i0 + tid; i < i1; i += blockDim.x) {
+        float sum = 0.f;
+        for (int r = 0; r < T; r++) {
+            float v;
+            if (r == rank) {
+                v = x[i];
+            } else {
+                const uint2 *cell = mine + (size_t)r * P.cap + i;
+                uint2 u = ld_cell(cell);
+                uint64_t t0 = 0;
+                for (uint32_t it = 0; u.y != e && !bad; it++) {
+                    if ((it & 63) == 0) {
+                        const uint64_t t = global_ns();
+                        if (it == 0) t0 = t;
+                        else if (t - t0 > SB_WAIT_NS) bad = true;
+                    }
+                    u = ld_cell(cell);
+                }
+                v = __uint_as_float(u.x);
+            }
+            sum = r == 0 ? v : __fadd_rn(sum, v);
+        }
+        if (bad) break;
+        x[i] = sum;
+    }
+    if (bad) atomicOr(P.error, 1u);
+    __syncthreads();  // every thread of the CTA has read x before its epoch advances
+    if (tid == 0) P.epoch[c] = e;
+}
+
 }  // namespace
+
+int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st) {
+    const int T = c.size;
+    SB_CHECK(T >= 2 && T <= TP_MAX_RANKS, SB_ERR_ARG, "peer all-reduce: %d ranks", T);
+    uint2 *recv = nullptr;
+    unsigned *misc = nullptr;
+    const size_t rbytes = sizeof(uint2) * 2 * (size_t)T * cap;
+    SB_CUDA_TRY(cudaMalloc(&recv, rbytes));
+    c.own[0] = recv;
+    SB_CUDA_TRY(cudaMalloc(&misc, sizeof(unsigned) * (TP_AR_CTAS + 1)));
+    c.own[1] = misc;
+    SB_CUDA_TRY(cudaMemsetAsync(recv, 0, rbytes, st));  // epoch 0: no call has written yet
+    SB_CUDA_TRY(cudaMemsetAsync(misc, 0, sizeof(unsigned) * (TP_AR_CTAS + 1), st));
+    // exchange the IPC handles through the communicator
+    cudaIpcMemHandle_t mine;
+    SB_CUDA_TRY(cudaIpcGetMemHandle(&mine, recv));
+    const size_t hb = sizeof mine;
+    static_assert(sizeof(mine) % 4 == 0, "handles are gathered as 32-bit words");
+    uint8_t *dev = nullptr;
+    SB_CUDA_TRY(cudaMalloc(&dev, hb * (T + 1)));
+    std::vector<uint8_t> all(hb * T);
+    int rc = SB_OK;
+    if (cudaMemcpyAsync(dev + hb * T, &mine, hb, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        rc = set_error(SB_ERR_CUDA, "peer all-reduce: handle upload failed");
+    if (rc == SB_OK) rc = tp_allgather32(c, dev + hb * T, dev, hb / 4, st);
+    if (rc == SB_OK && cudaMemcpyAsync(all.data(), dev, hb * T, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        rc = set_error(SB_ERR_CUDA, "peer all-reduce: handle download failed");
+    if (rc == SB_OK && cudaStreamSynchronize(st) != cudaSuccess)
+        rc = set_error(SB_ERR_CUDA, "peer all-reduce: handle exchange failed");
+    cudaFree(dev);
+    SB_TRY(rc);
+    TpPeers P;
+    P.cap = cap;
+    P.epoch = misc;
+    P.error = misc + TP_AR_CTAS;
+    bool ok = true;
+    for (int r = 0; r < T && ok; r++) {
+        if (r == c.rank) {
+            P.recv[r] = recv;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + hb * r, hb);
+        void *pr = nullptr;
+        if (cudaIpcOpenMemHandle(&pr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;  // no peer access between these GPUs: NCCL carries the sums
+            break;
+        }
+        P.recv[r] = static_cast<uint2 *>(pr);
+    }
+    c.peers = P;
+    c.p2p = ok;
+    if (!ok)
+        for (int r = 0; r < T; r++)
+            if (r != c.rank && P.recv[r]) cudaIpcCloseMemHandle(P.recv[r]);
+    return SB_OK;
+}
+
+int tp_check_error(const TpComm &c) {
+    if (!c.p2p) return SB_OK;
+    unsigned f = 0;
+    SB_CUDA_TRY(cudaMemcpy(&f, c.peers.error, sizeof f, cudaMemcpyDeviceToHost));
+    if (f) {
+        cudaMemset(c.peers.error, 0, sizeof f);
+        return set_error(SB_ERR_TIMEOUT, "peer all-reduce: a rank did not deliver its partial sums within 2 s");
+    }
+    return SB_OK;
+}
 
 int tp_unique_id(uint8_t *id) {
     const NcclApi &a = api();
@@ -116,6 +265,12 @@ int tp_init(TpComm &c, const uint8_t *id, int rank, int size, double timeout_s) 
 }
 
 void tp_destroy(TpComm &c) {
+    if (c.p2p)
+        for (int r = 0; r < c.size; r++)
+            if (r != c.rank) cudaIpcCloseMemHandle(c.peers.recv[r]);
+    c.p2p = false;
+    for (void *&p : c.own)
+        if (p) cudaFree(p), p = nullptr;
     if (!c.comm) return;
     const NcclApi &a = api();
     ncclComm_t comm = (ncclComm_t)c.comm;
@@ -128,6 +283,11 @@ void tp_destroy(TpComm &c) {
 }
 
 int tp_allreduce_f32(const TpComm &c, float *buf, size_t count, cudaStream_t st) {
+    if (c.p2p && count <= (size_t)c.peers.cap) {
+        const int G = std::max(1, std::min(TP_AR_CTAS, (int)((count + 1023) / 1024)));
+        SB_CUDA_TRY(launch(tp_ar_kernel, dim3(G), dim3(256), 0, st, true, buf, (int)count, c.peers, c.rank, c.size));
+        return SB_OK;
+    }
     const NcclApi &a = api();
     return enqueued(c, a.all_reduce(buf, buf, count, ncclFloat32, ncclSum, (ncclComm_t)c.comm, st), "ncclAllReduce");
 }

@@ -13,9 +13,27 @@
 
 namespace sb {
 
+constexpr int TP_MAX_RANKS = 8;
+constexpr int TP_AR_CTAS = 32;  // CTAs (and flag slots per source rank) of the peer all-reduce
+
+// Peer-memory all-reduce state.  Every rank owns recv[2][T][cap] 8-byte
+// cells (value bits, epoch) in its own HBM; the other ranks write into them
+// over NVLink through IPC mappings.  epoch[TP_AR_CTAS] counts the calls each
+// CTA index has made on this rank (the same on every rank, since all ranks
+// make the same calls).
+struct TpPeers {
+    uint2 *recv[TP_MAX_RANKS] = {};  // rank r's receive cells, mapped here
+    unsigned *epoch = nullptr;       // local
+    unsigned *error = nullptr;       // local: a wait that ran out
+    int cap = 0;                     // cells per (parity, source) slot
+};
+
 struct TpComm {
     void *comm = nullptr;  // ncclComm_t
     int rank = 0, size = 1;
+    TpPeers peers;
+    bool p2p = false;                    // peer all-reduce usable
+    void *own[2] = {};                   // local allocations (recv, epoch+error)
 };
 
 // Fresh unique id for a new communicator (rank 0 makes it, the caller sends
@@ -24,8 +42,16 @@ int tp_unique_id(uint8_t *id);
 // Join the communicator of `size` ranks; gives up after timeout_s seconds.
 int tp_init(TpComm &c, const uint8_t *id, int rank, int size, double timeout_s);
 void tp_destroy(TpComm &c);
-// Sum of `count` f32 values over the ranks, in place, on `st` (capturable).
+// Sum of `count` f32 values over the ranks, in place, on `st` (capturable):
+// the peer all-reduce when it is set up and count fits, else NCCL.  Every
+// rank receives the same sum (added in rank order).
 int tp_allreduce_f32(const TpComm &c, float *buf, size_t count, cudaStream_t st);
+// Map every rank's all-reduce buffers (cap floats per slot) into this
+// process over CUDA IPC (handles exchanged with an NCCL all-gather).  Leaves
+// p2p off (NCCL only) when the GPUs cannot reach each other's memory.
+int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st);
+// Reports (and clears) a timed-out flag wait of the peer all-reduce.
+int tp_check_error(const TpComm &c);
 // recv[r * count + i] = send_r[i], on `st` (capturable); elem_bytes 4.
 int tp_allgather32(const TpComm &c, const void *send, void *recv, size_t count, cudaStream_t st);
 
