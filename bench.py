@@ -5,8 +5,10 @@ model (dim 4096, 32 layers, 32 heads, ffn 11008, vocab 32000, RoPE theta 1e4),
 seeded 512-token prompt, then greedy decode at batch 1.  --workload
 llama3-8b-bs32: Llama-3-8B shape with GQA (32 query /
 8 KV heads, ffn 14336, vocab 128256, theta 5e5), 32 sequences with seeded
-2048-token prompts.  A step is one decode token of every sequence: K timed
-steps follow the prompt and W warm-up steps.
+2048-token prompts.  --workload llama3-70b-bs64:
+Llama-3-70B shape (dim 8192, 80 layers, 64 query / 8 KV heads, ffn 28672),
+64 sequences with seeded 1024-token prompts.  A step is one decode token of
+every sequence: K timed steps follow the prompt and W warm-up steps.
 
 * value      -- decode tokens/s with weights and KV resident in HBM (CUDA
                 events on the engine stream around K steps; at batch 1 each
@@ -61,6 +63,9 @@ WORKLOADS = {
     "llama3-8b-bs32": {"metric": "decode tok/s, 8B-shape GQA int8, bs32", "shape": "llama3_8b_shape", "batch": 32,
                        "prompt": 2048,
                        "desc": "llama3-8b-shape GQA int8 decode, 2048-token bf16 KV context (BASELINE configs[3])"},
+    "llama3-70b-bs64": {"metric": "decode tok/s, 70B-shape GQA int8, bs64", "shape": "llama3_70b_shape", "batch": 64,
+                        "prompt": 1024,
+                        "desc": "llama3-70b-shape GQA int8 decode, 1024-token bf16 KV context (BASELINE configs[4])"},
 }
 
 
@@ -317,7 +322,7 @@ def run_ours(args, rank: int, world: int, dist):
                 "seeded uniform prompt ids",
         "config": {"workload": wl["desc"], "batch": B, "prompt": args.prompt,
                    "context_mid": ctx_mid,
-                   "parallelism": (f"tp{tp} (NCCL all-reduce after o and down, NVLink)" if tp > 1 else
+                   "parallelism": (f"tp{tp} (one-shot peer all-reduce over NVLink after o and down)" if tp > 1 else
                                    f"replicas x{world}" if world > 1 else "single GPU"),
                    "l2": f"weights {wbytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
                    "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else

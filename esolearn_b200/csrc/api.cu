@@ -278,18 +278,20 @@ static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, in
     SB_CHECK(M >= 0, SB_ERR_ARG, "M < 0");
     const size_t esz = a_dtype == SB_DTYPE_BF16 ? 2 : 4;
     if (qgemm_supported(w->d, M)) {
-        // 5-32 rows on the tensor cores: scratch = planes, column sums, row exponents
+        // 5-64 rows on the tensor cores: scratch = planes, column sums, row exponents
         QGemmWs ws;
         ws.ld_acc = w->d.ntiles * 128;
         const size_t pb = align_up(qgemm_planes_bytes(w->d.K, M), 256);
         void *base = nullptr, *sums = nullptr;
-        SB_TRY(workspace_get(WS_GEMM, pb + 256 + 512, &base, (cudaStream_t)stream));
+        // planes, then rstd[QGM_MAX_M] doubles, then shift[QGM_MAX_M] ints
+        const size_t rb = sizeof(double) * QGM_MAX_M, sb = sizeof(int) * QGM_MAX_M;
+        SB_TRY(workspace_get(WS_GEMM, pb + rb + sb, &base, (cudaStream_t)stream));
         SB_TRY(workspace_get(WS_GEMM_SUMS, sizeof(long long) * (size_t)M * ws.ld_acc, &sums, (cudaStream_t)stream));
         char *b = static_cast<char *>(base);
         ws.planes = reinterpret_cast<uint8_t *>(b);
         ws.acc = reinterpret_cast<long long *>(sums);
         ws.rstd = reinterpret_cast<double *>(b + pb);
-        ws.shift = reinterpret_cast<int *>(b + pb + 256);
+        ws.shift = reinterpret_cast<int *>(b + pb + rb);
         QGemvArgs g;
         g.w = w->d;
         g.M = M;

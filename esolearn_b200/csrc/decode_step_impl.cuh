@@ -735,10 +735,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     // Arrive at the end of the current phase.
     auto arrive = [&]() {
         ds_sync();
-        if (tid == 0) {
-            __threadfence();
-            atomicAdd(a.sync, 1u);
-        }
+        // release at gpu scope: the CTA's writes (ordered before this thread by
+        // the named barrier) are visible to whoever acquires the new count
+        if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.sync), "r"(1u) : "memory");
         phase++;
     };
     // Wait until every CTA has arrived at the end of the previous phase.

@@ -112,7 +112,7 @@ struct sb_llama {
     int *ds_cand_idx = nullptr;
     unsigned *ds_sync = nullptr;
 
-    // batched steps of 5-32 sequences: tensor-core linears and their scratch
+    // batched steps of 5-64 sequences: tensor-core linears and their scratch
     QGemmWs gws;
 };
 
@@ -226,7 +226,7 @@ int tp_reduce_residual(sb_llama *m, int M, cudaStream_t st) {
 }
 
 // One linear of a step: the GEMV for up to 4 rows, the tensor-core GEMM for
-// 5-32 (every weight then has 128-column tiles).
+// 5-64 (every weight then has 128-column tiles).
 int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, bool pdl) {
     if (a.M > QG_MAX_M) return qgemm_launch(epi, a, m->gws, st, pdl);
     return qgemv_launch(epi, a, st, pdl);

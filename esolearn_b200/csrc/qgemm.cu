@@ -1,5 +1,5 @@
 // Batched int8 linear on tcgen05 tensor cores: the batched-decode form of
-// matmul_i8_f32 (backend/mod.rs:521-533, CPU cpu.rs:1129-1160) for 5-32 rows.
+// matmul_i8_f32 (backend/mod.rs:521-533, CPU cpu.rs:1129-1160) for 5-64 rows.
 //
 // Arithmetic.  Exactly the fixed point of the GEMV (qgemv.cu): each row is
 // scaled by a power of two so |a * 2^s| < 2^22 and rounded to an integer A;
@@ -8,7 +8,7 @@
 // (A operand, 128 output columns x K) with the unsigned planes plus one
 // all-ones row (B operand, 3M+1 rows x K) into int32 accumulators in TMEM
 // (tcgen05.mma kind::i8); |each accumulator| <= K * 127 * 255 < 2^31 for
-// K <= 16384.  Per output column and row:
+// K <= 32768.  Per output column and row:
 //   sum_k w a 2^s = D[plane0] + 2^8 D[plane1] + 2^16 D[plane2] - 2^23 D[ones]
 // (B rows: the ones row first, then the three planes of each activation row)
 // exactly, so results equal the GEMV path bit for bit whenever the row
@@ -42,14 +42,17 @@ namespace {
 
 constexpr int QGM_TN = 128;
 constexpr int QGM_UNIT_KS = 8;      // k-steps per 16 KB work unit (split granularity)
-constexpr int QGM_STAGE_KS = 16;    // k-steps per stage (two units)
-constexpr int QGM_WBYTES = QGM_STAGE_KS * QGM_TN * 16;  // 32 KB of weights per stage
+// A stage is two units (16 k-steps, 32 KB of weights) while the plane rows
+// are few, one unit beyond QGM_UPS2_NP plane rows so the ring keeps 4+ slots.
+constexpr int QGM_UPS2_NP = 112;
 constexpr int QGM_THREADS = 192;    // warps 0-3 TMEM drain, 4 MMA, 5 producer
 constexpr int QGM_MAX_NST = 6;
 
 __device__ unsigned qgm_error_flag = 0;
 
-__host__ __device__ inline int qgm_slot_bytes(int np) { return QGM_WBYTES + QGM_STAGE_KS * np * 16; }
+__host__ __device__ inline int qgm_ups(int np) { return np <= QGM_UPS2_NP ? 2 : 1; }
+__host__ __device__ inline int qgm_wbytes(int np) { return qgm_ups(np) * QGM_UNIT_KS * QGM_TN * 16; }
+__host__ __device__ inline int qgm_slot_bytes(int np) { return qgm_wbytes(np) + qgm_ups(np) * QGM_UNIT_KS * np * 16; }
 
 // ---- tcgen05 helpers (cta_group::1) ------------------------------------------------
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -74,10 +77,10 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 // The CTA's stages: units of 8 k-steps of a 128-column tile, tile-major,
-// CTA c takes [c*U/G, (c+1)*U/G), two units of one tile per stage.
+// CTA c takes [c*U/G, (c+1)*U/G), up to `ups` units of one tile per stage.
 struct QgmWalk {
-    int tile, ut, u, u1, upt, KS;
-    __device__ QgmWalk(int KS_, int ntiles, int G, int cta) : KS(KS_) {
+    int tile, ut, u, u1, upt, KS, ups;
+    __device__ QgmWalk(int KS_, int ntiles, int G, int cta, int ups_) : KS(KS_), ups(ups_) {
         upt = (KS + QGM_UNIT_KS - 1) / QGM_UNIT_KS;
         const int U = ntiles * upt;
         u = (int)((long long)U * cta / G);
@@ -89,7 +92,7 @@ struct QgmWalk {
     // Next stage: tile, first k-step, k-steps, and whether it ends the CTA's
     // segment of that tile.
     __device__ void next(int &t, int &k0, int &nks, bool &seg_end) {
-        const int n = (ut + 1 < upt && u + 1 < u1) ? 2 : 1;
+        const int n = (ups == 2 && ut + 1 < upt && u + 1 < u1) ? 2 : 1;
         t = tile;
         k0 = ut * QGM_UNIT_KS;
         nks = min(n * QGM_UNIT_KS, KS - k0);
@@ -108,7 +111,7 @@ struct QgmWalk {
 // independent 16-byte loads.  Blocks M.. write the ones row and the padding
 // rows of 16 chunks each.
 constexpr int QGM_PL_THREADS = 256;
-constexpr int QGM_PL_CHUNKS = 4;  // 16-k chunks per thread: K <= 256 * 4 * 16 = 16384
+constexpr int QGM_PL_CHUNKS = 8;  // 16-k chunks per thread: K <= 256 * 8 * 16 = 32768
 static_assert(QGM_PL_THREADS == 256, "the padding blocks map 16 chunks x 16 rows onto the threads");
 
 __device__ __forceinline__ void qgm_load16(const QGemvArgs &a, int m, int kc, bool vec, float v[16]) {
@@ -240,7 +243,10 @@ __global__ void __launch_bounds__(QGM_PL_THREADS) qgm_planes_kernel(const QGemvA
 // segment s go to buffer s & 1, so the drain of one segment overlaps the MMAs
 // of the next.  A drain warp reads its 32 lanes' plane columns with 16-column
 // tcgen05.ld loads and one wait, then recombines every row in registers.
-constexpr int QGM_DRAIN_LD = (QGM_MAX_M * 3 + 1 + 15) / 16;  // 16-column loads covering every plane row
+// A drain pass covers 32 rows: columns [0, 112) hold the ones row and rows
+// 0-31, columns [96, 208) rows 32-63.
+constexpr int QGM_DRAIN_LD = 7;
+constexpr int QGM_DRAIN_ROWS = 32;
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
     asm volatile(
@@ -248,6 +254,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
+}
+
+// Wait for this thread's tcgen05.ld results, then pass the registers
+// through an empty asm so no use of them can be scheduled before the wait
+// (the loads write their registers asynchronously).
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&d)[N]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(d[i]));
 }
 
 __global__ void __launch_bounds__(QGM_THREADS, 1)
@@ -259,11 +275,11 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
-    const int slot_bytes = qgm_slot_bytes(np);
+    const int slot_bytes = qgm_slot_bytes(np), wslot = qgm_wbytes(np), ups = qgm_ups(np);
     const uint32_t b_full = smem_u32(&bars[0]), b_empty = smem_u32(&bars[QGM_MAX_NST]);
     const uint32_t b_tfull = smem_u32(&bars[2 * QGM_MAX_NST]), b_tempty = smem_u32(&bars[2 * QGM_MAX_NST + 2]);
     const uint32_t b_done = smem_u32(&bars[2 * QGM_MAX_NST + 4]);
-    const int ncols = np <= 32 ? 32 : (np <= 64 ? 64 : 128);  // one buffer; two are allocated
+    const int ncols = np <= 32 ? 32 : (np <= 64 ? 64 : (np <= 128 ? 128 : 256));  // one buffer; two are allocated
     if (tid == 0) {
         for (int i = 0; i < nst; i++) {
             mbar_init(b_full + 8 * i, 1);
@@ -293,7 +309,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
     if (warp == 5) {
         // ---- producer: weights (immutable) may stream before the planes exist
         if (lane == 0) {
-            QgmWalk wk(w.KS, w.ntiles, G, cta);
+            QgmWalk wk(w.KS, w.ntiles, G, cta, ups);
             uint32_t it = 0, slot = 0, par = 0;
             bool waited = false;
             while (wk.more()) {
@@ -314,7 +330,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
                 tma_load_1d(dst, reinterpret_cast<const uint8_t *>(w.w) + ((size_t)t * w.KS + k0) * QGM_TN * 16, wbytes,
                             b_full + 8 * slot);
                 if (!waited) pdl_wait(), waited = true;  // the planes come from the previous kernel
-                tma_load_1d(dst + QGM_WBYTES, ws.planes + (size_t)k0 * np * 16, pbytes, b_full + 8 * slot);
+                tma_load_1d(dst + wslot, ws.planes + (size_t)k0 * np * 16, pbytes, b_full + 8 * slot);
                 it++;
                 if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
             }
@@ -322,7 +338,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
     } else if (warp == 4) {
         // ---- MMA issuer
         if (lane == 0) {
-            QgmWalk wk(w.KS, w.ntiles, G, cta);
+            QgmWalk wk(w.KS, w.ntiles, G, cta, ups);
             const uint32_t idesc = umma_idesc_i8(np);
             uint32_t slot = 0, par = 0, seg = 0;
             bool seg_start = true, ok = true;
@@ -340,7 +356,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = ring + slot * slot_bytes, p0 = a0 + QGM_WBYTES;
+                const uint32_t a0 = ring + slot * slot_bytes, p0 = a0 + wslot;
                 const uint32_t acc = tmem + buf * (uint32_t)ncols;
                 for (int kk = 0; kk < nks / 2; kk++) {
                     const uint64_t da = umma_sdesc(a0 + kk * 2 * QGM_TN * 16, QGM_TN * 16, 128);
@@ -363,10 +379,12 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
     } else {
         // ---- warps 0-3: drain TMEM per tile segment into exact int64 column sums
         pdl_wait();  // the previous finish kernel has cleared the sums
-        QgmWalk wk(w.KS, w.ntiles, G, cta);
+        QgmWalk wk(w.KS, w.ntiles, G, cta, ups);
         uint32_t seg = 0;
         const int col = warp * 32 + lane;  // output column within the tile (= TMEM lane)
-        const int nld = (3 * M + 1 + 15) >> 4;
+        const int rows_a = min(M, QGM_DRAIN_ROWS);
+        const int nld_a = (3 * rows_a + 1 + 15) >> 4;          // pass A: columns [0, 16 nld_a)
+        const int nld_b = M > QGM_DRAIN_ROWS ? (3 * M + 1 - 96 + 15) >> 4 : 0;  // pass B: [96, ...)
         while (wk.more()) {
             int t, k0, nks;
             bool se;
@@ -381,19 +399,16 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
             }
             tc_fence_after();
             const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16) + buf * (uint32_t)ncols;
+            long long *out = ws.acc + (size_t)t * QGM_TN + col;
             uint32_t d[QGM_DRAIN_LD * 16];
 #pragma unroll
             for (int j = 0; j < QGM_DRAIN_LD; j++)
-                if (j < nld) tmem_ld16(lane_base + 16 * j, d + 16 * j);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the registers hold the segment now
+                if (j < nld_a) tmem_ld16(lane_base + 16 * j, d + 16 * j);
+            tmem_wait_ld(d);
             // D[0] = sum_k w over this segment's k range (the ones row)
             const long long ones = (long long)(int)d[0];
-            long long *out = ws.acc + (size_t)t * QGM_TN + col;
 #pragma unroll
-            for (int m = 0; m < QGM_MAX_M; m++) {
+            for (int m = 0; m < QGM_DRAIN_ROWS; m++) {
                 if (m < M) {
                     const long long s = (long long)(int)d[1 + 3 * m] + ((long long)(int)d[2 + 3 * m] << 8) +
                                         ((long long)(int)d[3 + 3 * m] << 16) - (ones << 23);
@@ -402,6 +417,26 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
                                   (unsigned long long)s);
                 }
             }
+            if (nld_b > 0) {
+#pragma unroll
+                for (int j = 0; j < QGM_DRAIN_LD; j++)
+                    if (j < nld_b) tmem_ld16(lane_base + 96 + 16 * j, d + 16 * j);
+                tmem_wait_ld(d);
+#pragma unroll
+                for (int mm = 0; mm < QGM_DRAIN_ROWS; mm++) {
+                    const int m = QGM_DRAIN_ROWS + mm;  // columns 1+3m.. = 96 + (1+3mm)..
+                    if (m < M) {
+                        const long long s = (long long)(int)d[1 + 3 * mm] + ((long long)(int)d[2 + 3 * mm] << 8) +
+                                            ((long long)(int)d[3 + 3 * mm] << 16) - (ones << 23);
+                        if (s != 0)
+                            atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)m * ws.ld_acc),
+                                      (unsigned long long)s);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the segment has left TMEM
             seg++;
         }
     }
@@ -591,7 +626,7 @@ int finish_launch(const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool p
     // within two CTAs per SM
     const int cap = 2 * device_props().sm_count;
     int R = 2;
-    while (R < QGM_MAX_M && a.w.ntiles * ceil_div(a.M, R) > cap) R *= 2;
+    while (R < 32 && a.w.ntiles * ceil_div(a.M, R) > cap) R *= 2;
     const dim3 grid(a.w.ntiles, ceil_div(a.M, R));
     switch (R) {
     case 2: SB_CUDA_TRY(launch(qgm_finish_kernel<EPI, 1>, grid, dim3(QGM_FIN_THREADS), 0, st, pdl, a, ws)); break;
@@ -608,7 +643,7 @@ int finish_launch(const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool p
 size_t qgemm_planes_bytes(int K, int M) { return (size_t)ceil_div(K, 16) * qgemm_np(M) * 16; }
 
 bool qgemm_supported(const QWeightDesc &w, int M) {
-    return w.TN == QGM_TN && w.group == 0 && (w.KS % 2) == 0 && M > QG_MAX_M && M <= QGM_MAX_M && w.K <= 16384;
+    return w.TN == QGM_TN && w.group == 0 && (w.KS % 2) == 0 && M > QG_MAX_M && M <= QGM_MAX_M && w.K <= 32768;
 }
 
 int qgemm_check_error() {

@@ -1,12 +1,12 @@
 // Batched int8 linear on the 5th-generation tensor cores (tcgen05 + TMEM),
-// for 5 to 32 activation rows (batched decode, the quantized-linear sweep).
+// for 5 to 64 activation rows (batched decode, the quantized-linear sweep).
 #pragma once
 
 #include "qgemv.cuh"
 
 namespace sb {
 
-constexpr int QGM_MAX_M = 32;
+constexpr int QGM_MAX_M = 64;
 
 // Plane rows of the MMA's B operand for M activation rows: three byte planes
 // per row plus one all-ones row, padded to a multiple of 16.
@@ -23,7 +23,7 @@ struct QGemmWs {
 size_t qgemm_planes_bytes(int K, int M);
 
 // Whether the tensor-core path takes this weight and row count: 128-column
-// tiles, per-tensor scale, K a multiple of 32, 5 <= M <= 32.
+// tiles, per-tensor scale, K a multiple of 32 up to 32768, 5 <= M <= 64.
 bool qgemm_supported(const QWeightDesc &w, int M);
 
 // y = epilogue(x W) for M rows, as qgemv_launch (same QGemvArgs and epilogues)

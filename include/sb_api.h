@@ -72,7 +72,7 @@ sb_status sb_quantize_symmetric(const float *w, size_t n, int8_t *q, float *scal
 typedef struct sb_qweight sb_qweight;
 sb_status sb_qweight_create(int K, int N, int group, sb_qweight **out);
 /* Same with an explicit tile width tile_n in {16, 32, 64, 128, 256} (0 =
- * the GEMV's choice).  128-column tiles let 5-32-row products run on the
+ * the GEMV's choice).  128-column tiles let 5-64-row products run on the
  * tensor cores (see sb_matmul_i8_f32).  No reference counterpart: the
  * reference keeps [K,N] as is; this only picks the on-device packing. */
 sb_status sb_qweight_create_tn(int K, int N, int group, int tile_n, sb_qweight **out);
@@ -83,7 +83,7 @@ sb_status sb_qweight_destroy(sb_qweight *w);
 /* matmul_i8_f32 (backend/mod.rs:521-533; CPU cpu.rs:1129-1160):
  * c[M,N] = a[M,K] . dequant(q)[K,N], f32 accumulate.  a, c are device
  * pointers; a_dtype is SB_DTYPE_F32 or SB_DTYPE_BF16.  1-4 rows run the
- * GEMV; 5-32 rows of a per-tensor-scaled weight with 128-column tiles run
+ * GEMV; 5-64 rows of a per-tensor-scaled weight with 128-column tiles run
  * on the tcgen05 tensor cores (same fixed-point arithmetic, same results
  * as row-by-row GEMVs); other shapes run the GEMV 4 rows at a time.  Uses a library-owned
  * workspace on the current device. */

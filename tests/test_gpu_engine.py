@@ -160,13 +160,13 @@ def test_batched_decode_equals_independent_sequences(B):
         assert got[b].tolist() == om.generate_greedy(prompts[b], 33, kv_bf16=True).tolist(), b
 
 
-@pytest.mark.parametrize("B", [5, 8, 32])
+@pytest.mark.parametrize("B", [5, 8, 32, 64])
 def test_tensor_core_batched_decode_equals_independent_sequences(B):
-    # Batches of 5-32 run every projection through the tcgen05 GEMM (three
+    # Batches of 5-64 run every projection through the tcgen05 GEMM (three
     # launches per linear); greedy streams must equal the per-sequence oracle.
     c = small_config(layers=2, heads=8, kv=2)
     om = O.OracleLlama(orc_config(c, 128), 9)
-    e = engine_from_oracle(om, c, max_seq=128, max_batch=32, kv_dtype="bf16")
+    e = engine_from_oracle(om, c, max_seq=128, max_batch=max(B, 32), kv_dtype="bf16")
     assert e.step_launches(B) == 5 + 13 * c.n_layers
     assert e.step_launches(4) == 3 + 5 * c.n_layers
     prompts = np.stack([O.prompt_ids(200 + b, 12, c.vocab_size) for b in range(B)])
@@ -228,7 +228,7 @@ def test_seven_b_shape_two_layers():
 def test_capacity_and_argument_errors():
     c = small_config(layers=1)
     with pytest.raises(N.SbError):
-        QuantLlamaB200.new_random(c, seed=0, max_seq=32, max_batch=33)  # above the tensor-core path's 32 rows
+        QuantLlamaB200.new_random(c, seed=0, max_seq=32, max_batch=65)  # above the tensor-core path's 64 rows
     with pytest.raises(N.SbError):  # batches above 4 need 32-aligned hidden / ffn sizes
         QuantLlamaB200.new_random(small_config(h=256, heads=4, kv=4, layers=1, ffn=200), seed=0, max_seq=32,
                                   max_batch=8)

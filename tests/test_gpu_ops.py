@@ -77,6 +77,27 @@ def test_batched_tensor_core_matmul_equals_rowwise_gemv(M, K, N_, bf16):
     assert rel_err(out, ref) < TOL_F32
 
 
+@pytest.mark.parametrize("M", [33, 48, 64])
+@pytest.mark.parametrize("K,N_", [(4096, 4096), (512, 1536), (20480, 256), (96, 384)])
+def test_batched_tensor_core_matmul_33_to_64_rows(M, K, N_):
+    # 33-64 rows: the MMA's B operand grows to 3M+1 plane rows (up to 208),
+    # stages hold one unit and TMEM is drained in two passes; K beyond 16384
+    # keeps the int32 accumulators exact.  Bit-equal to row-wise GEMVs.
+    rng = np.random.default_rng(M * 131 + K + N_)
+    w = (rng.standard_normal((K, N_)) * 0.02).astype(np.float32)
+    q, s = O.quantize_symmetric(w)
+    q = q.reshape(K, N_)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    qw = QWeight(q, [s], tile_n=128)
+    at = torch.from_numpy(a).cuda()
+    out = matmul_i8_f32(at, qw).cpu().numpy()
+    rows = np.vstack([matmul_i8_f32(at[i:i + 1].contiguous(), qw).cpu().numpy() for i in range(M)])
+    torch.cuda.synchronize()
+    assert np.array_equal(out, rows)
+    ref = O.matmul_i8_f32(a, q, s, M, K, N_)
+    assert rel_err(out, ref) < TOL_F32
+
+
 @pytest.mark.parametrize("group", [32, 64])
 @pytest.mark.parametrize("M", [1, 4, 8])
 @pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008)])
