@@ -56,6 +56,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PROMPT_LEN = 512
+PREFILL_ROWS = 64
 
 WORKLOADS = {
     "llama2-7b-bs1": {"metric": "decode tok/s, 7B-shape int8, bs1", "shape": "llama2_7b_shape", "batch": 1,
@@ -220,12 +221,23 @@ def run_ours(args, rank: int, world: int, dist):
         obj = [tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         tp_kw = {"tp_rank": rank, "tp_size": tp, "tp_id": obj[0]}
-    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=B, kv_dtype="bf16", **tp_kw)
+    # rows per step: the decoded batch, and up to 64 prompt positions per
+    # batched-prefill step (the tensor-core linears take 5-64 rows)
+    rows = max(B, PREFILL_ROWS)
+    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=rows, kv_dtype="bf16", **tp_kw)
     # tensor-parallel ranks decode the same sequences; replicas decode their own
     rng = np.random.default_rng(1000 + (0 if tp > 1 else rank))
     prompts = rng.integers(0, cfg.vocab_size, (B, args.prompt), dtype=np.int64).astype(np.int32)
-    model.begin(prompts)
-    model.step(args.prompt - 1 + W)  # prefill (token by token, as generate() does) + warm-up
+    # batched prefill of the prompts (host-timed, includes its syncs), then warm-up steps
+    n_warm = min(args.prompt, rows + args.prompt % rows)  # every chunk shape the timed prefill uses
+    model.prefill(prompts[:, :n_warm])  # captures the step graphs outside the timed prefill
+    torch.cuda.synchronize()
+    t_pf0 = time.perf_counter()
+    model.prefill(prompts)
+    t_pf1 = time.perf_counter()
+    prefill = {"tok_s": B * args.prompt / (t_pf1 - t_pf0), "tokens": B * args.prompt, "ms": (t_pf1 - t_pf0) * 1e3,
+               "positions_per_step": rows, "timing": "host wall clock around sb_llama_prefill (synchronous)"}
+    model.step(W)
     st = torch.cuda.ExternalStream(model.stream())
     torch.cuda.synchronize()
 
@@ -328,6 +340,7 @@ def run_ours(args, rank: int, world: int, dist):
                    "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else
                               "CUDA graph of per-operation kernels per step, programmatic dependent launch")},
         "gpu_launches": launches_per_step * K,
+        "prefill": prefill,
         "roofline": roof,
         "clocks": clk,
     }

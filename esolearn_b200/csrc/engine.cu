@@ -430,9 +430,11 @@ int get_graph(sb_llama *m, int M, cudaGraphExec_t *out) {
         return SB_OK;
     }
     // Warm up once outside capture (sets kernel attributes, loads modules)
-    // from a valid state; callers set their own state afterwards.
-    std::vector<int32_t> zero(M, 0);
-    SB_TRY(set_state(m, M, zero.data(), zero.data(), zero.data()));
+    // at position -1, which writes no K/V row and reads no context, so the
+    // caches of live sequences are untouched; callers set their own state
+    // afterwards.
+    std::vector<int32_t> zero(M, 0), before(M, -1);
+    SB_TRY(set_state(m, M, zero.data(), before.data(), zero.data()));
     SB_TRY(enqueue_step(m, M, m->st, true, false));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     cudaGraph_t g = nullptr;
@@ -1036,6 +1038,59 @@ sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_p
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     m->active = batch;
     m->steps = 0;
+    return SB_OK;
+}
+
+sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n_prompt) {
+    SB_CHECK(m && prompts, SB_ERR_ARG, "sb_llama_prefill: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    SB_CHECK(n_prompt >= 1 && n_prompt < m->cfg.max_seq_len, SB_ERR_SHAPE, "prompt length %d", n_prompt);
+    for (size_t i = 0; i < (size_t)batch * n_prompt; i++)
+        SB_CHECK(prompts[i] >= 0 && prompts[i] < m->V, SB_ERR_ARG, "prompt token %d outside vocab", prompts[i]);
+    SB_TRY(check_ready(m));
+    const int C = m->B;  // prompt positions per batched step
+    const int tail = n_prompt % C;
+    // Capture every step shape used here and by the decode steps that follow
+    // before any state is set: a capture's warm-up step resets the sequence state.
+    cudaGraphExec_t g_full = nullptr, g_tail = nullptr, g_dec = nullptr;
+    if (!(batch == 1 && m->ds_ok)) SB_TRY(get_graph(m, batch, &g_dec));
+    if (n_prompt >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full));
+    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail));
+    std::vector<int> pt((size_t)m->B * m->pps);
+    std::vector<int32_t> tok(C), pos(C), zero(C, 0), first(batch);
+    for (int b = 0; b < batch; b++) {
+        // every row is a position of sequence b: all rows use its pages
+        for (int r = 0; r < m->B; r++)
+            for (int i = 0; i < m->pps; i++) pt[(size_t)r * m->pps + i] = b * m->pps + i;
+        SB_CUDA_TRY(cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->st));
+        int M = 0;
+        for (int p0 = 0; p0 < n_prompt; p0 += C) {
+            M = std::min(C, n_prompt - p0);
+            for (int r = 0; r < M; r++) tok[r] = prompts[(size_t)b * n_prompt + p0 + r], pos[r] = p0 + r;
+            SB_TRY(set_state(m, M, tok.data(), pos.data(), zero.data()));
+            if (M == 1 && m->ds_ok)
+                SB_TRY(ds_step(m));
+            else
+                SB_CUDA_TRY(cudaGraphLaunch(M == C ? g_full : g_tail, m->st));
+        }
+        // the argmax after the last prompt token is the first generated token
+        SB_CUDA_TRY(cudaMemcpyAsync(&first[b], m->d_last + (M - 1), sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    }
+    // sequences back on their own pages, positioned after the prompt
+    for (int r = 0; r < m->B; r++)
+        for (int i = 0; i < m->pps; i++) pt[(size_t)r * m->pps + i] = r * m->pps + i;
+    SB_CUDA_TRY(cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    SB_TRY(check_device_errors(m));
+    std::vector<int32_t> p1(batch, n_prompt), z(batch, 0), one(batch, 1);
+    SB_TRY(set_state(m, batch, first.data(), p1.data(), z.data()));
+    for (int b = 0; b < batch; b++)
+        SB_CUDA_TRY(cudaMemcpyAsync(m->d_out + (size_t)b * m->cfg.max_seq_len, &first[b], sizeof(int),
+                                    cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_ngen, one.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    m->active = batch;
+    m->steps = n_prompt;
     return SB_OK;
 }
 

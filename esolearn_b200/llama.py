@@ -296,12 +296,24 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_get_trace(self._h, _ptr(out)))
         return out
 
-    def generate_greedy(self, prompts, max_tokens: int) -> np.ndarray:
-        """generate (generate.rs:51-89) at temperature 0 for equal-length prompts."""
+    def generate_greedy(self, prompts, max_tokens: int, batched_prefill: bool = False) -> np.ndarray:
+        """generate (generate.rs:51-89) at temperature 0 for equal-length prompts.
+        batched_prefill: run the prompt as chunks of max_batch positions
+        (sb_llama_prefill) instead of one position per step."""
         pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
         out = np.empty((pr.shape[0], max_tokens), np.int32)
-        N.check(N.lib().sb_llama_generate_greedy(self._h, pr.shape[0], _ptr(pr), pr.shape[1], max_tokens, _ptr(out)))
-        return out
+        if not batched_prefill:
+            N.check(N.lib().sb_llama_generate_greedy(self._h, pr.shape[0], _ptr(pr), pr.shape[1], max_tokens,
+                                                     _ptr(out)))
+            return out
+        self.prefill(pr)
+        self.step(max_tokens - 1)
+        return self.tokens(pr.shape[0], max_tokens)
+
+    def prefill(self, prompts):
+        """Batched prefill (sb_llama_prefill): the sequences are then ready to decode with step()."""
+        pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        N.check(N.lib().sb_llama_prefill(self._h, pr.shape[0], _ptr(pr), pr.shape[1]))
 
     # -- benchmark helpers --------------------------------------------------
     def begin(self, prompts):

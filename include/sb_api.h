@@ -220,6 +220,14 @@ sb_status sb_llama_get_trace(sb_llama *m, float *out);
 /* Benchmark helpers: queue n decode steps of the current batch on the
  * engine stream (device-driven tokens and positions; no host sync). */
 sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt);
+/* Batched prefill, the decode-step counterpart of LlamaModel::forward over a
+ * prompt (llama.rs:683-700): each sequence's prompt runs in chunks of up to
+ * max_batch positions, every position one row of a batched step (all rows
+ * on that sequence's KV pages), so each chunk's projections are one
+ * tensor-core GEMM.  Leaves `batch` sequences as sb_llama_begin +
+ * sb_llama_step(n_prompt) would: the prompt cached, the argmax after the last
+ * prompt token recorded as generated token 0 and fed to the next step. */
+sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n_prompt);
 sb_status sb_llama_step(sb_llama *m, int n_steps);
 sb_status sb_llama_tokens(sb_llama *m, int32_t *out, int max_tokens, int *n_out);
 void *sb_llama_stream(sb_llama *m);

@@ -175,6 +175,20 @@ def test_tensor_core_batched_decode_equals_independent_sequences(B):
         assert got[b].tolist() == om.generate_greedy(prompts[b], 33, kv_bf16=True).tolist(), b
 
 
+@pytest.mark.parametrize("B,max_batch,n_prompt", [(1, 16, 40), (3, 16, 40), (2, 8, 17), (1, 1, 9)])
+def test_batched_prefill_matches_token_by_token(B, max_batch, n_prompt):
+    # sb_llama_prefill runs each prompt as chunks of max_batch positions (one
+    # batched step per chunk, rows sharing the sequence's pages); the greedy
+    # streams that follow must equal the oracle's token-by-token generate().
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 128), 9)
+    e = engine_from_oracle(om, c, max_seq=128, max_batch=max_batch, kv_dtype="bf16")
+    prompts = np.stack([O.prompt_ids(300 + b, n_prompt, c.vocab_size) for b in range(B)])
+    got = e.generate_greedy(prompts, 24, batched_prefill=True)
+    for b in range(B):
+        assert got[b].tolist() == om.generate_greedy(prompts[b], 24, kv_bf16=True).tolist(), b
+
+
 @pytest.mark.parametrize("desc,cfg,B", [
     ("small_gqa4", small_config(layers=2, heads=8, kv=2), 8),
     ("llama3_8b_shape_1layer", LlamaConfig(128256, 4096, 14336, 1, 32, 8, 8192, 1e-5, 500000.0, False,
