@@ -1,6 +1,8 @@
 // Paged, GQA-aware decode attention over a bf16 (or f32) KV cache.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (types only; the encoder is resolved at run time)
+
 #include "sb_common.cuh"
 
 namespace sb {
@@ -19,7 +21,19 @@ struct AttnArgs {
     float *out = nullptr;           // [B, n_heads*hd]
     float *part = nullptr;          // scratch [B][n_heads][n_splits][hd+2]
     unsigned *counters = nullptr;   // scratch [B][n_kv], zero between launches
+    // Tensor-map path (bf16 cache, 2-8 query heads per kv head, pages of a
+    // multiple of 64 positions): K and V of every layer as [rows][hd] 2-D
+    // tensors; this layer's (page, head, slot) row is tm_row0 + (page*n_kv +
+    // head)*page_size + slot.
+    int tma = 0;
+    long long tm_row0 = 0;
+    CUtensorMap tmk, tmv;
 };
+
+// Reports (and clears) a timed-out wait of the tensor-map kernel.
+int attn_tc_check_error();
+// Encode a [rows][hd] bf16 tensor map over a KV cache for the tensor-map path.
+int attn_make_tensor_map(CUtensorMap *map, const void *base, long long rows, int hd);
 
 // Splits per (sequence, kv head) for a given max context on this device:
 // enough CTAs for two waves, and at most about 256 positions per split.

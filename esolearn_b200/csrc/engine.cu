@@ -87,6 +87,8 @@ struct sb_llama {
     float *att_part = nullptr;
     unsigned *att_cnt = nullptr;
     int att_splits = 1;
+    bool att_tma = false;  // K/V tensor maps for the tensor-map attention kernel
+    CUtensorMap att_tmk, att_tmv;
 
     // sequence state
     SeqState seq;
@@ -286,6 +288,12 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.out = m->attn;
             a.part = m->att_part;
             a.counters = m->att_cnt;
+            if (m->att_tma) {
+                a.tma = 1;
+                a.tmk = m->att_tmk;
+                a.tmv = m->att_tmv;
+                a.tm_row0 = (long long)l * (long long)(m->layer_kv_elems / m->hd);
+            }
             SB_PROF(prof, 1, attn_launch(a, st, pdl));
         }
         {
@@ -420,6 +428,7 @@ int ds_step(sb_llama *m) {
 int check_device_errors(sb_llama *m) {
     if (m->ds_ok) SB_TRY(ds_check_error(m->ds_sync, m->st));
     SB_TRY(qgemm_check_error());
+    SB_TRY(attn_tc_check_error());
     if (m->tp > 1) SB_TRY(tp_check_error(m->comm));
     return qgemv_check_error();
 }
@@ -627,6 +636,12 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     const size_t esz = m->kv_f32 ? 4 : 2;
     if ((rc = dalloc(m, &m->kc, m->layer_kv_elems * esz * m->L)) != SB_OK) return fail(rc);
     if ((rc = dalloc(m, &m->vc, m->layer_kv_elems * esz * m->L)) != SB_OK) return fail(rc);
+    if (!m->kv_f32 && m->P % 64 == 0 && m->hd % 64 == 0) {
+        // every layer's K (and V) cache as one [rows][hd] tensor for the tensor-map attention
+        const long long rows = (long long)m->L * (long long)(m->layer_kv_elems / m->hd);
+        m->att_tma = attn_make_tensor_map(&m->att_tmk, m->kc, rows, m->hd) == SB_OK &&
+                     attn_make_tensor_map(&m->att_tmv, m->vc, rows, m->hd) == SB_OK;
+    }
     {
         std::vector<int> pt((size_t)m->B * m->pps);
         for (int b = 0; b < m->B; b++)
