@@ -216,6 +216,16 @@ struct StepProfiler {
     }
 };
 
+// Context splits of the tensor-map attention for M sequences: about four
+// CTAs per SM in total (its CTAs pipeline many tiles each, so fewer and longer
+// ones beat the two-wave choice of attn_pick_splits), within the split
+// scratch the engine allocated (M * splits <= B * att_splits).
+int tma_splits(const sb_llama *m, int M) {
+    const int want = (4 * device_props().sm_count + M * m->nkv / 2) / std::max(1, M * m->nkv);
+    const int cap = std::max(1, m->B * m->att_splits / M);
+    return std::max(1, std::min({want, cap, ceil_div(m->cfg.max_seq_len, 128)}));
+}
+
 // O and down projections add into the residual stream x.  Under tensor
 // parallelism each rank holds a row slice of the weight, so rank 0 adds its
 // partial product to x and the other ranks store theirs; the sum over ranks
@@ -284,7 +294,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.n_kv = m->nkv;
             a.hd = m->hd;
             a.page_size = m->P;
-            a.n_splits = m->att_splits;
+            a.n_splits = m->att_tma ? tma_splits(m, M) : m->att_splits;
             a.out = m->attn;
             a.part = m->att_part;
             a.counters = m->att_cnt;
