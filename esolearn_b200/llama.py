@@ -236,6 +236,15 @@ class QuantLlamaB200:
 
     # -- weights --------------------------------------------------------
     @classmethod
+    def from_safetensors(cls, config: LlamaConfig, paths, **kw) -> "QuantLlamaB200":
+        """LlamaModel::from_safetensors (llama.rs:768-958) + quantize_symmetric per projection."""
+        from .safetensors_io import load_into
+
+        m = cls(config, **kw)
+        load_into(m, config, paths)
+        return m
+
+    @classmethod
     def new_random(cls, config: LlamaConfig, seed: int, **kw) -> "QuantLlamaB200":
         """LlamaModel::new (llama.rs:593-680) + quantize_symmetric, on the device."""
         m = cls(config, **kw)

@@ -1,0 +1,116 @@
+"""Weight loading from HF safetensors shards (LlamaModel::from_safetensors,
+llama.rs:768-958): dtype conversion, [out,in] -> [in,out] transposes, the
+q|k|v fusion and per-tensor quantization must give exactly the int8 tensors
+and scales of the reference wiring."""
+import numpy as np
+import pytest
+
+import oracle as O
+from esolearn_b200 import LlamaConfig
+from esolearn_b200 import _native as N
+from esolearn_b200.safetensors_io import SafeTensorsShards, quantized_llama_tensors, write_safetensors
+
+
+def _cfg(tie=False):
+    return LlamaConfig(96, 64, 80, 2, 4, 2, 64, 1e-5, 10000.0, tie, None)
+
+
+def _hf_weights(c: LlamaConfig, seed: int):
+    rng = np.random.default_rng(seed)
+    h, F, V = c.hidden_size, c.intermediate_size, c.vocab_size
+    hd = c.head_dim()
+    qd, kd = c.n_heads * hd, c.n_kv_heads * hd
+    w = {"model.embed_tokens.weight": rng.standard_normal((V, h)) * 0.02, "model.norm.weight": 1 + 0.1 * rng.standard_normal(h)}
+    for i in range(c.n_layers):
+        p = f"model.layers.{i}"
+        w[f"{p}.self_attn.q_proj.weight"] = rng.standard_normal((qd, h)) * 0.02
+        w[f"{p}.self_attn.k_proj.weight"] = rng.standard_normal((kd, h)) * 0.02
+        w[f"{p}.self_attn.v_proj.weight"] = rng.standard_normal((kd, h)) * 0.02
+        w[f"{p}.self_attn.o_proj.weight"] = rng.standard_normal((h, qd)) * 0.02
+        w[f"{p}.mlp.gate_proj.weight"] = rng.standard_normal((F, h)) * 0.02
+        w[f"{p}.mlp.up_proj.weight"] = rng.standard_normal((F, h)) * 0.02
+        w[f"{p}.mlp.down_proj.weight"] = rng.standard_normal((h, F)) * 0.02
+        w[f"{p}.input_layernorm.weight"] = 1 + 0.1 * rng.standard_normal(h)
+        w[f"{p}.post_attention_layernorm.weight"] = 1 + 0.1 * rng.standard_normal(h)
+    if not c.tie_word_embeddings:
+        w["lm_head.weight"] = rng.standard_normal((V, h)) * 0.02
+    return {k: v.astype(np.float32) for k, v in w.items()}
+
+
+def _write_shards(tmp_path, w):
+    names = sorted(w)
+    half = len(names) // 2
+    proj = [n for n in names if "proj" in n]
+    paths = []
+    for k, part in enumerate((names[:half], names[half:])):
+        path = str(tmp_path / f"model-{k:05d}-of-00002.safetensors")
+        write_safetensors(path, {n: w[n] for n in part}, bf16=[n for n in part if n in proj])
+        paths.append(path)
+    return paths, set(proj)
+
+
+def _bf16(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("tie", [False, True])
+def test_loader_matches_reference_wiring(tmp_path, tie):
+    c = _cfg(tie)
+    w = _hf_weights(c, 3)
+    paths, bf = _write_shards(tmp_path, w)
+    src = {n: (_bf16(a) if n in bf else a) for n, a in w.items()}  # what the shards hold
+    got = list(quantized_llama_tensors(c, paths))
+    q_items = {(t[1], t[2]): (t[3], t[4]) for t in got if t[0] == "q"}
+    f_items = {(t[1], t[2]): t[3] for t in got if t[0] == "f"}
+    h = c.hidden_size
+    for i in range(c.n_layers):
+        p = f"model.layers.{i}"
+        qkv = np.concatenate([src[f"{p}.self_attn.{x}_proj.weight"].T for x in "qkv"], axis=1)
+        ref = {N.SB_W_QKV: qkv, N.SB_W_O: src[f"{p}.self_attn.o_proj.weight"].T,
+               N.SB_W_GATE: src[f"{p}.mlp.gate_proj.weight"].T, N.SB_W_UP: src[f"{p}.mlp.up_proj.weight"].T,
+               N.SB_W_DOWN: src[f"{p}.mlp.down_proj.weight"].T}
+        for slot, wf in ref.items():
+            qo, so = O.quantize_symmetric(np.ascontiguousarray(wf))  # quantize.rs:16-32 restated
+            qg, sg = q_items[(i, slot)]
+            assert qg.shape == wf.shape and sg == so and np.array_equal(qg.ravel(), qo), (i, slot)
+        assert np.array_equal(f_items[(N.SB_F_NORM_IN, i)], src[f"{p}.input_layernorm.weight"])
+        assert np.array_equal(f_items[(N.SB_F_NORM_POST, i)], src[f"{p}.post_attention_layernorm.weight"])
+    head = src["model.embed_tokens.weight" if tie else "lm_head.weight"]
+    qo, so = O.quantize_symmetric(head)
+    qg, sg = q_items[(-1, 0)]
+    assert qg.shape == (c.vocab_size, h) and sg == so and np.array_equal(qg.ravel(), qo)
+    assert np.array_equal(f_items[(N.SB_F_EMBED, 0)], src["model.embed_tokens.weight"])
+
+
+def test_dtype_conversion_is_exact(tmp_path):
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((5, 7)).astype(np.float32)
+    path = str(tmp_path / "t.safetensors")
+    write_safetensors(path, {"x": a, "y": a}, bf16=["y"])
+    st = SafeTensorsShards([path])
+    assert np.array_equal(st.f32("x"), a)
+    assert np.array_equal(st.f32("y"), _bf16(a))
+    with pytest.raises(N.SbError):
+        st.f32("missing")
+
+
+@pytest.mark.gpu
+def test_engine_from_safetensors_equals_engine_from_tensors(tmp_path):
+    # The same weights through from_safetensors and through load_qweight of
+    # the directly quantized tensors: identical logits and greedy streams.
+    from esolearn_b200 import QuantLlamaB200
+
+    N.check(N.lib().sb_init(0))
+    c = LlamaConfig(512, 512, 1376, 2, 8, 2, 64, 1e-5, 10000.0, False, None)
+    w = _hf_weights(c, 11)
+    paths, _ = _write_shards(tmp_path, w)
+    a = QuantLlamaB200.from_safetensors(c, paths, max_seq=64)
+    b = QuantLlamaB200(c, max_seq=64)
+    for t in quantized_llama_tensors(c, paths):
+        (b.load_qweight if t[0] == "q" else b.load_f32)(*t[1:])
+    prompt = O.prompt_ids(4, 8, c.vocab_size)
+    assert a.generate_greedy(prompt, 16).tolist() == b.generate_greedy(prompt, 16).tolist()
+    ca, cb = a.new_kv_cache(64), b.new_kv_cache(64)
+    for pos, t in enumerate(prompt):
+        assert np.array_equal(a.forward_with_cache(int(t), pos, ca), b.forward_with_cache(int(t), pos, cb))
