@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(ATC_THREADS) attn_tc_kernel(const AttnArgs a) 
     constexpr int NB = HD / 8;
     constexpr int CPR = HD / 8;      // 16-byte chunks per K/V row
 
-    extern __shared__ __align__(16) uint8_t smraw[];
+    extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ float s_m[ATC_WARPS][REP], s_l[ATC_WARPS][REP];
     __shared__ float s_fm[REP], s_fl[REP];
     __shared__ int s_last;
