@@ -72,6 +72,7 @@ SIGNATURES = {
     "sb_llama_create": (C.c_int, [C.POINTER(LlamaConfigC), C.POINTER(vp)]),
     "sb_llama_prefill": (C.c_int, [vp, C.c_int, vp, C.c_int]),
     "sb_tp_unique_id": (C.c_int, [vp]),
+    "sb_tp_probe_timeout": (C.c_int, [i32p, C.POINTER(C.c_double)]),
     "sb_llama_create_tp": (C.c_int, [C.POINTER(LlamaConfigC), C.c_int, C.c_int, vp, C.POINTER(vp)]),
     "sb_tp_shard_qweight": (C.c_int, [C.POINTER(LlamaConfigC), C.c_int, C.c_int, C.c_int, vp, vp, i32p, i32p]),
     "sb_llama_destroy": (C.c_int, [vp]),

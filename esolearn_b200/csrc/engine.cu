@@ -747,6 +747,11 @@ sb_status sb_tp_shard_qweight(const sb_llama_config *cfg, int slot, int tp_rank,
     return tp_shard(*cfg, slot, tp_rank, tp_size, full, shard, rows, cols);
 }
 
+sb_status sb_tp_probe_timeout(int *timed_out, double *seconds) {
+    SB_CHECK(timed_out && seconds, SB_ERR_ARG, "sb_tp_probe_timeout: null argument");
+    return tp_probe_timeout(timed_out, seconds);
+}
+
 sb_status sb_tp_unique_id(uint8_t *id) {
     SB_CHECK(id, SB_ERR_ARG, "sb_tp_unique_id: null argument");
     return tp_unique_id(id);

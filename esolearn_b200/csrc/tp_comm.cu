@@ -221,6 +221,47 @@ int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st) {
     return SB_OK;
 }
 
+int tp_probe_timeout(int *timed_out, double *seconds) {
+    // Two ranks on this device; the cells of "rank 1" are never written, so
+    // rank 0's wait for them must give up after the bound and raise the error
+    // word -- no fault, no trap, the context stays usable.
+    const int T = 2, cap = 1024;
+    uint2 *recv = nullptr;
+    unsigned *misc = nullptr;
+    float *x = nullptr;
+    int rc = SB_OK;
+    const size_t rbytes = sizeof(uint2) * 2 * (size_t)T * cap;
+    if (cudaMalloc(&recv, 2 * rbytes) != cudaSuccess || cudaMalloc(&misc, sizeof(unsigned) * (TP_AR_CTAS + 1)) !=
+        cudaSuccess || cudaMalloc(&x, sizeof(float) * cap) != cudaSuccess)
+        rc = set_error(SB_ERR_OOM, "peer all-reduce probe: allocation failed");
+    if (rc == SB_OK && (cudaMemset(recv, 0, 2 * rbytes) != cudaSuccess ||
+                        cudaMemset(misc, 0, sizeof(unsigned) * (TP_AR_CTAS + 1)) != cudaSuccess ||
+                        cudaMemset(x, 0, sizeof(float) * cap) != cudaSuccess))
+        rc = set_error(SB_ERR_CUDA, "peer all-reduce probe: memset failed");
+    unsigned err = 0;
+    if (rc == SB_OK) {
+        TpPeers P;
+        P.cap = cap;
+        P.recv[0] = recv;                       // this rank's cells
+        P.recv[1] = recv + 2 * (size_t)T * cap;  // stands for rank 1's: nothing answers
+        P.epoch = misc;
+        P.error = misc + TP_AR_CTAS;
+        const auto t0 = std::chrono::steady_clock::now();
+        tp_ar_kernel<<<1, 256>>>(x, cap, P, 0, T);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (e != cudaSuccess) rc = set_error(SB_ERR_CUDA, "peer all-reduce probe: %s", cudaGetErrorString(e));
+        if (rc == SB_OK && cudaMemcpy(&err, P.error, sizeof err, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = set_error(SB_ERR_CUDA, "peer all-reduce probe: readback failed");
+    }
+    cudaFree(recv);
+    cudaFree(misc);
+    cudaFree(x);
+    *timed_out = err != 0;
+    return rc;
+}
+
 int tp_check_error(const TpComm &c) {
     if (!c.p2p) return SB_OK;
     unsigned f = 0;

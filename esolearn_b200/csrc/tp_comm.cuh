@@ -52,6 +52,9 @@ int tp_allreduce_f32(const TpComm &c, float *buf, size_t count, cudaStream_t st)
 int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st);
 // Reports (and clears) a timed-out flag wait of the peer all-reduce.
 int tp_check_error(const TpComm &c);
+// Runs the peer all-reduce against a peer that never writes (one device);
+// *timed_out = 1 when its bounded wait gave up and raised the error word.
+int tp_probe_timeout(int *timed_out, double *seconds);
 // recv[r * count + i] = send_r[i], on `st` (capturable); elem_bytes 4.
 int tp_allgather32(const TpComm &c, const void *send, void *recv, size_t count, cudaStream_t st);
 

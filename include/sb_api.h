@@ -182,6 +182,13 @@ sb_status sb_tp_unique_id(uint8_t *id);
  * for the others: SB_ERR_TIMEOUT) and allocates its shard of the model. */
 sb_status sb_llama_create_tp(const sb_llama_config *cfg, int tp_rank, int tp_size, const uint8_t *id,
                              sb_llama **out);
+/* Diagnostic of the tensor-parallel failure path (no reference counterpart):
+ * runs one slice of the peer all-reduce on the current device against a
+ * stand-in peer that never writes.  Its bounded wait (about 2 s) must give up
+ * and raise the error word -- *timed_out = 1 -- leaving the device usable;
+ * *seconds is the wall time of the attempt.  The same bound turns a rank
+ * that stops answering mid-step into SB_ERR_TIMEOUT on the others. */
+sb_status sb_tp_probe_timeout(int *timed_out, double *seconds);
 /* Host-only: rank tp_rank's slice of the full reference tensor of `slot`
  * (SB_W_*; SB_W_LM_HEAD is [V,h]) in the reference layout, and its shape.
  * With full == NULL only rows/cols are returned. */

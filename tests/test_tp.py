@@ -225,3 +225,26 @@ def test_tensor_parallel_engine_matches_oracle(mode):
                                                         kv_bf16=True).tolist(), (r, b)
         assert rel_err(lg, ref_lg) < 1e-3
     assert np.array_equal(res[0][2], res[1][2])  # identical logits on both ranks
+
+
+@pytest.mark.gpu
+def test_peer_allreduce_wait_gives_up_and_device_stays_usable():
+    # A rank that never delivers its partial sums: the peer all-reduce's
+    # bounded wait (2 s of %globaltimer) raises its error word instead of
+    # hanging, and the device keeps working afterwards.
+    import ctypes as C
+
+    import torch
+
+    from esolearn_b200 import QWeight, matmul_i8_f32
+
+    N.check(N.lib().sb_init(0))
+    timed_out, secs = C.c_int32(0), C.c_double(0)
+    N.check(N.lib().sb_tp_probe_timeout(C.byref(timed_out), C.byref(secs)))
+    assert timed_out.value == 1
+    assert 1.5 < secs.value < 30.0, secs.value
+    rng = np.random.default_rng(0)
+    q = rng.integers(-127, 128, (64, 32), dtype=np.int8)
+    a = rng.standard_normal((2, 64)).astype(np.float32)
+    out = matmul_i8_f32(torch.from_numpy(a).cuda(), QWeight(q, [0.01])).cpu().numpy()
+    assert rel_err(out, O.matmul_i8_f32(a, q, np.float32(0.01), 2, 64, 32)) < 1e-5
