@@ -270,6 +270,35 @@ sb_status sb_qweight_destroy(sb_qweight *w) {
     return SB_OK;
 }
 
+// Rows [0, M) of a through the tensor-core GEMM (5-64 rows per launch).
+static sb_status qgemm_rows(const sb_qweight *w, const void *a, bool bf16, int M, const float *bias, float *c,
+                            cudaStream_t stream) {
+    // scratch = planes, column sums, row exponents
+    QGemmWs ws;
+    ws.ld_acc = w->d.ntiles * 128;
+    const size_t pb = align_up(qgemm_planes_bytes(w->d.K, M), 256);
+    void *base = nullptr, *sums = nullptr;
+    // planes, then rstd[QGM_MAX_M] doubles, then shift[QGM_MAX_M] ints
+    const size_t rb = sizeof(double) * QGM_MAX_M, sb = sizeof(int) * QGM_MAX_M;
+    SB_TRY(workspace_get(WS_GEMM, pb + rb + sb, &base, stream));
+    SB_TRY(workspace_get(WS_GEMM_SUMS, sizeof(long long) * (size_t)M * ws.ld_acc, &sums, stream));
+    char *b = static_cast<char *>(base);
+    ws.planes = reinterpret_cast<uint8_t *>(b);
+    ws.acc = reinterpret_cast<long long *>(sums);
+    ws.rstd = reinterpret_cast<double *>(b + pb);
+    ws.shift = reinterpret_cast<int *>(b + pb + rb);
+    QGemvArgs g;
+    g.w = w->d;
+    g.M = M;
+    g.x = a;
+    g.ldx = w->d.K;
+    g.x_bf16 = bf16;
+    g.out = c;
+    g.ldo = w->d.N;
+    g.bias = bias;
+    return qgemm_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, stream, false);
+}
+
 static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, int M, const float *bias, float *c,
                              void *stream) {
     SB_CHECK(w && a && c, SB_ERR_ARG, "sb_matmul_i8_f32: null argument");
@@ -277,31 +306,20 @@ static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, in
     SB_CHECK(a_dtype == SB_DTYPE_F32 || a_dtype == SB_DTYPE_BF16, SB_ERR_ARG, "bad activation dtype %d", a_dtype);
     SB_CHECK(M >= 0, SB_ERR_ARG, "M < 0");
     const size_t esz = a_dtype == SB_DTYPE_BF16 ? 2 : 4;
-    if (qgemm_supported(w->d, M)) {
-        // 5-64 rows on the tensor cores: scratch = planes, column sums, row exponents
-        QGemmWs ws;
-        ws.ld_acc = w->d.ntiles * 128;
-        const size_t pb = align_up(qgemm_planes_bytes(w->d.K, M), 256);
-        void *base = nullptr, *sums = nullptr;
-        // planes, then rstd[QGM_MAX_M] doubles, then shift[QGM_MAX_M] ints
-        const size_t rb = sizeof(double) * QGM_MAX_M, sb = sizeof(int) * QGM_MAX_M;
-        SB_TRY(workspace_get(WS_GEMM, pb + rb + sb, &base, (cudaStream_t)stream));
-        SB_TRY(workspace_get(WS_GEMM_SUMS, sizeof(long long) * (size_t)M * ws.ld_acc, &sums, (cudaStream_t)stream));
-        char *b = static_cast<char *>(base);
-        ws.planes = reinterpret_cast<uint8_t *>(b);
-        ws.acc = reinterpret_cast<long long *>(sums);
-        ws.rstd = reinterpret_cast<double *>(b + pb);
-        ws.shift = reinterpret_cast<int *>(b + pb + rb);
-        QGemvArgs g;
-        g.w = w->d;
-        g.M = M;
-        g.x = a;
-        g.ldx = w->d.K;
-        g.x_bf16 = a_dtype == SB_DTYPE_BF16;
-        g.out = c;
-        g.ldo = w->d.N;
-        g.bias = bias;
-        return qgemm_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, (cudaStream_t)stream, false);
+    const bool bf16 = a_dtype == SB_DTYPE_BF16;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (qgemm_supported(w->d, M)) return qgemm_rows(w, a, bf16, M, bias, c, st);
+    if (M > QGM_MAX_M && qgemm_supported(w->d, QGM_MAX_M)) {
+        // More than 64 rows: balanced chunks of 33-64 rows, one GEMM each, in
+        // stream order (each chunk's finish kernel clears the shared sums).
+        // Rows are independent, so the result equals the row-wise GEMVs.
+        const int nc = (M + QGM_MAX_M - 1) / QGM_MAX_M;
+        for (int i = 0; i < nc; i++) {
+            const int r0 = (int)((long long)M * i / nc), r1 = (int)((long long)M * (i + 1) / nc);
+            SB_TRY(qgemm_rows(w, static_cast<const char *>(a) + (size_t)r0 * w->d.K * esz, bf16, r1 - r0, bias,
+                              c + (size_t)r0 * w->d.N, st));
+        }
+        return SB_OK;
     }
     for (int r0 = 0; r0 < M; r0 += QG_MAX_M) {
         QGemvArgs g;
@@ -309,11 +327,11 @@ static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, in
         g.M = std::min(QG_MAX_M, M - r0);
         g.x = (const char *)a + (size_t)r0 * w->d.K * esz;
         g.ldx = w->d.K;
-        g.x_bf16 = a_dtype == SB_DTYPE_BF16;
+        g.x_bf16 = bf16;
         g.out = c + (size_t)r0 * w->d.N;
         g.ldo = w->d.N;
         g.bias = bias;
-        SB_TRY(qgemv_launch(bias ? QEPI_BIAS : QEPI_STORE, g, (cudaStream_t)stream, false));
+        SB_TRY(qgemv_launch(bias ? QEPI_BIAS : QEPI_STORE, g, st, false));
     }
     return SB_OK;
 }

@@ -119,7 +119,7 @@ class QWeight:
 
     def __init__(self, q: np.ndarray, scales, group: int = 0, tile_n: int = 0):
         """tile_n: on-device column tile width (0 = the GEMV's choice; 128
-        lets 5-64-row products run on the tensor cores)."""
+        lets products of 5 or more rows run on the tensor cores)."""
         q = np.ascontiguousarray(q, np.int8)
         self.K, self.N = q.shape
         self.group = group

@@ -83,10 +83,11 @@ sb_status sb_qweight_destroy(sb_qweight *w);
 /* matmul_i8_f32 (backend/mod.rs:521-533; CPU cpu.rs:1129-1160):
  * c[M,N] = a[M,K] . dequant(q)[K,N], f32 accumulate.  a, c are device
  * pointers; a_dtype is SB_DTYPE_F32 or SB_DTYPE_BF16.  1-4 rows run the
- * GEMV; 5-64 rows of a per-tensor-scaled weight with 128-column tiles run
- * on the tcgen05 tensor cores (same fixed-point arithmetic, same results
- * as row-by-row GEMVs); other shapes run the GEMV 4 rows at a time.  Uses a library-owned
- * workspace on the current device. */
+ * GEMV; 5 or more rows of a per-tensor-scaled weight with 128-column tiles
+ * run on the tcgen05 tensor cores, at most 64 rows per launch (same
+ * fixed-point arithmetic, same results as row-by-row GEMVs); other shapes
+ * run the GEMV 4 rows at a time.  Uses a library-owned workspace on the
+ * current device. */
 sb_status sb_matmul_i8_f32(const sb_qweight *w, const void *a, int a_dtype, int M, float *c,
                            void *stream);
 /* matmul_i8_f32_bias (backend/mod.rs:537-557): c = a . dequant(q) + bias. */

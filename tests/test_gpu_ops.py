@@ -98,9 +98,33 @@ def test_batched_tensor_core_matmul_33_to_64_rows(M, K, N_):
     assert rel_err(out, ref) < TOL_F32
 
 
+@pytest.mark.parametrize("M", [65, 128, 200])
+@pytest.mark.parametrize("K,N_", [(4096, 4096), (4096, 11008), (512, 1536)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_matmul_beyond_64_rows_runs_in_tensor_core_chunks(M, K, N_, bf16):
+    # More than 64 rows: balanced chunks of 33-64 rows, one tensor-core GEMM
+    # each, sharing one workspace in stream order.  Bit-equal to row-wise
+    # GEMVs (rows are independent), within the f32 bar of the oracle.
+    rng = np.random.default_rng(M * 7 + K + N_ + bf16)
+    w = (rng.standard_normal((K, N_)) * 0.02).astype(np.float32)
+    q, s = O.quantize_symmetric(w)
+    q = q.reshape(K, N_)
+    at = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32))
+    if bf16:
+        at = at.to(torch.bfloat16)
+    a = at.float().numpy()
+    at = at.cuda()
+    qw = QWeight(q, [s], tile_n=128)
+    out = matmul_i8_f32(at, qw).cpu().numpy()
+    rows = np.vstack([matmul_i8_f32(at[i:i + 1].contiguous(), qw).cpu().numpy() for i in range(M)])
+    torch.cuda.synchronize()
+    assert np.array_equal(out, rows)
+    assert rel_err(out, O.matmul_i8_f32(a, q, s, M, K, N_)) < TOL_F32
+
+
 @pytest.mark.parametrize("group", [32, 64])
-@pytest.mark.parametrize("M", [1, 4, 8])
-@pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008)])
+@pytest.mark.parametrize("M", [1, 4, 8, 32, 128])
+@pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008), (4096, 32000)])
 def test_matmul_grouped_bf16_sweep_shapes(group, M, K, N_):
     # Quantized-linear sweep inputs: int8 uniform in [-127,127], f32 group
     # scales = absmax/127 of N(0,0.02) groups, bf16 activations ~ N(0,1).
