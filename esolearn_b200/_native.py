@@ -65,6 +65,7 @@ SIGNATURES = {
     "sb_rope_with_freqs": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sb_swiglu": (C.c_int, [vp, vp, C.c_size_t, vp, vp]),
     "sb_argmax_rows": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
+    "sb_sample_rows": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, vp, vp, vp]),
     "sb_attn_decode_paged": (C.c_int, [vp, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
                                        C.c_int, C.c_int, C.c_int, vp, vp]),
     "sb_attn_decode_paged_noalloc": (C.c_int, [vp, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
@@ -82,6 +83,7 @@ SIGNATURES = {
     "sb_llama_load_f32": (C.c_int, [vp, C.c_int, C.c_int, vp]),
     "sb_llama_reset": (C.c_int, [vp]),
     "sb_llama_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
+    "sb_llama_sample": (C.c_int, [vp, C.c_int, C.c_float, C.c_int, C.c_float, vp, vp]),
     "sb_llama_generate_greedy": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, vp]),
     "sb_llama_set_trace": (C.c_int, [vp, C.c_int]),
     "sb_llama_get_trace": (C.c_int, [vp, vp]),

@@ -11,6 +11,7 @@
 #include "misc.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
+#include "sampler.cuh"
 
 namespace sb {
 
@@ -68,7 +69,7 @@ struct Workspace {
 // WS_GEMM_SUMS only ever holds the tensor-core GEMM's int64 column sums,
 // which must read zero before every call: a grown buffer is zero-filled and
 // every call clears what it used.
-enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_KINDS = 4 };
+enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_SAMPLE = 4, WS_KINDS = 5 };
 constexpr size_t WS_ATTN_COUNTER_BYTES = 64 * 1024;
 
 static int workspace_get(int kind, size_t bytes, void **out, cudaStream_t st) {
@@ -366,6 +367,20 @@ sb_status sb_swiglu(const float *gate, const float *up, size_t n, float *out, vo
 sb_status sb_argmax_rows(const float *x, int rows, int n, int32_t *out, void *stream) {
     SB_CHECK(x && out && rows >= 0 && n > 0, SB_ERR_ARG, "sb_argmax_rows: bad argument");
     return argmax_rows_launch(x, rows, n, out, (cudaStream_t)stream);
+}
+
+sb_status sb_sample_rows(const float *logits, int rows, int n, int ld, float temperature, int top_k, float top_p,
+                         uint64_t *rng_state, int32_t *out, void *stream) {
+    SB_CHECK(logits && rng_state && out, SB_ERR_ARG, "sb_sample_rows: null argument");
+    SB_CHECK(rows >= 0 && n >= 1 && ld >= n, SB_ERR_SHAPE, "sb_sample_rows: rows %d, n %d, ld %d", rows, n, ld);
+    SB_CHECK(!std::isnan(temperature) && !std::isnan(top_p) && top_k >= 0, SB_ERR_ARG,
+             "sb_sample_rows: temperature %g, top_k %d, top_p %g", (double)temperature, top_k, (double)top_p);
+    if (rows == 0) return SB_OK;
+    void *prob = nullptr;
+    if (!(temperature < 1e-8f))
+        SB_TRY(workspace_get(WS_SAMPLE, sizeof(double) * (size_t)rows * n, &prob, (cudaStream_t)stream));
+    return sample_rows_launch(logits, rows, n, ld, temperature, top_k, top_p, rng_state, static_cast<double *>(prob),
+                              out, (cudaStream_t)stream);
 }
 
 sb_status sb_attn_decode_paged(const float *q, const void *k_cache, const void *v_cache, int kv_dtype,

@@ -30,6 +30,7 @@
 #include "misc.cuh"
 #include "qgemm.cuh"
 #include "qgemv.cuh"
+#include "sampler.cuh"
 #include "tp_comm.cuh"
 
 namespace sb {
@@ -94,6 +95,9 @@ struct sb_llama {
     SeqState seq;
     int *d_tok = nullptr, *d_pos = nullptr, *d_prompt = nullptr, *d_plen = nullptr, *d_out = nullptr,
         *d_ngen = nullptr, *d_last = nullptr;
+    double *samp_prob = nullptr;  // device sampler: [B][V] probabilities, rng states, tokens
+    uint64_t *d_rng = nullptr;
+    int *d_samp = nullptr;
     int active = 0;  // batch of the current begin()
     int steps = 0;   // steps queued since begin()
 
@@ -1047,6 +1051,38 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
                 std::memcpy(logits + (size_t)b * m->V + (size_t)t * m->Vl,
                             lg_all.data() + ((size_t)t * batch + b) * m->Vl, sizeof(float) * m->Vl);
     return check_device_errors(m);
+}
+
+sb_status sb_llama_sample(sb_llama *m, int batch, float temperature, int top_k, float top_p, uint64_t *rng_state,
+                          int32_t *tokens) {
+    SB_CHECK(m && rng_state && tokens, SB_ERR_ARG, "sb_llama_sample: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    SB_CHECK(m->tp == 1, SB_ERR_UNSUPPORTED,
+             "sb_llama_sample: a tensor-parallel rank holds a vocabulary slice; gather the logits with "
+             "sb_llama_forward and sample on the host");
+    SB_CHECK(!std::isnan(temperature) && !std::isnan(top_p) && top_k >= 0, SB_ERR_ARG,
+             "sb_llama_sample: temperature %g, top_k %d, top_p %g", (double)temperature, top_k, (double)top_p);
+    if (!m->samp_prob) {
+        void *a = nullptr, *b = nullptr, *c = nullptr;
+        cudaError_t e = cudaMalloc(&a, sizeof(double) * (size_t)m->B * m->V);
+        if (e == cudaSuccess) m->allocs.push_back(a), e = cudaMalloc(&b, sizeof(uint64_t) * m->B);
+        if (e == cudaSuccess) m->allocs.push_back(b), e = cudaMalloc(&c, sizeof(int) * m->B);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(SB_ERR_OOM, "sb_llama_sample: %s", cudaGetErrorString(e));
+        }
+        m->allocs.push_back(c);
+        m->samp_prob = static_cast<double *>(a);
+        m->d_rng = static_cast<uint64_t *>(b);
+        m->d_samp = static_cast<int *>(c);
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_rng, rng_state, sizeof(uint64_t) * batch, cudaMemcpyHostToDevice, m->st));
+    SB_TRY(sample_rows_launch(m->logits, batch, m->V, m->Vl, temperature, top_k, top_p, m->d_rng, m->samp_prob,
+                              m->d_samp, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(tokens, m->d_samp, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(rng_state, m->d_rng, sizeof(uint64_t) * batch, cudaMemcpyDeviceToHost, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
 }
 
 sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_prompt) {

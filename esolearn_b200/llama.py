@@ -297,6 +297,18 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_forward(self._h, B, _ptr(t), _ptr(p), _ptr(lg) if want_logits else None, _ptr(am)))
         return lg, am
 
+    def sample(self, config: "SamplingConfig", rngs: Sequence["Rng"]) -> list:
+        """sample_token (generate.rs:92-165) on the device for each row of the
+        logits the last forward left there (sb_llama_sample); rngs[b]
+        advances exactly as Rng.f64() would on the host."""
+        st = np.array([r.state for r in rngs], np.uint64)
+        out = np.empty(len(rngs), np.int32)
+        N.check(N.lib().sb_llama_sample(self._h, len(rngs), float(config.temperature), int(config.top_k),
+                                        float(config.top_p), _ptr(st), _ptr(out)))
+        for r, v in zip(rngs, st):
+            r.state = int(v)
+        return out.tolist()
+
     def set_trace(self, on: bool):
         N.check(N.lib().sb_llama_set_trace(self._h, int(on)))
 
@@ -431,8 +443,12 @@ def sample_token(logits: np.ndarray, config: SamplingConfig, rng: Rng) -> int:
     return n - 1
 
 
-def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: SamplingConfig, rng: Rng) -> list:
-    """generate.rs:51-89.  Greedy runs entirely on the device."""
+def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: SamplingConfig, rng: Rng,
+             device_sampling: bool = True) -> list:
+    """generate.rs:51-89.  Greedy runs entirely on the device.  Sampled
+    generation samples on the device (only the token crosses to the host)
+    unless device_sampling is False or the model is tensor-parallel, in which
+    case the logits come back and sample_token runs on the host."""
     if len(prompt_tokens) == 0:
         raise ValueError("generate: prompt_tokens must not be empty")
     if config.temperature < 1e-8:
@@ -440,12 +456,40 @@ def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: Sampli
     max_seq = len(prompt_tokens) + config.max_tokens
     cache = model.new_kv_cache(max_seq)
     V = model.vocab_size()
+    on_device = device_sampling and model.tp_size == 1
+
+    def step(tok: int, pos: int, sample: bool):
+        if not on_device:
+            logits = model.forward_with_cache(tok, pos, cache)
+            return sample_token(logits[:V], config, rng) if sample else None
+        model.forward_batch([tok], [pos], slots=[cache.slot], want_logits=False)
+        cache.seq_len = pos + 1
+        return model.sample(config, [rng])[0] if sample else None
+
     out = []
     for pos, tok in enumerate(prompt_tokens):
-        logits = model.forward_with_cache(int(tok), pos, cache)
-        if pos == len(prompt_tokens) - 1:
-            out.append(sample_token(logits[:V], config, rng))
+        t = step(int(tok), pos, pos == len(prompt_tokens) - 1)
+        if t is not None:
+            out.append(t)
     for i in range(1, config.max_tokens):
-        logits = model.forward_with_cache(out[-1], len(prompt_tokens) + i - 1, cache)
-        out.append(sample_token(logits[:V], config, rng))
+        out.append(step(out[-1], len(prompt_tokens) + i - 1, True))
+    return out
+
+
+def sample_rows(logits, config: SamplingConfig, rng_states, out=None, stream: int = 0):
+    """sample_token (generate.rs:92-165) on the device for every row of a
+    torch CUDA [rows, n] f32 tensor (sb_sample_rows).  rng_states: torch
+    CUDA int64 [rows] holding the fastrand states (advanced in place, one
+    draw per sampled row).  Returns int32 [rows] token ids on the device."""
+    import torch
+
+    assert logits.is_cuda and logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1
+    rows, n = logits.shape
+    assert rng_states.is_cuda and rng_states.dtype == torch.int64 and rng_states.numel() == rows
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    st = C.c_void_p(stream or torch.cuda.current_stream(logits.device).cuda_stream)
+    N.check(N.lib().sb_sample_rows(C.c_void_p(logits.data_ptr()), rows, n, logits.stride(0),
+                                   float(config.temperature), int(config.top_k), float(config.top_p),
+                                   C.c_void_p(rng_states.data_ptr()), C.c_void_p(out.data_ptr()), st))
     return out

@@ -106,6 +106,18 @@ sb_status sb_rope_with_freqs(const float *x, int seq, int n_heads, int head_dim,
 sb_status sb_swiglu(const float *gate, const float *up, size_t n, float *out, void *stream);
 /* argmax over each row, ties -> last index (generate.rs:167-173). */
 sb_status sb_argmax_rows(const float *x, int rows, int n, int32_t *out, void *stream);
+/* sample_token (generate.rs:92-165) on the device, one token per row of
+ * logits [rows][ld] (the first n columns): temperature < 1e-8 is the argmax
+ * (no draw); otherwise f64 temperature scaling, top-k, softmax, top-p and
+ * weighted_sample in the reference's order.  rng_state: device [rows]
+ * fastrand (wyrand) states, advanced by one draw per sampled row, so the
+ * draws equal the reference's Rng::f64 stream.  Ties at the top-p cut are
+ * kept lowest index first; sums run in a fixed tree order, so a token can
+ * differ from the reference's only when the draw or top_p lies within f64
+ * rounding of a running sum.  out: device [rows].  Uses a library-owned
+ * workspace of rows * n doubles. */
+sb_status sb_sample_rows(const float *logits, int rows, int n, int ld, float temperature, int top_k,
+                         float top_p, uint64_t *rng_state, int32_t *out, void *stream);
 
 /* ---- paged GQA decode attention ----------------------------------------
  * Replaces llama.rs:414-456 (gather_reshape_repeat_kv + strided-batched
@@ -216,6 +228,13 @@ sb_status sb_llama_reset(sb_llama *m);
  * logits [batch, V] f32, argmax [batch] (ties -> last). */
 sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const int32_t *pos,
                            float *logits, int32_t *argmax);
+/* sample_token (generate.rs:92-165) for each of the `batch` rows of logits
+ * the last sb_llama_forward left on the device (see sb_sample_rows): only
+ * the tokens come back to the host, not [batch, V] logits.  rng_state: host
+ * [batch] fastrand states, advanced in place.  Single-GPU models only
+ * (SB_ERR_UNSUPPORTED under tensor parallelism). */
+sb_status sb_llama_sample(sb_llama *m, int batch, float temperature, int top_k, float top_p,
+                          uint64_t *rng_state, int32_t *tokens);
 /* generate (generate.rs:51-89) with temperature 0, for `batch` prompts of
  * equal length: prompts [batch, n_prompt], out [batch, max_tokens]. */
 sb_status sb_llama_generate_greedy(sb_llama *m, int batch, const int32_t *prompts, int n_prompt,
