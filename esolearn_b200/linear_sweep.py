@@ -9,8 +9,9 @@ source groups (group 0 = one per-tensor scale, the engine's format, packed in
 (11008, 4096), (4096, 32000)}; f32 output.
 
 Each cell: 3 warm-up calls, then `iters` calls, each preceded by a 256 MB
-write that evicts L2 (126 MB), timed with CUDA events on the launching stream
-(the median is reported).  Algorithmic bytes per call = K*N (int8) + 4*K*N/g
+write that evicts L2 (126 MB) and a ~0.5 ms device spin during which the host
+enqueues the call, timed with CUDA events on the launching stream (the median
+is reported).  Algorithmic bytes per call = K*N (int8) + 4*K*N/g
 (group scales) + 2*M*K (bf16 in) + 4*M*N (f32 out); FLOPs = 2*M*K*N.  GB/s is
 reported against the measured HBM copy bandwidth when a peaks file is given.
 
@@ -61,9 +62,12 @@ def time_cell(qw: QWeight, M: int, iters: int, flush) -> float:
     for _ in range(3):
         matmul_i8_f32(a, qw, out=out, stream=st.cuda_stream)
     times = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for _ in range(iters):
         flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # Keep the GPU busy (~0.5 ms) while the host enqueues the timed call,
+        # so the start event does not also time the host's launch path.
+        torch.cuda._sleep(1_000_000)
         e0.record(st)
         matmul_i8_f32(a, qw, out=out, stream=st.cuda_stream)
         e1.record(st)

@@ -180,27 +180,28 @@ def _tp_engine_run(rank, size, tid, mode):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("size", [2, 4])
 @pytest.mark.parametrize("mode", ["oracle", "random"])
-def test_tensor_parallel_engine_matches_oracle(mode):
-    # Two ranks (NCCL over NVLink): greedy streams for 1 and 3 sequences equal
-    # the unsharded oracle's for 32 tokens, logits within the f32 bar, on
-    # every rank.
+def test_tensor_parallel_engine_matches_oracle(mode, size):
+    # 2 or 4 ranks (NCCL over NVLink, peer-memory all-reduce): greedy streams
+    # for 1 and 3 sequences equal the unsharded oracle's for 32 tokens,
+    # logits within the f32 bar, on every rank.
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < size:
+        pytest.skip(f"needs {size} GPUs")
     from esolearn_b200 import tp_unique_id
 
     tid = tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_engine_worker, args=(r, 2, tid, mode, q), daemon=True) for r in range(2)]
+    procs = [ctx.Process(target=_tp_engine_worker, args=(r, size, tid, mode, q), daemon=True) for r in range(size)]
     for p in procs:
         p.start()
     res = {}
     try:
-        for _ in range(2):
+        for _ in range(size):
             r, t1, t3, lg = q.get(timeout=300)
             assert not (isinstance(t1, str) and t1 == "error"), f"rank {r}:\n{t3}"
             res[r] = (t1, t3, lg)
@@ -217,14 +218,15 @@ def test_tensor_parallel_engine_matches_oracle(mode):
     ref1 = om.generate_greedy(prompt, 32, kv_bf16=True)
     oc = om.new_cache(64, kv_bf16=True)
     ref_lg = np.stack([om.forward_with_cache(oc, int(t), pos) for pos, t in enumerate(prompt)])
-    for r in (0, 1):
+    for r in range(size):
         t1, t3, lg = res[r]
         assert t1.tolist() == ref1.tolist(), r
         for b in range(3):
             assert t3[b].tolist() == om.generate_greedy(O.prompt_ids(20 + b, 8, c.vocab_size), 32,
                                                         kv_bf16=True).tolist(), (r, b)
         assert rel_err(lg, ref_lg) < 1e-3
-    assert np.array_equal(res[0][2], res[1][2])  # identical logits on both ranks
+    for r in range(1, size):
+        assert np.array_equal(res[0][2], res[r][2])  # identical logits on every rank
 
 
 @pytest.mark.gpu
