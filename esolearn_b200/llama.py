@@ -236,12 +236,14 @@ class QuantLlamaB200:
 
     # -- weights --------------------------------------------------------
     @classmethod
-    def from_safetensors(cls, config: LlamaConfig, paths, **kw) -> "QuantLlamaB200":
-        """LlamaModel::from_safetensors (llama.rs:768-958) + quantize_symmetric per projection."""
+    def from_safetensors(cls, config: LlamaConfig, paths, cache: Optional[str] = None, **kw) -> "QuantLlamaB200":
+        """LlamaModel::from_safetensors (llama.rs:768-958) + quantize_symmetric per projection.
+        cache: a packed-int8 cache file, read when it exists, else written
+        from the shards during this load."""
         from .safetensors_io import load_into
 
         m = cls(config, **kw)
-        load_into(m, config, paths)
+        load_into(m, config, paths, cache=cache)
         return m
 
     @classmethod

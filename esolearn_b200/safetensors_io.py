@@ -10,6 +10,11 @@ lm_head stays [V, h] (llama.rs:943-948).  Each projection is then quantized
 per tensor with quantize_symmetric (quantize.rs:16-32, bit-exact through the
 C ABI) -- the int8 wiring the engine runs.  Shards are memory-mapped, so a
 tensor is read when it is converted.
+
+Packed-int8 cache: the quantized tensors (int8 [K,N] projections with their
+per-tensor scales, f32 embedding and norms) can be written once to a single
+safetensors file and loaded from it later without re-quantizing.  Its
+metadata records the model configuration, checked on load.
 """
 from __future__ import annotations
 
@@ -22,7 +27,8 @@ import numpy as np
 from . import _native as N
 from .llama import LlamaConfig, quantize_symmetric
 
-_DTYPES = {"F32": np.float32, "BF16": np.uint16, "F16": np.float16}
+_DTYPES = {"F32": np.float32, "BF16": np.uint16, "F16": np.float16, "I8": np.int8}
+CACHE_FORMAT = "scry-b200-int8/1"
 
 
 class SafeTensorsShards:
@@ -30,6 +36,7 @@ class SafeTensorsShards:
 
     def __init__(self, paths: Sequence[str]):
         self._where: Dict[str, Tuple[np.memmap, str, Tuple[int, ...], int, int]] = {}
+        self._meta: Dict[str, str] = {}
         for path in paths:
             with open(path, "rb") as f:
                 n = int.from_bytes(f.read(8), "little")
@@ -37,6 +44,7 @@ class SafeTensorsShards:
             data = np.memmap(path, dtype=np.uint8, mode="r", offset=8 + n)
             for name, info in header.items():
                 if name == "__metadata__":
+                    self._meta.update(info)
                     continue
                 b, e = info["data_offsets"]
                 self._where[name] = (data, info["dtype"], tuple(info["shape"]), b, e)
@@ -44,14 +52,22 @@ class SafeTensorsShards:
     def names(self):
         return list(self._where)
 
-    def f32(self, name: str) -> np.ndarray:
-        """The tensor as f32 (exact for F32, BF16 and F16 sources)."""
+    def metadata(self) -> dict:
+        return dict(self._meta)
+
+    def raw(self, name: str) -> np.ndarray:
+        """The tensor in its stored dtype (BF16 as uint16 bits)."""
         if name not in self._where:
             raise N.SbError(6, f"tensor '{name}' not found in any shard")
         data, dt, shape, b, e = self._where[name]
         if dt not in _DTYPES:
             raise N.SbError(6, f"unsupported dtype {dt} for tensor '{name}'")
-        raw = np.frombuffer(data[b:e], dtype=_DTYPES[dt]).reshape(shape)
+        return np.frombuffer(data[b:e], dtype=_DTYPES[dt]).reshape(shape)
+
+    def f32(self, name: str) -> np.ndarray:
+        """The tensor as f32 (exact for F32, BF16 and F16 sources)."""
+        raw = self.raw(name)
+        dt = self._where[name][1]
         if dt == "BF16":
             return (raw.astype(np.uint32) << 16).view(np.float32)
         return raw.astype(np.float32)
@@ -117,10 +133,116 @@ def quantized_llama_tensors(config: LlamaConfig, paths: Sequence[str]) -> Iterat
     yield ("q", -1, 0) + quantize_symmetric(head)
 
 
-def load_into(model, config: LlamaConfig, paths: Sequence[str]):
+# ---------------------------------------------------------------------------
+# packed-int8 cache
+
+_SLOT_NAMES = {N.SB_W_QKV: "qkv", N.SB_W_O: "o", N.SB_W_GATE: "gate", N.SB_W_UP: "up", N.SB_W_DOWN: "down"}
+_F_NAMES = {N.SB_F_EMBED: "embed", N.SB_F_NORM_IN: "norm_in", N.SB_F_NORM_POST: "norm_post",
+            N.SB_F_NORM_FINAL: "norm_final"}
+
+
+def _config_meta(config: LlamaConfig) -> str:
+    # every field that shapes or identifies the weights (the KV capacity does not)
+    fields = {k: (v.__dict__ if hasattr(v, "__dict__") else v) for k, v in vars(config).items() if k != "max_seq_len"}
+    return json.dumps(fields, sort_keys=True)
+
+
+def _cache_layout(config: LlamaConfig):
+    """(name, dtype, shape) of every cache entry, in the order
+    quantized_llama_tensors yields them (each projection's int8 tensor is
+    followed by its scale)."""
+    h, F, V = config.hidden_size, config.intermediate_size, config.vocab_size
+    hd = config.head_dim()
+    qd, kd = config.n_heads * hd, config.n_kv_heads * hd
+    shapes = {N.SB_W_QKV: (h, qd + 2 * kd), N.SB_W_O: (qd, h), N.SB_W_GATE: (h, F), N.SB_W_UP: (h, F),
+              N.SB_W_DOWN: (F, h)}
+    out = [("embed", "F32", (V, h))]
+    for i in range(config.n_layers):
+        for slot in (N.SB_W_QKV, N.SB_W_O, N.SB_W_GATE, N.SB_W_UP, N.SB_W_DOWN):
+            out.append((f"layers.{i}.{_SLOT_NAMES[slot]}.q", "I8", shapes[slot]))
+            out.append((f"layers.{i}.{_SLOT_NAMES[slot]}.scale", "F32", (1,)))
+        out.append((f"layers.{i}.norm_in", "F32", (h,)))
+        out.append((f"layers.{i}.norm_post", "F32", (h,)))
+    out.append(("norm_final", "F32", (h,)))
+    out.append(("lm_head.q", "I8", (V, h)))
+    out.append(("lm_head.scale", "F32", (1,)))
+    return out
+
+
+def _entry_arrays(t) -> list:
+    """The cache entries (arrays) of one yielded tensor tuple."""
+    if t[0] == "q":
+        return [np.ascontiguousarray(t[3], np.int8), np.array([t[4]], np.float32)]
+    return [np.ascontiguousarray(t[3], np.float32)]
+
+
+def write_quantized_cache(config: LlamaConfig, tensors: Iterator[tuple], path: str) -> Iterator[tuple]:
+    """Stream `tensors` (quantized_llama_tensors' tuples) into a packed-int8
+    cache at `path` while passing each tuple on, so a model can load and
+    write the cache in one pass.  Shapes come from the configuration, so the
+    header is written first and no tensor is held longer than its write."""
+    layout = _cache_layout(config)
+    header, off = {}, 0
+    for name, dt, shape in layout:
+        nbytes = int(np.prod(shape)) * (1 if dt == "I8" else 4)
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + nbytes]}
+        off += nbytes
+    header["__metadata__"] = {"format": CACHE_FORMAT, "config": _config_meta(config)}
+    hb = json.dumps(header).encode()
+    hb += b" " * (-len(hb) % 8)
+    tmp = path + ".partial"
+    k = 0
+    try:
+        with open(tmp, "wb") as f:
+            f.write(len(hb).to_bytes(8, "little"))
+            f.write(hb)
+            for t in tensors:
+                for arr in _entry_arrays(t):
+                    name, dt, shape = layout[k]
+                    if arr.shape != tuple(shape) or (arr.dtype == np.int8) != (dt == "I8"):
+                        raise N.SbError(4, f"cache entry '{name}': got {arr.dtype} {arr.shape}, expected {dt} {shape}")
+                    f.write(arr.tobytes())
+                    k += 1
+                yield t
+        if k != len(layout):
+            raise N.SbError(4, f"cache: {k} of {len(layout)} entries written")
+        os.replace(tmp, path)  # only a complete cache ever carries the final name
+    finally:
+        if os.path.exists(tmp):
+            os.remove(tmp)
+
+
+def cached_llama_tensors(config: LlamaConfig, path: str) -> Iterator[tuple]:
+    """quantized_llama_tensors' tuples read back from a packed-int8 cache."""
+    st = SafeTensorsShards([path])
+    meta = st.metadata()
+    if meta.get("format") != CACHE_FORMAT:
+        raise N.SbError(6, f"{path}: not a {CACHE_FORMAT} cache")
+    if meta.get("config") != _config_meta(config):
+        raise N.SbError(4, f"{path}: cache was written for another model configuration")
+    yield ("f", N.SB_F_EMBED, 0, st.raw("embed"))
+    for i in range(config.n_layers):
+        for slot in (N.SB_W_QKV, N.SB_W_O, N.SB_W_GATE, N.SB_W_UP, N.SB_W_DOWN):
+            nm = f"layers.{i}.{_SLOT_NAMES[slot]}"
+            yield ("q", i, slot, st.raw(nm + ".q"), np.float32(st.raw(nm + ".scale")[0]))
+        yield ("f", N.SB_F_NORM_IN, i, st.raw(f"layers.{i}.norm_in"))
+        yield ("f", N.SB_F_NORM_POST, i, st.raw(f"layers.{i}.norm_post"))
+    yield ("f", N.SB_F_NORM_FINAL, 0, st.raw("norm_final"))
+    yield ("q", -1, 0, st.raw("lm_head.q"), np.float32(st.raw("lm_head.scale")[0]))
+
+
+def load_into(model, config: LlamaConfig, paths: Sequence[str], cache: str = None):
     """Load HF shards into a QuantLlamaB200 (every rank of a tensor-parallel
-    model loads the same full tensors and keeps its slice)."""
-    for t in quantized_llama_tensors(config, paths):
+    model loads the same full tensors and keeps its slice).  With `cache`:
+    read the packed-int8 cache when it exists, else quantize the shards and
+    write it on the way."""
+    if cache and os.path.exists(cache):
+        tensors = cached_llama_tensors(config, cache)
+    elif cache:
+        tensors = write_quantized_cache(config, quantized_llama_tensors(config, paths), cache)
+    else:
+        tensors = quantized_llama_tensors(config, paths)
+    for t in tensors:
         if t[0] == "q":
             model.load_qweight(t[1], t[2], t[3], t[4])
         else:

@@ -8,7 +8,8 @@ import pytest
 import oracle as O
 from esolearn_b200 import LlamaConfig
 from esolearn_b200 import _native as N
-from esolearn_b200.safetensors_io import SafeTensorsShards, quantized_llama_tensors, write_safetensors
+from esolearn_b200.safetensors_io import (SafeTensorsShards, cached_llama_tensors, quantized_llama_tensors,
+                                         write_quantized_cache, write_safetensors)
 
 
 def _cfg(tie=False):
@@ -93,6 +94,63 @@ def test_dtype_conversion_is_exact(tmp_path):
     assert np.array_equal(st.f32("y"), _bf16(a))
     with pytest.raises(N.SbError):
         st.f32("missing")
+
+
+@pytest.mark.parametrize("tie", [False, True])
+def test_packed_int8_cache_round_trip(tmp_path, tie):
+    # Written while the shards are quantized (every tuple passed on
+    # unchanged), read back as the same tuples: int8 tensors, scales and f32
+    # tensors bit for bit, in the same order.
+    c = _cfg(tie)
+    paths, _ = _write_shards(tmp_path, _hf_weights(c, 5))
+    cache = str(tmp_path / "model.int8.safetensors")
+    passed = list(write_quantized_cache(c, quantized_llama_tensors(c, paths), cache))
+    direct = list(quantized_llama_tensors(c, paths))
+    back = list(cached_llama_tensors(c, cache))
+    assert len(passed) == len(direct) == len(back)
+    for a, b, r in zip(direct, passed, back):
+        assert a[:3] == b[:3] == r[:3]
+        assert np.array_equal(a[3], b[3]) and np.array_equal(a[3], r[3])
+        assert r[3].dtype == (np.int8 if a[0] == "q" else np.float32)
+        if a[0] == "q":
+            assert np.float32(a[4]) == np.float32(r[4])
+
+
+def test_packed_int8_cache_rejects_other_configs_and_partial_writes(tmp_path):
+    c = _cfg()
+    paths, _ = _write_shards(tmp_path, _hf_weights(c, 6))
+    cache = str(tmp_path / "model.int8.safetensors")
+    list(write_quantized_cache(c, quantized_llama_tensors(c, paths), cache))
+    other = LlamaConfig(96, 64, 80, 2, 4, 2, 64, 1e-5, 500000.0, False, None)
+    with pytest.raises(N.SbError) as ei:
+        list(cached_llama_tensors(other, cache))
+    assert ei.value.code == 4
+    # a load that stops half way leaves no file under the cache's name
+    half = str(tmp_path / "half.int8.safetensors")
+    gen = write_quantized_cache(c, quantized_llama_tensors(c, paths), half)
+    for _ in range(3):
+        next(gen)
+    gen.close()
+    import os
+
+    assert not os.path.exists(half) and not os.path.exists(half + ".partial")
+
+
+@pytest.mark.gpu
+def test_engine_from_packed_cache_equals_engine_from_shards(tmp_path):
+    from esolearn_b200 import QuantLlamaB200
+
+    N.check(N.lib().sb_init(0))
+    c = LlamaConfig(512, 512, 1376, 2, 8, 2, 64, 1e-5, 10000.0, False, None)
+    paths, _ = _write_shards(tmp_path, _hf_weights(c, 12))
+    cache = str(tmp_path / "model.int8.safetensors")
+    a = QuantLlamaB200.from_safetensors(c, paths, max_seq=64)
+    b = QuantLlamaB200.from_safetensors(c, paths, cache=cache, max_seq=64)  # writes the cache
+    d = QuantLlamaB200.from_safetensors(c, [], cache=cache, max_seq=64)     # reads it, no shards
+    prompt = O.prompt_ids(6, 8, c.vocab_size)
+    ref = a.generate_greedy(prompt, 16).tolist()
+    assert b.generate_greedy(prompt, 16).tolist() == ref
+    assert d.generate_greedy(prompt, 16).tolist() == ref
 
 
 @pytest.mark.gpu
