@@ -155,6 +155,38 @@ def matmul_i8_f32(a, w: QWeight, out=None, bias=None, stream: int = 0):
     return out
 
 
+class QuantLinear:
+    """nn::linear::Linear after quantize_weights() (linear.rs:9-13, 56-95), the
+    W8A32 layer every other `quantize` consumer uses (GPT-2's Linear layers;
+    Whisper's MLP fc1/fc2, scry-stt checkpoint/mod.rs:184-193):
+    forward(input[seq, in]) = matmul_i8_f32_bias(input, q, scale, bias) on the
+    device.  The weight is [in, out] as in the reference; the bias defaults to
+    zeros like Linear::new.  tile_n 128 sends 5+ rows to the tensor cores."""
+
+    def __init__(self, weight: np.ndarray, bias: Optional[np.ndarray] = None, tile_n: int = 128):
+        w = np.ascontiguousarray(weight, np.float32)
+        if w.ndim != 2:
+            raise N.SbError(4, f"Linear weight must be [in, out], got shape {w.shape}")
+        self.in_features, self.out_features = w.shape
+        self.weight_q, self.scale = quantize_symmetric(w)  # QuantState (linear.rs:9-13)
+        self._w = QWeight(self.weight_q, [self.scale], tile_n=tile_n)
+        b = np.zeros(self.out_features, np.float32) if bias is None else np.asarray(bias, np.float32)
+        if b.shape != (self.out_features,):
+            raise N.SbError(4, f"Linear bias must be [{self.out_features}], got shape {b.shape}")
+        self._bias_host = np.ascontiguousarray(b)
+        self._bias_dev = None
+
+    def forward(self, x, out=None, stream: int = 0):
+        """x: torch CUDA [seq, in] f32 or bf16 -> [seq, out] f32."""
+        import torch
+
+        if self._bias_dev is None or self._bias_dev.device != x.device:
+            self._bias_dev = torch.from_numpy(self._bias_host).to(x.device)
+        return matmul_i8_f32(x.contiguous(), self._w, out=out, bias=self._bias_dev, stream=stream)
+
+    __call__ = forward
+
+
 # ---------------------------------------------------------------------------
 # tensor parallelism (no reference counterpart)
 

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from esolearn_b200 import QWeight, matmul_i8_f32
+from esolearn_b200 import QuantLinear, QWeight, matmul_i8_f32
 from esolearn_b200 import _native as N
 from tests.gpu_util import rel_err
 
@@ -138,6 +138,25 @@ def test_matmul_grouped_bf16_sweep_shapes(group, M, K, N_):
     qw = QWeight(q, scales, group=group)
     out = matmul_i8_f32(a16.cuda(), qw).cpu().numpy()
     assert rel_err(out, ref) < TOL_GEMV
+
+
+@pytest.mark.parametrize("seq", [1, 3, 77, 200])
+@pytest.mark.parametrize("fin,fout", [(768, 2304), (768, 3072), (3072, 768), (512, 2048), (2048, 512)])
+def test_quant_linear_forward_matches_reference_linear(seq, fin, fout):
+    # nn::linear::Linear after quantize_weights() (linear.rs:56-95), the layer
+    # of the other quantize consumers: GPT-2 (768 -> 2304 / 3072, 3072 -> 768)
+    # and Whisper-base MLP (512 <-> 2048) shapes; 1-3 rows on the GEMV, 77 and
+    # 200 on the tensor cores (200 in four chunks), all with the bias epilogue.
+    rng = np.random.default_rng(seq + fin + fout)
+    w = (rng.standard_normal((fin, fout)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(fout) * 0.1).astype(np.float32)
+    lin = QuantLinear(w, b)
+    q, s = O.quantize_symmetric(w)
+    assert lin.scale == s and np.array_equal(lin.weight_q.ravel(), q)
+    x = rng.standard_normal((seq, fin)).astype(np.float32)
+    out = lin(dev(x)).cpu().numpy()
+    ref = O.matmul_i8_f32(x, q.reshape(fin, fout), s, seq, fin, fout) + b  # cpu.rs:554-570
+    assert rel_err(out, ref) < TOL_F32
 
 
 def test_matmul_bias_and_zero_weights():
