@@ -31,6 +31,50 @@ _DTYPES = {"F32": np.float32, "BF16": np.uint16, "F16": np.float16, "I8": np.int
 CACHE_FORMAT = "scry-b200-int8/1"
 
 
+# bytes per element of the safetensors dtypes (the loader converts F32 / BF16
+# / F16 and reads I8; the others are only size-checked)
+_ITEMSIZE = {"F64": 8, "F32": 4, "F16": 2, "BF16": 2, "I64": 8, "I32": 4, "I16": 2, "I8": 1, "U64": 8,
+             "U32": 4, "U16": 2, "U8": 1, "BOOL": 1, "F8_E4M3": 1, "F8_E5M2": 1}
+
+
+def _read_header(path: str):
+    """(header dict, header length, file size) of one file; a malformed file
+    raises SbError (the reference's loader returns ScryLlmError, error.rs:1-27)."""
+    size = os.path.getsize(path)
+    if size < 8:
+        raise N.SbError(6, f"{path}: {size} bytes, too short for a safetensors header")
+    with open(path, "rb") as f:
+        n = int.from_bytes(f.read(8), "little")
+        if n > size - 8:
+            raise N.SbError(6, f"{path}: header of {n} bytes runs past the end of the file ({size} bytes)")
+        raw = f.read(n)
+    try:
+        header = json.loads(raw)
+    except (UnicodeDecodeError, ValueError) as ex:
+        raise N.SbError(6, f"{path}: header is not valid JSON ({ex})") from None
+    if not isinstance(header, dict):
+        raise N.SbError(6, f"{path}: header is not a map of tensors")
+    return header, n, size
+
+
+def _check_entry(path: str, name: str, info, data_bytes: int):
+    """dtype, shape and byte range of one tensor, checked against the file."""
+    try:
+        dt = info["dtype"]
+        shape = tuple(int(d) for d in info["shape"])
+        b, e = (int(v) for v in info["data_offsets"])
+    except (KeyError, TypeError, ValueError):
+        raise N.SbError(6, f"{path}: tensor '{name}' has a malformed entry") from None
+    if not isinstance(dt, str) or any(d < 0 for d in shape):
+        raise N.SbError(6, f"{path}: tensor '{name}' has a malformed dtype or shape")
+    if not 0 <= b <= e <= data_bytes:
+        raise N.SbError(6, f"{path}: tensor '{name}' spans bytes [{b}, {e}) of a {data_bytes}-byte data section")
+    if dt in _ITEMSIZE and (e - b) != int(np.prod(shape, dtype=np.int64)) * _ITEMSIZE[dt]:
+        raise N.SbError(4, f"{path}: tensor '{name}' holds {e - b} bytes, its {dt} shape {list(shape)} needs "
+                           f"{int(np.prod(shape, dtype=np.int64)) * _ITEMSIZE[dt]}")
+    return dt, shape, b, e
+
+
 class SafeTensorsShards:
     """Read-only view of the tensors of one or more .safetensors files."""
 
@@ -38,16 +82,16 @@ class SafeTensorsShards:
         self._where: Dict[str, Tuple[np.memmap, str, Tuple[int, ...], int, int]] = {}
         self._meta: Dict[str, str] = {}
         for path in paths:
-            with open(path, "rb") as f:
-                n = int.from_bytes(f.read(8), "little")
-                header = json.loads(f.read(n))
-            data = np.memmap(path, dtype=np.uint8, mode="r", offset=8 + n)
+            header, n, size = _read_header(path)
+            data = np.memmap(path, dtype=np.uint8, mode="r", offset=8 + n) if size > 8 + n else np.zeros(0, np.uint8)
             for name, info in header.items():
                 if name == "__metadata__":
+                    if not isinstance(info, dict):
+                        raise N.SbError(6, f"{path}: __metadata__ is not a map")
                     self._meta.update(info)
                     continue
-                b, e = info["data_offsets"]
-                self._where[name] = (data, info["dtype"], tuple(info["shape"]), b, e)
+                dt, shape, b, e = _check_entry(path, name, info, size - 8 - n)
+                self._where[name] = (data, dt, shape, b, e)
 
     def names(self):
         return list(self._where)

@@ -136,6 +136,77 @@ def test_packed_int8_cache_rejects_other_configs_and_partial_writes(tmp_path):
     assert not os.path.exists(half) and not os.path.exists(half + ".partial")
 
 
+def _corrupt(tmp_path, name, mutate):
+    a = np.arange(12, dtype=np.float32).reshape(3, 4)
+    path = str(tmp_path / name)
+    write_safetensors(path, {"w": a})
+    raw = bytearray(open(path, "rb").read())
+    raw = mutate(raw)
+    open(path, "wb").write(bytes(raw))
+    return path
+
+
+def _header(raw):
+    n = int.from_bytes(raw[:8], "little")
+    return n, raw[8:8 + n]
+
+
+def _with_header(raw, text):
+    n, _ = _header(raw)
+    h = text.encode()
+    h += b" " * (-len(h) % 8)
+    return bytearray(len(h).to_bytes(8, "little")) + h + raw[8 + n:]
+
+
+@pytest.mark.parametrize("case", ["short", "header_past_end", "not_json", "not_a_map", "truncated_data",
+                                  "shape_mismatch", "bad_entry"])
+def test_malformed_weight_files_raise_clean_errors(tmp_path, case):
+    # Host-side fault injection for the weight path: every malformed file is
+    # an SbError at open (the reference loader's ScryLlmError), never a crash
+    # or a silently misread tensor.
+    def mutate(raw):
+        n, h = _header(raw)
+        if case == "short":
+            return raw[:5]
+        if case == "header_past_end":
+            return bytearray((n + 10_000).to_bytes(8, "little")) + raw[8:]
+        if case == "not_json":
+            return _with_header(raw, "{not json")
+        if case == "not_a_map":
+            return _with_header(raw, "[1, 2, 3]")
+        if case == "truncated_data":
+            return raw[:-8]
+        if case == "shape_mismatch":
+            return _with_header(raw, h.decode().replace("[3, 4]", "[4, 4]"))
+        if case == "bad_entry":
+            return _with_header(raw, '{"w": {"dtype": "F32", "shape": [3, 4]}}')
+        raise AssertionError(case)
+
+    path = _corrupt(tmp_path, case + ".safetensors", mutate)
+    with pytest.raises(N.SbError):
+        SafeTensorsShards([path])
+
+
+@pytest.mark.gpu
+def test_allocation_failure_is_an_error_and_the_device_stays_usable():
+    # Host-side fault injection for device memory: a KV cache far beyond the
+    # GPU's 180 GB (2^27 positions: 275 GB) makes sb_llama_create fail with
+    # SB_ERR_OOM, releasing what it had allocated; the device then builds and
+    # runs a small model normally.
+    from esolearn_b200 import QuantLlamaB200
+
+    N.check(N.lib().sb_init(0))
+    c = LlamaConfig(512, 512, 1376, 2, 8, 8, 1 << 27, 1e-5, 10000.0, False, None)
+    with pytest.raises(N.SbError) as ei:
+        QuantLlamaB200(c, max_seq=1 << 27)
+    assert ei.value.code == 5  # SB_ERR_OOM
+    small = LlamaConfig(512, 512, 1376, 2, 8, 8, 64, 1e-5, 10000.0, False, None)
+    e = QuantLlamaB200.new_random(small, 1, max_seq=64)
+    om = O.OracleLlama(O.make_config(512, 512, 1376, 2, 8, 8, 64, 1e-5, 10000.0, False), 1)
+    prompt = O.prompt_ids(2, 6, small.vocab_size)
+    assert e.generate_greedy(prompt, 8)[0].tolist() == om.generate_greedy(prompt, 8, kv_bf16=True).tolist()
+
+
 @pytest.mark.gpu
 def test_engine_from_packed_cache_equals_engine_from_shards(tmp_path):
     from esolearn_b200 import QuantLlamaB200
