@@ -192,7 +192,9 @@ sb_status sb_quantize_symmetric_host(const float *w, size_t n, int8_t *q, float 
     for (size_t i = 0; i < n; i++) {
         volatile float prod = w[i] * inv;
         float r = std::round((float)prod);
-        r = std::fmin(std::fmax(r, -127.0f), 127.0f);
+        // f32::clamp keeps NaN and `as i8` maps it to 0 (a NaN weight, or
+        // every weight once one is infinite: inv = 0 and inf * 0 = NaN)
+        r = std::isnan(r) ? 0.0f : std::fmin(std::fmax(r, -127.0f), 127.0f);
         q[i] = (int8_t)r;
     }
     *scale = s;

@@ -193,9 +193,11 @@ int argmax_rows_launch(const float *x, int rows, int n, int *out, cudaStream_t s
 // quantize_symmetric on device (quantize.rs:16-32)
 
 __device__ __forceinline__ int8_t quant_one(float w, float inv) {
-    float r = roundf(__fmul_rn(w, inv));  // f32::round: half away from zero
-    r = fminf(fmaxf(r, -127.0f), 127.0f);
-    return (int8_t)r;
+    const float r = roundf(__fmul_rn(w, inv));  // f32::round: half away from zero
+    // f32::clamp keeps NaN and `as i8` maps it to 0 (a NaN weight, or every
+    // weight once one is infinite: inv = 0 and inf * 0 = NaN)
+    if (r != r) return 0;
+    return (int8_t)fminf(fmaxf(r, -127.0f), 127.0f);
 }
 
 __global__ void absmax_kernel(const float *__restrict__ w, size_t n, unsigned *amax) {

@@ -114,7 +114,8 @@ float orc_quantize_symmetric(const float *w, size_t n, int8_t *q) {
         float r = roundf(w[i] * inv_scale);
         if (r < -127.0f) r = -127.0f;
         if (r > 127.0f) r = 127.0f;
-        q[i] = (int8_t)r;
+        /* f32::clamp leaves NaN as NaN and Rust's `as i8` maps NaN to 0 */
+        q[i] = isnan(r) ? (int8_t)0 : (int8_t)r;
     }
     return scale;
 }
@@ -145,7 +146,7 @@ void orc_quantize_grouped(const float *w, int k, int n, int group, int8_t *q, fl
                 float r = roundf(w[(size_t)p * n + j] * inv);
                 if (r < -127.0f) r = -127.0f;
                 if (r > 127.0f) r = 127.0f;
-                q[(size_t)p * n + j] = (int8_t)r;
+                q[(size_t)p * n + j] = isnan(r) ? (int8_t)0 : (int8_t)r; /* as quantize_symmetric */
             }
         }
     }

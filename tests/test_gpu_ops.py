@@ -258,6 +258,27 @@ def test_device_quantizer_bit_exact():
     assert np.array_equal(q.cpu().numpy(), qo)
 
 
+@pytest.mark.parametrize("vals,q,scale", [
+    ([float("nan"), 1.0, -3.0], [0, 42, -127], np.float32(3.0) / np.float32(127.0)),
+    ([float("inf"), 1.0, -2.0], [0, 0, 0], np.float32("inf")),
+    ([float("nan"), float("nan")], [0, 0], np.float32(0.0)),
+    ([1e-45, -1e-45], [127, -127], np.float32(0.0)),
+])
+def test_device_quantizer_special_values(vals, q, scale):
+    # Rust's float rules where quantize.rs meets non-finite weights: the
+    # absmax fold skips NaN, f32::clamp keeps NaN and `as i8` makes it 0.
+    w = np.array(vals, np.float32)
+    qo, so = O.quantize_symmetric(w)
+    assert np.ravel(qo).tolist() == q
+    wd = dev(w)
+    qd = torch.empty(w.size, dtype=torch.int8, device="cuda")
+    sd = torch.empty(1, dtype=torch.float32, device="cuda")
+    N.check(N.lib().sb_quantize_symmetric(vp(wd), w.size, vp(qd), vp(sd), None))
+    torch.cuda.synchronize()
+    assert qd.cpu().numpy().tolist() == q
+    assert sd.cpu().numpy().tobytes() == np.array([scale], np.float32).tobytes()
+
+
 def _paged(cache_rows, page_size, n_kv, hd, perm, total_pages):
     """Scatter contiguous [S, n_kv*hd] rows into pages [P][n_kv][page][hd] via a page table."""
     S = cache_rows.shape[0]
