@@ -510,6 +510,50 @@ def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: Sampli
     return out
 
 
+def generate_batch(model: QuantLlamaB200, prompts: Sequence[Sequence[int]], config: SamplingConfig,
+                   rngs: Sequence[Rng], device_sampling: bool = True) -> list:
+    """generate() (generate.rs:51-89) for several prompts at once, one engine
+    row per sequence: sequence b's tokens, and the final state of rngs[b],
+    equal generate(model, prompts[b], config, rngs[b]).  Prompts may differ in
+    length.  Every row advances one position per step and samples from the
+    step of its last prompt token on (max(1, max_tokens) tokens, like the
+    reference loop); a row that is done keeps stepping without drawing from
+    its generator.  Sampling runs on the device unless device_sampling is
+    False or the model is tensor-parallel."""
+    B = len(prompts)
+    if len(rngs) != B:
+        raise ValueError("generate_batch: one generator per prompt")
+    if any(len(p) == 0 for p in prompts):
+        raise ValueError("generate: prompt_tokens must not be empty")
+    if B == 0:
+        return []
+    if B > model.max_batch:
+        raise N.SbError(4, f"generate_batch: {B} prompts exceed the engine's max_batch {model.max_batch}")
+    lens = [len(p) for p in prompts]
+    n_out = max(1, config.max_tokens)
+    steps = max(lens) + n_out - 1
+    cache = model.new_kv_cache(steps)
+    V = model.vocab_size()
+    on_device = device_sampling and model.tp_size == 1
+    outs = [[] for _ in range(B)]
+    for t in range(steps):
+        toks = [int(prompts[b][t]) if t < lens[b] else outs[b][-1] for b in range(B)]
+        draw = [t >= lens[b] - 1 and len(outs[b]) < n_out for b in range(B)]
+        if on_device:
+            model.forward_batch(toks, [t] * B, want_logits=False)
+            if any(draw):
+                # rows that do not sample this step draw from a throwaway state
+                got = model.sample(config, [rngs[b] if draw[b] else Rng(0) for b in range(B)])
+        else:
+            lg, _ = model.forward_batch(toks, [t] * B)
+            got = [sample_token(lg[b][:V], config, rngs[b]) if draw[b] else 0 for b in range(B)]
+        for b in range(B):
+            if draw[b]:
+                outs[b].append(int(got[b]))
+    cache.seq_len = steps
+    return outs
+
+
 def sample_rows(logits, config: SamplingConfig, rng_states, out=None, stream: int = 0):
     """sample_token (generate.rs:92-165) on the device for every row of a
     torch CUDA [rows, n] f32 tensor (sb_sample_rows).  rng_states: torch
