@@ -9,6 +9,9 @@ arbitrary small inputs).  CPU only.
   `as i8` turns NaN into 0.
 * the safetensors parser: arbitrary bytes and arbitrary headers either parse
   into tensors whose byte ranges fit their shapes, or raise SbError.
+* tensor-parallel sharding (host C): for any divisible GQA shape and 1-8
+  ranks the shards partition every weight exactly; uneven splits are
+  SB_ERR_SHAPE.
 """
 import json
 
@@ -97,3 +100,61 @@ def test_parser_on_arbitrary_headers(tmp_path, header, data_len):
             assert st_.f32(name).shape == tuple(info["shape"])
         elif info["dtype"] == "I8":
             assert st_.raw(name).shape == tuple(info["shape"])
+
+
+@st.composite
+def _tp_case(draw):
+    T = draw(st.sampled_from([1, 2, 4, 8]))
+    kv = T * draw(st.integers(1, 2))
+    heads = kv * draw(st.sampled_from([1, 2, 4]))
+    hd = draw(st.sampled_from([2, 4, 8]))
+    ffn = T * draw(st.integers(1, 6))
+    vocab = T * draw(st.integers(1, 6))
+    return T, heads, kv, hd, ffn, vocab
+
+
+@settings(max_examples=120, deadline=None)
+@given(_tp_case(), st.integers(0, 2**31 - 1))
+def test_tp_shards_partition_every_weight_of_any_config(case, seed):
+    # The host sharder (sb_tp_shard_qweight): column slices of q|k|v (by
+    # heads, q, k and v separately), gate and up (by ffn columns); row slices
+    # of o, down and the [V, h] lm_head.  Concatenating the T shards the way
+    # the algebra says gives back the full tensor, for any divisible shape.
+    from esolearn_b200 import LlamaConfig, tp_shard_qweight, tp_shard_shape
+
+    T, heads, kv, hd, ffn, vocab = case
+    h = heads * hd
+    c = LlamaConfig(vocab, h, ffn, 1, heads, kv, 16, 1e-5, 10000.0, False, None)
+    Qf, KVf = heads * hd, kv * hd
+    rng = np.random.default_rng(seed)
+    shapes = {N.SB_W_QKV: (h, Qf + 2 * KVf), N.SB_W_O: (Qf, h), N.SB_W_GATE: (h, ffn), N.SB_W_UP: (h, ffn),
+              N.SB_W_DOWN: (ffn, h), N.SB_W_LM_HEAD: (vocab, h)}
+    for slot, shape in shapes.items():
+        w = rng.integers(-127, 128, shape, dtype=np.int8)
+        parts = [tp_shard_qweight(c, slot, r, T, w) for r in range(T)]
+        assert all(p.shape == tp_shard_shape(c, slot, r, T) for r, p in enumerate(parts))
+        if slot == N.SB_W_QKV:
+            q, k = Qf // T, KVf // T
+            re = np.concatenate([np.concatenate([p[:, :q] for p in parts], 1),
+                                 np.concatenate([p[:, q:q + k] for p in parts], 1),
+                                 np.concatenate([p[:, q + k:] for p in parts], 1)], 1)
+        elif slot in (N.SB_W_GATE, N.SB_W_UP):
+            re = np.concatenate(parts, 1)
+        else:
+            re = np.concatenate(parts, 0)
+        assert np.array_equal(re, w), slot
+
+
+@settings(max_examples=60, deadline=None)
+@given(st.integers(1, 8), st.integers(1, 12), st.integers(1, 40))
+def test_tp_uneven_splits_are_shape_errors(T, heads, ffn):
+    from esolearn_b200 import LlamaConfig, tp_shard_shape
+
+    c = LlamaConfig(8 * T, heads * 4, ffn, 1, heads, heads, 16, 1e-5, 10000.0, False, None)
+    ok = heads % T == 0 and ffn % T == 0
+    try:
+        tp_shard_shape(c, N.SB_W_GATE, 0, T)
+        tp_shard_shape(c, N.SB_W_O, 0, T)
+        assert ok
+    except N.SbError as e:
+        assert not ok and e.code == 4
