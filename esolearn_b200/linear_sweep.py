@@ -103,12 +103,16 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--peaks", default=os.path.join(os.path.dirname(os.path.dirname(__file__)), "MEASURED_PEAKS.json"))
     ap.add_argument("--json", default=None, help="also write the results here")
+    ap.add_argument("--rows", type=int, nargs="+", default=ROWS, help="M values (default: 1 8 32 128)")
+    ap.add_argument("--groups", type=int, nargs="+", default=GROUPS, help="0 = per-tensor, 32, 64")
+    ap.add_argument("--shapes", nargs="+", default=[f"{k}x{n}" for k, n in SHAPES], help="KxN, e.g. 4096x11008")
     args = ap.parse_args()
+    shapes = [tuple(int(v) for v in sh.lower().split("x")) for sh in args.shapes]
     peak = None
     if args.peaks and os.path.exists(args.peaks):
         with open(args.peaks) as f:
             peak = float(json.load(f).get("hbm_gbs") or 0) or None
-    res = run(args.iters, peak)
+    res = run(args.iters, peak, shapes=shapes, rows=args.rows, groups=args.groups)
     print("| K | N | group | M | µs | GB/s | frac of measured HBM | TFLOP/s |")
     print("|---|---|---|---|---|---|---|---|")
     for r in res:
