@@ -27,11 +27,19 @@ every sequence: K timed steps follow the prompt and W warm-up steps.
                 traffic -- DRAM bytes of one launch from an ncu capture
                 (profiles/decode_step_7b_bs1_traffic.json).
 * cpu_baseline -- the reference's CPU path (the oracle restatement of
-                cpu.rs) timed on this host on a bounded sample, scaled to a
-                full 7B token.
+                cpu.rs, every layer of the workload's shape, one sequence)
+                timed on this host's cores: 1 warm-up + up to 4 timed steps
+                at the workload's context.
+* extra      -- (1 GPU, default workload) the metric's other parts measured
+                in the same run: "bs32", the Llama-3-8B-shape batch-32 decode
+                with 2048-token contexts (value, roofline, e2e, clocks), and
+                "quant_linear_sweep", GB/s of every configs[1] cell
+                (M in {1, 8, 32, 128}, per-tensor and group-32 scales).
 
---impl reference times that CPU path alone (the reference is Rust and cannot
-be built here; the oracle restates it operation by operation).
+--impl reference times that CPU path alone: W warm-up and K timed decode
+steps of the full model (stopped early, and the step count reported, if the
+timed loop passes 150 s).  The reference is Rust and cannot be built here;
+the oracle restates it operation by operation.
 Multi-GPU (torchrun, N ranks): tensor parallelism over the N GPUs -- every
 rank holds 1/N of every projection and of the KV heads, the partial o and
 down products are summed with an NCCL all-reduce over NVLink, and the greedy
@@ -139,46 +147,46 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside)}
 
 
-def cpu_reference_tok_s(shape, budget_s: float = 20.0):
-    """The reference CPU decode (oracle restatement of cpu.rs) on a bounded sample.
-
-    Sample: the workload's model shape with 2 decoder layers + its lm_head,
-    seeded weights; 4 decode steps after a 4-token prefix are timed and the
-    per-layer time is scaled to the full depth.  The reference decodes one
-    sequence at a time, so its tok/s is the same at any batch.  Returns
-    (tok/s, cores, sample)."""
+def cpu_reference_decode(shape, context: int, warmup: int, steps: int, budget_s: float | None = None):
+    """The reference CPU decode (the oracle's operation-by-operation
+    restatement of cpu.rs, every layer of the workload's shape) timed on this
+    host with all its threads: `warmup` untimed then `steps` timed
+    forward_with_cache calls of one sequence at contexts context .. context +
+    warmup + steps - 1, greedy-fed.  The K/V cache is filled to `context`
+    positions with seeded values instead of running the prompt (the decode
+    cost depends on the context length only), and the int8 weights are seeded
+    uniform values (the cost does not depend on them).  budget_s stops the
+    timed loop early (at least one step).  The reference decodes one sequence
+    at a time, so its tok/s is the same at any batch.
+    Returns (tok/s, cores, steps timed, sample description)."""
     import oracle as O
 
     cores = os.cpu_count() or 1
     O.set_threads(cores)
-    L = 2
     V, h, F = shape.vocab_size, shape.hidden_size, shape.intermediate_size
-    cfg = O.make_config(V, h, F, L, shape.n_heads, shape.n_kv_heads, 64, 1e-5, shape.rope_theta, False)
-    m = O.OracleLlama(cfg, 0)
-    cache = m.new_cache(64)
-    toks = O.prompt_ids(0, 8, V)
-    for pos in range(4):
-        m.forward_with_cache(cache, int(toks[pos]), pos)
-    times = []
-    t_start = time.perf_counter()
-    for pos in range(4, 8):
-        t0 = time.perf_counter()
-        m.forward_with_cache(cache, int(toks[pos]), pos)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
-            break
-    t_step = float(np.median(times))
-    # lm_head share: time the [1,h]x[h,V] int8 matmul alone
-    q = np.zeros((V, h), np.int8)
-    x = np.ones(h, np.float32)
+    max_seq = context + warmup + steps + 1
+    cfg = O.make_config(V, h, F, shape.n_layers, shape.n_heads, shape.n_kv_heads, max_seq, 1e-5, shape.rope_theta,
+                        False)
+    m = O.OracleLlama(cfg, 0, uniform=True)
+    cache = m.new_cache(max_seq, kv_bf16=False)  # the reference's f32 cache
+    cache.fill(context, 1)
+    tok, pos = 1, context
+    for _ in range(warmup):
+        tok = O.argmax(m.forward_with_cache(cache, tok, pos))
+        pos += 1
+    n = 0
     t0 = time.perf_counter()
-    O.matmul_i8_f32_tb(x, q, 0.01, 1, h, V)
-    t_head = time.perf_counter() - t0
-    t_layer = max(t_step - t_head, 1e-9) / L
-    t_token = shape.n_layers * t_layer + t_head
-    return 1.0 / t_token, cores, (f"h{h}/ffn{F}/vocab{V}, {L} of {shape.n_layers} layers + lm_head, {len(times)} "
-                                  f"decode steps at context 5-8, per-layer time x{shape.n_layers} + lm_head; "
-                                  f"{cores} OpenMP threads")
+    while n < steps:
+        tok = O.argmax(m.forward_with_cache(cache, tok, pos))
+        pos += 1
+        n += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    del cache, m
+    sample = (f"h{h}/ffn{F}/vocab{V}, all {shape.n_layers} layers + lm_head, {n} timed decode steps after {warmup} "
+              f"warm-up at contexts {context}-{pos - 1} (f32 cache), one sequence, {cores} OpenMP threads")
+    return n / dt, cores, n, sample
 
 
 def run_reference(args, rank: int, world: int):
@@ -187,33 +195,36 @@ def run_reference(args, rank: int, world: int):
     from esolearn_b200 import LlamaConfig
 
     wl = WORKLOADS[args.workload]
-    tok_s, cores, sample = cpu_reference_tok_s(getattr(LlamaConfig, wl["shape"])())
+    shape = getattr(LlamaConfig, wl["shape"])()
+    # bounded so the whole run stays within a few minutes at any shape
+    tok_s, cores, n, sample = cpu_reference_decode(shape, args.prompt, args.warmup, args.steps, budget_s=150.0)
     print(json.dumps({
         "impl": "reference", "metric": wl["metric"], "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / tok_s, "higher_is_better": True,
+        "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 / tok_s, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 activations", "data": "synthetic",
-        "config": {"workload": wl["desc"] + " (reference CPU path, sampled; one sequence at a time)",
-                   "batch": args.batch, "prompt": args.prompt},
+        "config": {"workload": wl["desc"] + " (reference CPU path; one sequence at a time)",
+                   "batch": args.batch, "prompt": args.prompt, "context": [args.prompt, args.prompt + args.warmup + n - 1]},
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def run_ours(args, rank: int, world: int, dist):
+def measure_decode(wl_name: str, B: int, prompt: int, K: int, W: int, rank: int, world: int, dist, replicas: bool,
+                   want_e2e: bool = True, sample_clocks: bool = True):
+    """Decode throughput of one workload: build the seeded model on the device,
+    prefill the prompts, W warm-up steps, then K timed steps (CUDA events on the
+    engine stream, max over ranks) and K steps through sb_llama_forward with
+    host buffers (e2e).  Returns the pieces of the JSON line (same on every
+    rank after the max-reductions)."""
     import torch
 
     from esolearn_b200 import LlamaConfig, QuantLlamaB200
-    from esolearn_b200 import _native as N
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    N.check(N.lib().sb_init(local))
-    wl = WORKLOADS[args.workload]
+    wl = WORKLOADS[wl_name]
     cfg = getattr(LlamaConfig, wl["shape"])()
-    B = args.batch
-    K, W = args.steps, args.warmup
-    max_seq = args.prompt + W + K + 8
-    tp = world if (world > 1 and not args.replicas) else 1
+    max_seq = prompt + W + K + 8
+    tp = world if (world > 1 and not replicas) else 1
     tp_kw = {}
     if tp > 1:
         from esolearn_b200 import tp_unique_id
@@ -227,25 +238,27 @@ def run_ours(args, rank: int, world: int, dist):
     model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=rows, kv_dtype="bf16", **tp_kw)
     # tensor-parallel ranks decode the same sequences; replicas decode their own
     rng = np.random.default_rng(1000 + (0 if tp > 1 else rank))
-    prompts = rng.integers(0, cfg.vocab_size, (B, args.prompt), dtype=np.int64).astype(np.int32)
+    prompts = rng.integers(0, cfg.vocab_size, (B, prompt), dtype=np.int64).astype(np.int32)
     # batched prefill of the prompts (host-timed, includes its syncs), then warm-up steps
-    n_warm = min(args.prompt, rows + args.prompt % rows)  # every chunk shape the timed prefill uses
+    n_warm = min(prompt, rows + prompt % rows)  # every chunk shape the timed prefill uses
     model.prefill(prompts[:, :n_warm])  # captures the step graphs outside the timed prefill
     torch.cuda.synchronize()
     t_pf0 = time.perf_counter()
     model.prefill(prompts)
     t_pf1 = time.perf_counter()
-    prefill = {"tok_s": B * args.prompt / (t_pf1 - t_pf0), "tokens": B * args.prompt, "ms": (t_pf1 - t_pf0) * 1e3,
+    prefill = {"tok_s": B * prompt / (t_pf1 - t_pf0), "tokens": B * prompt, "ms": (t_pf1 - t_pf0) * 1e3,
                "positions_per_step": rows, "timing": "host wall clock around sb_llama_prefill (synchronous)"}
     model.step(W)
     st = torch.cuda.ExternalStream(model.stream())
     torch.cuda.synchronize()
 
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    smi_index = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
-    clocks = ClockSampler(smi_index)
-    clocks.start()
-    time.sleep(0.3)
+    clocks = None
+    if sample_clocks:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        smi_index = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+        clocks = ClockSampler(smi_index)
+        clocks.start()
+        time.sleep(0.3)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -262,19 +275,21 @@ def run_ours(args, rank: int, world: int, dist):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    clk = clocks.summary(t_wall0, t_wall1)
-    clocks.stop()
-    ctx_mid = args.prompt + W + K / 2
+    clk = None
+    if clocks is not None:
+        clk = clocks.summary(t_wall0, t_wall1)
+        clocks.stop()
+    ctx_mid = prompt + W + K / 2
     wbytes, kv_per_pos = model.step_bytes()
     n_jobs = 1 if tp > 1 else world  # independent decode jobs in the run
     value = n_jobs * B * K / (ms / 1000.0)
     launches_per_step = model.step_launches(B)
     peak, peak_kind = read_peaks()
     step_alg_bytes = wbytes + kv_per_pos * ctx_mid * B
+    achieved = step_alg_bytes / (ms / K / 1000.0) / 1e9
     if launches_per_step == 1:
         # one persistent kernel per step: its average launch duration is the step time
         traffic = read_traffic()
-        achieved = step_alg_bytes / (ms / K / 1000.0) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_source": peak_kind, "kernel": "decode_step_kernel (persistent: every projection + attention)",
                 "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
@@ -286,10 +301,9 @@ def run_ours(args, rank: int, world: int, dist):
         prof = [model.profile_step() for _ in range(4)]
         lin_ms = float(np.median([p[0] for p in prof]))
         att_ms = float(np.median([p[1] for p in prof]))
-        achieved = step_alg_bytes / (ms / K / 1000.0) / 1e9
         lin_kernel = "qgm_gemm_kernel (tcgen05)" if B > 4 else "qgemv_kernel"
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_source": peak_kind, "kernel": f"whole step: {lin_kernel} linears + attn_decode_kernel",
+                "peak_source": peak_kind, "kernel": f"whole step: {lin_kernel} linears + attention",
                 "traffic": None, "algorithmic_bytes_per_step": step_alg_bytes, "step_ms": ms / K,
                 "linears": {"bytes": wbytes, "eager_ms": lin_ms, "gbs": wbytes / (lin_ms / 1000.0) / 1e9},
                 "attention": {"bytes": kv_per_pos * ctx_mid * B, "eager_ms": att_ms,
@@ -297,19 +311,18 @@ def run_ours(args, rank: int, world: int, dist):
 
     # e2e: reference-facing call with host buffers every step (tokens in, argmax out)
     e2e = None
-    if not args.no_e2e:
+    if want_e2e:
         # Re-decode the timed positions (each step rewrites its own KV row
         # before reading the context), so every e2e step sees the same
         # context length as the matching timed step.
         toks = model.tokens(B, max_seq)
         last = toks[:, -1].copy() if toks.shape[1] else np.zeros(B, np.int32)
-        p0 = args.prompt + W
-        n_e2e = K
+        p0 = prompt + W
         pinned_tok = torch.empty(B, dtype=torch.int32).pin_memory()
         for i in range(3):
             model.forward_batch(last.tolist(), [p0 - 3 + i] * B, want_logits=False)
         t0 = time.perf_counter()
-        for i in range(n_e2e):
+        for i in range(K):
             pinned_tok.numpy()[:] = last
             _, am = model.forward_batch(pinned_tok.numpy(), [p0 + i] * B, want_logits=False)
             last = am
@@ -319,36 +332,91 @@ def run_ours(args, rank: int, world: int, dist):
             tt = torch.tensor([e2e_s], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e2e_s = float(tt.item())
-        e2e = {"value": n_jobs * B * n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
-               "d2h_bytes_per_step": 4 * B, "steps": n_e2e,
+        e2e = {"value": n_jobs * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+               "d2h_bytes_per_step": 4 * B, "steps": K,
                "api": "sb_llama_forward (token, position in; argmax out; stream-synchronous)"}
+    model.close()
+    del model
+    torch.cuda.synchronize()
+    return {"cfg": cfg, "tp": tp, "value": value, "ms": ms, "ctx_mid": ctx_mid, "wbytes": wbytes,
+            "launches_per_step": launches_per_step, "prefill": prefill, "roofline": roof, "clocks": clk, "e2e": e2e}
 
+
+def quant_linear_sweep_summary(iters: int = 5):
+    """The quantized-linear sweep on this GPU, compact:
+    GB/s (fraction of measured HBM) per (K, N, group, M) cell, M in {1, 8, 32,
+    128}, per-tensor scale and group 32 (group 64 times within a few % of 32)."""
+    from esolearn_b200 import linear_sweep
+
+    peak, kind = read_peaks()
+    cells = linear_sweep.run(iters=iters, peak_gbs=peak, groups=[0, 32])
+    out = {"timing": f"CUDA events, L2 flushed before each call, median of {iters}",
+           "bytes": "K*N int8 + 4*K*N/g scales + 2*M*K bf16 in + 4*M*N f32 out", "peak_gbs": peak,
+           "peak_source": kind, "cells": []}
+    for r in cells:
+        out["cells"].append({"K": r["K"], "N": r["N"], "group": r["group"], "M": r["M"], "us": round(r["us"], 2),
+                             "gbs": round(r["gbs"], 1), "frac": round(r["gbs"] / peak, 3),
+                             "tflops": round(r["tflops"], 2)})
+    return out
+
+
+def run_ours(args, rank: int, world: int, dist):
+    import torch
+
+    from esolearn_b200 import _native as N
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    N.check(N.lib().sb_init(local))
+    wl = WORKLOADS[args.workload]
+    B, K, W = args.batch, args.steps, args.warmup
+    r = measure_decode(args.workload, B, args.prompt, K, W, rank, world, dist, args.replicas, not args.no_e2e)
+    tp = r["tp"]
+    extra = {}
+    if world == 1 and not args.no_extra and args.workload == "llama2-7b-bs1":
+        # the metric's other parts, on the same GPU in the same run: batch 32
+        # (8B-shape GQA, 2048-token contexts) and the quantized-linear sweep
+        wl32 = WORKLOADS["llama3-8b-bs32"]
+        r32 = measure_decode("llama3-8b-bs32", wl32["batch"], wl32["prompt"], K, W, rank, world, dist, False, True,
+                             sample_clocks=True)
+        extra["bs32"] = {"metric": wl32["metric"], "value": r32["value"], "unit": "tok/s",
+                         "ms_per_step": r32["ms"] / K, "steps": K, "warmup": W,
+                         "config": {"workload": wl32["desc"], "batch": wl32["batch"], "prompt": wl32["prompt"],
+                                    "context_mid": r32["ctx_mid"]},
+                         "gpu_launches": r32["launches_per_step"] * K, "prefill": r32["prefill"],
+                         "roofline": r32["roofline"], "e2e": r32["e2e"], "clocks": r32["clocks"]}
+        extra["quant_linear_sweep"] = quant_linear_sweep_summary()
     if rank != 0:
         return
     res = {
-        "metric": wl["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
+        "metric": wl["metric"], "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": r["ms"] / K, "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak",
         "vs_baseline": None,
         "dtype": "int8 weights x f32 activations (exact int32 dp4a products), f32 accumulate; bf16 KV",
         "data": "synthetic: seeded random-init weights (fastrand/Box-Muller N(0,0.02), LlamaModel::new order), "
                 "seeded uniform prompt ids",
         "config": {"workload": wl["desc"], "batch": B, "prompt": args.prompt,
-                   "context_mid": ctx_mid,
+                   "context_mid": r["ctx_mid"],
                    "parallelism": (f"tp{tp} (one-shot peer all-reduce over NVLink after o and down)" if tp > 1 else
                                    f"replicas x{world}" if world > 1 else "single GPU"),
-                   "l2": f"weights {wbytes / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)", "kv_dtype": "bf16",
-                   "launch": ("one persistent cooperative kernel per step" if launches_per_step == 1 else
+                   "l2": f"weights {r['wbytes'] / 1e9:.1f} GB per step >> 126 MB L2 (no flush needed)",
+                   "kv_dtype": "bf16",
+                   "launch": ("one persistent cooperative kernel per step" if r["launches_per_step"] == 1 else
                               "CUDA graph of per-operation kernels per step, programmatic dependent launch")},
-        "gpu_launches": launches_per_step * K,
-        "prefill": prefill,
-        "roofline": roof,
-        "clocks": clk,
+        "gpu_launches": r["launches_per_step"] * K,
+        "prefill": r["prefill"],
+        "roofline": r["roofline"],
+        "clocks": r["clocks"],
     }
-    if e2e:
-        res["e2e"] = e2e
+    if r["e2e"]:
+        res["e2e"] = r["e2e"]
     if not args.no_cpu:
-        tok_s, cores, sample = cpu_reference_tok_s(cfg)
+        # bounded sample of the reference CPU path: the full model, 1 warm-up
+        # and up to 4 timed steps at the workload's context
+        tok_s, cores, n, sample = cpu_reference_decode(r["cfg"], args.prompt, 1, 4, budget_s=30.0)
         res["cpu_baseline"] = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+    if extra:
+        res["extra"] = extra
     print(json.dumps(res), flush=True)
 
 
@@ -363,6 +431,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=None, help="prompt length (default: the workload's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the bs32 workload and the linear sweep (N=1)")
     ap.add_argument("--replicas", action="store_true", help="N>1: independent replicas instead of tensor parallelism")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]

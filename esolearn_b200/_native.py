@@ -94,6 +94,7 @@ SIGNATURES = {
     "sb_llama_profile_step": (C.c_int, [vp, f32p, f32p, f32p, i32p]),
     "sb_llama_step_bytes": (C.c_int, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "sb_llama_step_launches": (C.c_int, [vp, C.c_int, i32p]),
+    "sb_llama_attn_plan": (C.c_int, [vp, C.c_int, i32p, i32p, i32p]),
 }
 
 _lib = None

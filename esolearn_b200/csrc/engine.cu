@@ -1241,6 +1241,23 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
     return SB_OK;
 }
 
+sb_status sb_llama_attn_plan(sb_llama *m, int batch, int *splits, int *tensor_map, int *chunk) {
+    SB_CHECK(m, SB_ERR_ARG, "sb_llama_attn_plan: null model");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    int s = 0, tm = 0, ch = 0;
+    if (batch == 1 && m->ds_ok) {
+        ch = m->ds_chunk;  // KV positions per ring stage of the persistent step
+    } else {
+        tm = m->att_tma ? 1 : 0;
+        s = m->att_tma ? tma_splits(m, batch) : m->att_splits;
+        ch = m->att_tma ? 64 : 0;  // the tensor-map kernel's tile
+    }
+    if (splits) *splits = s;
+    if (tensor_map) *tensor_map = tm;
+    if (chunk) *chunk = ch;
+    return SB_OK;
+}
+
 sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_bytes_per_pos) {
     SB_CHECK(m, SB_ERR_ARG, "null model");
     const double h = m->h, F = m->F, V = m->V;

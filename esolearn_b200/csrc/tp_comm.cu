@@ -325,8 +325,12 @@ void tp_destroy(TpComm &c) {
 
 int tp_allreduce_f32(const TpComm &c, float *buf, size_t count, cudaStream_t st) {
     if (c.p2p && count <= (size_t)c.peers.cap) {
-        const int G = std::max(1, std::min(TP_AR_CTAS, (int)((count + 1023) / 1024)));
-        SB_CUDA_TRY(launch(tp_ar_kernel, dim3(G), dim3(256), 0, st, true, buf, (int)count, c.peers, c.rank, c.size));
+        // Always all TP_AR_CTAS CTAs, whatever the count: every CTA index then
+        // advances its epoch on every call, so all epochs stay equal and a cell
+        // left by an earlier call (possibly of another count, hence another
+        // slice map) never carries the epoch a reader of this call waits for.
+        SB_CUDA_TRY(launch(tp_ar_kernel, dim3(TP_AR_CTAS), dim3(256), 0, st, true, buf, (int)count, c.peers, c.rank,
+                           c.size));
         return SB_OK;
     }
     const NcclApi &a = api();

@@ -400,6 +400,12 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_step_launches(self._h, batch, C.byref(n)))
         return n.value
 
+    def attn_plan(self, batch: int = 1):
+        """(context splits, tensor-map kernel?, chunk) of a step's attention (sb_llama_attn_plan)."""
+        s, t, c = C.c_int32(), C.c_int32(), C.c_int32()
+        N.check(N.lib().sb_llama_attn_plan(self._h, batch, C.byref(s), C.byref(t), C.byref(c)))
+        return s.value, bool(t.value), c.value
+
     def step_bytes(self):
         w, kv = C.c_double(), C.c_double()
         N.check(N.lib().sb_llama_step_bytes(self._h, C.byref(w), C.byref(kv)))

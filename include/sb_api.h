@@ -273,6 +273,14 @@ sb_status sb_llama_step_bytes(sb_llama *m, double *weight_bytes, double *kv_byte
  * shapes), else the per-operation kernel count.  No reference counterpart
  * (the reference runs on the CPU); it documents which device path runs. */
 sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches);
+/* How the attention of one decode step of `batch` sequences divides its
+ * work (no reference counterpart; it documents which device path runs and
+ * lets tests assert that a multi-split path was exercised).  Persistent
+ * batch-1 step: *splits = 0, *tensor_map = 0, *chunk = KV positions per ring
+ * stage (the (kv head, chunk) units are spread over all SMs).  Batched step:
+ * *splits = context splits per (sequence, kv head), *tensor_map = 1 when the
+ * tensor-map kernel runs (then *chunk = 64, its tile), else 0. */
+sb_status sb_llama_attn_plan(sb_llama *m, int batch, int *splits, int *tensor_map, int *chunk);
 
 #ifdef __cplusplus
 }

@@ -71,6 +71,8 @@ def lib():
         "orc_argmax": (C.c_int64, [f32p, C.c_size_t]),
         "orc_llama_new_random": (C.c_void_p, [C.POINTER(OrcConfig), C.c_uint64]),
         "orc_llama_new_empty": (C.c_void_p, [C.POINTER(OrcConfig)]),
+        "orc_llama_new_uniform": (C.c_void_p, [C.POINTER(OrcConfig), C.c_uint64]),
+        "orc_cache_fill": (None, [C.c_void_p, C.c_int, C.c_uint64]),
         "orc_llama_free": (None, [C.c_void_p]),
         "orc_llama_weight": (C.c_void_p, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float),
                                           C.POINTER(C.c_int), C.POINTER(C.c_int)]),
@@ -82,6 +84,10 @@ def lib():
         "orc_cache_free": (None, [C.c_void_p]),
         "orc_forward_with_cache": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, f32p, C.c_void_p]),
         "orc_generate_greedy": (None, [C.c_void_p, i32p, C.c_int, C.c_int, C.c_int, i32p]),
+        "orc_forward_tokens": (None, [C.c_void_p, C.c_void_p, i32p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+        "orc_cache_clone": (C.c_void_p, [C.c_void_p]),
+        "orc_cache_truncate": (None, [C.c_void_p, C.c_int]),
+        "orc_cache_len": (C.c_int, [C.c_void_p]),
         "orc_sample_token": (C.c_int64, [f32p, C.c_size_t, C.c_float, C.c_size_t, C.c_float, u64p]),
         "orc_set_threads": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
@@ -264,10 +270,17 @@ SLOTS = ("qkv", "o", "gate", "up", "down")
 class OracleLlama:
     """Quantized LlamaModel (llama.rs) with a contiguous f32 (or bf16-rounded) cache."""
 
-    def __init__(self, cfg: OrcConfig, seed: int | None = 0):
+    def __init__(self, cfg: OrcConfig, seed: int | None = 0, uniform: bool = False):
+        """seed None: empty model; uniform: seeded uniform int8 weights (for
+        timing the CPU path, no parity meaning); else LlamaModel::new."""
         self.cfg = cfg
         L = lib()
-        self.h = L.orc_llama_new_random(C.byref(cfg), seed) if seed is not None else L.orc_llama_new_empty(C.byref(cfg))
+        if seed is None:
+            self.h = L.orc_llama_new_empty(C.byref(cfg))
+        elif uniform:
+            self.h = L.orc_llama_new_uniform(C.byref(cfg), seed)
+        else:
+            self.h = L.orc_llama_new_random(C.byref(cfg), seed)
         self.hd = cfg.hidden_size // cfg.n_heads
 
     def __del__(self):
@@ -312,6 +325,19 @@ class OracleLlama:
                                      tr.ctypes.data_as(C.c_void_p) if trace else None)
         return (logits, tr) if trace else logits
 
+    def forward_tokens(self, cache: "OracleCache", tokens, pos0: int, all_logits: bool = False):
+        """len(tokens) consecutive forward_with_cache calls (positions pos0, pos0+1, ...),
+        evaluated layer by layer; bit-identical to the per-token loop.  Returns the
+        last token's logits [V], or every token's [n, V] with all_logits."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        V = self.cfg.vocab_size
+        last = np.empty(V, np.float32)
+        allv = np.empty((t.size, V), np.float32) if all_logits else None
+        lib().orc_forward_tokens(self.h, cache.h, t, t.size, pos0,
+                                 allv.ctypes.data_as(C.c_void_p) if all_logits else None,
+                                 last.ctypes.data_as(C.c_void_p))
+        return allv if all_logits else last
+
     def generate_greedy(self, prompt, max_tokens: int, kv_bf16: bool = False) -> np.ndarray:
         prompt = np.ascontiguousarray(prompt, np.int32)
         out = np.empty(max_tokens, np.int32)
@@ -320,9 +346,22 @@ class OracleLlama:
 
 
 class OracleCache:
-    def __init__(self, model: OracleLlama, max_seq: int, kv_bf16: bool):
+    def __init__(self, model: OracleLlama, max_seq: int, kv_bf16: bool, _handle=None):
         self.model = model
-        self.h = lib().orc_cache_new(model.h, max_seq, int(kv_bf16))
+        self.h = _handle if _handle is not None else lib().orc_cache_new(model.h, max_seq, int(kv_bf16))
+
+    def clone(self) -> "OracleCache":
+        return OracleCache(self.model, 0, False, _handle=lib().orc_cache_clone(self.h))
+
+    def truncate(self, n: int):
+        lib().orc_cache_truncate(self.h, n)
+
+    def fill(self, n: int, seed: int = 0):
+        """Seeded K/V values in rows 0..n-1, length n (timing only)."""
+        lib().orc_cache_fill(self.h, n, seed)
+
+    def __len__(self) -> int:
+        return lib().orc_cache_len(self.h)
 
     def __del__(self):
         if getattr(self, "h", None) and _lib is not None:

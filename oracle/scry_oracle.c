@@ -4,7 +4,7 @@
  * TEST INFRASTRUCTURE ONLY (the parity checker and the timed CPU baseline);
  * the B200 product never links it.  See scry_oracle.h for the contract.
  *
- * Build: oracle/Makefile (gcc -O2 -ffp-contract=off -fopenmp).  Contraction
+ * Build: oracle/Makefile (gcc -O3 -ffp-contract=off -fopenmp; hot loops cloned per ISA).  Contraction
  * must stay off: the reference is Rust, which rounds every f32/f64 multiply
  * and add separately.  Parallel loops split work only across independent
  * output elements, so every element is summed in the reference's order and
@@ -157,28 +157,49 @@ void orc_quantize_grouped(const float *w, int k, int n, int group, int8_t *q, fl
 /* ------------------------------------------------------------------------ */
 #define JCHUNK 256
 
+/* The hot loops are compiled for several instruction sets and picked at load
+ * time (GCC target_clones); every variant performs the same IEEE operations
+ * in the same order (-ffp-contract=off, no fast-math), only wider. */
+#if defined(__GNUC__) && defined(__x86_64__) && !defined(__clang__)
+#define ORC_CLONES __attribute__((target_clones("avx512f", "avx2", "default")))
+#else
+#define ORC_CLONES
+#endif
+#define IBLK 8
+
+ORC_CLONES
 void orc_matmul_i8_f32(const float *a, const int8_t *q, float scale, int m, int k, int n,
                        float *c) {
     /* cpu.rs:1129-1160.  c[i,j] accumulates, in f32, the terms
      * (f32)(f64(a[i,p]) * (f64(q[p,j]) * f64(scale))) for p = 0..k-1 in order
-     * (the 32^3 tiling visits p ascending for every fixed (i,j)). */
+     * (the 32^3 tiling visits p ascending for every fixed (i,j)).  Here the
+     * exact f64 product q[p,j] * scale (8 x 24 significant bits) is formed
+     * once per (p, j) and shared by a block of rows; each (i,j) still sees
+     * its terms in ascending p. */
     const double sd = (double)scale;
     int nchunks = (n + JCHUNK - 1) / JCHUNK;
 #pragma omp parallel for schedule(dynamic, 1)
     for (int cj = 0; cj < nchunks; cj++) {
         int j0 = cj * JCHUNK, j1 = j0 + JCHUNK < n ? j0 + JCHUNK : n;
-        for (int i = 0; i < m; i++) {
-            float *crow = c + (size_t)i * n;
-            for (int j = j0; j < j1; j++) crow[j] = 0.0f;
+        double wd[JCHUNK];
+        for (int i0 = 0; i0 < m; i0 += IBLK) {
+            int i1 = i0 + IBLK < m ? i0 + IBLK : m;
+            for (int i = i0; i < i1; i++)
+                for (int j = j0; j < j1; j++) c[(size_t)i * n + j] = 0.0f;
             for (int p = 0; p < k; p++) {
-                double av = (double)a[(size_t)i * k + p];
                 const int8_t *qrow = q + (size_t)p * n;
-                for (int j = j0; j < j1; j++) crow[j] += (float)(av * ((double)qrow[j] * sd));
+                for (int j = j0; j < j1; j++) wd[j - j0] = (double)qrow[j] * sd;
+                for (int i = i0; i < i1; i++) {
+                    double av = (double)a[(size_t)i * k + p];
+                    float *crow = c + (size_t)i * n + j0;
+                    for (int j = 0; j < j1 - j0; j++) crow[j] += (float)(av * wd[j]);
+                }
             }
         }
     }
 }
 
+ORC_CLONES
 void orc_matmul_i8_f32_tb(const float *a, const int8_t *q_t, float scale, int m, int k, int n,
                           float *c) {
     const double sd = (double)scale;
@@ -479,6 +500,47 @@ orc_llama *orc_llama_new_random(const orc_config *cfg, uint64_t seed) {
     return m;
 }
 
+static inline uint64_t orc_hash(uint64_t seed, uint64_t i) { return wy_mix(seed + (i + 1) * WY0); }
+
+/* n int8 values in [-127, 127], eight per 64-bit hash of (seed, base + i/8). */
+static void orc_fill_i8(int8_t *w, size_t n, uint64_t seed, uint64_t base) {
+    size_t words = (n + 7) / 8;
+#pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < words; i++) {
+        uint64_t r = orc_hash(seed, base / 8 + i);
+        for (int b = 0; b < 8 && 8 * i + b < n; b++) w[8 * i + b] = (int8_t)((int)((r >> (8 * b)) & 0xff) % 255 - 127);
+    }
+}
+
+orc_llama *orc_llama_new_uniform(const orc_config *cfg, uint64_t seed) {
+    /* A model of the given shape for timing the CPU path: int8 values uniform
+     * in [-127, 127] from a counter-based hash, per-tensor scales of the
+     * magnitude quantize_symmetric gives N(0, 0.02) weights, embeddings
+     * uniform in [-0.05, 0.05].  The arithmetic of every op is independent of
+     * the values, so the decode costs what a LlamaModel::new model costs,
+     * without 2 x 6.7 G Box-Muller draws at the 7B shape. */
+    orc_llama *m = orc_llama_new_empty(cfg);
+    int h = cfg->hidden_size, V = cfg->vocab_size, L = cfg->n_layers;
+    uint64_t base = 0;
+    for (int l = 0; l < L; l++)
+        for (int s = 0; s < 5; s++) {
+            int k, n;
+            wshape(m, s, &k, &n);
+            size_t cnt = (size_t)k * n;
+            int8_t *w = m->w[l * 5 + s];
+            orc_fill_i8(w, cnt, seed, base);
+            base += cnt;
+            m->scale[l * 5 + s] = 0.09f / 127.0f;
+        }
+    size_t nemb = (size_t)V * h;
+    orc_fill_i8(m->lm_head, nemb, seed, base);
+#pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < nemb; i++)
+        m->embed[i] = (float)(bits_to_unit_f64(orc_hash(seed ^ 0x5bd1e995ULL, i)) * 0.1 - 0.05);
+    m->lm_scale = 0.09f / 127.0f;
+    return m;
+}
+
 void orc_llama_free(orc_llama *m) {
     if (!m) return;
     for (int i = 0; i < m->cfg.n_layers * 5; i++) free(m->w[i]);
@@ -617,6 +679,136 @@ void orc_forward_with_cache(const orc_llama *m, orc_cache *c, int token, int pos
     orc_matmul_i8_f32_tb(xn, m->lm_head, m->lm_scale, 1, h, V, logits); /* llama.rs:761-762 */
     free(x); free(xn); free(qkv); free(qr); free(kr); free(gate); free(up); free(proj);
     free(head_out); free(kexp); free(vexp); free(scores); free(attn);
+}
+
+void orc_forward_tokens(const orc_llama *m, orc_cache *c, const int *tokens, int n, int pos0,
+                        float *logits_all, float *logits_last) {
+    /* n consecutive calls of orc_forward_with_cache (tokens[i] at position
+     * pos0 + i, appended at rows seq_len + i), evaluated layer by layer for
+     * all n tokens at once so every weight is streamed once per layer instead
+     * of once per token.  Each output element is computed by the same
+     * operations in the same order as in the per-token path: the int8
+     * matmuls and RMSNorm act row by row (cpu.rs:1129-1160, :574-599), RoPE
+     * per position (cpu.rs:635-664), and token i attends to rows
+     * 0..seq_len+i of the gathered cache (llama.rs:414-456) -- so the logits
+     * and the cache equal those of the token-by-token loop of generate()
+     * (generate.rs:68-75) bit for bit.  Test infrastructure: it makes long
+     * prompts affordable for the parity tests. */
+    if (n <= 0) return;
+    const orc_config *cfg = &m->cfg;
+    int h = cfg->hidden_size, F = cfg->intermediate_size, V = cfg->vocab_size;
+    int nh = cfg->n_heads, nkv = cfg->n_kv_heads, hd = m->hd;
+    int q_dim = m->q_dim, kv_dim = m->kv_dim, qkv_dim = m->qkv_dim;
+    int row0 = c->seq_len, full = row0 + n;
+    size_t nn = (size_t)n;
+    float *x = (float *)malloc(sizeof(float) * nn * h);
+    float *xn = (float *)malloc(sizeof(float) * nn * h);
+    float *qkv = (float *)malloc(sizeof(float) * nn * qkv_dim);
+    float *qr = (float *)malloc(sizeof(float) * nn * q_dim);
+    float *kr = (float *)malloc(sizeof(float) * nn * kv_dim);
+    float *gate = (float *)malloc(sizeof(float) * nn * F);
+    float *up = (float *)malloc(sizeof(float) * nn * F);
+    float *proj = (float *)malloc(sizeof(float) * nn * h);
+    float *head_out = (float *)malloc(sizeof(float) * nn * q_dim);
+    float *kexp = (float *)malloc(sizeof(float) * (size_t)nh * full * hd);
+    float *vexp = (float *)malloc(sizeof(float) * (size_t)nh * full * hd);
+    float qscale = (float)(1.0 / sqrt((double)hd)); /* llama.rs:394 */
+    for (int i = 0; i < n; i++) memcpy(x + (size_t)i * h, m->embed + (size_t)tokens[i] * h, sizeof(float) * h);
+    for (int l = 0; l < cfg->n_layers; l++) {
+        orc_rmsnorm(x, m->norm_in + (size_t)l * h, n, h, cfg->rms_norm_eps, xn);
+        orc_matmul_i8_f32(xn, m->w[l * 5 + ORC_QKV], m->scale[l * 5 + ORC_QKV], n, h, qkv_dim, qkv);
+        for (int i = 0; i < n; i++) {
+            const float *qi = qkv + (size_t)i * qkv_dim;
+            orc_rope(qi, 1, nh, hd, pos0 + i, m->freqs, qr + (size_t)i * q_dim);
+            orc_scale(qr + (size_t)i * q_dim, q_dim, qscale, qr + (size_t)i * q_dim);
+            orc_rope(qi + q_dim, 1, nkv, hd, pos0 + i, m->freqs, kr + (size_t)i * kv_dim);
+            float *kc = c->k[l] + (size_t)(row0 + i) * kv_dim, *vc = c->v[l] + (size_t)(row0 + i) * kv_dim;
+            for (int e = 0; e < kv_dim; e++) {
+                float kv_k = kr[(size_t)i * kv_dim + e], kv_v = qi[q_dim + kv_dim + e];
+                kc[e] = c->kv_bf16 ? round_bf16(kv_k) : kv_k;
+                vc[e] = c->kv_bf16 ? round_bf16(kv_v) : kv_v;
+            }
+        }
+        orc_gather_reshape_repeat_kv(c->k[l], full, nkv, nh, hd, kexp);
+        orc_gather_reshape_repeat_kv(c->v[l], full, nkv, nh, hd, vexp);
+#pragma omp parallel for schedule(dynamic, 1)
+        for (int i = 0; i < n; i++) {
+            int cl = row0 + i + 1;
+            float *sc = (float *)malloc(sizeof(float) * (size_t)nh * cl);
+            float *at = (float *)malloc(sizeof(float) * (size_t)nh * cl);
+            for (int hh = 0; hh < nh; hh++)
+                orc_gemv_trans_b(qr + (size_t)i * q_dim + (size_t)hh * hd, kexp + (size_t)hh * full * hd, hd, cl,
+                                 sc + (size_t)hh * cl);
+            orc_softmax(sc, nh, cl, at);
+            for (int hh = 0; hh < nh; hh++)
+                orc_gemv(at + (size_t)hh * cl, vexp + (size_t)hh * full * hd, cl, hd,
+                         head_out + (size_t)i * q_dim + (size_t)hh * hd);
+            free(sc);
+            free(at);
+        }
+        orc_matmul_i8_f32(head_out, m->w[l * 5 + ORC_O], m->scale[l * 5 + ORC_O], n, q_dim, h, proj);
+        for (size_t i = 0; i < nn * h; i++) x[i] = x[i] + proj[i]; /* llama.rs:564 */
+        orc_rmsnorm(x, m->norm_post + (size_t)l * h, n, h, cfg->rms_norm_eps, xn);
+        orc_matmul_i8_f32(xn, m->w[l * 5 + ORC_GATE], m->scale[l * 5 + ORC_GATE], n, h, F, gate);
+        orc_matmul_i8_f32(xn, m->w[l * 5 + ORC_UP], m->scale[l * 5 + ORC_UP], n, h, F, up);
+        orc_swiglu(gate, up, nn * F, gate);
+        orc_matmul_i8_f32(gate, m->w[l * 5 + ORC_DOWN], m->scale[l * 5 + ORC_DOWN], n, F, h, proj);
+        for (size_t i = 0; i < nn * h; i++) x[i] = x[i] + proj[i]; /* llama.rs:568 */
+    }
+    c->seq_len = full;
+    if (logits_all) {
+        orc_rmsnorm(x, m->norm_final, n, h, cfg->rms_norm_eps, xn);
+        orc_matmul_i8_f32_tb(xn, m->lm_head, m->lm_scale, n, h, V, logits_all);
+        if (logits_last) memcpy(logits_last, logits_all + (size_t)(n - 1) * V, sizeof(float) * V);
+    } else if (logits_last) {
+        orc_rmsnorm(x + (size_t)(n - 1) * h, m->norm_final, 1, h, cfg->rms_norm_eps, xn);
+        orc_matmul_i8_f32_tb(xn, m->lm_head, m->lm_scale, 1, h, V, logits_last);
+    }
+    free(x); free(xn); free(qkv); free(qr); free(kr); free(gate); free(up); free(proj);
+    free(head_out); free(kexp); free(vexp);
+}
+
+orc_cache *orc_cache_clone(const orc_cache *src) {
+    /* Clone of LlamaKvCache (its storages are Clone; kv_cache.rs:69-79). */
+    orc_cache *c = (orc_cache *)calloc(1, sizeof *c);
+    *c = *src;
+    c->k = (float **)calloc(c->n_layers, sizeof(float *));
+    c->v = (float **)calloc(c->n_layers, sizeof(float *));
+    for (int l = 0; l < c->n_layers; l++) {
+        size_t b = sizeof(float) * (size_t)c->max_seq * c->kv_dim;
+        c->k[l] = (float *)malloc(b);
+        c->v[l] = (float *)malloc(b);
+        memcpy(c->k[l], src->k[l], b);
+        memcpy(c->v[l], src->v[l], b);
+    }
+    return c;
+}
+
+void orc_cache_truncate(orc_cache *c, int len) {
+    /* Sets the pub seq_len field of every LlamaLayerKvCache (kv_cache.rs:75):
+     * later appends overwrite rows from len on. */
+    if (len >= 0 && len <= c->seq_len) c->seq_len = len;
+}
+
+int orc_cache_len(const orc_cache *c) { return c->seq_len; }
+
+void orc_cache_fill(orc_cache *c, int len, uint64_t seed) {
+    /* Rows 0..len-1 of every layer's K and V set to values uniform in
+     * [-1, 1] (bf16-rounded for a bf16 cache), as if len positions had been
+     * decoded: a context of that length for timing the CPU path. */
+    if (len < 0 || len > c->max_seq) return;
+    for (int l = 0; l < c->n_layers; l++) {
+        size_t cnt = (size_t)len * c->kv_dim;
+        uint64_t off = (uint64_t)l * 2 * (uint64_t)c->max_seq * c->kv_dim;
+#pragma omp parallel for schedule(static)
+        for (size_t i = 0; i < cnt; i++) {
+            float kv = (float)(bits_to_unit_f64(orc_hash(seed, off + i)) * 2.0 - 1.0);
+            float vv = (float)(bits_to_unit_f64(orc_hash(seed, off + cnt + i)) * 2.0 - 1.0);
+            c->k[l][i] = c->kv_bf16 ? round_bf16(kv) : kv;
+            c->v[l][i] = c->kv_bf16 ? round_bf16(vv) : vv;
+        }
+    }
+    c->seq_len = len;
 }
 
 void orc_generate_greedy(const orc_llama *m, const int *prompt, int n_prompt, int max_tokens,

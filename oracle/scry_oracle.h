@@ -109,6 +109,9 @@ enum { ORC_QKV = 0, ORC_O = 1, ORC_GATE = 2, ORC_UP = 3, ORC_DOWN = 4 };
  * quantize_symmetric -- the fused qkv_proj as one tensor, o/gate/up/down and
  * the lm_head ([V,h], per-tensor scale) each as one tensor. */
 orc_llama *orc_llama_new_random(const orc_config *cfg, uint64_t seed);
+/* A model of the given shape with seeded uniform int8 weights, for timing
+ * the CPU path only (no parity meaning). */
+orc_llama *orc_llama_new_uniform(const orc_config *cfg, uint64_t seed);
 /* Quantize an f32 model given tensor by tensor (same layout as llama.rs). */
 orc_llama *orc_llama_new_empty(const orc_config *cfg);
 void orc_llama_free(orc_llama *m);
@@ -128,6 +131,17 @@ void orc_cache_free(orc_cache *c);
  * non-NULL it receives the residual stream after every layer [n_layers, h]. */
 void orc_forward_with_cache(const orc_llama *m, orc_cache *c, int token, int pos, float *logits,
                             float *trace);
+/* n consecutive forward_with_cache calls (tokens[i] at position pos0 + i)
+ * evaluated layer by layer for all n tokens; bit-identical logits and cache.
+ * logits_all [n, V] and logits_last [V] are optional. */
+void orc_forward_tokens(const orc_llama *m, orc_cache *c, const int *tokens, int n, int pos0,
+                        float *logits_all, float *logits_last);
+/* Deep copy of a cache; truncation to len cached positions; its length. */
+orc_cache *orc_cache_clone(const orc_cache *src);
+void orc_cache_truncate(orc_cache *c, int len);
+int orc_cache_len(const orc_cache *c);
+/* Fill rows 0..len-1 with seeded values and set the length (timing only). */
+void orc_cache_fill(orc_cache *c, int len, uint64_t seed);
 /* generate (generate.rs:51-89) with temperature 0 (greedy). */
 void orc_generate_greedy(const orc_llama *m, const int *prompt, int n_prompt, int max_tokens,
                          int kv_bf16, int *out_tokens);

@@ -308,3 +308,26 @@ def test_kv_bf16_variant_close_to_f32():
         a = m.forward_with_cache(c32, tok, pos)
         b = m.forward_with_cache(c16, tok, pos)
         assert np.abs(a - b).max() / np.abs(a).max() < 2e-2
+
+
+def test_forward_tokens_equals_token_by_token_loop():
+    # orc_forward_tokens (test infrastructure for long prompts) must give the
+    # logits and cache of consecutive forward_with_cache calls bit for bit,
+    # also when continuing a cache; clone + truncate rewinds a sequence.
+    cfg = O.make_config(512, 256, 192, 2, 4, 2, 96, 1e-5, 10000.0, False)
+    om = O.OracleLlama(cfg, 4)
+    toks = O.prompt_ids(9, 60, cfg.vocab_size)
+    seq = om.new_cache(96, kv_bf16=True)
+    ref = np.stack([om.forward_with_cache(seq, int(t), p) for p, t in enumerate(toks)])
+    bat = om.new_cache(96, kv_bf16=True)
+    got = np.concatenate([om.forward_tokens(bat, toks[:25], 0, all_logits=True),
+                          om.forward_tokens(bat, toks[25:], 25, all_logits=True)])
+    assert np.array_equal(got, ref)
+    assert len(bat) == 60
+    assert np.array_equal(om.forward_tokens(om.new_cache(96), toks[:7], 0),
+                          om.forward_tokens(om.new_cache(96), toks[:7], 0, all_logits=True)[-1])
+    c = bat.clone()
+    c.truncate(40)
+    assert len(c) == 40 and len(bat) == 60
+    assert np.array_equal(om.forward_with_cache(c, int(toks[40]), 40), ref[40])
+    assert np.array_equal(om.forward_with_cache(bat, 5, 60), om.forward_with_cache(seq, 5, 60))

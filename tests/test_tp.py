@@ -146,11 +146,37 @@ def _tp_engine_worker(rank, size, tid, mode, out):
         out.put((rank, "error", traceback.format_exc(), None))
 
 
+VARYING_BATCHES = (64, 8, 64, 8, 1, 64, 1, 1, 64)
+
+
+def _varying_config():
+    # hidden 4096: every batched all-reduce of M >= 8 rows carries M*h >= 32768 values
+    return small_config(h=4096, layers=1, heads=32, kv=8, ffn=512, vocab=1024)
+
+
+def _varying_tokens(i, M):
+    return O.prompt_ids(500 + i, M, _varying_config().vocab_size)
+
+
 def _tp_engine_run(rank, size, tid, mode):
     import torch
 
     torch.cuda.set_device(rank)
     N.check(N.lib().sb_init(rank))
+    if mode == "varying":
+        # The batch size changes from step to step (64, 8, 1 rows), so the
+        # residual all-reduces alternate between large and small vectors; a
+        # cell left by an earlier all-reduce must never pass for this one's.
+        c = _varying_config()
+        om = O.OracleLlama(orc_config(c, 64), 6)
+        e = engine_from_oracle(om, c, max_seq=64, max_batch=64, kv_dtype="bf16", tp_rank=rank, tp_size=size,
+                               tp_id=tid)
+        outs = []
+        for i, M in enumerate(VARYING_BATCHES):
+            lg, _ = e.forward_batch(_varying_tokens(i, M).tolist(), [0] * M)
+            outs.append(lg)
+        e.close()
+        return rank, outs, None, None
     if mode == "oracle":
         c = _tp_config()
         om = O.OracleLlama(orc_config(c, 128), 5)
@@ -227,6 +253,50 @@ def test_tensor_parallel_engine_matches_oracle(mode, size):
         assert rel_err(lg, ref_lg) < 1e-3
     for r in range(1, size):
         assert np.array_equal(res[0][2], res[r][2])  # identical logits on every rank
+
+
+@pytest.mark.gpu
+def test_tensor_parallel_batch_size_changes_between_steps():
+    # 2 ranks; consecutive steps of 64, 8 and 1 rows (h 4096): every row's
+    # logits equal the unsharded oracle's (fresh sequence, position 0) within
+    # the f32 bar on both ranks, with identical bits on the two ranks.
+    import torch
+    import torch.multiprocessing as mp
+
+    size = 2
+    if torch.cuda.device_count() < size:
+        pytest.skip(f"needs {size} GPUs")
+    from esolearn_b200 import tp_unique_id
+
+    tid = tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_engine_worker, args=(r, size, tid, "varying", q), daemon=True)
+             for r in range(size)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(size):
+            r, outs, err, _ = q.get(timeout=300)
+            assert not (isinstance(outs, str) and outs == "error"), f"rank {r}:\n{err}"
+            res[r] = outs
+        for p in procs:
+            p.join(60)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    c = _varying_config()
+    om = O.OracleLlama(orc_config(c, 64), 6)
+    memo = {}
+    for i, M in enumerate(VARYING_BATCHES):
+        for b, t in enumerate(_varying_tokens(i, M).tolist()):
+            if t not in memo:
+                memo[t] = om.forward_with_cache(om.new_cache(4, kv_bf16=True), t, 0)
+            assert rel_err(res[0][i][b], memo[t]) < 1e-3, (i, M, b)
+            assert np.array_equal(res[0][i][b], res[1][i][b]), (i, M, b)
 
 
 @pytest.mark.gpu
