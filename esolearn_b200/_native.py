@@ -61,6 +61,12 @@ SIGNATURES = {
     "sb_qweight_destroy": (C.c_int, [vp]),
     "sb_matmul_i8_f32": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp]),
     "sb_matmul_i8_f32_bias": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
+    "sb_i8_from_vec": (C.c_int, [vp, C.c_size_t, C.POINTER(vp)]),
+    "sb_i8_to_vec": (C.c_int, [vp, vp, C.c_size_t]),
+    "sb_i8_len": (C.c_int, [vp, C.POINTER(C.c_size_t)]),
+    "sb_i8_destroy": (C.c_int, [vp]),
+    "sb_i8_matmul_f32": (C.c_int, [vp, vp, C.c_float, C.c_int, C.c_int, C.c_int, vp, vp]),
+    "sb_i8_matmul_f32_bias": (C.c_int, [vp, vp, C.c_float, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "sb_rmsnorm": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_float, vp, vp]),
     "sb_rope_with_freqs": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sb_swiglu": (C.c_int, [vp, vp, C.c_size_t, vp, vp]),
@@ -83,6 +89,7 @@ SIGNATURES = {
     "sb_llama_load_f32": (C.c_int, [vp, C.c_int, C.c_int, vp]),
     "sb_llama_reset": (C.c_int, [vp]),
     "sb_llama_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
+    "sb_llama_forward_seq": (C.c_int, [vp, vp, C.c_int, vp]),
     "sb_llama_sample": (C.c_int, [vp, C.c_int, C.c_float, C.c_int, C.c_float, vp, vp]),
     "sb_llama_generate_greedy": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, vp]),
     "sb_llama_set_trace": (C.c_int, [vp, C.c_int]),

@@ -109,6 +109,21 @@ struct sb_qweight {
     bool loaded = false;
 };
 
+// I8Storage as the reference's backends hand it over: the int8 bytes of a
+// weight with no shape (i8_from_vec(Vec<i8>), backend/mod.rs:18).  The bytes
+// stay on the device as given; the first matmul_i8_f32 on the storage learns
+// its [k, n] shape and packs a copy into 128-column tiles (the layout both the
+// GEMV and the tensor-core GEMM stream), which later calls with that shape
+// reuse.  The scale travels with every call, as in the reference trait.
+struct sb_i8 {
+    int8_t *raw = nullptr;
+    size_t n = 0;
+    std::mutex mu;             // guards the packed copy (clones share the storage)
+    uint4 *packed = nullptr;   // [k, n] packed, or nullptr
+    int pk = 0, pn = 0;        // its shape
+    int dev = -1;              // device of the bytes
+};
+
 extern "C" {
 
 int sb_last_error(char *buf, size_t len) {
@@ -273,13 +288,49 @@ sb_status sb_qweight_destroy(sb_qweight *w) {
     return SB_OK;
 }
 
+// The packed copy of storage b for a [k, n] view, made on first use.
+static sb_status i8_packed(sb_i8 *b, int k, int n, cudaStream_t st, QWeightDesc *d) {
+    std::lock_guard<std::mutex> lock(b->mu);
+    if (!b->packed || b->pk != k || b->pn != n) {
+        const size_t bytes = qweight_bytes(k, n, 128);
+        uint4 *p = nullptr;
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(SB_ERR_OOM, "matmul_i8_f32: packing a [%d, %d] weight: %s", k, n, cudaGetErrorString(e));
+        }
+        const int rc = qweight_pack(b->raw, k, n, 128, 0, 0, p, st);
+        if (rc != SB_OK) {
+            cudaFree(p);
+            return rc;
+        }
+        if (b->packed) {
+            // an earlier view of these bytes: its kernels were queued on some
+            // stream before this call; let them finish before freeing
+            SB_CUDA_TRY(cudaDeviceSynchronize());
+            cudaFree(b->packed);
+        }
+        b->packed = p;
+        b->pk = k;
+        b->pn = n;
+    }
+    d->w = b->packed;
+    d->K = k;
+    d->N = n;
+    d->KS = ceil_div(k, 16);
+    d->TN = 128;
+    d->ntiles = ceil_div(n, 128);
+    d->group = 0;
+    return SB_OK;
+}
+
 // Rows [0, M) of a through the tensor-core GEMM (5-64 rows per launch).
-static sb_status qgemm_rows(const sb_qweight *w, const void *a, bool bf16, int M, const float *bias, float *c,
+static sb_status qgemm_rows(const QWeightDesc &wd, const void *a, bool bf16, int M, const float *bias, float *c,
                             cudaStream_t stream) {
     // scratch = planes, column sums, row exponents
     QGemmWs ws;
-    ws.ld_acc = w->d.ntiles * 128;
-    const size_t pb = align_up(qgemm_planes_bytes(w->d.K, M), 256);
+    ws.ld_acc = wd.ntiles * 128;
+    const size_t pb = align_up(qgemm_planes_bytes(wd.K, M), 256);
     void *base = nullptr, *sums = nullptr;
     // planes, then rstd[QGM_MAX_M] doubles, then shift[QGM_MAX_M] ints
     const size_t rb = sizeof(double) * QGM_MAX_M, sb = sizeof(int) * QGM_MAX_M;
@@ -291,52 +342,57 @@ static sb_status qgemm_rows(const sb_qweight *w, const void *a, bool bf16, int M
     ws.rstd = reinterpret_cast<double *>(b + pb);
     ws.shift = reinterpret_cast<int *>(b + pb + rb);
     QGemvArgs g;
-    g.w = w->d;
+    g.w = wd;
     g.M = M;
     g.x = a;
-    g.ldx = w->d.K;
+    g.ldx = wd.K;
     g.x_bf16 = bf16;
     g.out = c;
-    g.ldo = w->d.N;
+    g.ldo = wd.N;
     g.bias = bias;
     return qgemm_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, stream, false);
 }
 
-static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, int M, const float *bias, float *c,
+static sb_status matmul_desc(const QWeightDesc &wd, const void *a, int a_dtype, int M, const float *bias, float *c,
                              void *stream) {
-    SB_CHECK(w && a && c, SB_ERR_ARG, "sb_matmul_i8_f32: null argument");
-    SB_CHECK(w->loaded, SB_ERR_STATE, "sb_matmul_i8_f32: weight not loaded");
     SB_CHECK(a_dtype == SB_DTYPE_F32 || a_dtype == SB_DTYPE_BF16, SB_ERR_ARG, "bad activation dtype %d", a_dtype);
     SB_CHECK(M >= 0, SB_ERR_ARG, "M < 0");
     const size_t esz = a_dtype == SB_DTYPE_BF16 ? 2 : 4;
     const bool bf16 = a_dtype == SB_DTYPE_BF16;
     const cudaStream_t st = (cudaStream_t)stream;
-    if (qgemm_supported(w->d, M)) return qgemm_rows(w, a, bf16, M, bias, c, st);
-    if (M > QGM_MAX_M && qgemm_supported(w->d, QGM_MAX_M)) {
+    if (qgemm_supported(wd, M)) return qgemm_rows(wd, a, bf16, M, bias, c, st);
+    if (M > QGM_MAX_M && qgemm_supported(wd, QGM_MAX_M)) {
         // More than 64 rows: balanced chunks of 33-64 rows, one GEMM each, in
         // stream order (each chunk's finish kernel clears the shared sums).
         // Rows are independent, so the result equals the row-wise GEMVs.
         const int nc = (M + QGM_MAX_M - 1) / QGM_MAX_M;
         for (int i = 0; i < nc; i++) {
             const int r0 = (int)((long long)M * i / nc), r1 = (int)((long long)M * (i + 1) / nc);
-            SB_TRY(qgemm_rows(w, static_cast<const char *>(a) + (size_t)r0 * w->d.K * esz, bf16, r1 - r0, bias,
-                              c + (size_t)r0 * w->d.N, st));
+            SB_TRY(qgemm_rows(wd, static_cast<const char *>(a) + (size_t)r0 * wd.K * esz, bf16, r1 - r0, bias,
+                              c + (size_t)r0 * wd.N, st));
         }
         return SB_OK;
     }
     for (int r0 = 0; r0 < M; r0 += QG_MAX_M) {
         QGemvArgs g;
-        g.w = w->d;
+        g.w = wd;
         g.M = std::min(QG_MAX_M, M - r0);
-        g.x = (const char *)a + (size_t)r0 * w->d.K * esz;
-        g.ldx = w->d.K;
+        g.x = (const char *)a + (size_t)r0 * wd.K * esz;
+        g.ldx = wd.K;
         g.x_bf16 = bf16;
-        g.out = c + (size_t)r0 * w->d.N;
-        g.ldo = w->d.N;
+        g.out = c + (size_t)r0 * wd.N;
+        g.ldo = wd.N;
         g.bias = bias;
         SB_TRY(qgemv_launch(bias ? QEPI_BIAS : QEPI_STORE, g, st, false));
     }
     return SB_OK;
+}
+
+static sb_status matmul_impl(const sb_qweight *w, const void *a, int a_dtype, int M, const float *bias, float *c,
+                             void *stream) {
+    SB_CHECK(w && a && c, SB_ERR_ARG, "sb_matmul_i8_f32: null argument");
+    SB_CHECK(w->loaded, SB_ERR_STATE, "sb_matmul_i8_f32: weight not loaded");
+    return matmul_desc(w->d, a, a_dtype, M, bias, c, stream);
 }
 
 sb_status sb_matmul_i8_f32(const sb_qweight *w, const void *a, int a_dtype, int M, float *c, void *stream) {
@@ -347,6 +403,71 @@ sb_status sb_matmul_i8_f32_bias(const sb_qweight *w, const void *a, int a_dtype,
                                 void *stream) {
     SB_CHECK(bias, SB_ERR_ARG, "sb_matmul_i8_f32_bias: null bias");
     return matmul_impl(w, a, a_dtype, M, bias, c, stream);
+}
+
+sb_status sb_i8_from_vec(const int8_t *data, size_t n, sb_i8 **out) {
+    SB_CHECK(out && (data || n == 0), SB_ERR_ARG, "sb_i8_from_vec: null argument");
+    sb_i8 *b = new sb_i8();
+    b->n = n;
+    cudaGetDevice(&b->dev);
+    cudaError_t e = cudaMalloc(&b->raw, n ? n : 16);
+    if (e == cudaSuccess && n) e = cudaMemcpy(b->raw, data, n, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(b->raw);
+        delete b;
+        return set_error(SB_ERR_OOM, "sb_i8_from_vec(%zu bytes): %s", n, cudaGetErrorString(e));
+    }
+    *out = b;
+    return SB_OK;
+}
+
+sb_status sb_i8_to_vec(const sb_i8 *b, int8_t *data, size_t n) {
+    SB_CHECK(b && (data || n == 0), SB_ERR_ARG, "sb_i8_to_vec: null argument");
+    SB_CHECK(n == b->n, SB_ERR_SHAPE, "sb_i8_to_vec: storage holds %zu bytes, buffer %zu", b->n, n);
+    if (n) SB_CUDA_TRY(cudaMemcpy(data, b->raw, n, cudaMemcpyDeviceToHost));
+    return SB_OK;
+}
+
+sb_status sb_i8_len(const sb_i8 *b, size_t *n) {
+    SB_CHECK(b && n, SB_ERR_ARG, "sb_i8_len: null argument");
+    *n = b->n;
+    return SB_OK;
+}
+
+sb_status sb_i8_destroy(sb_i8 *b) {
+    if (!b) return SB_OK;
+    cudaFree(b->raw);
+    cudaFree(b->packed);
+    delete b;
+    return SB_OK;
+}
+
+static sb_status i8_matmul(const float *a, sb_i8 *b_q, float scale, const float *bias, int m, int k, int n, float *c,
+                           void *stream) {
+    SB_CHECK(b_q && (a || m == 0) && (c || m == 0), SB_ERR_ARG, "matmul_i8_f32: null argument");
+    SB_CHECK(m >= 0 && k > 0 && n > 0, SB_ERR_SHAPE, "matmul_i8_f32: m %d, k %d, n %d", m, k, n);
+    SB_CHECK((size_t)k * (size_t)n <= b_q->n, SB_ERR_SHAPE, "matmul_i8_f32: [%d, %d] view of a %zu-byte storage", k,
+             n, b_q->n);
+    int dev = 0;
+    SB_CUDA_TRY(cudaGetDevice(&dev));
+    SB_CHECK(dev == b_q->dev, SB_ERR_STATE, "matmul_i8_f32: storage lives on device %d, current device %d", b_q->dev,
+             dev);
+    if (m == 0) return SB_OK;
+    QWeightDesc d;
+    SB_TRY(i8_packed(b_q, k, n, (cudaStream_t)stream, &d));
+    d.scale = scale;
+    return matmul_desc(d, a, SB_DTYPE_F32, m, bias, c, stream);
+}
+
+sb_status sb_i8_matmul_f32(const float *a, sb_i8 *b_q, float scale, int m, int k, int n, float *c, void *stream) {
+    return i8_matmul(a, b_q, scale, nullptr, m, k, n, c, stream);
+}
+
+sb_status sb_i8_matmul_f32_bias(const float *a, sb_i8 *b_q, float scale, const float *bias, int m, int k, int n,
+                                float *c, void *stream) {
+    SB_CHECK(bias, SB_ERR_ARG, "matmul_i8_f32_bias: null bias");
+    return i8_matmul(a, b_q, scale, bias, m, k, n, c, stream);
 }
 
 sb_status sb_rmsnorm(const float *x, const float *w, int rows, int d, float eps, float *out, void *stream) {

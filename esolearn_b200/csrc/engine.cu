@@ -1160,6 +1160,67 @@ sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n
     return SB_OK;
 }
 
+sb_status sb_llama_forward_seq(sb_llama *m, const int32_t *tokens, int n, float *logits) {
+    SB_CHECK(m && tokens && logits, SB_ERR_ARG, "sb_llama_forward_seq: null argument");
+    SB_CHECK(n >= 1 && n <= m->cfg.max_seq_len, SB_ERR_SHAPE, "sb_llama_forward_seq: %d tokens, cache of %d", n,
+             m->cfg.max_seq_len);
+    for (int i = 0; i < n; i++)
+        SB_CHECK(tokens[i] >= 0 && tokens[i] < m->V, SB_ERR_ARG, "token %d outside vocab %d", tokens[i], m->V);
+    SB_TRY(check_ready(m));
+    const int C = m->B;  // positions per batched step
+    const int tail = n % C;
+    // capture the chunk shapes first (a capture's warm-up resets the state)
+    cudaGraphExec_t g_full = nullptr, g_tail = nullptr;
+    if (n >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full));
+    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail));
+    // every row of a chunk is a position of sequence 0: all rows use its pages
+    std::vector<int> pt((size_t)m->B * m->pps);
+    for (int r = 0; r < m->B; r++)
+        for (int i = 0; i < m->pps; i++) pt[(size_t)r * m->pps + i] = i;
+    SB_CUDA_TRY(cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->st));
+    std::vector<int32_t> tok(C), pos(C), zero(C, 0);
+    std::vector<float> gathered;
+    int rc = SB_OK;
+    for (int p0 = 0; p0 < n && rc == SB_OK; p0 += C) {
+        const int M = std::min(C, n - p0);
+        for (int r = 0; r < M; r++) tok[r] = tokens[p0 + r], pos[r] = p0 + r;
+        rc = set_state(m, M, tok.data(), pos.data(), zero.data());
+        if (rc != SB_OK) break;
+        if (M == 1 && m->ds_ok) {
+            rc = ds_step(m);
+        } else if (cudaGraphLaunch(M == C ? g_full : g_tail, m->st) != cudaSuccess) {
+            rc = set_error(SB_ERR_CUDA, "sb_llama_forward_seq: graph launch failed");
+        }
+        if (rc != SB_OK) break;
+        if (m->tp == 1) {
+            if (cudaMemcpyAsync(logits + (size_t)p0 * m->V, m->logits, sizeof(float) * (size_t)M * m->V,
+                                cudaMemcpyDeviceToHost, m->st) != cudaSuccess)
+                rc = set_error(SB_ERR_CUDA, "sb_llama_forward_seq: logits copy failed");
+        } else {
+            // every rank's vocabulary slice: [rank][row][Vl] -> host [row][V]
+            rc = tp_allgather32(m->comm, m->logits, m->logits_all, (size_t)M * m->Vl, m->st);
+            gathered.resize((size_t)M * m->V);
+            if (rc == SB_OK && cudaMemcpyAsync(gathered.data(), m->logits_all, sizeof(float) * gathered.size(),
+                                               cudaMemcpyDeviceToHost, m->st) != cudaSuccess)
+                rc = set_error(SB_ERR_CUDA, "sb_llama_forward_seq: logits copy failed");
+            if (rc == SB_OK && cudaStreamSynchronize(m->st) != cudaSuccess)
+                rc = set_error(SB_ERR_CUDA, "sb_llama_forward_seq: synchronize failed");
+            for (int t = 0; t < m->tp && rc == SB_OK; t++)
+                for (int b = 0; b < M; b++)
+                    std::memcpy(logits + (size_t)(p0 + b) * m->V + (size_t)t * m->Vl,
+                                gathered.data() + ((size_t)t * M + b) * m->Vl, sizeof(float) * m->Vl);
+        }
+    }
+    // sequences back on their own pages
+    for (int r = 0; r < m->B; r++)
+        for (int i = 0; i < m->pps; i++) pt[(size_t)r * m->pps + i] = r * m->pps + i;
+    SB_CUDA_TRY(cudaMemcpyAsync(m->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    SB_TRY(rc);
+    m->active = 0;
+    return check_device_errors(m);
+}
+
 sb_status sb_llama_step(sb_llama *m, int n_steps) {
     SB_CHECK(m && m->active > 0, SB_ERR_STATE, "sb_llama_step: call sb_llama_begin first");
     cudaGraphExec_t g = nullptr;

@@ -155,6 +155,64 @@ def matmul_i8_f32(a, w: QWeight, out=None, bias=None, stream: int = 0):
     return out
 
 
+class I8Storage:
+    """DeviceBackend::I8Storage (backend/mod.rs:15-21): int8 bytes on the
+    device with no shape, made by i8_from_vec.  Clones share the storage."""
+
+    def __init__(self, data):
+        d = np.ascontiguousarray(np.asarray(data, np.int8).ravel())
+        h = C.c_void_p()
+        N.check(N.lib().sb_i8_from_vec(_ptr(d), d.size, C.byref(h)))
+        self._h = h
+        self.n = d.size
+
+    def __len__(self) -> int:
+        return self.n
+
+    def __del__(self):
+        if getattr(self, "_h", None) and N._lib is not None:
+            N._lib.sb_i8_destroy(self._h)
+            self._h = None
+
+
+class B200Backend:
+    """The quantized part of MathBackend (backend/mod.rs) over this library,
+    with the reference trait's names and arguments: Storage is a torch CUDA
+    f32 tensor, I8Storage an I8Storage; every op returns a new tensor."""
+
+    @staticmethod
+    def i8_from_vec(data) -> I8Storage:
+        return I8Storage(data)
+
+    @staticmethod
+    def i8_to_vec(storage: I8Storage) -> np.ndarray:
+        out = np.empty(len(storage), np.int8)
+        N.check(N.lib().sb_i8_to_vec(storage._h, _ptr(out), out.size))
+        return out
+
+    @staticmethod
+    def matmul_i8_f32(a, b_q: I8Storage, scale: float, m: int, k: int, n: int, bias=None):
+        """backend/mod.rs:521-557: [m,k] f32 . dequant([k,n] int8, scale) (+ bias) -> [m,n] f32."""
+        import torch
+
+        assert a.is_cuda and a.dtype == torch.float32 and a.is_contiguous() and a.numel() == m * k
+        c = torch.empty((m, n), dtype=torch.float32, device=a.device)
+        st = C.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
+        if bias is None:
+            N.check(N.lib().sb_i8_matmul_f32(C.c_void_p(a.data_ptr()), b_q._h, float(scale), m, k, n,
+                                             C.c_void_p(c.data_ptr()), st))
+        else:
+            assert bias.is_cuda and bias.dtype == torch.float32 and bias.numel() == n
+            N.check(N.lib().sb_i8_matmul_f32_bias(C.c_void_p(a.data_ptr()), b_q._h, float(scale),
+                                                  C.c_void_p(bias.data_ptr()), m, k, n, C.c_void_p(c.data_ptr()),
+                                                  st))
+        return c
+
+    @staticmethod
+    def matmul_i8_f32_bias(a, b_q: I8Storage, scale: float, bias, m: int, k: int, n: int):
+        return B200Backend.matmul_i8_f32(a, b_q, scale, m, k, n, bias=bias)
+
+
 class QuantLinear:
     """nn::linear::Linear after quantize_weights() (linear.rs:9-13, 56-95), the
     W8A32 layer every other `quantize` consumer uses (GPT-2's Linear layers;
@@ -312,6 +370,15 @@ class QuantLlamaB200:
             raise N.SbError(4, f"cache of {max_seq} positions exceeds the engine's {self.max_seq}")
         N.check(N.lib().sb_llama_reset(self._h))
         return LlamaKvCacheHandle(self, max_seq)
+
+    def forward(self, token_ids: Sequence[int]) -> np.ndarray:
+        """CausalLM::forward (generate.rs:9, llama.rs:683-700): logits [seq, vocab]
+        of every position, as batched prefill chunks (sb_llama_forward_seq).
+        Overwrites sequence slot 0's cached positions."""
+        t = np.ascontiguousarray(token_ids, np.int32)
+        out = np.empty((t.size, self.config.vocab_size), np.float32)
+        N.check(N.lib().sb_llama_forward_seq(self._h, _ptr(t), t.size, _ptr(out)))
+        return out
 
     def forward_with_cache(self, token_id: int, pos: int, cache: LlamaKvCacheHandle) -> np.ndarray:
         """forward_with_llama_cache (llama.rs:744-763): logits [vocab] of one token."""

@@ -94,6 +94,33 @@ sb_status sb_matmul_i8_f32(const sb_qweight *w, const void *a, int a_dtype, int 
 sb_status sb_matmul_i8_f32_bias(const sb_qweight *w, const void *a, int a_dtype, int M,
                                 const float *bias, float *c, void *stream);
 
+/* ---- I8Storage exactly as the reference trait hands it over -------------
+ * DeviceBackend::i8_from_vec(data: Vec<i8>) -> I8Storage (backend/mod.rs:18)
+ * carries no shape, and MathBackend::matmul_i8_f32(a, b_q, scale, m, k, n)
+ * (backend/mod.rs:521-533) passes the scale and the [k, n] view with every
+ * call.  sb_i8 is that storage: the bytes are copied to the current device
+ * as given (row-major [k, n] in the reference layout, linear.rs:17); the
+ * first matmul on it with a given (k, n) packs a copy into 128-column tiles
+ * (the layout the GEMV and the tensor-core GEMM stream) and later calls with
+ * that view reuse it.  A storage may be shared by several owners (the
+ * trait's Clone), one call at a time. */
+typedef struct sb_i8 sb_i8;
+/* i8_from_vec (backend/mod.rs:18): n int8 values from host memory. */
+sb_status sb_i8_from_vec(const int8_t *data, size_t n, sb_i8 **out);
+/* i8_to_vec (backend/mod.rs:20): the n bytes back to host memory. */
+sb_status sb_i8_to_vec(const sb_i8 *b, int8_t *data, size_t n);
+sb_status sb_i8_len(const sb_i8 *b, size_t *n);
+sb_status sb_i8_destroy(sb_i8 *b);
+/* matmul_i8_f32 (backend/mod.rs:521-533; CPU cpu.rs:1129-1160):
+ * c[m,n] = a[m,k] . (b_q[k,n] * scale), f32 accumulate.  a, c: device f32
+ * (the Storage of the trait).  SB_ERR_SHAPE when k*n exceeds the storage.
+ * Same kernels and arithmetic as sb_matmul_i8_f32. */
+sb_status sb_i8_matmul_f32(const float *a, sb_i8 *b_q, float scale, int m, int k, int n, float *c,
+                           void *stream);
+/* matmul_i8_f32_bias (backend/mod.rs:537-557): c = a . dequant(b_q) + bias[n]. */
+sb_status sb_i8_matmul_f32_bias(const float *a, sb_i8 *b_q, float scale, const float *bias, int m,
+                                int k, int n, float *c, void *stream);
+
 /* ---- Llama ops of MathBackend (device pointers) ------------------------ */
 /* rmsnorm (backend/mod.rs rmsnorm; cpu.rs:574-599). */
 sb_status sb_rmsnorm(const float *x, const float *w, int rows, int d, float eps, float *out,
@@ -228,6 +255,13 @@ sb_status sb_llama_reset(sb_llama *m);
  * logits [batch, V] f32, argmax [batch] (ties -> last). */
 sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const int32_t *pos,
                            float *logits, int32_t *argmax);
+/* CausalLM::forward (generate.rs:9; LlamaModel::forward, llama.rs:683-700):
+ * logits [n, V] (host) of every position of the token sequence, run from
+ * position 0 as batched prefill chunks of max_batch positions (every
+ * projection of a chunk one tensor-core GEMM when max_batch >= 5).  Uses
+ * sequence slot 0's KV pages as its scratch: slot 0's cached positions are
+ * overwritten (other slots are untouched).  n <= max_seq_len. */
+sb_status sb_llama_forward_seq(sb_llama *m, const int32_t *tokens, int n, float *logits);
 /* sample_token (generate.rs:92-165) for each of the `batch` rows of logits
  * the last sb_llama_forward left on the device (see sb_sample_rows): only
  * the tokens come back to the host, not [batch, V] logits.  rng_state: host

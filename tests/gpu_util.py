@@ -40,3 +40,22 @@ def engine_from_oracle(om: O.OracleLlama, c: LlamaConfig, **kw) -> QuantLlamaB20
 
 def small_config(h=512, layers=2, heads=8, kv=8, ffn=1376, vocab=4096, theta=10000.0, tie=False, scaling=None):
     return LlamaConfig(vocab, h, ffn, layers, heads, kv, 4096, 1e-5, theta, tie, scaling)
+
+
+def greedy_agreement(got, ref, ref_logits, tol: float = 1e-3) -> int:
+    """Number of leading tokens of an engine greedy stream `got` that equal the
+    oracle's `ref`.  Every token must match, except where the oracle's own
+    logits at that step put the two tokens within `tol` x max|logit| of each
+    other (a near-tie that rounding at the logits tolerance may resolve either
+    way); the streams are compared up to that step only.  Raises if the streams
+    part anywhere else."""
+    got, ref = list(got), list(ref)
+    for j, (g, r) in enumerate(zip(got, ref)):
+        if g == r:
+            continue
+        lg = np.asarray(ref_logits[j], np.float64)
+        gap = abs(lg[r] - lg[g])
+        assert gap <= tol * np.abs(lg).max(), (
+            f"token {j}: engine {g}, oracle {r}, oracle logit gap {gap:.3e} > {tol} x max|logit|")
+        return j
+    return len(ref)

@@ -255,3 +255,23 @@ def test_capacity_and_argument_errors():
         e.forward_batch([1], [32])  # position beyond the cache
     # the engine still works afterwards
     assert e.generate_greedy(np.array([1, 2], np.int32), 4).shape == (1, 4)
+
+
+@pytest.mark.parametrize("max_batch,n", [(8, 37), (64, 150), (1, 12)])
+def test_full_sequence_forward_logits(max_batch, n):
+    # CausalLM::forward (generate.rs:9, llama.rs:683-700): logits [seq, V] of
+    # every position in one call, run as batched prefill chunks (tensor-core
+    # linears at 5+ rows; the persistent step at max_batch 1), against the
+    # oracle's per-position logits (bf16 cache on both sides).
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 256), 13)
+    e = engine_from_oracle(om, c, max_seq=256, max_batch=max_batch, kv_dtype="bf16")
+    toks = O.prompt_ids(77, n, c.vocab_size)
+    got = e.forward(toks)
+    ref = om.forward_tokens(om.new_cache(256, kv_bf16=True), toks, 0, all_logits=True)
+    assert got.shape == (n, c.vocab_size)
+    for p in range(n):
+        assert rel_err(got[p], ref[p]) < TOL_F32, p
+    # the engine decodes normally afterwards
+    prompt = O.prompt_ids(78, 6, c.vocab_size)
+    assert e.generate_greedy(prompt, 8)[0].tolist() == om.generate_greedy(prompt, 8, kv_bf16=True).tolist()

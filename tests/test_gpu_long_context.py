@@ -12,7 +12,11 @@ vocabulary, depth) and full-size where the kernels' work split depends on it
 hold them to the oracle (the reference decode, llama.rs:744-763, with every
 projection through matmul_i8_f32) with a bf16-rounded cache like the engine's:
 
-* greedy streams identical for 32 generated tokens on every row;
+* greedy streams identical for 32 generated tokens on every row -- except
+  at a step where the oracle's top two logits lie within the logits tolerance
+  of each other (a near-tie: 64 rows x 32 tokens of a random-init model meet
+  one now and then), where either token is accepted and the row is compared
+  up to that step only (gpu_util.greedy_agreement);
 * logits of every row within 1e-3 max relative error, each row at its own
   context length (rows rewound to different steps of their stream);
 * the attention plan the engine reports shows that the multi-split path ran.
@@ -28,7 +32,7 @@ import pytest
 import oracle as O
 from esolearn_b200 import LlamaConfig
 from esolearn_b200 import _native as N
-from tests.gpu_util import engine_from_oracle, orc_config, rel_err, small_config
+from tests.gpu_util import engine_from_oracle, greedy_agreement, orc_config, rel_err, small_config
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3  # f32 accumulate on both sides, same bf16 cache rounding
@@ -107,13 +111,15 @@ def test_long_context_batched_decode_matches_oracle(desc, cfg, B, n_prefix, n_ta
     # pages), then 31 batched decode steps of all B rows
     got = e.generate_greedy(prompts, n_gen, batched_prefill=True)
     ref, ref_logits = _streams(om, prefix, tails, n_gen, max_seq)
-    for b in range(B):
-        assert got[b].tolist() == ref[b].tolist(), (desc, b)
-    steps = [(7 * b + 3) % n_gen for b in range(B)]
+    agree = [greedy_agreement(got[b], ref[b], ref_logits[b], TOL) for b in range(B)]
+    assert sum(a == n_gen for a in agree) >= B - 2, agree  # near-ties are rare
+    # a step's inputs are equal on both sides up to the first disagreement
+    steps = [min((7 * b + 3) % n_gen, agree[b]) for b in range(B)]
     lg, am = _rewound_logits(e, prompts, got, steps)
     for b in range(B):
         assert rel_err(lg[b], ref_logits[b][steps[b]]) < TOL, (desc, b, steps[b])
-        assert int(am[b]) == int(ref[b][steps[b]]), (desc, b)
+        if steps[b] < agree[b]:
+            assert int(am[b]) == int(ref[b][steps[b]]), (desc, b)
 
 
 @pytest.mark.parametrize("rep", [4, 8])
@@ -132,7 +138,7 @@ def test_long_context_persistent_step_gqa(rep):
     prompt = np.concatenate([prefix, tails[0]]).astype(np.int32)
     got = e.generate_greedy(prompt, 32)[0]
     ref, ref_logits = _streams(om, prefix, tails, 32, max_seq)
-    assert got.tolist() == ref[0].tolist()
+    assert greedy_agreement(got, ref[0], ref_logits[0], TOL) == 32
     for j in (0, 17, 31):
         lg, _ = _rewound_logits(e, prompt[None, :], got[None, :], [j])
         assert rel_err(lg[0], ref_logits[0][j]) < TOL, j
@@ -152,7 +158,7 @@ def test_seven_b_shape_persistent_step_nine_chunks_per_layer():
     assert -(-(len(prompt) + 1) // chunk) >= 9
     got = e.generate_greedy(prompt, 32)[0]
     ref, ref_logits = _streams(om, prompt[:-1], prompt[None, -1:], 32, max_seq)
-    assert got.tolist() == ref[0].tolist()
+    assert greedy_agreement(got, ref[0], ref_logits[0], TOL) == 32
     for j in (0, 31):
         lg, _ = _rewound_logits(e, prompt[None, :], got[None, :], [j])
         assert rel_err(lg[0], ref_logits[0][j]) < TOL, j
@@ -179,9 +185,9 @@ def test_seventy_b_head_layout_one_layer(B):
     prompts = np.stack([O.prompt_ids(4000 + b, n_prompt, cfg.vocab_size) for b in range(B)])
     got = e.generate_greedy(prompts, 8, batched_prefill=B > 1)
     ref, ref_logits = _streams(om, np.zeros(0, np.int32), prompts, 8, max_seq)
-    for b in range(B):
-        assert got[b].tolist() == ref[b].tolist(), b
-    steps = [(3 * b + 1) % 8 for b in range(B)]
+    agree = [greedy_agreement(got[b], ref[b], ref_logits[b], TOL) for b in range(B)]
+    assert sum(a == 8 for a in agree) >= B - 1, agree
+    steps = [min((3 * b + 1) % 8, agree[b]) for b in range(B)]
     lg, _ = _rewound_logits(e, prompts, got, steps)
     for b in range(B):
         assert rel_err(lg[b], ref_logits[b][steps[b]]) < TOL, (b, steps[b])

@@ -332,3 +332,30 @@ def test_paged_gqa_decode_attention(kv_dtype, n_q, n_kv, hd):
     got = out.cpu().numpy()
     for b in range(B):
         assert rel_err(got[b], refs[b]) < 1e-5, b
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 64, 100])
+def test_i8_storage_matmul_as_the_reference_trait_calls_it(m):
+    # MathBackend::matmul_i8_f32(a, b_q, scale, m, k, n) (backend/mod.rs:521-533)
+    # with b_q from i8_from_vec(Vec<i8>) -- no shape until the call -- and the
+    # scale passed per call; the _bias form adds bias[n] (mod.rs:537-557).
+    from esolearn_b200 import B200Backend
+
+    rng = np.random.default_rng(m)
+    k, n = 512, 384
+    q = rng.integers(-127, 128, (k, n), dtype=np.int8)
+    b_q = B200Backend.i8_from_vec(q.ravel())
+    assert np.array_equal(B200Backend.i8_to_vec(b_q), q.ravel())
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    for scale in (np.float32(0.0123), np.float32(0.5)):
+        got = B200Backend.matmul_i8_f32(dev(a), b_q, scale, m, k, n).cpu().numpy()
+        assert rel_err(got, O.matmul_i8_f32(a, q, scale, m, k, n)) < 2e-5
+        gb = B200Backend.matmul_i8_f32_bias(dev(a), b_q, scale, dev(bias), m, k, n).cpu().numpy()
+        assert rel_err(gb, O.matmul_i8_f32(a, q, scale, m, k, n) + bias[None, :]) < 2e-5
+    # another view of the same bytes (the storage has no shape of its own)
+    q2 = q.ravel()[: 256 * 768].reshape(256, 768)
+    got2 = B200Backend.matmul_i8_f32(dev(np.ascontiguousarray(a[:, :256])), b_q, np.float32(0.02), m, 256, 768)
+    assert rel_err(got2.cpu().numpy(), O.matmul_i8_f32(a[:, :256], q2, np.float32(0.02), m, 256, 768)) < 2e-5
+    with pytest.raises(N.SbError):  # a view larger than the storage
+        B200Backend.matmul_i8_f32(dev(a), b_q, np.float32(1.0), m, k, n + 1)
