@@ -102,6 +102,8 @@ SIGNATURES = {
     "sb_llama_step_bytes": (C.c_int, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "sb_llama_step_launches": (C.c_int, [vp, C.c_int, i32p]),
     "sb_llama_attn_plan": (C.c_int, [vp, C.c_int, i32p, i32p, i32p]),
+    "sb_llama_set_timeline": (C.c_int, [vp, C.c_int]),
+    "sb_llama_get_timeline": (C.c_int, [vp, vp, C.c_size_t, i32p, i32p]),
 }
 
 _lib = None

@@ -23,25 +23,27 @@ constexpr int DS_QMAX_F = 16;  // ... for the SwiGLU row of width F (<= 16384)
 constexpr int DS_MAX_NST = 16;
 
 struct DsSmem {
-    size_t ring, pa, red, qs, kvnew, bars, total;
+    size_t ring, pa, qs, kvnew, bars, total;
 };
 
-// pa: the fixed-point planes of a GEMV input; during attention, the
+// pa: the fixed-point planes of a GEMV input (the tensor cores' B operand);
+// during attention, the
 // cross-warp reduction of the per-head outputs; in the attention-combine
 // input stage, the table of partial-record weights (mtab bytes).
 __host__ __device__ inline DsSmem ds_layout(int nst, int ksmax, int rep, int hd, int chunk, int mtab) {
     DsSmem L;
     L.ring = 0;
     L.pa = (size_t)nst * DS_STAGE;
-    size_t pa = (size_t)48 * ksmax;
+    // planes: (ksmax + 1) k-steps of 48 bytes; the MMA's B descriptor reads
+    // up to 304 bytes past a k-step's start (rows it ignores)
+    size_t pa = (size_t)48 * (ksmax + 1) + 320;
     const size_t att_red = (size_t)8 * rep * (hd + 2) * 4;
     if (att_red > pa) pa = att_red;
     if ((size_t)mtab > pa) pa = (size_t)mtab;
-    L.red = L.pa + ((pa + 127) & ~(size_t)127);
-    L.qs = L.red + (size_t)8 * DS_TN * 8;
+    L.qs = L.pa + ((pa + 127) & ~(size_t)127);
     L.kvnew = L.qs + (size_t)rep * hd * 4;
     L.bars = L.kvnew + (size_t)2 * hd * 4;
-    L.total = L.bars + (size_t)2 * nst * 8;
+    L.total = L.bars + (size_t)(2 * nst + 5) * 8;  // full[nst], empty[nst], tmem full[2], tmem empty[2], done
     return L;
 }
 
@@ -83,6 +85,7 @@ struct DsArgs {
     int *cand_idx = nullptr;
     unsigned *sync = nullptr;   // [0] phase arrivals, [1] exits, [2] abort flag (zeroed by the host)
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
+    unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][3] (%globaltimer ns)
     int nst = 0;                // ring stages
     int mtab_bytes = 0;         // attention-combine table (ds_mtab_bytes)
 };

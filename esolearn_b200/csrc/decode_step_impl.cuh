@@ -13,6 +13,7 @@
 #include <algorithm>
 
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
 
 namespace sb {
 namespace {
@@ -28,6 +29,7 @@ struct DsShared {
     int shift;
     int abort;  // a bounded wait ran out: skip the rest of the step
     int last;
+    uint32_t tmem;  // base of this CTA's tensor-memory accumulators
 };
 __shared__ DsShared ds_sh;
 
@@ -137,6 +139,13 @@ __device__ __forceinline__ void ds_quantize(const float4 (&v)[QMAX], float ssq, 
         ds_sh.shift = s2 < -126 ? -126 : (s2 > 126 ? 126 : s2);
     }
     ds_sync();
+    // Planes for the tensor cores: k-step-major [KS + 1][3 digits][16 bytes]
+    // (the MMA's B operand, 3 rows of 16 k per k-step, 48 bytes apart), the
+    // last k-step all zero (an odd k-step count ends on it).  Each fixed-point
+    // value A (|A| <= 2^22) is written as signed base-256 digits
+    // A = d0 + 2^8 d1 + 2^16 d2 with d0, d1 in [-128, 127] and |d2| <= 65, so
+    // every plane is an s8 operand and sum_k w*A = D0 + 2^8 D1 + 2^16 D2
+    // exactly (each |D| <= K * 127 * 128 < 2^31).
     uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
     const float sc = __int_as_float((ds_sh.shift + 127) << 23);  // 2^shift, exact
 #pragma unroll
@@ -150,14 +159,21 @@ __device__ __forceinline__ void ds_quantize(const float4 (&v)[QMAX], float ssq, 
             // round to nearest even: |t| < 2^22, so t + 1.5*2^23 has ulp 1
             const float t = __fmul_rn(xs4[i], sc);
             const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
-            w0 |= (uint32_t)(A & 0xff) << (8 * i);
-            w1 |= (uint32_t)((A >> 8) & 0xff) << (8 * i);
-            w2 |= (uint32_t)((A >> 16) & 0xff) << (8 * i);
+            const int d0 = ((A + 128) & 0xff) - 128;
+            const int A1 = (A - d0) >> 8;
+            const int d1 = ((A1 + 128) & 0xff) - 128;
+            const int d2 = (A1 - d1) >> 8;
+            w0 |= (uint32_t)(d0 & 0xff) << (8 * i);
+            w1 |= (uint32_t)(d1 & 0xff) << (8 * i);
+            w2 |= (uint32_t)(d2 & 0xff) << (8 * i);
         }
-        planes[0 * nq + q] = w0;
-        planes[1 * nq + q] = w1;
-        planes[2 * nq + q] = w2;
+        uint32_t *pk = planes + (size_t)(q >> 2) * 12 + (q & 3);
+        pk[0] = w0;
+        pk[4] = w1;
+        pk[8] = w2;
     }
+    if (tid < 12) planes[(size_t)(nq >> 2) * 12 + tid] = 0u;  // the zero k-step after the last
+    fence_proxy_async_smem();  // the tensor core reads the planes
     ds_sync();
 }
 
@@ -373,72 +389,99 @@ struct DsWalk {
     }
 };
 
-// Consumes this CTA's stages of one GEMV and adds the exact column sums into
-// out.  Returns the updated count of consumed ring stages.
-__device__ __noinline__ uint32_t ds_gemv(uint32_t it, int nst, uint32_t bars, int KS, int ntiles, long long *out,
-                                         int G, int cta, uint32_t pa_off, uint32_t red_off) {
+// Consumes this CTA's stages of one GEMV on the tensor cores and adds the
+// exact column sums into out.  Warp 4's lane 0 issues, per ring stage, the
+// tcgen05.mma kind::i8 products of the stage's 128 weight columns (A, s8,
+// straight from the ring slot) with the input's three digit planes (B, s8)
+// into an int32 accumulator in TMEM (M = 128 columns, N = 16: rows 0-2 are the
+// digits, rows 3-15 read neighbouring planes and are ignored), and commits them
+// to the slot's "empty" barrier, so the slot is released once the tensor core
+// has read it.  At the end of the CTA's segment of a tile it commits to a
+// "TMEM full" barrier; warps 0-3 (TMEM lanes 0-127 = the tile's columns)
+// read the three digit sums, recombine them in int64 and add them to out.
+// Two accumulator buffers alternate by segment, so the drain of one overlaps
+// the products of the next.  `seg` counts segments over the whole step (it
+// drives the TMEM barriers' phases); every thread returns the updated stage
+// and segment counts.
+__device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst, uint32_t bars, int KS, int ntiles,
+                                         long long *out, int G, int cta, uint32_t pa_off) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    DsWalk wk(KS, ntiles, G, cta);
-    if (!wk.more()) return it;
-    const uint4 *ring4 = reinterpret_cast<const uint4 *>(ds_smem);
-    const uint4 *planes4 = reinterpret_cast<const uint4 *>(ds_smem + pa_off);
-    long long *red = reinterpret_cast<long long *>(ds_smem + red_off);
+    const uint32_t b_full = bars, b_empty = bars + 8 * nst, b_tfull = bars + 16 * nst, b_tempty = b_tfull + 16;
+    const uint32_t ring = smem_u32(ds_smem), planes = ring + pa_off, tmem = ds_sh.tmem;
     bool failed = ds_sh.abort != 0;
-    uint32_t slot = it % nst, par = (it / nst) & 1;
-    int acc[4][3];
-#pragma unroll
-    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = 0;
-    auto flush = [&](int t) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            red[warp * DS_TN + lane + 32 * j] = combine_planes(acc[j][0], acc[j][1], acc[j][2]);
-            acc[j][0] = acc[j][1] = acc[j][2] = 0;
+    if (warp == 4) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_i8(DS_TN, 16, 1, 1);
+            uint32_t slot = it % nst, par = (it / nst) & 1, seg = seg_io;
+            bool seg_start = true;
+            DsWalk wk(KS, ntiles, G, cta);
+            while (wk.more() && !failed) {
+                int t, k0, nks;
+                wk.next(t, k0, nks);
+                const bool seg_end = !wk.more() || wk.tile != t;
+                const uint32_t buf = seg & 1;
+                // the buffer's previous segment (seg - 2) has left TMEM
+                if (seg_start && seg >= 2 && !mbar_wait(b_tempty + 8 * buf, ((seg >> 1) - 1) & 1)) failed = true;
+                if (!failed && !mbar_wait(b_full + 8 * slot, par)) failed = true;
+                if (failed) break;
+                tc_fence_after();
+                const uint32_t a0 = ring + slot * DS_STAGE, acc = tmem + buf * 16;
+                for (int kk = 0; kk < (nks + 1) >> 1; kk++) {
+                    const uint64_t da = umma_sdesc(a0 + kk * 2 * DS_TN * 16, DS_TN * 16, 128);
+                    const uint64_t db = umma_sdesc(planes + (uint32_t)(k0 + 2 * kk) * 48, 48, 128);
+                    umma_i8(acc, da, db, idesc, (seg_start && kk == 0) ? 0u : 1u);
+                }
+                umma_commit(b_empty + 8 * slot);  // the slot is free once these products are done
+                seg_start = false;
+                if (seg_end) {
+                    umma_commit(b_tfull + 8 * buf);  // the segment's sums are complete in TMEM
+                    seg++;
+                    seg_start = true;
+                }
+                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+            }
+            if (failed) ds_sh.abort = 1;
         }
-        ds_sync();
-        if (tid < DS_TN && !failed) {
-            long long s = 0;
-#pragma unroll
-            for (int w = 0; w < DS_CONSUMERS / 32; w++) s += red[w * DS_TN + tid];
-            if (s != 0)
-                atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)t * DS_TN + tid), (unsigned long long)s);
+    } else if (warp < 4) {
+        uint32_t seg = seg_io;
+        DsWalk wk(KS, ntiles, G, cta);
+        while (wk.more() && !failed) {
+            int t, k0, nks;
+            wk.next(t, k0, nks);
+            if (wk.more() && wk.tile == t) continue;  // not the end of a tile segment
+            const uint32_t buf = seg & 1;
+            const bool ok = mbar_wait(b_tfull + 8 * buf, (seg >> 1) & 1);
+            if (__any_sync(0xffffffffu, !ok)) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            uint32_t d[4];
+            tmem_ld4(tmem + ((uint32_t)(warp * 32) << 16) + buf * 16, d);
+            tmem_wait_ld(d);
+            const long long sum =
+                (long long)(int)d[0] + ((long long)(int)d[1] << 8) + ((long long)(int)d[2] << 16);
+            if (sum != 0)
+                atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)t * DS_TN + warp * 32 + lane),
+                          (unsigned long long)sum);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the segment has left TMEM
+            seg++;
         }
-        ds_sync();
-    };
-    int cur = wk.tile;
+        if (failed && lane == 0) ds_sh.abort = 1;
+    }
+    // every thread advances the stage and segment counts by this GEMV's
+    uint32_t ns = 0, nseg = 0;
+    DsWalk wk(KS, ntiles, G, cta);
     while (wk.more()) {
         int t, k0, nks;
         wk.next(t, k0, nks);
-        if (t != cur) {
-            flush(cur);
-            cur = t;
-        }
-        if (!failed && !mbar_wait(bars + 8 * slot, par)) {
-            failed = true;
-            ds_sh.abort = 1;
-        }
-        if (!failed) {
-            const uint4 *wst = ring4 + (size_t)slot * (DS_STAGE / 16) + warp * DS_TN + lane;
-#pragma unroll
-            for (int kk = 0; kk < DS_KPS / 8; kk++) {
-                const int kl = warp + 8 * kk;
-                if (kl < nks) {
-                    const int ks = k0 + kl;
-                    uint4 w[4];
-#pragma unroll
-                    for (int j = 0; j < 4; j++) w[j] = wst[kk * 8 * DS_TN + 32 * j];
-                    const uint4 p0 = planes4[ks], p1 = planes4[KS + ks], p2 = planes4[2 * KS + ks];
-#pragma unroll
-                    for (int j = 0; j < 4; j++) dot16(w[j], p0, p1, p2, acc[j][0], acc[j][1], acc[j][2]);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
-        if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
-        it++;
+        ns++;
+        if (!wk.more() || wk.tile != t) nseg++;
     }
-    flush(cur);
-    return it;
+    seg_io += nseg;
+    return it + ns;
 }
 
 // ---- attention consumer -------------------------------------------------------
@@ -619,8 +662,8 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        ds_sync();  // every warp has read the slot
+        if (tid == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
         if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
         it++;
     }
@@ -641,22 +684,34 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     const int nst = a.nst;
     const int ksmax = max(max(a.ks_h, a.ks_q), a.ks_f);
     const DsSmem L = ds_layout(nst, ksmax, REP, HD, a.chunk, a.mtab_bytes);
-    const uint32_t bars = smem_u32(smem + L.bars);  // full[nst], empty[nst]
+    // full[nst], empty[nst], TMEM full[2], TMEM empty[2], MMA done
+    const uint32_t bars = smem_u32(smem + L.bars);
+    const uint32_t b_done = bars + 8 * (2 * nst + 4);
     const uint32_t ring = smem_u32(smem + L.ring);
     unsigned *const abort_flag = a.sync + 2;
 
     if (tid == 0) {
         for (int i = 0; i < nst; i++) {
             mbar_init(bars + 8 * i, 1);
-            mbar_init(bars + 8 * (nst + i), DS_CONSUMERS / 32);
+            // released by one arrival: the tensor core's commit (weights) or
+            // one thread after all warps read the slot (K/V rows)
+            mbar_init(bars + 8 * (nst + i), 1);
         }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bars + 8 * (2 * nst + i), 1);      // TMEM full: the issuer's commit
+            mbar_init(bars + 8 * (2 * nst + 2 + i), 4);  // TMEM empty: one arrival per draining warp
+        }
+        mbar_init(b_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         sh.abort = 0;
         sh.shift = 0;
         sh.rstd = 1.0;
         sh.last = 0;
     }
+    if (warp == 0) tmem_alloc(&sh.tmem, 32);  // two 16-column int32 accumulators
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
 
     // Step constants: the position decoded, the context and its KV chunks.
     const int pos = a.seq.pos[0];
@@ -730,11 +785,19 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
 
     // ---- consumers (warps 0-7)
     uint32_t it = 0;     // stages consumed; mirrors the producer's count
+    uint32_t seg = 0;    // tensor-core tile segments completed (TMEM barrier phases)
     unsigned phase = 0;  // phases completed by this CTA
 
+    // Optional timeline: %globaltimer at the start of phase p (after its
+    // barrier), after its input stage, and at its end (before the arrival),
+    // per CTA: stamps[(p * G + cta) * 3 + i].
+    auto mark = [&](int i) {
+        if (a.stamps && tid == 0) a.stamps[((size_t)phase * G + cta) * 3 + i] = global_ns();
+    };
     // Arrive at the end of the current phase.
     auto arrive = [&]() {
         ds_sync();
+        mark(2);
         // release at gpu scope: the CTA's writes (ordered before this thread by
         // the named barrier) are visible to whoever acquires the new count
         if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.sync), "r"(1u) : "memory");
@@ -766,6 +829,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         const bool go = !sh.abort;
         ds_sync();
         if (!go && tid == 0) atomicExch(abort_flag, 1u);
+        mark(0);
         return go;
     };
     // Zero this CTA's share of an int64 column-sum buffer (n columns).
@@ -792,7 +856,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     const int npad_qkv = a.nt_qkv * DS_TN, npad_o = a.nt_o * DS_TN, npad_gu = a.nt_gu * DS_TN,
               npad_down = a.nt_down * DS_TN, npad_lm = a.nt_lm * DS_TN;
     const bool writer = cta == 0;
-    const uint32_t pa_off = (uint32_t)L.pa, red_off = (uint32_t)L.red;
+    const uint32_t pa_off = (uint32_t)L.pa;
     const int rmax = G / a.nkv + 2;  // records per head: a head's units span at most this many CTAs
 
     // token of this step (embedding lookup, cpu.rs:485-498)
@@ -806,6 +870,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         ds_prefetch_l2(a.rope_cos + (size_t)rp * (HD / 2), sizeof(float) * (HD / 2), cta, G);
         ds_prefetch_l2(a.rope_sin + (size_t)rp * (HD / 2), sizeof(float) * (HD / 2), cta, G);
     }
+    mark(0);     // phase 0 starts with the kernel
     int xv = 0;  // index of the current residual version in a.x
     bool go = true;
     for (int l = 0; l < a.L; l++) {
@@ -826,12 +891,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                        (writer && a.trace) ? a.trace + (size_t)(l - 1) * a.h : nullptr, pa_off);
                 xv ^= 1;
             }
-            it = ds_gemv(it, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off, red_off);
+            mark(1);
+            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off);
         }
         arrive();
         // ---- attention
         if (go) go = wait_all();
-        if (go) attention(l);
+        if (go) {
+            mark(1);
+            attention(l);
+        }
         arrive();
         // ---- O: input = combined attention output
         ds_prefetch_l2(a.norm_post + (size_t)l * a.h, sizeof(float) * a.h, cta, G);
@@ -842,7 +911,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 ds_in_att<HD, REP, 4>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
             else
                 ds_in_att<HD, REP, DS_QMAX_H>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
-            it = ds_gemv(it, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off, red_off);
+            mark(1);
+            it = ds_gemv(it, seg, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off);
         }
         arrive();
         // ---- gate/up: input = RMSNorm(x + o)
@@ -853,12 +923,14 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                    a.norm_post + (size_t)l * a.h, a.h, a.ks_h, a.eps,
                                    writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
             xv ^= 1;
-            it = ds_gemv(it, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off, red_off);
+            mark(1);
+            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off);
         }
         arrive();
         // ---- SwiGLU (llama.rs:490-500), this CTA's share of the F outputs
         if (go) go = wait_all();
         if (go) {
+            mark(1);
             const long long *gu = accbuf(j + 2);
             const int f0 = (int)((long long)a.F * cta / G), f1 = (int)((long long)a.F * (cta + 1) / G);
             const double fg = gemv_factor(sh.shift, ly.scale[2], sh.rstd), fu = gemv_factor(sh.shift, ly.scale_up, sh.rstd);
@@ -877,7 +949,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) {
             zero_acc(accbuf(j + 1), npad_o);
             ds_in_rows<DS_QMAX_F>(a.act, false, nullptr, a.F, a.ks_f, a.eps, nullptr, pa_off);
-            it = ds_gemv(it, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off, red_off);
+            mark(1);
+            it = ds_gemv(it, seg, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off);
         }
         arrive();
     }
@@ -889,7 +962,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(jl - 1), a.layers[a.L - 1].scale[3], sh.shift, sh.rstd,
                                a.norm_final, a.h, a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
                                (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
-        it = ds_gemv(it, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off, red_off);
+        mark(1);
+        it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off);
     }
     arrive();
     // ---- logits and this CTA's argmax candidate (ties -> larger index,
@@ -962,6 +1036,15 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         a.sync[0] = 0;
         a.sync[1] = 0;
     }
+    // ---- release the tensor memory once no tensor-core work is in flight
+    if (warp == 4 && lane == 0) {
+        umma_commit(b_done);  // completes when every product this thread issued has
+        if (!mbar_wait(b_done, 0)) atomicExch(abort_flag, 1u);
+    }
+    tc_fence_before();
+    ds_sync();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(sh.tmem, 32);
 }
 
 template <int HD, int REP, typename KV>

@@ -117,6 +117,7 @@ struct sb_llama {
     float *ds_part = nullptr, *ds_cand_val = nullptr;
     int *ds_cand_idx = nullptr;
     unsigned *ds_sync = nullptr;
+    unsigned long long *ds_stamps = nullptr;  // timeline of the last step (sb_llama_set_timeline)
 
     // batched steps of 5-64 sequences: tensor-core linears and their scratch
     QGemmWs gws;
@@ -435,6 +436,7 @@ int ds_step(sb_llama *m) {
     a.trace = m->trace ? m->trace_buf : nullptr;
     a.nst = m->ds_nst;
     a.mtab_bytes = ds_mtab_bytes(m->nh, m->nkv);
+    a.stamps = m->ds_stamps;
     return ds_launch(a, m->nh / m->nkv, m->st);
 }
 
@@ -1299,6 +1301,31 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
         *launches = 5 + 13 * m->L;  // embed, 4 linears x 3 + attention per layer, lm_head x 3, argmax
     else
         *launches = 3 + 5 * m->L;  // embed, 5 per layer, lm_head, argmax
+    return SB_OK;
+}
+
+sb_status sb_llama_set_timeline(sb_llama *m, int enabled) {
+    SB_CHECK(m, SB_ERR_ARG, "sb_llama_set_timeline: null model");
+    SB_CHECK(m->ds_ok, SB_ERR_UNSUPPORTED, "sb_llama_set_timeline: this model does not run the persistent step");
+    if (enabled && !m->ds_stamps) {
+        const size_t n = (size_t)(6 * m->L + 2) * ds_grid() * 3;
+        SB_TRY(dalloc_t(m, &m->ds_stamps, n));
+    }
+    if (!enabled) m->ds_stamps = nullptr;  // the buffer stays in m->allocs until destroy
+    return SB_OK;
+}
+
+sb_status sb_llama_get_timeline(sb_llama *m, uint64_t *out, size_t cap, int *phases, int *ctas) {
+    SB_CHECK(m && phases && ctas, SB_ERR_ARG, "sb_llama_get_timeline: null argument");
+    SB_CHECK(m->ds_stamps, SB_ERR_STATE, "sb_llama_get_timeline: timeline not enabled");
+    *phases = 6 * m->L + 2;
+    *ctas = ds_grid();
+    const size_t n = (size_t)(*phases) * (*ctas) * 3;
+    if (out) {
+        SB_CHECK(cap >= n, SB_ERR_SHAPE, "sb_llama_get_timeline: %zu slots, %zu needed", cap, n);
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        SB_CUDA_TRY(cudaMemcpy(out, m->ds_stamps, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
+    }
     return SB_OK;
 }
 

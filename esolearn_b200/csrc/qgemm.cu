@@ -35,6 +35,7 @@
 #include <algorithm>
 
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
 
 namespace sb {
 
@@ -54,28 +55,8 @@ __host__ __device__ inline int qgm_ups(int np) { return np <= QGM_UPS2_NP ? 2 : 
 __host__ __device__ inline int qgm_wbytes(int np) { return qgm_ups(np) * QGM_UNIT_KS * QGM_TN * 16; }
 __host__ __device__ inline int qgm_slot_bytes(int np) { return qgm_wbytes(np) + qgm_ups(np) * QGM_UNIT_KS * np * 16; }
 
-// ---- tcgen05 helpers (cta_group::1) ------------------------------------------------
-__device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    // K-major, no swizzle: LBO = byte distance between 16-byte k chunks,
-    // SBO = byte distance between 8-row groups; descriptor version 1.
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
-}
 // kind::i8, signed A (weights), unsigned B (planes), s32 accumulate, both K-major.
-__device__ __forceinline__ uint32_t umma_idesc_i8(int n) {
-    return (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(QGM_TN >> 4) << 24);
-}
-__device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
-    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }" ::"r"(
-                     tmem),
-                 "l"(da), "l"(db), "r"(idesc), "r"(acc)
-                 : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ uint32_t qgm_idesc(int n) { return umma_idesc_i8(QGM_TN, n, 1, 0); }
 // The CTA's stages: units of 8 k-steps of a 128-column tile, tile-major,
 // CTA c takes [c*U/G, (c+1)*U/G), up to `ups` units of one tile per stage.
 struct QgmWalk {
@@ -248,24 +229,6 @@ __global__ void __launch_bounds__(QGM_PL_THREADS) qgm_planes_kernel(const QGemvA
 constexpr int QGM_DRAIN_LD = 7;
 constexpr int QGM_DRAIN_ROWS = 32;
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
-// Wait for this thread's tcgen05.ld results, then pass the registers
-// through an empty asm so no use of them can be scheduled before the wait
-// (the loads write their registers asynchronously).
-template <int N>
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&d)[N]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < N; i++) asm volatile("" : "+r"(d[i]));
-}
-
 __global__ void __launch_bounds__(QGM_THREADS, 1)
     qgm_gemm_kernel(const QWeightDesc w, const QGemmWs ws, int M, int np, int nst) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -339,7 +302,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
         // ---- MMA issuer
         if (lane == 0) {
             QgmWalk wk(w.KS, w.ntiles, G, cta, ups);
-            const uint32_t idesc = umma_idesc_i8(np);
+            const uint32_t idesc = qgm_idesc(np);
             uint32_t slot = 0, par = 0, seg = 0;
             bool seg_start = true, ok = true;
             while (wk.more() && ok) {

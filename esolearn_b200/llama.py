@@ -473,6 +473,18 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_attn_plan(self._h, batch, C.byref(s), C.byref(t), C.byref(c)))
         return s.value, bool(t.value), c.value
 
+    def set_timeline(self, on: bool):
+        """Record per-phase, per-CTA %globaltimer stamps in every later persistent step."""
+        N.check(N.lib().sb_llama_set_timeline(self._h, int(on)))
+
+    def timeline(self) -> np.ndarray:
+        """Stamps of the last persistent step: [phases, ctas, 3] ns (start, input done, end)."""
+        p, c = C.c_int32(), C.c_int32()
+        N.check(N.lib().sb_llama_get_timeline(self._h, None, 0, C.byref(p), C.byref(c)))
+        out = np.zeros((p.value, c.value, 3), np.uint64)
+        N.check(N.lib().sb_llama_get_timeline(self._h, _ptr(out), out.size, C.byref(p), C.byref(c)))
+        return out
+
     def step_bytes(self):
         w, kv = C.c_double(), C.c_double()
         N.check(N.lib().sb_llama_step_bytes(self._h, C.byref(w), C.byref(kv)))

@@ -14,6 +14,14 @@ before it captures the graph, so a profiler that should see decode steps at
 
     python -m esolearn_b200.profile_decode --ctx 584 --steps 2
     python -m esolearn_b200.profile_decode --shape llama3_8b_shape --batch 32 --layers 2 --ctx 2068
+    python -m esolearn_b200.profile_decode --ctx 584 --steps 4 --timeline
+
+--timeline (batch 1, persistent step) records the step kernel's per-phase
+%globaltimer stamps (sb_llama_set_timeline) in the last step and prints, per
+phase kind, the mean over layers of: the grid-barrier wait (a CTA's end of the
+previous phase to its start of this one, mean over CTAs), the input stage and
+the work (mean over CTAs), and the phase's span on the critical path (last
+arrival of the previous phase to last arrival of this one), in microseconds.
 """
 from __future__ import annotations
 
@@ -34,6 +42,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--timeline", action="store_true", help="per-phase timeline of the last persistent step")
     args = ap.parse_args(argv)
 
     cfg = getattr(LlamaConfig, args.shape)()
@@ -42,13 +51,49 @@ def main(argv=None):
     N.check(N.lib().sb_init(args.device))
     model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=args.ctx + args.steps + 8, max_batch=args.batch)
     B = args.batch
+    if args.timeline:
+        model.set_timeline(True)
     times = []
     for i in range(args.steps):
         t0 = time.perf_counter()
         model.forward_batch([1] * B, [args.ctx + i] * B, want_logits=False)
         times.append((time.perf_counter() - t0) * 1e3)
-    print(json.dumps({"shape": args.shape, "layers": cfg.n_layers, "batch": B, "ctx": args.ctx, "steps": args.steps,
-                      "launches_per_step": model.step_launches(B), "host_ms_per_call": times}))
+    out = {"shape": args.shape, "layers": cfg.n_layers, "batch": B, "ctx": args.ctx, "steps": args.steps,
+           "launches_per_step": model.step_launches(B), "host_ms_per_call": times}
+    if args.timeline:
+        out["timeline_us"] = timeline_summary(model.timeline(), cfg.n_layers)
+    print(json.dumps(out))
+
+
+PHASES = ("qkv", "attention", "o", "gate_up", "swiglu", "down")
+
+
+def timeline_summary(ts, n_layers: int) -> dict:
+    """Per-phase-kind means (us) of a step timeline [phases, ctas, 3] (ns)."""
+    import numpy as np
+
+    t = ts.astype(np.float64)
+    P = t.shape[0]
+    res = {}
+    kinds = [(k, [6 * l + i for l in range(n_layers)]) for i, k in enumerate(PHASES)]
+    kinds.append(("lm_head", [6 * n_layers]))
+    for name, idx in kinds:
+        wait, inp, work, span = [], [], [], []
+        for p in idx:
+            if p == 0 or p >= P:
+                continue
+            wait.append(np.mean(t[p, :, 0] - t[p - 1, :, 2]))
+            inp.append(np.mean(t[p, :, 1] - t[p, :, 0]))
+            work.append(np.mean(t[p, :, 2] - t[p, :, 1]))
+            span.append(np.max(t[p, :, 2]) - np.max(t[p - 1, :, 2]))
+        if span:
+            res[name] = {"barrier": np.mean(wait) / 1e3, "input": np.mean(inp) / 1e3, "work": np.mean(work) / 1e3,
+                         "span": np.mean(span) / 1e3}
+    first, last = t[0, :, 0].min(), t[6 * n_layers, :, 2].max()
+    res["layers_total"] = (t[6 * n_layers - 1, :, 2].max() - first) / 1e3
+    res["per_layer"] = res["layers_total"] / n_layers
+    res["step_to_lm_end"] = (last - first) / 1e3
+    return res
 
 
 if __name__ == "__main__":

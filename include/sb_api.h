@@ -315,6 +315,16 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches);
  * *splits = context splits per (sequence, kv head), *tensor_map = 1 when the
  * tensor-map kernel runs (then *chunk = 64, its tile), else 0. */
 sb_status sb_llama_attn_plan(sb_llama *m, int batch, int *splits, int *tensor_map, int *chunk);
+/* Timeline of the persistent batch-1 step (a profiling aid; no reference
+ * counterpart).  When enabled, every later step records, per phase p (6 per
+ * layer: qkv, attention, o, gate/up, SwiGLU, down; then lm_head and the
+ * argmax) and per CTA c, three %globaltimer readings in ns: the phase's start
+ * after its grid barrier, the end of its input stage, and its end before the
+ * arrival: out[(p * ctas + c) * 3 + i].  SB_ERR_UNSUPPORTED when the model
+ * does not run the persistent step.  get: *phases and *ctas always; out
+ * (cap slots) when non-NULL, for the last step. */
+sb_status sb_llama_set_timeline(sb_llama *m, int enabled);
+sb_status sb_llama_get_timeline(sb_llama *m, uint64_t *out, size_t cap, int *phases, int *ctas);
 
 #ifdef __cplusplus
 }
