@@ -21,9 +21,20 @@ constexpr int DS_KV_HALF = DS_STAGE / 2;         // bytes of K (and of V) per at
 constexpr int DS_QMAX_H = 8;   // input quads per consumer thread for rows of width h or q_dim (<= 8192)
 constexpr int DS_QMAX_F = 16;  // ... for the SwiGLU row of width F (<= 16384)
 constexpr int DS_MAX_NST = 16;
+constexpr int DS_STAMPS = 5;  // timeline readings per phase and CTA
+// GEMV products of the step on the tcgen05 tensor cores (true) or with dp4a
+// on the CUDA cores (false); the same exact integer sums either way.  Measured
+// on the 7B shape at context 584 (per layer): dp4a 66.7 us, tensor cores
+// 77.4 us -- a batch-1 stage is 8 MMAs of N = 16, and the issuer needs about
+// 1 us per 32 KB stage even with the stage resident, against ~0.4 us for the
+// eight dp4a warps; so the CUDA-core consumer is the default.
+constexpr bool DS_TC_GEMV = false;
+// Independent int32 accumulators (16 TMEM columns each) that consecutive
+// tensor-core products of a tile segment rotate over.
+constexpr int DS_NACC = 4;
 
 struct DsSmem {
-    size_t ring, pa, qs, kvnew, bars, total;
+    size_t ring, pa, red, qs, kvnew, bars, total;
 };
 
 // pa: the fixed-point planes of a GEMV input (the tensor cores' B operand);
@@ -40,7 +51,8 @@ __host__ __device__ inline DsSmem ds_layout(int nst, int ksmax, int rep, int hd,
     const size_t att_red = (size_t)8 * rep * (hd + 2) * 4;
     if (att_red > pa) pa = att_red;
     if ((size_t)mtab > pa) pa = (size_t)mtab;
-    L.qs = L.pa + ((pa + 127) & ~(size_t)127);
+    L.red = L.pa + ((pa + 127) & ~(size_t)127);
+    L.qs = L.red + (DS_TC_GEMV ? 0 : (size_t)8 * DS_TN * 8);  // CUDA-core consumer's reduction
     L.kvnew = L.qs + (size_t)rep * hd * 4;
     L.bars = L.kvnew + (size_t)2 * hd * 4;
     L.total = L.bars + (size_t)(2 * nst + 5) * 8;  // full[nst], empty[nst], tmem full[2], tmem empty[2], done
@@ -85,7 +97,7 @@ struct DsArgs {
     int *cand_idx = nullptr;
     unsigned *sync = nullptr;   // [0] phase arrivals, [1] exits, [2] abort flag (zeroed by the host)
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
-    unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][3] (%globaltimer ns)
+    unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
     int nst = 0;                // ring stages
     int mtab_bytes = 0;         // attention-combine table (ds_mtab_bytes)
 };

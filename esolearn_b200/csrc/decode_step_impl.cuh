@@ -403,8 +403,9 @@ struct DsWalk {
 // the products of the next.  `seg` counts segments over the whole step (it
 // drives the TMEM barriers' phases); every thread returns the updated stage
 // and segment counts.
-__device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst, uint32_t bars, int KS, int ntiles,
-                                         long long *out, int G, int cta, uint32_t pa_off) {
+__device__ __forceinline__ uint32_t ds_gemv_tc(uint32_t it, uint32_t &seg_io, int nst, uint32_t bars, int KS,
+                                                int ntiles, long long *out, int G, int cta, uint32_t pa_off,
+                                                unsigned long long *ready) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t b_full = bars, b_empty = bars + 8 * nst, b_tfull = bars + 16 * nst, b_tempty = b_tfull + 16;
     const uint32_t ring = smem_u32(ds_smem), planes = ring + pa_off, tmem = ds_sh.tmem;
@@ -414,6 +415,7 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
             const uint32_t idesc = umma_idesc_i8(DS_TN, 16, 1, 1);
             uint32_t slot = it % nst, par = (it / nst) & 1, seg = seg_io;
             bool seg_start = true;
+            int mi = 0;  // products issued in the current segment
             DsWalk wk(KS, ntiles, G, cta);
             while (wk.more() && !failed) {
                 int t, k0, nks;
@@ -424,12 +426,20 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
                 if (seg_start && seg >= 2 && !mbar_wait(b_tempty + 8 * buf, ((seg >> 1) - 1) & 1)) failed = true;
                 if (!failed && !mbar_wait(b_full + 8 * slot, par)) failed = true;
                 if (failed) break;
+                if (ready) {  // timeline: first and last weight stage ready
+                    const unsigned long long tn = global_ns();
+                    if (mi == 0 && seg == seg_io) ready[0] = tn;
+                    ready[1] = tn;
+                }
                 tc_fence_after();
-                const uint32_t a0 = ring + slot * DS_STAGE, acc = tmem + buf * 16;
-                for (int kk = 0; kk < (nks + 1) >> 1; kk++) {
+                const uint32_t a0 = ring + slot * DS_STAGE, acc = tmem + buf * (16 * DS_NACC);
+                for (int kk = 0; kk < (nks + 1) >> 1; kk++, mi++) {
                     const uint64_t da = umma_sdesc(a0 + kk * 2 * DS_TN * 16, DS_TN * 16, 128);
                     const uint64_t db = umma_sdesc(planes + (uint32_t)(k0 + 2 * kk) * 48, 48, 128);
-                    umma_i8(acc, da, db, idesc, (seg_start && kk == 0) ? 0u : 1u);
+                    // consecutive products go to independent accumulators, so
+                    // they need not wait on one another; product mi of the
+                    // segment starts accumulator mi when mi < DS_NACC
+                    umma_i8(acc + 16 * (mi % DS_NACC), da, db, idesc, mi < DS_NACC ? 0u : 1u);
                 }
                 umma_commit(b_empty + 8 * slot);  // the slot is free once these products are done
                 seg_start = false;
@@ -437,6 +447,7 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
                     umma_commit(b_tfull + 8 * buf);  // the segment's sums are complete in TMEM
                     seg++;
                     seg_start = true;
+                    mi = 0;
                 }
                 if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
             }
@@ -444,10 +455,12 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
         }
     } else if (warp < 4) {
         uint32_t seg = seg_io;
+        int nmma = 0;  // products of the current segment (the accumulators in use)
         DsWalk wk(KS, ntiles, G, cta);
         while (wk.more() && !failed) {
             int t, k0, nks;
             wk.next(t, k0, nks);
+            nmma += (nks + 1) >> 1;
             if (wk.more() && wk.tile == t) continue;  // not the end of a tile segment
             const uint32_t buf = seg & 1;
             const bool ok = mbar_wait(b_tfull + 8 * buf, (seg >> 1) & 1);
@@ -456,11 +469,18 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
                 break;
             }
             tc_fence_after();
-            uint32_t d[4];
-            tmem_ld4(tmem + ((uint32_t)(warp * 32) << 16) + buf * 16, d);
+            uint32_t d[4 * DS_NACC];
+            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16) + buf * (16 * DS_NACC);
+#pragma unroll
+            for (int j = 0; j < DS_NACC; j++) tmem_ld4(lb + 16 * j, d + 4 * j);
             tmem_wait_ld(d);
-            const long long sum =
-                (long long)(int)d[0] + ((long long)(int)d[1] << 8) + ((long long)(int)d[2] << 16);
+            long long sum = 0;
+#pragma unroll
+            for (int j = 0; j < DS_NACC; j++)
+                if (j < nmma)  // accumulators the segment never reached hold stale sums
+                    sum += (long long)(int)d[4 * j] + ((long long)(int)d[4 * j + 1] << 8) +
+                           ((long long)(int)d[4 * j + 2] << 16);
+            nmma = 0;
             if (sum != 0)
                 atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)t * DS_TN + warp * 32 + lane),
                           (unsigned long long)sum);
@@ -482,6 +502,108 @@ __device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg_io, int nst,
     }
     seg_io += nseg;
     return it + ns;
+}
+
+// The same products on the CUDA cores: 8 warps, each owning 4 columns x 1
+// k-step of a stage per pass, dp4a of the 16 int8 weights against the three
+// signed digit planes, int32 sums recombined in int64 per tile segment and
+// reduced over the warps in shared memory (red: [8 warps][128] int64).
+__device__ __forceinline__ void dot16s(const uint4 &w, const uint4 &p0, const uint4 &p1, const uint4 &p2, int &a0,
+                                       int &a1, int &a2) {
+    a0 = dp4a_ss(w.x, p0.x, a0);
+    a0 = dp4a_ss(w.y, p0.y, a0);
+    a0 = dp4a_ss(w.z, p0.z, a0);
+    a0 = dp4a_ss(w.w, p0.w, a0);
+    a1 = dp4a_ss(w.x, p1.x, a1);
+    a1 = dp4a_ss(w.y, p1.y, a1);
+    a1 = dp4a_ss(w.z, p1.z, a1);
+    a1 = dp4a_ss(w.w, p1.w, a1);
+    a2 = dp4a_ss(w.x, p2.x, a2);
+    a2 = dp4a_ss(w.y, p2.y, a2);
+    a2 = dp4a_ss(w.z, p2.z, a2);
+    a2 = dp4a_ss(w.w, p2.w, a2);
+}
+
+__device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t bars, int KS, int ntiles,
+                                                  long long *out, int G, int cta, uint32_t pa_off, uint32_t red_off,
+                                                  unsigned long long *ready) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    DsWalk wk(KS, ntiles, G, cta);
+    if (!wk.more()) return it;
+    const uint4 *ring4 = reinterpret_cast<const uint4 *>(ds_smem);
+    const uint4 *planes4 = reinterpret_cast<const uint4 *>(ds_smem + pa_off);
+    long long *red = reinterpret_cast<long long *>(ds_smem + red_off);
+    bool failed = ds_sh.abort != 0;
+    uint32_t slot = it % nst, par = (it / nst) & 1;
+    int acc[4][3];
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = 0;
+    auto flush = [&](int t) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            red[warp * DS_TN + lane + 32 * j] = combine_planes(acc[j][0], acc[j][1], acc[j][2]);
+            acc[j][0] = acc[j][1] = acc[j][2] = 0;
+        }
+        ds_sync();
+        if (tid < DS_TN && !failed) {
+            long long s = 0;
+#pragma unroll
+            for (int w = 0; w < DS_CONSUMERS / 32; w++) s += red[w * DS_TN + tid];
+            if (s != 0)
+                atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)t * DS_TN + tid), (unsigned long long)s);
+        }
+        ds_sync();
+    };
+    int cur = wk.tile;
+    bool first = true;
+    while (wk.more()) {
+        int t, k0, nks;
+        wk.next(t, k0, nks);
+        if (t != cur) {
+            flush(cur);
+            cur = t;
+        }
+        if (!failed && !mbar_wait(bars + 8 * slot, par)) {
+            failed = true;
+            ds_sh.abort = 1;
+        }
+        if (ready && tid == 0) {  // timeline: first and last weight stage ready
+            const unsigned long long tn = global_ns();
+            if (first) ready[0] = tn;
+            ready[1] = tn;
+        }
+        first = false;
+        if (!failed) {
+            const uint4 *wst = ring4 + (size_t)slot * (DS_STAGE / 16) + warp * DS_TN + lane;
+#pragma unroll
+            for (int kk = 0; kk < DS_KPS / 8; kk++) {
+                const int kl = warp + 8 * kk;
+                if (kl < nks) {
+                    const int ks = k0 + kl;
+                    uint4 w[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) w[j] = wst[kk * 8 * DS_TN + 32 * j];
+                    const uint4 p0 = planes4[3 * ks], p1 = planes4[3 * ks + 1], p2 = planes4[3 * ks + 2];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) dot16s(w[j], p0, p1, p2, acc[j][0], acc[j][1], acc[j][2]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+        it++;
+    }
+    flush(cur);
+    return it;
+}
+
+// One GEMV of the step: the tensor-core or the CUDA-core consumer.
+__device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg, int nst, uint32_t bars, int KS, int ntiles,
+                                         long long *out, int G, int cta, uint32_t pa_off, uint32_t red_off,
+                                         unsigned long long *ready) {
+    if constexpr (DS_TC_GEMV) return ds_gemv_tc(it, seg, nst, bars, KS, ntiles, out, G, cta, pa_off, ready);
+    else return ds_gemv_simt(it, nst, bars, KS, ntiles, out, G, cta, pa_off, red_off, ready);
 }
 
 // ---- attention consumer -------------------------------------------------------
@@ -662,8 +784,13 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                 }
             }
         }
-        ds_sync();  // every warp has read the slot
-        if (tid == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        if constexpr (DS_TC_GEMV) {
+            ds_sync();  // every warp has read the slot
+            if (tid == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        } else {
+            __syncwarp();
+            if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
+        }
         if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
         it++;
     }
@@ -693,9 +820,10 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     if (tid == 0) {
         for (int i = 0; i < nst; i++) {
             mbar_init(bars + 8 * i, 1);
-            // released by one arrival: the tensor core's commit (weights) or
-            // one thread after all warps read the slot (K/V rows)
-            mbar_init(bars + 8 * (nst + i), 1);
+            // tensor-core consumer: released by one arrival, the tensor core's
+            // commit (weights) or one thread after all warps read the slot
+            // (K/V rows); CUDA-core consumer: one arrival per warp
+            mbar_init(bars + 8 * (nst + i), DS_TC_GEMV ? 1 : DS_CONSUMERS / 32);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bars + 8 * (2 * nst + i), 1);      // TMEM full: the issuer's commit
@@ -708,7 +836,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         sh.rstd = 1.0;
         sh.last = 0;
     }
-    if (warp == 0) tmem_alloc(&sh.tmem, 32);  // two 16-column int32 accumulators
+    if (warp == 0) tmem_alloc(&sh.tmem, 2 * 16 * DS_NACC);  // two buffers of DS_NACC 16-column accumulators
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -788,16 +916,20 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     uint32_t seg = 0;    // tensor-core tile segments completed (TMEM barrier phases)
     unsigned phase = 0;  // phases completed by this CTA
 
-    // Optional timeline: %globaltimer at the start of phase p (after its
-    // barrier), after its input stage, and at its end (before the arrival),
-    // per CTA: stamps[(p * G + cta) * 3 + i].
+    // Optional timeline, per phase p and CTA: %globaltimer at the phase's
+    // start (after its barrier), after its input stage, when its first and
+    // its last weight stage were ready (GEMV phases), and at its end (before
+    // the arrival): stamps[(p * G + cta) * DS_STAMPS + i], i = 0, 1, 2, 3, 4.
     auto mark = [&](int i) {
-        if (a.stamps && tid == 0) a.stamps[((size_t)phase * G + cta) * 3 + i] = global_ns();
+        if (a.stamps && tid == 0) a.stamps[((size_t)phase * G + cta) * DS_STAMPS + i] = global_ns();
+    };
+    auto ready_slot = [&]() -> unsigned long long * {
+        return a.stamps ? a.stamps + ((size_t)phase * G + cta) * DS_STAMPS + 2 : nullptr;
     };
     // Arrive at the end of the current phase.
     auto arrive = [&]() {
         ds_sync();
-        mark(2);
+        mark(4);
         // release at gpu scope: the CTA's writes (ordered before this thread by
         // the named barrier) are visible to whoever acquires the new count
         if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.sync), "r"(1u) : "memory");
@@ -856,7 +988,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     const int npad_qkv = a.nt_qkv * DS_TN, npad_o = a.nt_o * DS_TN, npad_gu = a.nt_gu * DS_TN,
               npad_down = a.nt_down * DS_TN, npad_lm = a.nt_lm * DS_TN;
     const bool writer = cta == 0;
-    const uint32_t pa_off = (uint32_t)L.pa;
+    const uint32_t pa_off = (uint32_t)L.pa, red_off = (uint32_t)L.red;
     const int rmax = G / a.nkv + 2;  // records per head: a head's units span at most this many CTAs
 
     // token of this step (embedding lookup, cpu.rs:485-498)
@@ -892,7 +1024,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 xv ^= 1;
             }
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off);
+            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- attention
@@ -912,7 +1044,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             else
                 ds_in_att<HD, REP, DS_QMAX_H>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off);
+            it = ds_gemv(it, seg, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- gate/up: input = RMSNorm(x + o)
@@ -924,7 +1056,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                    writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
             xv ^= 1;
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off);
+            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- SwiGLU (llama.rs:490-500), this CTA's share of the F outputs
@@ -950,7 +1082,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             zero_acc(accbuf(j + 1), npad_o);
             ds_in_rows<DS_QMAX_F>(a.act, false, nullptr, a.F, a.ks_f, a.eps, nullptr, pa_off);
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off);
+            it = ds_gemv(it, seg, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
     }
@@ -963,7 +1095,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                a.norm_final, a.h, a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
                                (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
         mark(1);
-        it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off);
+        it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off, red_off, ready_slot());
     }
     arrive();
     // ---- logits and this CTA's argmax candidate (ties -> larger index,
@@ -1044,7 +1176,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     tc_fence_before();
     ds_sync();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(sh.tmem, 32);
+    if (warp == 0) tmem_dealloc(sh.tmem, 2 * 16 * DS_NACC);
 }
 
 template <int HD, int REP, typename KV>

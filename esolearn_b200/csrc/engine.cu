@@ -1308,7 +1308,7 @@ sb_status sb_llama_set_timeline(sb_llama *m, int enabled) {
     SB_CHECK(m, SB_ERR_ARG, "sb_llama_set_timeline: null model");
     SB_CHECK(m->ds_ok, SB_ERR_UNSUPPORTED, "sb_llama_set_timeline: this model does not run the persistent step");
     if (enabled && !m->ds_stamps) {
-        const size_t n = (size_t)(6 * m->L + 2) * ds_grid() * 3;
+        const size_t n = (size_t)(6 * m->L + 2) * ds_grid() * DS_STAMPS;
         SB_TRY(dalloc_t(m, &m->ds_stamps, n));
     }
     if (!enabled) m->ds_stamps = nullptr;  // the buffer stays in m->allocs until destroy
@@ -1320,7 +1320,7 @@ sb_status sb_llama_get_timeline(sb_llama *m, uint64_t *out, size_t cap, int *pha
     SB_CHECK(m->ds_stamps, SB_ERR_STATE, "sb_llama_get_timeline: timeline not enabled");
     *phases = 6 * m->L + 2;
     *ctas = ds_grid();
-    const size_t n = (size_t)(*phases) * (*ctas) * 3;
+    const size_t n = (size_t)(*phases) * (*ctas) * DS_STAMPS;
     if (out) {
         SB_CHECK(cap >= n, SB_ERR_SHAPE, "sb_llama_get_timeline: %zu slots, %zu needed", cap, n);
         SB_CUDA_TRY(cudaStreamSynchronize(m->st));

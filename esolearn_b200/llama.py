@@ -478,10 +478,11 @@ class QuantLlamaB200:
         N.check(N.lib().sb_llama_set_timeline(self._h, int(on)))
 
     def timeline(self) -> np.ndarray:
-        """Stamps of the last persistent step: [phases, ctas, 3] ns (start, input done, end)."""
+        """Stamps of the last persistent step: [phases, ctas, 5] ns (start, input done,
+        first and last weight stage ready, end)."""
         p, c = C.c_int32(), C.c_int32()
         N.check(N.lib().sb_llama_get_timeline(self._h, None, 0, C.byref(p), C.byref(c)))
-        out = np.zeros((p.value, c.value, 3), np.uint64)
+        out = np.zeros((p.value, c.value, 5), np.uint64)
         N.check(N.lib().sb_llama_get_timeline(self._h, _ptr(out), out.size, C.byref(p), C.byref(c)))
         return out
 

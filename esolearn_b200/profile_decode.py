@@ -69,7 +69,7 @@ PHASES = ("qkv", "attention", "o", "gate_up", "swiglu", "down")
 
 
 def timeline_summary(ts, n_layers: int) -> dict:
-    """Per-phase-kind means (us) of a step timeline [phases, ctas, 3] (ns)."""
+    """Per-phase-kind means (us) of a step timeline [phases, ctas, 5] (ns)."""
     import numpy as np
 
     t = ts.astype(np.float64)
@@ -78,19 +78,27 @@ def timeline_summary(ts, n_layers: int) -> dict:
     kinds = [(k, [6 * l + i for l in range(n_layers)]) for i, k in enumerate(PHASES)]
     kinds.append(("lm_head", [6 * n_layers]))
     for name, idx in kinds:
-        wait, inp, work, span = [], [], [], []
+        wait, inp, work, span, r0, r1, tail = [], [], [], [], [], [], []
         for p in idx:
             if p == 0 or p >= P:
                 continue
-            wait.append(np.mean(t[p, :, 0] - t[p - 1, :, 2]))
+            wait.append(np.mean(t[p, :, 0] - t[p - 1, :, 4]))
             inp.append(np.mean(t[p, :, 1] - t[p, :, 0]))
-            work.append(np.mean(t[p, :, 2] - t[p, :, 1]))
-            span.append(np.max(t[p, :, 2]) - np.max(t[p - 1, :, 2]))
+            work.append(np.mean(t[p, :, 4] - t[p, :, 1]))
+            span.append(np.max(t[p, :, 4]) - np.max(t[p - 1, :, 4]))
+            g = t[p, :, 2] > 0  # CTAs with weight stages in this phase
+            if g.any():
+                r0.append(np.mean(t[p, g, 2] - t[p, g, 1]))
+                r1.append(np.mean(t[p, g, 3] - t[p, g, 1]))
+                tail.append(np.mean(t[p, g, 4] - t[p, g, 3]))
         if span:
             res[name] = {"barrier": np.mean(wait) / 1e3, "input": np.mean(inp) / 1e3, "work": np.mean(work) / 1e3,
                          "span": np.mean(span) / 1e3}
-    first, last = t[0, :, 0].min(), t[6 * n_layers, :, 2].max()
-    res["layers_total"] = (t[6 * n_layers - 1, :, 2].max() - first) / 1e3
+            if r0:  # input done -> first / last weight stage ready, last stage ready -> phase end
+                res[name].update({"first_ready": np.mean(r0) / 1e3, "last_ready": np.mean(r1) / 1e3,
+                                  "after_last": np.mean(tail) / 1e3})
+    first, last = t[0, :, 0].min(), t[6 * n_layers, :, 4].max()
+    res["layers_total"] = (t[6 * n_layers - 1, :, 4].max() - first) / 1e3
     res["per_layer"] = res["layers_total"] / n_layers
     res["step_to_lm_end"] = (last - first) / 1e3
     return res

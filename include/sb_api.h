@@ -318,9 +318,10 @@ sb_status sb_llama_attn_plan(sb_llama *m, int batch, int *splits, int *tensor_ma
 /* Timeline of the persistent batch-1 step (a profiling aid; no reference
  * counterpart).  When enabled, every later step records, per phase p (6 per
  * layer: qkv, attention, o, gate/up, SwiGLU, down; then lm_head and the
- * argmax) and per CTA c, three %globaltimer readings in ns: the phase's start
- * after its grid barrier, the end of its input stage, and its end before the
- * arrival: out[(p * ctas + c) * 3 + i].  SB_ERR_UNSUPPORTED when the model
+ * argmax) and per CTA c, five %globaltimer readings in ns: the phase's start
+ * after its grid barrier, the end of its input stage, the moments its first
+ * and its last weight stage were ready (GEMV phases; 0 otherwise), and its
+ * end before the arrival: out[(p * ctas + c) * 5 + i].  SB_ERR_UNSUPPORTED when the model
  * does not run the persistent step.  get: *phases and *ctas always; out
  * (cap slots) when non-NULL, for the last step. */
 sb_status sb_llama_set_timeline(sb_llama *m, int enabled);
