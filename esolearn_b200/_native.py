@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(_PKG, "libscryb200.so")
 SB_OK = 0
 STATUS_NAMES = {0: "SB_OK", 1: "SB_ERR_CUDA", 2: "SB_ERR_NCCL", 3: "SB_ERR_TIMEOUT", 4: "SB_ERR_SHAPE",
                 5: "SB_ERR_OOM", 6: "SB_ERR_ARG", 7: "SB_ERR_STATE", 8: "SB_ERR_UNSUPPORTED"}
-SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
+SB_DTYPE_F32, SB_DTYPE_BF16, SB_DTYPE_F16 = 0, 1, 2
 SB_KV_BF16, SB_KV_F32 = 0, 1
 SB_W_QKV, SB_W_O, SB_W_GATE, SB_W_UP, SB_W_DOWN, SB_W_LM_HEAD = range(6)
 SB_TP_ID_BYTES = 128
@@ -87,6 +87,9 @@ SIGNATURES = {
     "sb_llama_load_qweight": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_float]),
     "sb_llama_get_qweight": (C.c_int, [vp, C.c_int, C.c_int, vp, f32p]),
     "sb_llama_load_f32": (C.c_int, [vp, C.c_int, C.c_int, vp]),
+    "sb_llama_load_hf": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp), C.POINTER(C.c_int64),
+                                   C.c_int64]),
+    "sb_llama_load_hf_f32": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, C.c_int64]),
     "sb_llama_reset": (C.c_int, [vp]),
     "sb_llama_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
     "sb_llama_forward_seq": (C.c_int, [vp, vp, C.c_int, vp]),

@@ -70,6 +70,8 @@ struct sb_llama {
     float *embed = nullptr, *norm_in = nullptr, *norm_post = nullptr, *norm_final = nullptr;
     int8_t *stage = nullptr;  // gate staging for gate/up pairing
     size_t stage_bytes = 0;
+    void *raw = nullptr;      // checkpoint tensors as read (sb_llama_load_hf), grown on demand
+    size_t raw_bytes = 0;
     int staged_gate_layer = -1;
     float staged_gate_scale = 0.0f;
     unsigned *amax = nullptr;
@@ -770,6 +772,7 @@ sb_status sb_llama_destroy(sb_llama *m) {
         if (g) cudaGraphExecDestroy(g);  // graphs hold NCCL calls: release them before the communicator
     tp_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
+    if (m->raw) cudaFree(m->raw);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
     return SB_OK;
@@ -850,6 +853,177 @@ sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *
     SB_TRY(qweight_pack(m->stage, K, N, d->TN, 0, 0, const_cast<uint4 *>(d->w), m->st));
     d->scale = scale;
     ly.has[slot] = true;
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+namespace {
+
+size_t dtype_bytes(int dtype) { return dtype == SB_DTYPE_F32 ? 4 : 2; }
+
+// The raw-tensor staging buffer, at least `bytes` (the old one is freed).
+int raw_reserve(sb_llama *m, size_t bytes) {
+    if (m->raw_bytes >= bytes) return SB_OK;
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    if (m->raw) cudaFree(m->raw);
+    m->raw = nullptr;
+    m->raw_bytes = 0;
+    cudaError_t e = cudaMalloc(&m->raw, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(SB_ERR_OOM, "checkpoint staging of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    m->raw_bytes = bytes;
+    return SB_OK;
+}
+
+// Upload the parts (host, dtype, rows x cols each) one after another into
+// the raw staging buffer; *dev[i] receives each part's device address.
+int raw_upload(sb_llama *m, int dtype, int n_parts, const void *const *parts, const int64_t *rows, int64_t cols,
+               const void **dev) {
+    const size_t es = dtype_bytes(dtype);
+    size_t total = 0;
+    for (int i = 0; i < n_parts; i++) total += align_up((size_t)rows[i] * (size_t)cols * es, 256);
+    SB_TRY(raw_reserve(m, total));
+    size_t off = 0;
+    for (int i = 0; i < n_parts; i++) {
+        const size_t b = (size_t)rows[i] * (size_t)cols * es;
+        char *d = static_cast<char *>(m->raw) + off;
+        SB_CUDA_TRY(cudaMemcpyAsync(d, parts[i], b, cudaMemcpyHostToDevice, m->st));
+        dev[i] = d;
+        off += align_up(b, 256);
+    }
+    return SB_OK;
+}
+
+// quantize_symmetric of the full tensor `full` (its absmax), values of this
+// rank's slice `part`, into m->stage + stage_off as [N, K]; the scale to *scale.
+int quantize_src(sb_llama *m, const SrcSpec &full, const SrcSpec &part, size_t stage_off, float *scale) {
+    SB_TRY(src_absmax(full, m->amax, m->st));
+    SB_TRY(src_quantize(part, m->amax, m->stage + stage_off, m->scale_dev, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(scale, m->scale_dev, 4, cudaMemcpyDeviceToHost, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+}  // namespace
+
+sb_status sb_llama_load_hf(sb_llama *m, int layer, int slot, int dtype, int n_parts, const void *const *parts,
+                           const int64_t *part_rows, int64_t cols) {
+    SB_CHECK(m && parts && part_rows, SB_ERR_ARG, "sb_llama_load_hf: null argument");
+    SB_CHECK(dtype == SB_DTYPE_F32 || dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16, SB_ERR_ARG,
+             "sb_llama_load_hf: dtype %d", dtype);
+    SB_CHECK(layer < m->L && (layer < 0 || (slot >= 0 && slot < 5)), SB_ERR_ARG, "bad layer %d / slot %d", layer,
+             slot);
+    const int T = m->tp, r = m->tp_rank, h = m->h;
+    const int F = m->F, Ff = F * T, q = m->q_dim, kv = m->kv_dim, Qf = q * T, KVf = kv * T, V = m->V, Vl = m->Vl;
+    const int want_parts = (layer >= 0 && slot == SB_W_QKV) ? 3 : 1;
+    SB_CHECK(n_parts == want_parts, SB_ERR_ARG, "sb_llama_load_hf: %d parts, expected %d", n_parts, want_parts);
+    for (int i = 0; i < n_parts; i++) SB_CHECK(parts[i], SB_ERR_ARG, "sb_llama_load_hf: null part %d", i);
+    // expected HF shapes [out, in] of the FULL tensors
+    int64_t er[3] = {0, 0, 0}, ec = 0;
+    if (layer < 0) er[0] = V, ec = h;
+    else if (slot == SB_W_QKV) er[0] = Qf, er[1] = KVf, er[2] = KVf, ec = h;
+    else if (slot == SB_W_O) er[0] = h, ec = Qf;
+    else if (slot == SB_W_DOWN) er[0] = h, ec = Ff;
+    else er[0] = Ff, ec = h;  // gate, up
+    for (int i = 0; i < n_parts; i++)
+        SB_CHECK(part_rows[i] == er[i] && cols == ec, SB_ERR_SHAPE,
+                 "sb_llama_load_hf: part %d is [%lld, %lld], expected [%lld, %lld]", i, (long long)part_rows[i],
+                 (long long)cols, (long long)er[i], (long long)ec);
+    const void *dev[3] = {nullptr, nullptr, nullptr};
+    SB_TRY(raw_upload(m, dtype, n_parts, parts, part_rows, cols, dev));
+    SrcSpec full, part;
+    full.dtype = dtype;
+    for (int i = 0; i < n_parts; i++) full.p[i] = dev[i], full.ld[i] = cols;
+    full.nseg = n_parts;
+    if (layer < 0) {  // lm_head [V,h] (llama.rs:943-948): K = h, N = this rank's vocabulary rows
+        full.K = h, full.N = V;
+        part = full;
+        part.N = Vl, part.row0[0] = (long long)r * Vl;
+        float sc = 0.f;
+        SB_TRY(quantize_src(m, full, part, 0, &sc));
+        SB_TRY(qweight_pack(m->stage, h, Vl, m->lm.TN, 0, 1, const_cast<uint4 *>(m->lm.w), m->st));
+        m->lm.scale = sc;
+        m->has_lm = true;
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        return SB_OK;
+    }
+    sb_llama::Layer &ly = m->layers[layer];
+    switch (slot) {
+    case SB_W_QKV:  // fuse_qkv_weights (llama.rs:1009-1029): q | k | v columns, one scale
+        full.K = h, full.N = Qf + 2 * KVf;
+        full.c0[1] = Qf, full.c0[2] = Qf + KVf;
+        part = full;
+        part.N = q + 2 * kv;
+        part.c0[1] = q, part.c0[2] = q + kv;
+        part.row0[0] = (long long)r * q, part.row0[1] = (long long)r * kv, part.row0[2] = (long long)r * kv;
+        SB_TRY(quantize_src(m, full, part, 0, &ly.qkv.scale));
+        SB_TRY(qweight_pack(m->stage, h, ly.qkv.N, ly.qkv.TN, 0, 1, const_cast<uint4 *>(ly.qkv.w), m->st));
+        break;
+    case SB_W_O:  // rows (in) of this rank's heads
+        full.K = Qf, full.N = h;
+        part = full;
+        part.K = q, part.k0 = (long long)r * q;
+        SB_TRY(quantize_src(m, full, part, 0, &ly.o.scale));
+        SB_TRY(qweight_pack(m->stage, q, h, ly.o.TN, 0, 1, const_cast<uint4 *>(ly.o.w), m->st));
+        break;
+    case SB_W_DOWN:  // rows (in) of this rank's ffn features
+        full.K = Ff, full.N = h;
+        part = full;
+        part.K = F, part.k0 = (long long)r * F;
+        SB_TRY(quantize_src(m, full, part, 0, &ly.down.scale));
+        SB_TRY(qweight_pack(m->stage, F, h, ly.down.TN, 0, 1, const_cast<uint4 *>(ly.down.w), m->st));
+        break;
+    case SB_W_GATE:
+    case SB_W_UP: {  // this rank's ffn columns; gate and up are packed together once both are staged
+        full.K = h, full.N = Ff;
+        part = full;
+        part.N = F, part.row0[0] = (long long)r * F;
+        if (slot == SB_W_GATE) {
+            SB_TRY(quantize_src(m, full, part, 0, &m->staged_gate_scale));
+            m->staged_gate_layer = layer;
+            ly.has[SB_W_GATE] = true;
+            return SB_OK;
+        }
+        SB_CHECK(m->staged_gate_layer == layer, SB_ERR_STATE, "sb_llama_load_hf: load gate before up for layer %d",
+                 layer);
+        float su = 0.f;
+        SB_TRY(quantize_src(m, full, part, (size_t)h * F, &su));
+        SB_TRY(qweight_pack(m->stage, h, ly.gu.N, ly.gu.TN, F, 1, const_cast<uint4 *>(ly.gu.w), m->st));
+        ly.gu.scale = m->staged_gate_scale;
+        ly.gu.scale_up = su;
+        m->staged_gate_layer = -1;
+        break;
+    }
+    }
+    ly.has[slot] = true;
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    return SB_OK;
+}
+
+sb_status sb_llama_load_hf_f32(sb_llama *m, int which, int layer, int dtype, const void *data, int64_t n) {
+    SB_CHECK(m && data, SB_ERR_ARG, "sb_llama_load_hf_f32: null argument");
+    SB_CHECK(dtype == SB_DTYPE_F32 || dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16, SB_ERR_ARG,
+             "sb_llama_load_hf_f32: dtype %d", dtype);
+    float *dst = nullptr;
+    int64_t want = m->h;
+    switch (which) {
+    case SB_F_EMBED: dst = m->embed, want = (int64_t)m->V * m->h; break;
+    case SB_F_NORM_IN:
+    case SB_F_NORM_POST:
+        SB_CHECK(layer >= 0 && layer < m->L, SB_ERR_ARG, "sb_llama_load_hf_f32: layer %d", layer);
+        dst = (which == SB_F_NORM_IN ? m->norm_in : m->norm_post) + (size_t)layer * m->h;
+        break;
+    case SB_F_NORM_FINAL: dst = m->norm_final; break;
+    default: return set_error(SB_ERR_ARG, "sb_llama_load_hf_f32: tensor kind %d", which);
+    }
+    SB_CHECK(n == want, SB_ERR_SHAPE, "sb_llama_load_hf_f32: %lld values, expected %lld", (long long)n,
+             (long long)want);
+    const void *dev = nullptr;
+    const int64_t rows = n;
+    SB_TRY(raw_upload(m, dtype, 1, &data, &rows, 1, &dev));
+    SB_TRY(src_to_f32(dev, dtype, (size_t)n, dst, m->st));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     return SB_OK;
 }

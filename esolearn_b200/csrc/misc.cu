@@ -2,6 +2,8 @@
 // seeded on-device weight generator.
 #include "misc.cuh"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 namespace sb {
@@ -309,6 +311,74 @@ __global__ void gen_normal_kernel(uint64_t seed, uint64_t first, size_t n, float
 
 int gen_normal_f32(uint64_t seed, uint64_t first_sample, size_t n, float *out, cudaStream_t st) {
     gen_normal_kernel<<<gen_blocks(n), 256, 0, st>>>(seed, first_sample, n, out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// checkpoint tensors (LlamaModel::from_safetensors, llama.rs:768-958): the
+// F32 / BF16 / F16 -> f32 conversion (llama.rs:795-808, exact), the [out, in]
+// -> [in, out] transpose (llama.rs:815-825) and the q|k|v concatenation
+// (llama.rs:1009-1029) are folded into the index map of SrcSpec.
+
+__device__ __forceinline__ float src_elem(const void *p, int dtype, long long i) {
+    if (dtype == SB_DTYPE_BF16) return __uint_as_float((uint32_t)static_cast<const uint16_t *>(p)[i] << 16);
+    if (dtype == SB_DTYPE_F16) return __half2float(static_cast<const __half *>(p)[i]);
+    return static_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ float src_value(const SrcSpec &g, int r, int c) {
+    int i = 0;
+    if (g.nseg > 1 && c >= g.c0[1]) i = 1;
+    if (g.nseg > 2 && c >= g.c0[2]) i = 2;
+    const long long row = g.row0[i] + (c - g.c0[i]);
+    return src_elem(g.p[i], g.dtype, row * g.ld[i] + g.k0 + r);
+}
+
+__global__ void src_absmax_kernel(SrcSpec g, unsigned *amax) {
+    const size_t n = (size_t)g.K * g.N;
+    float m = 0.0f;
+    // consecutive threads take consecutive k of one source row (coalesced)
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(src_value(g, (int)(e % g.K), (int)(e / g.K))));
+    m = warp_max_f(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(m));
+}
+
+__global__ void src_quantize_kernel(SrcSpec g, const unsigned *amax, int8_t *q, float *scale_out) {
+    const float am = __uint_as_float(*amax);
+    const float scale = am / 127.0f;
+    const float inv = 1.0f / scale;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = am == 0.0f ? 0.0f : scale;
+    const size_t n = (size_t)g.K * g.N;
+    // q is [N, K] (the source's row order): reads and writes both coalesced
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e % g.K), c = (int)(e / g.K);
+        q[e] = am == 0.0f ? (int8_t)0 : quant_one(src_value(g, r, c), inv);
+    }
+}
+
+int src_absmax(const SrcSpec &g, unsigned *amax, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(unsigned), st));
+    src_absmax_kernel<<<gen_blocks((size_t)g.K * g.N), 256, 0, st>>>(g, amax);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+int src_quantize(const SrcSpec &part, const unsigned *amax, int8_t *q, float *scale_out, cudaStream_t st) {
+    src_quantize_kernel<<<gen_blocks((size_t)part.K * part.N), 256, 0, st>>>(part, amax, q, scale_out);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
+
+__global__ void src_to_f32_kernel(const void *src, int dtype, size_t n, float *out) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = src_elem(src, dtype, (long long)i);
+}
+
+int src_to_f32(const void *src, int dtype, size_t n, float *out, cudaStream_t st) {
+    if (n == 0) return SB_OK;
+    src_to_f32_kernel<<<gen_blocks(n), 256, 0, st>>>(src, dtype, n, out);
     SB_CUDA_TRY(cudaGetLastError());
     return SB_OK;
 }

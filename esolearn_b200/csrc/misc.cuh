@@ -62,4 +62,29 @@ int gen_quantize(const GenSpec &g, uint64_t seed, const unsigned *amax, int8_t *
 // out[i] = sample(first_sample + i), i < n (f32 embedding table).
 int gen_normal_f32(uint64_t seed, uint64_t first_sample, size_t n, float *out, cudaStream_t st);
 
+// A [K, N] matrix read from up to three checkpoint tensors in the HF layout
+// [out, in] (row = output column n, the source is transposed), stacked
+// along n: column n of segment i (n in [c0[i], c0[i+1])) is source row
+// row0[i] + n - c0[i] of p[i], and k is source column k0 + k; ld = elements
+// per source row.  dtype: SB_DTYPE_F32, SB_DTYPE_BF16 or SB_DTYPE_F16.  With
+// row0 / k0 offsets the same tensors give a tensor-parallel rank's slice.
+struct SrcSpec {
+    int K = 0, N = 0;
+    int nseg = 1;
+    int c0[3] = {0, 0, 0};
+    const void *p[3] = {nullptr, nullptr, nullptr};
+    long long ld[3] = {0, 0, 0};
+    long long row0[3] = {0, 0, 0};
+    long long k0 = 0;
+    int dtype = 0;
+};
+// absmax of every value of g (the full tensor); then q = quantize_symmetric
+// of the values of `part` with the scale of that absmax, written [N, K]
+// row-major (the transpose of the reference [K, N] layout), the scale also
+// to *scale_out (device).  Bit-exact with the host quantizer.
+int src_absmax(const SrcSpec &g, unsigned *amax, cudaStream_t st);
+int src_quantize(const SrcSpec &part, const unsigned *amax, int8_t *q, float *scale_out, cudaStream_t st);
+// f32 copy of n values of dtype at src (device), e.g. an embedding table.
+int src_to_f32(const void *src, int dtype, size_t n, float *out, cudaStream_t st);
+
 }  // namespace sb

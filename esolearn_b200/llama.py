@@ -326,14 +326,17 @@ class QuantLlamaB200:
 
     # -- weights --------------------------------------------------------
     @classmethod
-    def from_safetensors(cls, config: LlamaConfig, paths, cache: Optional[str] = None, **kw) -> "QuantLlamaB200":
+    def from_safetensors(cls, config: LlamaConfig, paths, cache: Optional[str] = None, device_quantize: bool = True,
+                         **kw) -> "QuantLlamaB200":
         """LlamaModel::from_safetensors (llama.rs:768-958) + quantize_symmetric per projection.
-        cache: a packed-int8 cache file, read when it exists, else written
-        from the shards during this load."""
+        device_quantize: convert, transpose, fuse and quantize on the GPU
+        (sb_llama_load_hf) instead of the host.  cache: a packed-int8 cache
+        file, read when it exists, else written from the shards during this
+        load (host quantization)."""
         from .safetensors_io import load_into
 
         m = cls(config, **kw)
-        load_into(m, config, paths, cache=cache)
+        load_into(m, config, paths, cache=cache, device=device_quantize)
         return m
 
     @classmethod

@@ -108,6 +108,11 @@ class SafeTensorsShards:
             raise N.SbError(6, f"unsupported dtype {dt} for tensor '{name}'")
         return np.frombuffer(data[b:e], dtype=_DTYPES[dt]).reshape(shape)
 
+    def dtype(self, name: str) -> str:
+        if name not in self._where:
+            raise N.SbError(6, f"tensor '{name}' not found in any shard")
+        return self._where[name][1]
+
     def f32(self, name: str) -> np.ndarray:
         """The tensor as f32 (exact for F32, BF16 and F16 sources)."""
         raw = self.raw(name)
@@ -175,6 +180,59 @@ def quantized_llama_tensors(config: LlamaConfig, paths: Sequence[str]) -> Iterat
     yield ("f", N.SB_F_NORM_FINAL, 0, st.f32("model.norm.weight"))
     head = st.f32("model.embed_tokens.weight" if config.tie_word_embeddings else "lm_head.weight")
     yield ("q", -1, 0) + quantize_symmetric(head)
+
+
+_SB_DTYPE = {"F32": N.SB_DTYPE_F32, "BF16": N.SB_DTYPE_BF16, "F16": N.SB_DTYPE_F16}
+
+
+def load_hf_device(model, config: LlamaConfig, paths: Sequence[str]):
+    """The same wiring as quantized_llama_tensors, done on the device: every
+    tensor's bytes go to the GPU as stored (memory-mapped shards, no host
+    conversion) and sb_llama_load_hf converts, transposes, fuses q|k|v,
+    quantizes and packs them there (bit-exact with the host path).  Every
+    rank of a tensor-parallel model passes the full tensors."""
+    import ctypes as C
+
+    st = SafeTensorsShards(paths)
+    h, F, V = config.hidden_size, config.intermediate_size, config.vocab_size
+    hd = config.head_dim()
+    qd, kd = config.n_heads * hd, config.n_kv_heads * hd
+
+    def raw(name, shape):
+        dt = st.dtype(name)
+        if dt not in _SB_DTYPE:
+            raise N.SbError(6, f"tensor '{name}': dtype {dt} is not F32, BF16 or F16")
+        a = st.raw(name)
+        if a.shape != tuple(shape):
+            raise N.SbError(4, f"tensor '{name}' has shape {a.shape}, expected {tuple(shape)}")
+        return a, _SB_DTYPE[dt]
+
+    def proj(layer, slot, names, rows, cols):
+        arrs = [raw(n, (r, cols)) for n, r in zip(names, rows)]
+        dts = {d for _, d in arrs}
+        if len(dts) != 1:
+            raise N.SbError(6, f"tensors {names} mix dtypes")
+        ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a, _ in arrs])
+        rr = (C.c_int64 * len(arrs))(*rows)
+        N.check(N.lib().sb_llama_load_hf(model._h, layer, slot, dts.pop(), len(arrs), ptrs, rr, cols))
+
+    def f32(which, layer, name, shape):
+        a, dt = raw(name, shape)
+        N.check(N.lib().sb_llama_load_hf_f32(model._h, which, layer, dt, C.c_void_p(a.ctypes.data), a.size))
+
+    f32(N.SB_F_EMBED, 0, "model.embed_tokens.weight", (V, h))
+    for i in range(config.n_layers):
+        p = f"model.layers.{i}"
+        proj(i, N.SB_W_QKV, [f"{p}.self_attn.{x}_proj.weight" for x in "qkv"], [qd, kd, kd], h)
+        proj(i, N.SB_W_O, [f"{p}.self_attn.o_proj.weight"], [h], qd)
+        proj(i, N.SB_W_GATE, [f"{p}.mlp.gate_proj.weight"], [F], h)
+        proj(i, N.SB_W_UP, [f"{p}.mlp.up_proj.weight"], [F], h)
+        proj(i, N.SB_W_DOWN, [f"{p}.mlp.down_proj.weight"], [h], F)
+        f32(N.SB_F_NORM_IN, i, f"{p}.input_layernorm.weight", (h,))
+        f32(N.SB_F_NORM_POST, i, f"{p}.post_attention_layernorm.weight", (h,))
+    f32(N.SB_F_NORM_FINAL, 0, "model.norm.weight", (h,))
+    head = "model.embed_tokens.weight" if config.tie_word_embeddings else "lm_head.weight"
+    proj(-1, 0, [head], [V], h)
 
 
 # ---------------------------------------------------------------------------
@@ -275,11 +333,15 @@ def cached_llama_tensors(config: LlamaConfig, path: str) -> Iterator[tuple]:
     yield ("q", -1, 0, st.raw("lm_head.q"), np.float32(st.raw("lm_head.scale")[0]))
 
 
-def load_into(model, config: LlamaConfig, paths: Sequence[str], cache: str = None):
+def load_into(model, config: LlamaConfig, paths: Sequence[str], cache: str = None, device: bool = True):
     """Load HF shards into a QuantLlamaB200 (every rank of a tensor-parallel
-    model loads the same full tensors and keeps its slice).  With `cache`:
-    read the packed-int8 cache when it exists, else quantize the shards and
-    write it on the way."""
+    model loads the same full tensors and keeps its slice).  Without a cache
+    the conversion and quantization run on the device (device=True, the
+    default) or on the host.  With `cache`: read the packed-int8 cache when it
+    exists, else quantize the shards on the host and write it on the way."""
+    if not cache and device:
+        load_hf_device(model, config, paths)
+        return
     if cache and os.path.exists(cache):
         tensors = cached_llama_tensors(config, cache)
     elif cache:

@@ -35,7 +35,7 @@ enum {
     SB_ERR_UNSUPPORTED = 8, /* configuration not built into this library */
 };
 
-enum { SB_DTYPE_F32 = 0, SB_DTYPE_BF16 = 1 };
+enum { SB_DTYPE_F32 = 0, SB_DTYPE_BF16 = 1, SB_DTYPE_F16 = 2 };
 enum { SB_KV_BF16 = 0, SB_KV_F32 = 1 };
 
 /* Message of the last failure on this thread; returns its status code. */
@@ -246,6 +246,26 @@ sb_status sb_llama_load_qweight(sb_llama *m, int layer, int slot, const int8_t *
  * sb_llama_load_qweight; the lm_head comes back as [V,h]).  q: host buffer
  * of K*N bytes; scale: host float. */
 sb_status sb_llama_get_qweight(sb_llama *m, int layer, int slot, int8_t *q, float *scale);
+/* LlamaModel::from_safetensors for one projection (llama.rs:768-958), with
+ * the checkpoint's own bytes: every part is a host tensor in the HF layout
+ * [out, in] (row-major) and dtype SB_DTYPE_F32, SB_DTYPE_BF16 or SB_DTYPE_F16.
+ * On the device: the exact conversion to f32 (llama.rs:795-808), the
+ * transpose to [in, out] (llama.rs:815-825), for slot SB_W_QKV the q|k|v
+ * column concatenation of parts q [n_heads*hd, h], k and v [n_kv*hd, h]
+ * (llama.rs:1009-1029), quantize_symmetric of the whole tensor (quantize.rs
+ * :16-32, bit-exact with sb_quantize_symmetric_host) and the packing.
+ * layer -1 is the lm_head [V, h] (llama.rs:943-948); other slots take one
+ * part: o [h, q], gate and up [ffn, h] (gate before up), down [h, ffn].
+ * Under tensor parallelism the parts are the FULL tensors and the rank keeps
+ * its slice, the scale being the full tensor's.  The raw bytes pass through
+ * a staging buffer the model keeps (grown to the largest tensor) until
+ * sb_llama_destroy. */
+sb_status sb_llama_load_hf(sb_llama *m, int layer, int slot, int dtype, int n_parts,
+                           const void *const *parts, const int64_t *part_rows, int64_t cols);
+/* The f32 tensors from checkpoint bytes (converted on the device): which =
+ * SB_F_EMBED ([V,h], n = V*h), SB_F_NORM_IN / SB_F_NORM_POST of `layer` or
+ * SB_F_NORM_FINAL (n = h). */
+sb_status sb_llama_load_hf_f32(sb_llama *m, int which, int layer, int dtype, const void *data, int64_t n);
 /* Load an f32 tensor: embed [V,h] or a norm weight [h]. */
 sb_status sb_llama_load_f32(sb_llama *m, int which, int layer, const float *data);
 /* Forget all cached positions (LlamaKvCache::new). */

@@ -246,3 +246,53 @@ def test_engine_from_safetensors_equals_engine_from_tensors(tmp_path):
     ca, cb = a.new_kv_cache(64), b.new_kv_cache(64)
     for pos, t in enumerate(prompt):
         assert np.array_equal(a.forward_with_cache(int(t), pos, ca), b.forward_with_cache(int(t), pos, cb))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("tie", [False, True])
+def test_device_load_equals_host_quantized_tensors(tmp_path, dtype, tie):
+    # sb_llama_load_hf: the checkpoint bytes converted, transposed, fused and
+    # quantized on the GPU must give the host path's int8 tensors and scales
+    # bit for bit (llama.rs:768-958 wiring + quantize.rs:16-32), for BF16, F16
+    # and F32 shards, tied and untied lm_heads.
+    from esolearn_b200 import QuantLlamaB200
+    from esolearn_b200.safetensors_io import load_hf_device
+
+    N.check(N.lib().sb_init(0))
+    c = LlamaConfig(512, 256, 192, 2, 4, 2, 64, 1e-5, 10000.0, tie, None)
+    w = _hf_weights(c, 21 + tie)
+    if dtype == "f16":
+        w = {k: v.astype(np.float16).astype(np.float32) for k, v in w.items()}
+    path = str(tmp_path / "model.safetensors")
+    if dtype == "f16":  # write F16 tensors directly
+        import json
+        header, blobs, off = {}, [], 0
+        for name, a in w.items():
+            raw = a.astype(np.float16).tobytes()
+            header[name] = {"dtype": "F16", "shape": list(a.shape), "data_offsets": [off, off + len(raw)]}
+            blobs.append(raw)
+            off += len(raw)
+        hb = json.dumps(header).encode()
+        hb += b" " * (-len(hb) % 8)
+        with open(path, "wb") as f:
+            f.write(len(hb).to_bytes(8, "little"))
+            f.write(hb)
+            for raw in blobs:
+                f.write(raw)
+    else:
+        write_safetensors(path, w, bf16=list(w) if dtype == "bf16" else [])
+    e = QuantLlamaB200(c, max_seq=64)
+    load_hf_device(e, c, [path])
+    for t in quantized_llama_tensors(c, [path]):
+        if t[0] != "q":
+            continue
+        q, s = e.get_qweight(t[1], t[2])
+        assert s == t[4], (t[1], t[2])
+        assert np.array_equal(q, t[3]), (t[1], t[2], int((q != t[3]).sum()))
+    ref = QuantLlamaB200(c, max_seq=64)
+    for t in quantized_llama_tensors(c, [path]):
+        (ref.load_qweight if t[0] == "q" else ref.load_f32)(*t[1:])
+    ce, cr = e.new_kv_cache(64), ref.new_kv_cache(64)
+    for pos, tok in enumerate(O.prompt_ids(8, 6, c.vocab_size)):
+        assert np.array_equal(e.forward_with_cache(int(tok), pos, ce), ref.forward_with_cache(int(tok), pos, cr))
