@@ -69,7 +69,7 @@ struct Workspace {
 // WS_GEMM_SUMS only ever holds the tensor-core GEMM's int64 column sums,
 // which must read zero before every call: a grown buffer is zero-filled and
 // every call clears what it used.
-enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_SAMPLE = 4, WS_KINDS = 5 };
+enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_SAMPLE = 4, WS_GROUPED = 5, WS_KINDS = 6 };
 constexpr size_t WS_ATTN_COUNTER_BYTES = 64 * 1024;
 
 static int workspace_get(int kind, size_t bytes, void **out, cudaStream_t st) {
@@ -353,6 +353,31 @@ static sb_status qgemm_rows(const QWeightDesc &wd, const void *a, bool bf16, int
     return qgemm_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, stream, false);
 }
 
+// Rows [0, M) (5-32) of a group-scaled weight through the tensor cores.
+static sb_status qgemm_grouped_rows(const QWeightDesc &wd, const void *a, bool bf16, int M, const float *bias,
+                                    float *c, cudaStream_t stream) {
+    QGemmWs ws;
+    const size_t pb = align_up(qgemm_planes_bytes(wd.K, M), 256);
+    const size_t rb = sizeof(double) * QGM_MAX_M, sb = sizeof(int) * QGM_MAX_M;
+    void *base = nullptr, *part = nullptr;
+    SB_TRY(workspace_get(WS_GEMM, pb + rb + sb, &base, stream));
+    SB_TRY(workspace_get(WS_GROUPED, sizeof(double) * qgemm_grouped_part_doubles(wd), &part, stream));
+    char *b = static_cast<char *>(base);
+    ws.planes = reinterpret_cast<uint8_t *>(b);
+    ws.rstd = reinterpret_cast<double *>(b + pb);
+    ws.shift = reinterpret_cast<int *>(b + pb + rb);
+    QGemvArgs g;
+    g.w = wd;
+    g.M = M;
+    g.x = a;
+    g.ldx = wd.K;
+    g.x_bf16 = bf16;
+    g.out = c;
+    g.ldo = wd.N;
+    g.bias = bias;
+    return qgemm_grouped_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, static_cast<double *>(part), stream, false);
+}
+
 static sb_status matmul_desc(const QWeightDesc &wd, const void *a, int a_dtype, int M, const float *bias, float *c,
                              void *stream) {
     SB_CHECK(a_dtype == SB_DTYPE_F32 || a_dtype == SB_DTYPE_BF16, SB_ERR_ARG, "bad activation dtype %d", a_dtype);
@@ -370,6 +395,17 @@ static sb_status matmul_desc(const QWeightDesc &wd, const void *a, int a_dtype, 
             const int r0 = (int)((long long)M * i / nc), r1 = (int)((long long)M * (i + 1) / nc);
             SB_TRY(qgemm_rows(wd, static_cast<const char *>(a) + (size_t)r0 * wd.K * esz, bf16, r1 - r0, bias,
                               c + (size_t)r0 * wd.N, st));
+        }
+        return SB_OK;
+    }
+    if (M > QG_MAX_M && qgemm_grouped_supported(wd, std::min(M, 32))) {
+        // Group-scaled weights, 5+ rows: balanced chunks of at most 32 rows on
+        // the tensor cores (rows are independent).
+        const int nc = (M + 31) / 32;
+        for (int i = 0; i < nc; i++) {
+            const int r0 = (int)((long long)M * i / nc), r1 = (int)((long long)M * (i + 1) / nc);
+            SB_TRY(qgemm_grouped_rows(wd, static_cast<const char *>(a) + (size_t)r0 * wd.K * esz, bf16, r1 - r0,
+                                      bias, c + (size_t)r0 * wd.N, st));
         }
         return SB_OK;
     }

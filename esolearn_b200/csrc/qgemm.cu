@@ -574,6 +574,201 @@ __global__ void __launch_bounds__(QGM_FIN_THREADS) qgm_finish_kernel(const QGemv
     }
 }
 
+// ---- grouped scales (g = 32 or 64 rows of K per f32 scale and column) -------------
+// y[m,n] = 2^-s_m sum_g scale[g,n] sum_{k in g} A[m,k] q[k,n]: each group's
+// integer sum needs its own scale, so every group gets its own accumulator.
+// CTA (tile, piece) owns a contiguous run of whole groups of one tile.  The
+// producer streams stages of up to 16 k-steps of weights with the matching
+// plane rows (as in qgm_gemm_kernel); the MMA thread issues a group's g/32
+// products (K = 32 each) into one of QGG_NB TMEM buffers and commits it; the
+// four drain warps read the group's sums (one column per lane, every plane
+// row), release the buffer, and add sum * scale in f64 to per-row registers
+// -- groups in ascending order.  The CTA's f64 partials go to
+// part[tile][piece][row][128] without atomics; the finish kernel adds the
+// pieces of a tile in piece order, so the result does not depend on timing.
+constexpr int QGG_MAX_M = 32;  // rows per launch (3 * 32 + 1 = 97 plane rows, 112 TMEM columns)
+constexpr int QGG_NB = 4;      // TMEM accumulator buffers of 128 columns
+constexpr int QGG_STAGE_KS = 16;
+
+__host__ __device__ inline int qgg_slot_bytes(int np) { return QGG_STAGE_KS * (QGM_TN + np) * 16; }
+
+__global__ void __launch_bounds__(QGM_THREADS, 1)
+    qgg_gemm_kernel(const QWeightDesc w, const QGemmWs ws, double *part, int M, int np, int nst, int S) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    // full[nst], empty[nst], tmem full[NB], tmem empty[NB], mma done
+    __shared__ __align__(8) unsigned long long bars[2 * QGM_MAX_NST + 2 * QGG_NB + 1];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile = blockIdx.x, piece = blockIdx.y;
+    const int R = w.group / 16;                 // k-steps per group
+    const int NG = w.KS / R;                    // groups per tile
+    const int g0 = (int)((long long)NG * piece / S), g1 = (int)((long long)NG * (piece + 1) / S);
+    const int ks0 = g0 * R, ks1 = g1 * R;
+    const int slot_bytes = qgg_slot_bytes(np), wslot = QGG_STAGE_KS * QGM_TN * 16;
+    const uint32_t b_full = smem_u32(&bars[0]), b_empty = smem_u32(&bars[QGM_MAX_NST]);
+    const uint32_t b_tfull = smem_u32(&bars[2 * QGM_MAX_NST]), b_tempty = b_tfull + 8 * QGG_NB;
+    const uint32_t b_done = b_tempty + 8 * QGG_NB;
+    if (tid == 0) {
+        for (int i = 0; i < nst; i++) {
+            mbar_init(b_full + 8 * i, 1);
+            mbar_init(b_empty + 8 * i, 1);  // arrived by tcgen05.commit
+        }
+        for (int i = 0; i < QGG_NB; i++) {
+            mbar_init(b_tfull + 8 * i, 1);
+            mbar_init(b_tempty + 8 * i, 4);  // one arrival per draining warp
+        }
+        mbar_init(b_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_abort = 0;
+    }
+    if (warp == 0) tmem_alloc(&s_tmem, 128 * QGG_NB);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    pdl_launch_dependents();
+    const uint32_t tmem = s_tmem;
+    const uint32_t ring = smem_u32(smem);
+
+    if (warp == 5) {
+        if (lane == 0) {  // producer
+            uint32_t it = 0, slot = 0, par = 0;
+            bool waited = false;
+            for (int ks = ks0; ks < ks1; ks += QGG_STAGE_KS) {
+                const int nks = min(QGG_STAGE_KS, ks1 - ks);
+                if (it >= (uint32_t)nst) {
+                    if (!waited) pdl_wait(), waited = true;
+                    if (*(volatile int *)&s_abort || !mbar_wait(b_empty + 8 * slot, par ^ 1)) {
+                        atomicOr(&qgm_error_flag, 1u);
+                        s_abort = 1;
+                        break;
+                    }
+                }
+                const uint32_t wbytes = (uint32_t)nks * QGM_TN * 16, pbytes = (uint32_t)nks * np * 16;
+                const uint32_t dst = ring + slot * slot_bytes;
+                mbar_expect_tx(b_full + 8 * slot, wbytes + pbytes);
+                tma_load_1d(dst, reinterpret_cast<const uint8_t *>(w.w) + ((size_t)tile * w.KS + ks) * QGM_TN * 16,
+                            wbytes, b_full + 8 * slot);
+                if (!waited) pdl_wait(), waited = true;  // the planes come from the previous kernel
+                tma_load_1d(dst + wslot, ws.planes + (size_t)ks * np * 16, pbytes, b_full + 8 * slot);
+                it++;
+                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+            }
+        }
+    } else if (warp == 4) {
+        if (lane == 0) {  // MMA issuer
+            const uint32_t idesc = qgm_idesc(np);
+            uint32_t slot = 0, par = 0;
+            int gi = 0;
+            bool ok = true;
+            for (int ks = ks0; ks < ks1 && ok; ks += QGG_STAGE_KS) {
+                const int nks = min(QGG_STAGE_KS, ks1 - ks);
+                if (!mbar_wait(b_full + 8 * slot, par)) ok = false;
+                tc_fence_after();
+                const uint32_t a0 = ring + slot * slot_bytes, p0 = a0 + wslot;
+                for (int gk = 0; gk < nks && ok; gk += R, gi++) {
+                    const uint32_t buf = gi % QGG_NB;
+                    if (gi >= QGG_NB && !mbar_wait(b_tempty + 8 * buf, (gi / QGG_NB - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kk = 0; kk < R / 2; kk++) {
+                        const int k = gk + 2 * kk;
+                        const uint64_t da = umma_sdesc(a0 + k * QGM_TN * 16, QGM_TN * 16, 128);
+                        const uint64_t db = umma_sdesc(p0 + k * np * 16, np * 16, 128);
+                        umma_i8(tmem + buf * 128, da, db, idesc, kk == 0 ? 0u : 1u);
+                    }
+                    umma_commit(b_tfull + 8 * buf);  // the group's sums are complete
+                }
+                umma_commit(b_empty + 8 * slot);  // the slot is free once these products are done
+                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
+            }
+            if (!ok) {
+                atomicOr(&qgm_error_flag, 1u);
+                s_abort = 1;
+            }
+            umma_commit(b_done);
+            if (!mbar_wait(b_done, 0)) atomicOr(&qgm_error_flag, 1u);
+        }
+    } else if (warp < 4) {
+        // ---- drain: one column per lane, every row, groups in order
+        pdl_wait();
+        const int col = warp * 32 + lane;
+        const float *gs = w.gscale + (size_t)tile * NG * QGM_TN + col;
+        const int nld = np >> 4;
+        double acc[QGG_MAX_M];
+#pragma unroll
+        for (int m = 0; m < QGG_MAX_M; m++) acc[m] = 0.0;
+        float sc_next = g0 < g1 ? __ldg(gs + (size_t)g0 * QGM_TN) : 0.f;
+        for (int g = g0, gi = 0; g < g1; g++, gi++) {
+            const uint32_t buf = gi % QGG_NB;
+            const float sc = sc_next;
+            if (g + 1 < g1) sc_next = __ldg(gs + (size_t)(g + 1) * QGM_TN);
+            const bool ok = !s_abort && mbar_wait(b_tfull + 8 * buf, (gi / QGG_NB) & 1);
+            if (__any_sync(0xffffffffu, !ok)) {
+                atomicOr(&qgm_error_flag, 1u);
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            uint32_t d[7 * 16];
+            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16) + buf * 128;
+#pragma unroll
+            for (int j = 0; j < 7; j++)
+                if (j < nld) tmem_ld16(lb + 16 * j, d + 16 * j);
+            tmem_wait_ld(d);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the buffer may take the next group
+            const long long ones = (long long)(int)d[0];
+            const double scd = (double)sc;
+#pragma unroll
+            for (int m = 0; m < QGG_MAX_M; m++) {
+                if (m < M) {
+                    const long long t = (long long)(int)d[1 + 3 * m] + ((long long)(int)d[2 + 3 * m] << 8) +
+                                        ((long long)(int)d[3 + 3 * m] << 16) - (ones << 23);
+                    acc[m] = fma((double)t, scd, acc[m]);
+                }
+            }
+        }
+        double *out = part + ((size_t)tile * S + piece) * QGG_MAX_M * QGM_TN + col;
+#pragma unroll
+        for (int m = 0; m < QGG_MAX_M; m++)
+            if (m < M) out[(size_t)m * QGM_TN] = acc[m];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 128 * QGG_NB);
+}
+
+// y[m, n] = 2^-s_m * sum over the tile's pieces (in order) of the partials;
+// then the STORE or BIAS epilogue.  One thread per (row, column).
+template <int EPI>
+__global__ void __launch_bounds__(QGM_TN) qgg_finish_kernel(const QGemvArgs a, const QGemmWs ws, const double *part,
+                                                            int S) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tile = blockIdx.x, m = blockIdx.y, c = threadIdx.x;
+    const int n = tile * QGM_TN + c;
+    if (n >= a.w.N) return;
+    const double *p = part + ((size_t)tile * S * QGG_MAX_M + m) * QGM_TN + c;
+    double t = 0.0;
+    for (int i = 0; i < S; i++) t += p[(size_t)i * QGG_MAX_M * QGM_TN];
+    float y = (float)(t * pow2_neg(ws.shift[m]) * ws.rstd[m]);
+    if (EPI == QEPI_BIAS) y = __fadd_rn(y, a.bias[n]);
+    a.out[(size_t)m * a.ldo + n] = y;
+}
+
+int qgg_nst(int np, int *limit_out) {
+    static int lim[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!lim[dev & 63]) SB_TRY(allow_max_dynamic_smem(qgg_gemm_kernel, &lim[dev & 63]));
+    *limit_out = lim[dev & 63];
+    return std::min(QGM_MAX_NST, lim[dev & 63] / qgg_slot_bytes(np));
+}
+
 int qgm_nst(int np, int *limit_out) {
     static int lim[64] = {};
     int dev = 0;
@@ -607,6 +802,44 @@ size_t qgemm_planes_bytes(int K, int M) { return (size_t)ceil_div(K, 16) * qgemm
 
 bool qgemm_supported(const QWeightDesc &w, int M) {
     return w.TN == QGM_TN && w.group == 0 && (w.KS % 2) == 0 && M > QG_MAX_M && M <= QGM_MAX_M && w.K <= 32768;
+}
+
+bool qgemm_grouped_supported(const QWeightDesc &w, int M) {
+    return w.TN == QGM_TN && (w.group == 32 || w.group == 64) && w.gscale && w.K % w.group == 0 && M > QG_MAX_M &&
+           M <= QGG_MAX_M && w.K <= 32768;
+}
+
+int qgemm_grouped_pieces(const QWeightDesc &w) {
+    const int NG = w.KS / (w.group / 16);
+    return std::max(1, std::min(NG, ceil_div(2 * device_props().sm_count, w.ntiles)));
+}
+
+size_t qgemm_grouped_part_doubles(const QWeightDesc &w) {
+    return (size_t)w.ntiles * qgemm_grouped_pieces(w) * QGG_MAX_M * QGM_TN;
+}
+
+int qgemm_grouped_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, double *part, cudaStream_t st, bool pdl) {
+    SB_CHECK(qgemm_grouped_supported(a.w, a.M), SB_ERR_UNSUPPORTED,
+             "qgemm (grouped): weight/rows not supported (TN %d, group %d, M %d)", a.w.TN, a.w.group, a.M);
+    SB_CHECK(epi == QEPI_STORE || epi == QEPI_BIAS, SB_ERR_UNSUPPORTED, "qgemm (grouped): epilogue %d", epi);
+    SB_CHECK(a.norm_w == nullptr, SB_ERR_ARG, "qgemm (grouped): no fused RMSNorm");
+    SB_CHECK(ws.planes && ws.shift && ws.rstd && part, SB_ERR_ARG, "qgemm (grouped): missing scratch");
+    const int np = qgemm_np(a.M);
+    int limit = 0;
+    const int nst = qgg_nst(np, &limit);
+    SB_CHECK(nst >= 2, SB_ERR_SHAPE, "qgemm (grouped): %d B per stage (limit %d)", qgg_slot_bytes(np), limit);
+    SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + ceil_div(a.w.KS, 16)), dim3(QGM_PL_THREADS), 0, st, pdl, a, ws,
+                       np));
+    const int S = qgemm_grouped_pieces(a.w);
+    SB_CUDA_TRY(launch(qgg_gemm_kernel, dim3(a.w.ntiles, S), dim3(QGM_THREADS), (size_t)nst * qgg_slot_bytes(np), st,
+                       pdl, a.w, ws, part, a.M, np, nst, S));
+    if (epi == QEPI_BIAS)
+        SB_CUDA_TRY(launch(qgg_finish_kernel<QEPI_BIAS>, dim3(a.w.ntiles, a.M), dim3(QGM_TN), 0, st, pdl, a, ws,
+                           (const double *)part, S));
+    else
+        SB_CUDA_TRY(launch(qgg_finish_kernel<QEPI_STORE>, dim3(a.w.ntiles, a.M), dim3(QGM_TN), 0, st, pdl, a, ws,
+                           (const double *)part, S));
+    return SB_OK;
 }
 
 int qgemm_check_error() {

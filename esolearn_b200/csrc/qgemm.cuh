@@ -31,6 +31,14 @@ bool qgemm_supported(const QWeightDesc &w, int M);
 // through the tensor cores into exact int64 column sums, finish (scale +
 // epilogue; clears the sums).  pdl enables programmatic dependent launch.
 int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl);
+// Group-scaled weights (g = 32 or 64) on the tensor cores, 5 to 32 rows per
+// launch: one TMEM accumulator per group, the group scales applied in f64 as
+// the groups are drained; per-(tile, piece) f64 partials in `part`
+// (qgemm_grouped_part_doubles of them) are summed in piece order by the finish
+// kernel.  Epilogues STORE and BIAS.
+bool qgemm_grouped_supported(const QWeightDesc &w, int M);
+size_t qgemm_grouped_part_doubles(const QWeightDesc &w);
+int qgemm_grouped_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, double *part, cudaStream_t st, bool pdl);
 // Reports (and clears) a timed-out pipeline wait of the GEMM kernel.
 int qgemm_check_error();
 

@@ -3,8 +3,8 @@ timed on the device for every cell of the sweep configuration.
 
 Inputs follow the sweep's definition: int8 weights uniform in [-127, 127];
 f32 scales per group of 32 or 64 input rows equal to absmax/127 of N(0, 0.02)
-source groups (group 0 = one per-tensor scale, the engine's format, packed in
-128-column tiles so 5+ rows run on the tensor cores); bf16 activations
+source groups (group 0 = one per-tensor scale, the engine's format; every
+weight packed in 128-column tiles so 5+ rows run on the tensor cores); bf16 activations
 ~ N(0, 1); M in {1, 8, 32, 128}; (K, N) in {(4096, 4096), (4096, 11008),
 (11008, 4096), (4096, 32000)}; f32 output.
 
@@ -44,7 +44,7 @@ def make_weight(K: int, N_: int, group: int, seed: int):
     for g in range(K // group):  # one group of source rows at a time keeps host memory small
         src = rng.standard_normal((group, N_), dtype=np.float32) * np.float32(0.02)
         scales[g] = np.abs(src).max(axis=0) / np.float32(127.0)
-    return QWeight(q, scales, group=group)
+    return QWeight(q, scales, group=group, tile_n=128)
 
 
 def algorithmic_bytes(M: int, K: int, N_: int, group: int) -> int:

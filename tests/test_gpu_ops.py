@@ -138,6 +138,30 @@ def test_matmul_grouped_bf16_sweep_shapes(group, M, K, N_):
     qw = QWeight(q, scales, group=group)
     out = matmul_i8_f32(a16.cuda(), qw).cpu().numpy()
     assert rel_err(out, ref) < TOL_GEMV
+    # 128-column tiles: 5+ rows take the tensor-core path (one accumulator per
+    # group, chunks of at most 32 rows), 1-4 rows the GEMV
+    qt = QWeight(q, scales, group=group, tile_n=128)
+    out_t = matmul_i8_f32(a16.cuda(), qt).cpu().numpy()
+    assert rel_err(out_t, ref) < TOL_GEMV
+    again = matmul_i8_f32(a16.cuda(), qt).cpu().numpy()
+    assert np.array_equal(again, out_t)  # deterministic: pieces are added in a fixed order
+
+
+@pytest.mark.parametrize("M", [5, 17, 32, 33, 77])
+@pytest.mark.parametrize("group", [32, 64])
+def test_grouped_tensor_core_rows_and_bias(M, group):
+    # Row counts around the 32-row chunking, with the bias epilogue (QuantLinear
+    # with group scales), against the derived grouped oracle.
+    rng = np.random.default_rng(M * 3 + group)
+    K, N_ = 1024, 640
+    q = rng.integers(-127, 128, (K, N_), dtype=np.int8)
+    scales = (rng.random((K // group, N_)) * 1e-3 + 1e-4).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    bias = rng.standard_normal(N_).astype(np.float32)
+    ref = O.matmul_i8_f32_grouped(x, q, scales, group, M, K, N_) + bias[None, :]
+    qt = QWeight(q, scales, group=group, tile_n=128)
+    out = matmul_i8_f32(dev(x), qt, bias=dev(bias)).cpu().numpy()
+    assert rel_err(out, ref) < TOL_GEMV
 
 
 @pytest.mark.parametrize("seq", [1, 3, 77, 200])
