@@ -589,10 +589,13 @@ __global__ void __launch_bounds__(QGM_FIN_THREADS) qgm_finish_kernel(const QGemv
 constexpr int QGG_MAX_M = 32;  // rows per launch (3 * 32 + 1 = 97 plane rows, 112 TMEM columns)
 constexpr int QGG_NB = 4;      // TMEM accumulator buffers of 128 columns
 constexpr int QGG_STAGE_KS = 16;
+// warps 0-3 and 6-9 drain (two teams of four, each team one column per lane
+// and half of the rows), 4 issues the MMAs, 5 produces
+constexpr int QGG_THREADS = 320;
 
 __host__ __device__ inline int qgg_slot_bytes(int np) { return QGG_STAGE_KS * (QGM_TN + np) * 16; }
 
-__global__ void __launch_bounds__(QGM_THREADS, 1)
+__global__ void __launch_bounds__(QGG_THREADS, 1)
     qgg_gemm_kernel(const QWeightDesc w, const QGemmWs ws, double *part, int M, int np, int nst, int S) {
     extern __shared__ __align__(1024) uint8_t smem[];
     // full[nst], empty[nst], tmem full[NB], tmem empty[NB], mma done
@@ -616,7 +619,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
         }
         for (int i = 0; i < QGG_NB; i++) {
             mbar_init(b_tfull + 8 * i, 1);
-            mbar_init(b_tempty + 8 * i, 4);  // one arrival per draining warp
+            mbar_init(b_tempty + 8 * i, 8);  // one arrival per draining warp
         }
         mbar_init(b_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -691,15 +694,18 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
             umma_commit(b_done);
             if (!mbar_wait(b_done, 0)) atomicOr(&qgm_error_flag, 1u);
         }
-    } else if (warp < 4) {
-        // ---- drain: one column per lane, every row, groups in order
+    } else {
+        // ---- drain: one column per lane, half of the rows per team, groups in order
         pdl_wait();
-        const int col = warp * 32 + lane;
+        const int q = warp & 3;                   // TMEM lane quarter of this warp
+        const int team = warp < 4 ? 0 : 1;  // rows [0, 16) or [16, 32)
+        const int col = q * 32 + lane;
         const float *gs = w.gscale + (size_t)tile * NG * QGM_TN + col;
         const int nld = np >> 4;
-        double acc[QGG_MAX_M];
+        constexpr int HALF = QGG_MAX_M / 2;
+        double acc[HALF];
 #pragma unroll
-        for (int m = 0; m < QGG_MAX_M; m++) acc[m] = 0.0;
+        for (int m = 0; m < HALF; m++) acc[m] = 0.0;
         float sc_next = g0 < g1 ? __ldg(gs + (size_t)g0 * QGM_TN) : 0.f;
         for (int g = g0, gi = 0; g < g1; g++, gi++) {
             const uint32_t buf = gi % QGG_NB;
@@ -713,7 +719,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
             }
             tc_fence_after();
             uint32_t d[7 * 16];
-            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16) + buf * 128;
+            const uint32_t lb = tmem + ((uint32_t)(q * 32) << 16) + buf * 128;
 #pragma unroll
             for (int j = 0; j < 7; j++)
                 if (j < nld) tmem_ld16(lb + 16 * j, d + 16 * j);
@@ -723,19 +729,31 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
             if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the buffer may take the next group
             const long long ones = (long long)(int)d[0];
             const double scd = (double)sc;
+            // static register indices: each team's rows are a compile-time range
+            if (team == 0) {
 #pragma unroll
-            for (int m = 0; m < QGG_MAX_M; m++) {
-                if (m < M) {
-                    const long long t = (long long)(int)d[1 + 3 * m] + ((long long)(int)d[2 + 3 * m] << 8) +
-                                        ((long long)(int)d[3 + 3 * m] << 16) - (ones << 23);
-                    acc[m] = fma((double)t, scd, acc[m]);
-                }
+                for (int i = 0; i < HALF; i++)
+                    if (i < M) {
+                        const long long t = (long long)(int)d[1 + 3 * i] + ((long long)(int)d[2 + 3 * i] << 8) +
+                                            ((long long)(int)d[3 + 3 * i] << 16) - (ones << 23);
+                        // |t| < 2^51: exact to f64 with an integer add and one f64 add
+                        acc[i] = fma(i64_to_f64(t), scd, acc[i]);
+                    }
+            } else {
+#pragma unroll
+                for (int i = 0; i < HALF; i++)
+                    if (HALF + i < M) {
+                        const int m = HALF + i;
+                        const long long t = (long long)(int)d[1 + 3 * m] + ((long long)(int)d[2 + 3 * m] << 8) +
+                                            ((long long)(int)d[3 + 3 * m] << 16) - (ones << 23);
+                        acc[i] = fma(i64_to_f64(t), scd, acc[i]);
+                    }
             }
         }
         double *out = part + ((size_t)tile * S + piece) * QGG_MAX_M * QGM_TN + col;
 #pragma unroll
-        for (int m = 0; m < QGG_MAX_M; m++)
-            if (m < M) out[(size_t)m * QGM_TN] = acc[m];
+        for (int i = 0; i < HALF; i++)
+            if (team * HALF + i < M) out[(size_t)(team * HALF + i) * QGM_TN] = acc[i];
     }
     tc_fence_before();
     __syncthreads();
@@ -831,7 +849,7 @@ int qgemm_grouped_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, double 
     SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + ceil_div(a.w.KS, 16)), dim3(QGM_PL_THREADS), 0, st, pdl, a, ws,
                        np));
     const int S = qgemm_grouped_pieces(a.w);
-    SB_CUDA_TRY(launch(qgg_gemm_kernel, dim3(a.w.ntiles, S), dim3(QGM_THREADS), (size_t)nst * qgg_slot_bytes(np), st,
+    SB_CUDA_TRY(launch(qgg_gemm_kernel, dim3(a.w.ntiles, S), dim3(QGG_THREADS), (size_t)nst * qgg_slot_bytes(np), st,
                        pdl, a.w, ws, part, a.M, np, nst, S));
     if (epi == QEPI_BIAS)
         SB_CUDA_TRY(launch(qgg_finish_kernel<QEPI_BIAS>, dim3(a.w.ntiles, a.M), dim3(QGM_TN), 0, st, pdl, a, ws,

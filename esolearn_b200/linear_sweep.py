@@ -3,8 +3,9 @@ timed on the device for every cell of the sweep configuration.
 
 Inputs follow the sweep's definition: int8 weights uniform in [-127, 127];
 f32 scales per group of 32 or 64 input rows equal to absmax/127 of N(0, 0.02)
-source groups (group 0 = one per-tensor scale, the engine's format; every
-weight packed in 128-column tiles so 5+ rows run on the tensor cores); bf16 activations
+source groups (group 0 = one per-tensor scale, the engine's format, packed in
+128-column tiles; grouped weights are packed in the GEMV's own tile width for
+1-4 rows and in 128-column tiles, which run on the tensor cores, for 5+); bf16 activations
 ~ N(0, 1); M in {1, 8, 32, 128}; (K, N) in {(4096, 4096), (4096, 11008),
 (11008, 4096), (4096, 32000)}; f32 output.
 
@@ -33,18 +34,22 @@ ROWS = [1, 8, 32, 128]
 GROUPS = [0, 32, 64]
 
 
-def make_weight(K: int, N_: int, group: int, seed: int):
-    """The sweep's weight for one (K, N, group) cell."""
+def make_weight(K: int, N_: int, group: int, seed: int, tile_n: int = 128):
+    """The sweep's weight for one (K, N, group) cell (QWeight, or a dict of
+    them by tile width when tile_n is a tuple)."""
     rng = np.random.default_rng(seed)
     q = rng.integers(-127, 128, (K, N_), dtype=np.int8)
     if group == 0:
         src = rng.standard_normal((K, N_), dtype=np.float32) * np.float32(0.02)
-        return QWeight(q, [np.float32(np.abs(src).max() / np.float32(127.0))], tile_n=128)
-    scales = np.empty((K // group, N_), np.float32)
-    for g in range(K // group):  # one group of source rows at a time keeps host memory small
-        src = rng.standard_normal((group, N_), dtype=np.float32) * np.float32(0.02)
-        scales[g] = np.abs(src).max(axis=0) / np.float32(127.0)
-    return QWeight(q, scales, group=group, tile_n=128)
+        scales = [np.float32(np.abs(src).max() / np.float32(127.0))]
+    else:
+        scales = np.empty((K // group, N_), np.float32)
+        for g in range(K // group):  # one group of source rows at a time keeps host memory small
+            src = rng.standard_normal((group, N_), dtype=np.float32) * np.float32(0.02)
+            scales[g] = np.abs(src).max(axis=0) / np.float32(127.0)
+    if isinstance(tile_n, tuple):
+        return {tn: QWeight(q, scales, group=group, tile_n=tn) for tn in tile_n}
+    return QWeight(q, scales, group=group, tile_n=tile_n)
 
 
 def algorithmic_bytes(M: int, K: int, N_: int, group: int) -> int:
@@ -85,8 +90,12 @@ def run(iters: int = 10, peak_gbs: float | None = None, shapes=SHAPES, rows=ROWS
     results = []
     for (K, N_) in shapes:
         for group in groups:
-            qw = make_weight(K, N_, group, seed=K * 7 + N_ + group)
+            # per-tensor: the engine's 128-column packing; grouped: the GEMV's
+            # own tile width for 1-4 rows, 128-column tiles (tensor cores) beyond
+            tns = (128,) if group == 0 else (0, 128)
+            qws = make_weight(K, N_, group, seed=K * 7 + N_ + group, tile_n=tns)
             for M in rows:
+                qw = qws[128] if (group == 0 or M > 4) else qws[0]
                 t = time_cell(qw, M, iters, flush)
                 b = algorithmic_bytes(M, K, N_, group)
                 r = {"K": K, "N": N_, "group": group, "M": M, "us": t * 1e6, "gbs": b / t / 1e9,
@@ -94,7 +103,7 @@ def run(iters: int = 10, peak_gbs: float | None = None, shapes=SHAPES, rows=ROWS
                 if peak_gbs:
                     r["hbm_frac"] = r["gbs"] / peak_gbs
                 results.append(r)
-            del qw
+            del qws, qw
     return results
 
 
