@@ -100,7 +100,7 @@ int ds_check_error(unsigned *sync_dev, cudaStream_t st) {
     SB_CUDA_TRY(cudaMemcpyAsync(&f, sync_dev + 2, sizeof f, cudaMemcpyDeviceToHost, st));
     SB_CUDA_TRY(cudaStreamSynchronize(st));
     if (f) {
-        SB_CUDA_TRY(cudaMemsetAsync(sync_dev, 0, 3 * sizeof(unsigned), st));
+        SB_CUDA_TRY(cudaMemsetAsync(sync_dev, 0, DS_SYNC_WORDS * sizeof(unsigned), st));
         SB_CUDA_TRY(cudaStreamSynchronize(st));
         return set_error(SB_ERR_TIMEOUT, "decode step: a bounded wait timed out; the step was abandoned");
     }

@@ -22,6 +22,10 @@ constexpr int DS_QMAX_H = 8;   // input quads per consumer thread for rows of wi
 constexpr int DS_QMAX_F = 16;  // ... for the SwiGLU row of width F (<= 16384)
 constexpr int DS_MAX_NST = 16;
 constexpr int DS_STAMPS = 5;  // timeline readings per phase and CTA
+// Words of the step's sync array: phase counter, exits, abort flag, then per
+// layer parity the bound on |attention output| and max|SwiGLU output| (f32
+// bits, raised with atomicMax) that set the o and down inputs' exponents.
+constexpr int DS_SYNC_ATT_BOUND = 4, DS_SYNC_ACT_BOUND = 6, DS_SYNC_WORDS = 8;
 // GEMV products of the step on the tcgen05 tensor cores (true) or with dp4a
 // on the CUDA cores (false); the same exact integer sums either way.  Measured
 // on the 7B shape at context 584 (per layer): dp4a 66.7 us, tensor cores
@@ -95,7 +99,8 @@ struct DsArgs {
     float *logits = nullptr;    // [V]
     float *cand_val = nullptr;  // [grid] per-CTA argmax candidates
     int *cand_idx = nullptr;
-    unsigned *sync = nullptr;   // [0] phase arrivals, [1] exits, [2] abort flag (zeroed by the host)
+    unsigned *sync = nullptr;   // [DS_SYNC_WORDS]: [0] phase arrivals, [1] exits, [2] abort flag, [4..7]
+                                // bounds (zeroed by the host once, reset by every step)
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
     unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
     int nst = 0;                // ring stages

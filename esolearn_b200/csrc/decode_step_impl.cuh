@@ -24,6 +24,7 @@ extern __shared__ __align__(1024) uint8_t ds_smem[];
 struct DsShared {
     double red_d[8][2];
     float cand_v[8];
+    float red_f[8];
     int cand_i[8];
     double rstd;  // of the last GEMV input stage
     int shift;
@@ -263,19 +264,88 @@ __device__ __noinline__ void ds_in_resid(const float *x_src, const long long *ac
     ds_quantize<QMAX>(v, ssq, amx, K, nq, norm != nullptr, eps, pa_off);
 }
 
-// Input = the attention output: each q head's partial records (one per CTA
-// that worked on its kv head) combined in CTA order,
+// ---- partial input stages ------------------------------------------------------
+// A CTA's GEMV units read only some k-steps of the input row: its range of
+// the tile-major unit sequence covers k-steps [ka, ka + na) of one tile and,
+// when it runs into the next tile, [0, nb).  (A range of a whole tile or
+// more reads every k-step.)
+__device__ __forceinline__ void ds_needed(int KS, int ntiles, int G, int cta, int &ka, int &na, int &nb) {
+    const int upt = (KS + DS_UNIT_KS - 1) / DS_UNIT_KS;
+    const int U = ntiles * upt;
+    const int u0 = (int)((long long)U * cta / G), u1 = (int)((long long)U * (cta + 1) / G);
+    const int n = u1 - u0;
+    ka = 0, na = 0, nb = 0;
+    if (n <= 0) return;
+    if (n >= upt) {
+        na = KS;
+        return;
+    }
+    const int ut0 = u0 % upt;
+    ka = ut0 * DS_UNIT_KS;
+    if (ut0 + n <= upt) {
+        na = min(n * DS_UNIT_KS, KS - ka);
+    } else {
+        na = KS - ka;
+        nb = (ut0 + n - upt) * DS_UNIT_KS;
+    }
+}
+
+// Fixed-point exponent of a row whose |values| are at most mx (the same rule
+// as ds_quantize: |a * 2^shift| < 2^22).
+__device__ __forceinline__ int ds_shift_of(float mx) {
+    int e = 0;
+    if (mx > 0.f) frexpf(mx, &e);
+    const int s2 = mx > 0.f ? 22 - e : 0;
+    return s2 < -126 ? -126 : (s2 > 126 ? 126 : s2);
+}
+
+// Digit planes of quad q (4 values) at scale sc = 2^shift (see ds_quantize).
+__device__ __forceinline__ void ds_put_quad(uint32_t *planes, int q, float4 v, float sc) {
+    const float xs4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float t = __fmul_rn(xs4[i], sc);
+        const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+        const int d0 = ((A + 128) & 0xff) - 128;
+        const int A1 = (A - d0) >> 8;
+        const int d1 = ((A1 + 128) & 0xff) - 128;
+        const int d2 = (A1 - d1) >> 8;
+        w0 |= (uint32_t)(d0 & 0xff) << (8 * i);
+        w1 |= (uint32_t)(d1 & 0xff) << (8 * i);
+        w2 |= (uint32_t)(d2 & 0xff) << (8 * i);
+    }
+    uint32_t *pk = planes + (size_t)(q >> 2) * 12 + (q & 3);
+    pk[0] = w0;
+    pk[4] = w1;
+    pk[8] = w2;
+}
+
+// Input = the attention output, only the K rows this CTA's units of the
+// projection read (the heads they span): each q head's partial records (one
+// per CTA that worked on its kv head) combined in CTA order,
 //   out = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c,  M = max_c m_c.
-// The (m, l) of all records first go to a table in shared memory (aliasing
-// the planes, which are written only after the last read of the table).
-template <int HD, int REP, int QMAX>
-__device__ __forceinline__ void ds_in_att(const float *part, unsigned U, int nch, int G, int nh, int K, int KS,
-                                          int rmax, size_t pa_off) {
-    const int tid = threadIdx.x, nq = KS * 4;
+// The (m, l) of the records first go to a table in shared memory (aliasing
+// the planes, which are written only after the last read of the table).  The
+// exponent comes from `bound`, an upper bound on |attention output| over the
+// whole row that the attention phase published (each output is a convex
+// combination of the records' o/l), so no CTA needs the whole row.  rstd = 1.
+template <int HD, int REP>
+__device__ __noinline__ void ds_in_att_part(const float *part, unsigned U, int nch, int G, int nh, int K, int KS,
+                                            int ntiles_next, int rmax, float bound, size_t pa_off) {
+    const int tid = threadIdx.x, cta = blockIdx.x;
+    int ka, na, nb;
+    ds_needed(KS, ntiles_next, G, cta, ka, na, nb);
+    const int ea0 = 16 * ka, ea1 = min(K, 16 * (ka + na)), eb1 = min(K, 16 * nb);
+    auto needed = [&](int hq) {
+        const int e0 = hq * HD, e1 = e0 + HD;
+        return (e0 < ea1 && e1 > ea0) || (e0 < eb1);
+    };
     float *tab = reinterpret_cast<float *>(ds_smem + pa_off);  // [nh][rmax] (w, l), then [nh] sums
     float *lsum = tab + (size_t)2 * nh * rmax;
     for (int i = tid; i < nh * rmax; i += DS_CONSUMERS) {
         const int hq = i / rmax, k = i - hq * rmax;
+        if (!needed(hq)) continue;
         const int g = hq / REP, r = hq - g * REP;
         const unsigned ub = (unsigned)g * nch;
         const int c = ds_owner(ub, U, G) + k;
@@ -290,6 +360,7 @@ __device__ __forceinline__ void ds_in_att(const float *part, unsigned U, int nch
     }
     ds_sync();
     for (int hq = tid; hq < nh; hq += DS_CONSUMERS) {
+        if (!needed(hq)) continue;
         float *t = tab + (size_t)2 * hq * rmax;
         float M = -INFINITY;
         for (int k = 0; k < rmax; k++) M = fmaxf(M, t[2 * k]);
@@ -303,63 +374,91 @@ __device__ __forceinline__ void ds_in_att(const float *part, unsigned U, int nch
         lsum[hq] = Ls;
     }
     ds_sync();
-    // Each thread combines its QMAX quads; the loads of all its quads for
-    // RCH records at a time are issued before any is used.
-    constexpr int RCH = 3;
-    float4 v[QMAX];
-    float O[QMAX][4];
-    const float *rec0[QMAX];
-    const float *tq[QMAX];
-#pragma unroll
-    for (int j = 0; j < QMAX; j++) {
-        const int k0 = (tid + j * DS_CONSUMERS) * 4;
-        O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
-        rec0[j] = nullptr;
-        tq[j] = tab;
-        if (k0 < K) {
-            const int hq = k0 / HD, d0 = k0 - hq * HD;
-            const int g = hq / REP, r = hq - g * REP;
-            const int cf = ds_owner((unsigned)g * nch, U, G);
-            tq[j] = tab + (size_t)2 * hq * rmax;
-            rec0[j] = part + (((size_t)g * G + cf) * REP + r) * DS_REC(HD) + d0;
-        }
-    }
+    const int nqa = 4 * na, nqt = 4 * (na + nb);
+    float4 xs[DS_QMAX_H];
     const size_t cstride = (size_t)REP * DS_REC(HD);
-    for (int kb = 0; kb < rmax; kb += RCH) {
-        float4 o[QMAX][RCH];
-        float w[QMAX][RCH];
 #pragma unroll
-        for (int j = 0; j < QMAX; j++)
+    for (int j = 0; j < DS_QMAX_H; j++) {
+        const int idx = tid + j * DS_CONSUMERS;
+        xs[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (idx >= nqt) continue;
+        const int q = idx < nqa ? 4 * ka + idx : idx - nqa;
+        const int k0 = 4 * q;
+        if (k0 >= K) continue;
+        const int hq = k0 / HD, d0 = k0 - hq * HD;
+        const int g = hq / REP, r = hq - g * REP;
+        const int cf = ds_owner((unsigned)g * nch, U, G);
+        const float *rec0 = part + (((size_t)g * G + cf) * REP + r) * DS_REC(HD) + d0;
+        const float *tq = tab + (size_t)2 * hq * rmax;
+        float O[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int kb = 0; kb < rmax; kb += 4) {
+            float w[4];
+            float4 o[4];
 #pragma unroll
-            for (int i = 0; i < RCH; i++) {
-                w[j][i] = (rec0[j] && kb + i < rmax) ? tq[j][2 * (kb + i)] : 0.f;
-                o[j][i] = w[j][i] != 0.f ? ldcg4(rec0[j] + (size_t)(kb + i) * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < 4; i++) {
+                w[i] = kb + i < rmax ? tq[2 * (kb + i)] : 0.f;
+                o[i] = w[i] != 0.f ? ldcg4(rec0 + (size_t)(kb + i) * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-        for (int j = 0; j < QMAX; j++)
-#pragma unroll
-            for (int i = 0; i < RCH; i++) {
-                if (w[j][i] == 0.f) continue;
-                O[j][0] = fmaf(o[j][i].x, w[j][i], O[j][0]);
-                O[j][1] = fmaf(o[j][i].y, w[j][i], O[j][1]);
-                O[j][2] = fmaf(o[j][i].z, w[j][i], O[j][2]);
-                O[j][3] = fmaf(o[j][i].w, w[j][i], O[j][3]);
+            for (int i = 0; i < 4; i++) {
+                if (w[i] == 0.f) continue;
+                O[0] = fmaf(o[i].x, w[i], O[0]);
+                O[1] = fmaf(o[i].y, w[i], O[1]);
+                O[2] = fmaf(o[i].z, w[i], O[2]);
+                O[3] = fmaf(o[i].w, w[i], O[3]);
             }
-    }
-    float ssq = 0.f, amx = 0.f;
-    const float4 one = make_float4(1.f, 1.f, 1.f, 1.f);
-#pragma unroll
-    for (int j = 0; j < QMAX; j++) {
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int k0 = (tid + j * DS_CONSUMERS) * 4;
-        if (k0 < K) {
-            const float Ls = lsum[k0 / HD];
-            if (Ls > 0.f) x = make_float4(O[j][0] / Ls, O[j][1] / Ls, O[j][2] / Ls, O[j][3] / Ls);
         }
-        ds_accum(x, one, false, ssq, amx, v[j]);
+        const float Ls = lsum[hq];
+        if (Ls > 0.f) xs[j] = make_float4(O[0] / Ls, O[1] / Ls, O[2] / Ls, O[3] / Ls);
     }
+    const int shift = ds_shift_of(bound);
     ds_sync();  // the table is read; the planes may overwrite it
-    ds_quantize<QMAX>(v, ssq, amx, K, nq, false, 0.f, pa_off);
+    if (tid == 0) ds_sh.shift = shift, ds_sh.rstd = 1.0;
+    uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
+    const float sc = __int_as_float((shift + 127) << 23);
+#pragma unroll
+    for (int j = 0; j < DS_QMAX_H; j++) {
+        const int idx = tid + j * DS_CONSUMERS;
+        if (idx >= nqt) continue;
+        ds_put_quad(planes, idx < nqa ? 4 * ka + idx : idx - nqa, xs[j], sc);
+    }
+    if (tid < 12) planes[(size_t)KS * 12 + tid] = 0u;  // the zero k-step after the last
+    fence_proxy_async_smem();
+    ds_sync();
+}
+
+// Input = a row written by other CTAs in this step (the SwiGLU output), only
+// the k-steps this CTA's units read, at the exponent of `bound` = max|row|
+// (published by the phase that wrote the row; exact, so the planes equal
+// those of a whole-row input stage).  No norm, rstd = 1.
+__device__ __noinline__ void ds_in_rows_part(const float *row, int K, int KS, int ntiles_next, int G, float bound,
+                                             size_t pa_off) {
+    const int tid = threadIdx.x, cta = blockIdx.x;
+    int ka, na, nb;
+    ds_needed(KS, ntiles_next, G, cta, ka, na, nb);
+    const int nqa = 4 * na, nqt = 4 * (na + nb);
+    float4 xs[DS_QMAX_F];
+#pragma unroll
+    for (int j = 0; j < DS_QMAX_F; j++) {
+        const int idx = tid + j * DS_CONSUMERS;
+        xs[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (idx >= nqt) continue;
+        const int k0 = 4 * (idx < nqa ? 4 * ka + idx : idx - nqa);
+        if (k0 < K) xs[j] = ldcg4(row + k0);
+    }
+    const int shift = ds_shift_of(bound);
+    if (tid == 0) ds_sh.shift = shift, ds_sh.rstd = 1.0;
+    uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
+    const float sc = __int_as_float((shift + 127) << 23);
+#pragma unroll
+    for (int j = 0; j < DS_QMAX_F; j++) {
+        const int idx = tid + j * DS_CONSUMERS;
+        if (idx >= nqt) continue;
+        ds_put_quad(planes, idx < nqa ? 4 * ka + idx : idx - nqa, xs[j], sc);
+    }
+    if (tid < 12) planes[(size_t)KS * 12 + tid] = 0u;
+    fence_proxy_async_smem();
+    ds_sync();
 }
 
 // ---- GEMV consumer ------------------------------------------------------------
@@ -621,7 +720,8 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                                               const float *cos_row, const float *sin_row, KV *kcl, KV *vcl,
                                               const int *page_table, float *part, int nkv, int q_dim, int kv_dim,
                                               int page_size, int chunk, float q_scale, int G, int cta,
-                                              uint32_t qs_off, uint32_t kvnew_off, uint32_t pa_off) {
+                                              uint32_t qs_off, uint32_t kvnew_off, uint32_t pa_off,
+                                              unsigned *bound_word) {
     using KL = DsKv<KV>;
     constexpr int DPL = HD / 32;  // dims per lane
     constexpr int BR = 4;         // rows per warp per shuffle round
@@ -635,6 +735,7 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
     uint32_t slot = it % nst, par = (it / nst) & 1;
     float q[REP][DPL], o[REP][DPL], m[REP], ls[REP];
     int cur = -1;
+    float bmax = 0.f;  // max over this CTA's records of |o / l| (a bound on every attention output)
     // RoPE of the element pair (d, d^1) of a head whose columns start at
     // col (rope_with_freqs_preloaded, cpu.rs:650-661).
     auto roped = [&](int col, int d) {
@@ -702,6 +803,7 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                 Lz = fmaf(aw[HD + 1], sw, Lz);
             }
             rec[(size_t)r * DS_REC(HD) + d] = O;
+            if (Lz > 0.f) bmax = fmaxf(bmax, fabsf(O / Lz));
             if (d == 0) {
                 rec[(size_t)r * DS_REC(HD) + HD] = M;
                 rec[(size_t)r * DS_REC(HD) + HD + 1] = Lz;
@@ -795,6 +897,15 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
         it++;
     }
     if (cur >= 0) finish(cur);
+    // publish the bound: positive floats order like their bit patterns
+    bmax = warp_max_f(bmax);
+    if (lane == 0) ds_sh.red_f[warp] = bmax;
+    ds_sync();
+    if (tid == 0) {
+        float b = 0.f;
+        for (int w = 0; w < DS_CONSUMERS / 32; w++) b = fmaxf(b, ds_sh.red_f[w]);
+        if (b > 0.f) atomicMax(bound_word, __float_as_uint(b));
+    }
     return it;
 }
 
@@ -981,7 +1092,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             reinterpret_cast<KV *>(static_cast<char *>(a.kc) + (size_t)l * a.layer_kv_bytes),
             reinterpret_cast<KV *>(static_cast<char *>(a.vc) + (size_t)l * a.layer_kv_bytes), a.page_table, a.part,
             a.nkv, a.q_dim, a.kv_dim, a.page_size, a.chunk, a.q_scale, G, cta, (uint32_t)L.qs, (uint32_t)L.kvnew,
-            (uint32_t)L.pa);
+            (uint32_t)L.pa, a.sync + DS_SYNC_ATT_BOUND + (l & 1));
     };
 
     auto accbuf = [&](int j) { return a.acc + (size_t)(j % 3) * a.acc_n; };
@@ -1011,6 +1122,10 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         // ---- QKV: input = RMSNorm(x) (x = embedding, or x + down of the previous layer)
         if (go && l > 0) go = wait_all();
         if (go) {
+            if (writer && tid == 0) {  // the next layer's bounds start at zero (last read two layers ago)
+                a.sync[DS_SYNC_ATT_BOUND + ((l + 1) & 1)] = 0u;
+                a.sync[DS_SYNC_ACT_BOUND + ((l + 1) & 1)] = 0u;
+            }
             if (j >= 2) zero_acc(accbuf(j - 2), npad_gu);
             const float *nw = a.norm_in + (size_t)l * a.h;
             if (l == 0) {
@@ -1039,10 +1154,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) go = wait_all();
         if (go) {
             if (l > 0) zero_acc(accbuf(j - 1), npad_down);
-            if (a.q_dim <= 4 * DS_CONSUMERS * 4)
-                ds_in_att<HD, REP, 4>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
-            else
-                ds_in_att<HD, REP, DS_QMAX_H>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
+            const float ab = __uint_as_float(ld_acquire(a.sync + DS_SYNC_ATT_BOUND + (l & 1)));
+            ds_in_att_part<HD, REP>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, a.nt_o, rmax, ab, pa_off);
             mark(1);
             it = ds_gemv(it, seg, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off, red_off, ready_slot());
         }
@@ -1066,12 +1179,24 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             const long long *gu = accbuf(j + 2);
             const int f0 = (int)((long long)a.F * cta / G), f1 = (int)((long long)a.F * (cta + 1) / G);
             const double fg = gemv_factor(sh.shift, ly.scale[2], sh.rstd), fu = gemv_factor(sh.shift, ly.scale_up, sh.rstd);
+            float amx = 0.f;
             for (int f = f0 + tid; f < f1; f += DS_CONSUMERS) {
                 const int col = (f >> 4) * 32 + (f & 15);
                 const long long tg = __ldcg(gu + col), tu = __ldcg(gu + col + 16);
                 const float yg = gemv_out(tg, fg);
                 const float yu = gemv_out(tu, fu);
-                a.act[f] = __fmul_rn(silu_f64(yg), yu);
+                const float v = __fmul_rn(silu_f64(yg), yu);
+                a.act[f] = v;
+                amx = fmaxf(amx, fabsf(v));
+            }
+            // max|act| over the row, for the down projection's exponent
+            amx = warp_max_f(amx);
+            if (lane == 0) sh.red_f[warp] = amx;
+            ds_sync();
+            if (tid == 0) {
+                float b = 0.f;
+                for (int w = 0; w < DS_CONSUMERS / 32; w++) b = fmaxf(b, sh.red_f[w]);
+                if (b > 0.f) atomicMax(a.sync + DS_SYNC_ACT_BOUND + (l & 1), __float_as_uint(b));
             }
         }
         arrive();
@@ -1080,7 +1205,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) go = wait_all();
         if (go) {
             zero_acc(accbuf(j + 1), npad_o);
-            ds_in_rows<DS_QMAX_F>(a.act, false, nullptr, a.F, a.ks_f, a.eps, nullptr, pa_off);
+            const float fb = __uint_as_float(ld_acquire(a.sync + DS_SYNC_ACT_BOUND + (l & 1)));
+            ds_in_rows_part(a.act, a.F, a.ks_f, a.nt_down, G, fb, pa_off);
             mark(1);
             it = ds_gemv(it, seg, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off, red_off, ready_slot());
         }
@@ -1167,6 +1293,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         }
         a.sync[0] = 0;
         a.sync[1] = 0;
+        for (int i = DS_SYNC_ATT_BOUND; i < DS_SYNC_WORDS; i++) a.sync[i] = 0;  // layer 0's bounds, next step
     }
     // ---- release the tensor memory once no tensor-core work is in flight
     if (warp == 4 && lane == 0) {

@@ -714,7 +714,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
         if ((rc = dalloc_t(m, &m->ds_part, ds_part_floats(m->nkv, m->nh / m->nkv, m->hd))) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_cand_val, (size_t)G)) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_cand_idx, (size_t)G)) != SB_OK) return fail(rc);
-        if ((rc = dalloc_t(m, &m->ds_sync, 4)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_sync, DS_SYNC_WORDS)) != SB_OK) return fail(rc);
     }
     if (B > QG_MAX_M) {
         int nt = m->lm.ntiles;
