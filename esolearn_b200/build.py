@@ -21,6 +21,10 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
+# SB_STEP_TIMELINE=1: the profiling build, with the persistent step's phase
+# timeline compiled in (sb_llama_set_timeline); the default build has none.
+if os.environ.get("SB_STEP_TIMELINE") == "1":
+    FLAGS.append("-DSB_STEP_TIMELINE")
 
 
 def _needs(target: str, deps: list[str]) -> bool:

@@ -84,6 +84,14 @@ int ds_plan(int ksmax, int rep, int hd, int chunk, int kv_f32, int mtab, int *ns
 
 int ds_grid() { return device_props().sm_count; }
 
+bool ds_timeline_built() {
+#ifdef SB_STEP_TIMELINE
+    return true;
+#else
+    return false;
+#endif
+}
+
 int ds_mtab_bytes(int nh, int nkv) { return (2 * nh * (ds_grid() / nkv + 2) + nh) * 4; }
 
 size_t ds_part_floats(int nkv, int rep, int hd) { return (size_t)nkv * ds_grid() * rep * DS_REC(hd); }
@@ -100,7 +108,7 @@ int ds_check_error(unsigned *sync_dev, cudaStream_t st) {
     SB_CUDA_TRY(cudaMemcpyAsync(&f, sync_dev + 2, sizeof f, cudaMemcpyDeviceToHost, st));
     SB_CUDA_TRY(cudaStreamSynchronize(st));
     if (f) {
-        SB_CUDA_TRY(cudaMemsetAsync(sync_dev, 0, DS_SYNC_WORDS * sizeof(unsigned), st));
+        SB_CUDA_TRY(cudaMemsetAsync(sync_dev, 0, 3 * sizeof(unsigned), st));
         SB_CUDA_TRY(cudaStreamSynchronize(st));
         return set_error(SB_ERR_TIMEOUT, "decode step: a bounded wait timed out; the step was abandoned");
     }

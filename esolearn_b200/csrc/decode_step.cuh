@@ -22,44 +22,27 @@ constexpr int DS_QMAX_H = 8;   // input quads per consumer thread for rows of wi
 constexpr int DS_QMAX_F = 16;  // ... for the SwiGLU row of width F (<= 16384)
 constexpr int DS_MAX_NST = 16;
 constexpr int DS_STAMPS = 5;  // timeline readings per phase and CTA
-// Words of the step's sync array: phase counter, exits, abort flag, then per
-// layer parity the bound on |attention output| and max|SwiGLU output| (f32
-// bits, raised with atomicMax) that set the o and down inputs' exponents.
-constexpr int DS_SYNC_ATT_BOUND = 4, DS_SYNC_ACT_BOUND = 6, DS_SYNC_WORDS = 8;
-// GEMV products of the step on the tcgen05 tensor cores (true) or with dp4a
-// on the CUDA cores (false); the same exact integer sums either way.  Measured
-// on the 7B shape at context 584 (per layer): dp4a 66.7 us, tensor cores
-// 77.4 us -- a batch-1 stage is 8 MMAs of N = 16, and the issuer needs about
-// 1 us per 32 KB stage even with the stage resident, against ~0.4 us for the
-// eight dp4a warps; so the CUDA-core consumer is the default.
-constexpr bool DS_TC_GEMV = false;
-// Independent int32 accumulators (16 TMEM columns each) that consecutive
-// tensor-core products of a tile segment rotate over.
-constexpr int DS_NACC = 4;
 
 struct DsSmem {
     size_t ring, pa, red, qs, kvnew, bars, total;
 };
 
-// pa: the fixed-point planes of a GEMV input (the tensor cores' B operand);
-// during attention, the
+// pa: the fixed-point planes of a GEMV input; during attention, the
 // cross-warp reduction of the per-head outputs; in the attention-combine
 // input stage, the table of partial-record weights (mtab bytes).
 __host__ __device__ inline DsSmem ds_layout(int nst, int ksmax, int rep, int hd, int chunk, int mtab) {
     DsSmem L;
     L.ring = 0;
     L.pa = (size_t)nst * DS_STAGE;
-    // planes: (ksmax + 1) k-steps of 48 bytes; the MMA's B descriptor reads
-    // up to 304 bytes past a k-step's start (rows it ignores)
-    size_t pa = (size_t)48 * (ksmax + 1) + 320;
+    size_t pa = (size_t)48 * ksmax;
     const size_t att_red = (size_t)8 * rep * (hd + 2) * 4;
     if (att_red > pa) pa = att_red;
     if ((size_t)mtab > pa) pa = (size_t)mtab;
     L.red = L.pa + ((pa + 127) & ~(size_t)127);
-    L.qs = L.red + (DS_TC_GEMV ? 0 : (size_t)8 * DS_TN * 8);  // CUDA-core consumer's reduction
+    L.qs = L.red + (size_t)8 * DS_TN * 8;
     L.kvnew = L.qs + (size_t)rep * hd * 4;
     L.bars = L.kvnew + (size_t)2 * hd * 4;
-    L.total = L.bars + (size_t)(2 * nst + 5) * 8;  // full[nst], empty[nst], tmem full[2], tmem empty[2], done
+    L.total = L.bars + (size_t)2 * nst * 8;
     return L;
 }
 
@@ -99,8 +82,7 @@ struct DsArgs {
     float *logits = nullptr;    // [V]
     float *cand_val = nullptr;  // [grid] per-CTA argmax candidates
     int *cand_idx = nullptr;
-    unsigned *sync = nullptr;   // [DS_SYNC_WORDS]: [0] phase arrivals, [1] exits, [2] abort flag, [4..7]
-                                // bounds (zeroed by the host once, reset by every step)
+    unsigned *sync = nullptr;   // [0] phase arrivals, [1] exits, [2] abort flag (zeroed by the host)
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
     unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
     int nst = 0;                // ring stages
@@ -114,6 +96,8 @@ bool ds_supported(int h, int F, int q_dim, int hd, int rep, int kv_f32, int page
 int ds_plan(int ksmax, int rep, int hd, int chunk, int kv_f32, int mtab, int *nst, size_t *smem);
 // Number of CTAs (one per SM).
 int ds_grid();
+// Whether the step kernels were compiled with the phase timeline (SB_STEP_TIMELINE).
+bool ds_timeline_built();
 size_t ds_part_floats(int nkv, int rep, int hd);
 int ds_mtab_bytes(int nh, int nkv);
 int ds_launch(const DsArgs &a, int rep, cudaStream_t st);

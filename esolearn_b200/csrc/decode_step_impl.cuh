@@ -13,7 +13,6 @@
 #include <algorithm>
 
 #include "pipeline.cuh"
-#include "tcgen05.cuh"
 
 namespace sb {
 namespace {
@@ -24,13 +23,11 @@ extern __shared__ __align__(1024) uint8_t ds_smem[];
 struct DsShared {
     double red_d[8][2];
     float cand_v[8];
-    float red_f[8];
     int cand_i[8];
     double rstd;  // of the last GEMV input stage
     int shift;
     int abort;  // a bounded wait ran out: skip the rest of the step
     int last;
-    uint32_t tmem;  // base of this CTA's tensor-memory accumulators
 };
 __shared__ DsShared ds_sh;
 
@@ -140,13 +137,6 @@ __device__ __forceinline__ void ds_quantize(const float4 (&v)[QMAX], float ssq, 
         ds_sh.shift = s2 < -126 ? -126 : (s2 > 126 ? 126 : s2);
     }
     ds_sync();
-    // Planes for the tensor cores: k-step-major [KS + 1][3 digits][16 bytes]
-    // (the MMA's B operand, 3 rows of 16 k per k-step, 48 bytes apart), the
-    // last k-step all zero (an odd k-step count ends on it).  Each fixed-point
-    // value A (|A| <= 2^22) is written as signed base-256 digits
-    // A = d0 + 2^8 d1 + 2^16 d2 with d0, d1 in [-128, 127] and |d2| <= 65, so
-    // every plane is an s8 operand and sum_k w*A = D0 + 2^8 D1 + 2^16 D2
-    // exactly (each |D| <= K * 127 * 128 < 2^31).
     uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
     const float sc = __int_as_float((ds_sh.shift + 127) << 23);  // 2^shift, exact
 #pragma unroll
@@ -160,21 +150,14 @@ __device__ __forceinline__ void ds_quantize(const float4 (&v)[QMAX], float ssq, 
             // round to nearest even: |t| < 2^22, so t + 1.5*2^23 has ulp 1
             const float t = __fmul_rn(xs4[i], sc);
             const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
-            const int d0 = ((A + 128) & 0xff) - 128;
-            const int A1 = (A - d0) >> 8;
-            const int d1 = ((A1 + 128) & 0xff) - 128;
-            const int d2 = (A1 - d1) >> 8;
-            w0 |= (uint32_t)(d0 & 0xff) << (8 * i);
-            w1 |= (uint32_t)(d1 & 0xff) << (8 * i);
-            w2 |= (uint32_t)(d2 & 0xff) << (8 * i);
+            w0 |= (uint32_t)(A & 0xff) << (8 * i);
+            w1 |= (uint32_t)((A >> 8) & 0xff) << (8 * i);
+            w2 |= (uint32_t)((A >> 16) & 0xff) << (8 * i);
         }
-        uint32_t *pk = planes + (size_t)(q >> 2) * 12 + (q & 3);
-        pk[0] = w0;
-        pk[4] = w1;
-        pk[8] = w2;
+        planes[0 * nq + q] = w0;
+        planes[1 * nq + q] = w1;
+        planes[2 * nq + q] = w2;
     }
-    if (tid < 12) planes[(size_t)(nq >> 2) * 12 + tid] = 0u;  // the zero k-step after the last
-    fence_proxy_async_smem();  // the tensor core reads the planes
     ds_sync();
 }
 
@@ -264,88 +247,19 @@ __device__ __noinline__ void ds_in_resid(const float *x_src, const long long *ac
     ds_quantize<QMAX>(v, ssq, amx, K, nq, norm != nullptr, eps, pa_off);
 }
 
-// ---- partial input stages ------------------------------------------------------
-// A CTA's GEMV units read only some k-steps of the input row: its range of
-// the tile-major unit sequence covers k-steps [ka, ka + na) of one tile and,
-// when it runs into the next tile, [0, nb).  (A range of a whole tile or
-// more reads every k-step.)
-__device__ __forceinline__ void ds_needed(int KS, int ntiles, int G, int cta, int &ka, int &na, int &nb) {
-    const int upt = (KS + DS_UNIT_KS - 1) / DS_UNIT_KS;
-    const int U = ntiles * upt;
-    const int u0 = (int)((long long)U * cta / G), u1 = (int)((long long)U * (cta + 1) / G);
-    const int n = u1 - u0;
-    ka = 0, na = 0, nb = 0;
-    if (n <= 0) return;
-    if (n >= upt) {
-        na = KS;
-        return;
-    }
-    const int ut0 = u0 % upt;
-    ka = ut0 * DS_UNIT_KS;
-    if (ut0 + n <= upt) {
-        na = min(n * DS_UNIT_KS, KS - ka);
-    } else {
-        na = KS - ka;
-        nb = (ut0 + n - upt) * DS_UNIT_KS;
-    }
-}
-
-// Fixed-point exponent of a row whose |values| are at most mx (the same rule
-// as ds_quantize: |a * 2^shift| < 2^22).
-__device__ __forceinline__ int ds_shift_of(float mx) {
-    int e = 0;
-    if (mx > 0.f) frexpf(mx, &e);
-    const int s2 = mx > 0.f ? 22 - e : 0;
-    return s2 < -126 ? -126 : (s2 > 126 ? 126 : s2);
-}
-
-// Digit planes of quad q (4 values) at scale sc = 2^shift (see ds_quantize).
-__device__ __forceinline__ void ds_put_quad(uint32_t *planes, int q, float4 v, float sc) {
-    const float xs4[4] = {v.x, v.y, v.z, v.w};
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float t = __fmul_rn(xs4[i], sc);
-        const int A = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
-        const int d0 = ((A + 128) & 0xff) - 128;
-        const int A1 = (A - d0) >> 8;
-        const int d1 = ((A1 + 128) & 0xff) - 128;
-        const int d2 = (A1 - d1) >> 8;
-        w0 |= (uint32_t)(d0 & 0xff) << (8 * i);
-        w1 |= (uint32_t)(d1 & 0xff) << (8 * i);
-        w2 |= (uint32_t)(d2 & 0xff) << (8 * i);
-    }
-    uint32_t *pk = planes + (size_t)(q >> 2) * 12 + (q & 3);
-    pk[0] = w0;
-    pk[4] = w1;
-    pk[8] = w2;
-}
-
-// Input = the attention output, only the K rows this CTA's units of the
-// projection read (the heads they span): each q head's partial records (one
-// per CTA that worked on its kv head) combined in CTA order,
+// Input = the attention output: each q head's partial records (one per CTA
+// that worked on its kv head) combined in CTA order,
 //   out = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c,  M = max_c m_c.
-// The (m, l) of the records first go to a table in shared memory (aliasing
-// the planes, which are written only after the last read of the table).  The
-// exponent comes from `bound`, an upper bound on |attention output| over the
-// whole row that the attention phase published (each output is a convex
-// combination of the records' o/l), so no CTA needs the whole row.  rstd = 1.
-template <int HD, int REP>
-__device__ __noinline__ void ds_in_att_part(const float *part, unsigned U, int nch, int G, int nh, int K, int KS,
-                                            int ntiles_next, int rmax, float bound, size_t pa_off) {
-    const int tid = threadIdx.x, cta = blockIdx.x;
-    int ka, na, nb;
-    ds_needed(KS, ntiles_next, G, cta, ka, na, nb);
-    const int ea0 = 16 * ka, ea1 = min(K, 16 * (ka + na)), eb1 = min(K, 16 * nb);
-    auto needed = [&](int hq) {
-        const int e0 = hq * HD, e1 = e0 + HD;
-        return (e0 < ea1 && e1 > ea0) || (e0 < eb1);
-    };
+// The (m, l) of all records first go to a table in shared memory (aliasing
+// the planes, which are written only after the last read of the table).
+template <int HD, int REP, int QMAX>
+__device__ __forceinline__ void ds_in_att(const float *part, unsigned U, int nch, int G, int nh, int K, int KS,
+                                          int rmax, size_t pa_off) {
+    const int tid = threadIdx.x, nq = KS * 4;
     float *tab = reinterpret_cast<float *>(ds_smem + pa_off);  // [nh][rmax] (w, l), then [nh] sums
     float *lsum = tab + (size_t)2 * nh * rmax;
     for (int i = tid; i < nh * rmax; i += DS_CONSUMERS) {
         const int hq = i / rmax, k = i - hq * rmax;
-        if (!needed(hq)) continue;
         const int g = hq / REP, r = hq - g * REP;
         const unsigned ub = (unsigned)g * nch;
         const int c = ds_owner(ub, U, G) + k;
@@ -360,7 +274,6 @@ __device__ __noinline__ void ds_in_att_part(const float *part, unsigned U, int n
     }
     ds_sync();
     for (int hq = tid; hq < nh; hq += DS_CONSUMERS) {
-        if (!needed(hq)) continue;
         float *t = tab + (size_t)2 * hq * rmax;
         float M = -INFINITY;
         for (int k = 0; k < rmax; k++) M = fmaxf(M, t[2 * k]);
@@ -374,91 +287,63 @@ __device__ __noinline__ void ds_in_att_part(const float *part, unsigned U, int n
         lsum[hq] = Ls;
     }
     ds_sync();
-    const int nqa = 4 * na, nqt = 4 * (na + nb);
-    float4 xs[DS_QMAX_H];
-    const size_t cstride = (size_t)REP * DS_REC(HD);
+    // Each thread combines its QMAX quads; the loads of all its quads for
+    // RCH records at a time are issued before any is used.
+    constexpr int RCH = 3;
+    float4 v[QMAX];
+    float O[QMAX][4];
+    const float *rec0[QMAX];
+    const float *tq[QMAX];
 #pragma unroll
-    for (int j = 0; j < DS_QMAX_H; j++) {
-        const int idx = tid + j * DS_CONSUMERS;
-        xs[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx >= nqt) continue;
-        const int q = idx < nqa ? 4 * ka + idx : idx - nqa;
-        const int k0 = 4 * q;
-        if (k0 >= K) continue;
-        const int hq = k0 / HD, d0 = k0 - hq * HD;
-        const int g = hq / REP, r = hq - g * REP;
-        const int cf = ds_owner((unsigned)g * nch, U, G);
-        const float *rec0 = part + (((size_t)g * G + cf) * REP + r) * DS_REC(HD) + d0;
-        const float *tq = tab + (size_t)2 * hq * rmax;
-        float O[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int kb = 0; kb < rmax; kb += 4) {
-            float w[4];
-            float4 o[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                w[i] = kb + i < rmax ? tq[2 * (kb + i)] : 0.f;
-                o[i] = w[i] != 0.f ? ldcg4(rec0 + (size_t)(kb + i) * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                if (w[i] == 0.f) continue;
-                O[0] = fmaf(o[i].x, w[i], O[0]);
-                O[1] = fmaf(o[i].y, w[i], O[1]);
-                O[2] = fmaf(o[i].z, w[i], O[2]);
-                O[3] = fmaf(o[i].w, w[i], O[3]);
-            }
+    for (int j = 0; j < QMAX; j++) {
+        const int k0 = (tid + j * DS_CONSUMERS) * 4;
+        O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
+        rec0[j] = nullptr;
+        tq[j] = tab;
+        if (k0 < K) {
+            const int hq = k0 / HD, d0 = k0 - hq * HD;
+            const int g = hq / REP, r = hq - g * REP;
+            const int cf = ds_owner((unsigned)g * nch, U, G);
+            tq[j] = tab + (size_t)2 * hq * rmax;
+            rec0[j] = part + (((size_t)g * G + cf) * REP + r) * DS_REC(HD) + d0;
         }
-        const float Ls = lsum[hq];
-        if (Ls > 0.f) xs[j] = make_float4(O[0] / Ls, O[1] / Ls, O[2] / Ls, O[3] / Ls);
     }
-    const int shift = ds_shift_of(bound);
+    const size_t cstride = (size_t)REP * DS_REC(HD);
+    for (int kb = 0; kb < rmax; kb += RCH) {
+        float4 o[QMAX][RCH];
+        float w[QMAX][RCH];
+#pragma unroll
+        for (int j = 0; j < QMAX; j++)
+#pragma unroll
+            for (int i = 0; i < RCH; i++) {
+                w[j][i] = (rec0[j] && kb + i < rmax) ? tq[j][2 * (kb + i)] : 0.f;
+                o[j][i] = w[j][i] != 0.f ? ldcg4(rec0[j] + (size_t)(kb + i) * cstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+        for (int j = 0; j < QMAX; j++)
+#pragma unroll
+            for (int i = 0; i < RCH; i++) {
+                if (w[j][i] == 0.f) continue;
+                O[j][0] = fmaf(o[j][i].x, w[j][i], O[j][0]);
+                O[j][1] = fmaf(o[j][i].y, w[j][i], O[j][1]);
+                O[j][2] = fmaf(o[j][i].z, w[j][i], O[j][2]);
+                O[j][3] = fmaf(o[j][i].w, w[j][i], O[j][3]);
+            }
+    }
+    float ssq = 0.f, amx = 0.f;
+    const float4 one = make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+    for (int j = 0; j < QMAX; j++) {
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int k0 = (tid + j * DS_CONSUMERS) * 4;
+        if (k0 < K) {
+            const float Ls = lsum[k0 / HD];
+            if (Ls > 0.f) x = make_float4(O[j][0] / Ls, O[j][1] / Ls, O[j][2] / Ls, O[j][3] / Ls);
+        }
+        ds_accum(x, one, false, ssq, amx, v[j]);
+    }
     ds_sync();  // the table is read; the planes may overwrite it
-    if (tid == 0) ds_sh.shift = shift, ds_sh.rstd = 1.0;
-    uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
-    const float sc = __int_as_float((shift + 127) << 23);
-#pragma unroll
-    for (int j = 0; j < DS_QMAX_H; j++) {
-        const int idx = tid + j * DS_CONSUMERS;
-        if (idx >= nqt) continue;
-        ds_put_quad(planes, idx < nqa ? 4 * ka + idx : idx - nqa, xs[j], sc);
-    }
-    if (tid < 12) planes[(size_t)KS * 12 + tid] = 0u;  // the zero k-step after the last
-    fence_proxy_async_smem();
-    ds_sync();
-}
-
-// Input = a row written by other CTAs in this step (the SwiGLU output), only
-// the k-steps this CTA's units read, at the exponent of `bound` = max|row|
-// (published by the phase that wrote the row; exact, so the planes equal
-// those of a whole-row input stage).  No norm, rstd = 1.
-__device__ __noinline__ void ds_in_rows_part(const float *row, int K, int KS, int ntiles_next, int G, float bound,
-                                             size_t pa_off) {
-    const int tid = threadIdx.x, cta = blockIdx.x;
-    int ka, na, nb;
-    ds_needed(KS, ntiles_next, G, cta, ka, na, nb);
-    const int nqa = 4 * na, nqt = 4 * (na + nb);
-    float4 xs[DS_QMAX_F];
-#pragma unroll
-    for (int j = 0; j < DS_QMAX_F; j++) {
-        const int idx = tid + j * DS_CONSUMERS;
-        xs[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (idx >= nqt) continue;
-        const int k0 = 4 * (idx < nqa ? 4 * ka + idx : idx - nqa);
-        if (k0 < K) xs[j] = ldcg4(row + k0);
-    }
-    const int shift = ds_shift_of(bound);
-    if (tid == 0) ds_sh.shift = shift, ds_sh.rstd = 1.0;
-    uint32_t *planes = reinterpret_cast<uint32_t *>(ds_smem + pa_off);
-    const float sc = __int_as_float((shift + 127) << 23);
-#pragma unroll
-    for (int j = 0; j < DS_QMAX_F; j++) {
-        const int idx = tid + j * DS_CONSUMERS;
-        if (idx >= nqt) continue;
-        ds_put_quad(planes, idx < nqa ? 4 * ka + idx : idx - nqa, xs[j], sc);
-    }
-    if (tid < 12) planes[(size_t)KS * 12 + tid] = 0u;
-    fence_proxy_async_smem();
-    ds_sync();
+    ds_quantize<QMAX>(v, ssq, amx, K, nq, false, 0.f, pa_off);
 }
 
 // ---- GEMV consumer ------------------------------------------------------------
@@ -488,144 +373,11 @@ struct DsWalk {
     }
 };
 
-// Consumes this CTA's stages of one GEMV on the tensor cores and adds the
-// exact column sums into out.  Warp 4's lane 0 issues, per ring stage, the
-// tcgen05.mma kind::i8 products of the stage's 128 weight columns (A, s8,
-// straight from the ring slot) with the input's three digit planes (B, s8)
-// into an int32 accumulator in TMEM (M = 128 columns, N = 16: rows 0-2 are the
-// digits, rows 3-15 read neighbouring planes and are ignored), and commits them
-// to the slot's "empty" barrier, so the slot is released once the tensor core
-// has read it.  At the end of the CTA's segment of a tile it commits to a
-// "TMEM full" barrier; warps 0-3 (TMEM lanes 0-127 = the tile's columns)
-// read the three digit sums, recombine them in int64 and add them to out.
-// Two accumulator buffers alternate by segment, so the drain of one overlaps
-// the products of the next.  `seg` counts segments over the whole step (it
-// drives the TMEM barriers' phases); every thread returns the updated stage
-// and segment counts.
-__device__ __forceinline__ uint32_t ds_gemv_tc(uint32_t it, uint32_t &seg_io, int nst, uint32_t bars, int KS,
-                                                int ntiles, long long *out, int G, int cta, uint32_t pa_off,
-                                                unsigned long long *ready) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t b_full = bars, b_empty = bars + 8 * nst, b_tfull = bars + 16 * nst, b_tempty = b_tfull + 16;
-    const uint32_t ring = smem_u32(ds_smem), planes = ring + pa_off, tmem = ds_sh.tmem;
-    bool failed = ds_sh.abort != 0;
-    if (warp == 4) {
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc_i8(DS_TN, 16, 1, 1);
-            uint32_t slot = it % nst, par = (it / nst) & 1, seg = seg_io;
-            bool seg_start = true;
-            int mi = 0;  // products issued in the current segment
-            DsWalk wk(KS, ntiles, G, cta);
-            while (wk.more() && !failed) {
-                int t, k0, nks;
-                wk.next(t, k0, nks);
-                const bool seg_end = !wk.more() || wk.tile != t;
-                const uint32_t buf = seg & 1;
-                // the buffer's previous segment (seg - 2) has left TMEM
-                if (seg_start && seg >= 2 && !mbar_wait(b_tempty + 8 * buf, ((seg >> 1) - 1) & 1)) failed = true;
-                if (!failed && !mbar_wait(b_full + 8 * slot, par)) failed = true;
-                if (failed) break;
-                if (ready) {  // timeline: first and last weight stage ready
-                    const unsigned long long tn = global_ns();
-                    if (mi == 0 && seg == seg_io) ready[0] = tn;
-                    ready[1] = tn;
-                }
-                tc_fence_after();
-                const uint32_t a0 = ring + slot * DS_STAGE, acc = tmem + buf * (16 * DS_NACC);
-                for (int kk = 0; kk < (nks + 1) >> 1; kk++, mi++) {
-                    const uint64_t da = umma_sdesc(a0 + kk * 2 * DS_TN * 16, DS_TN * 16, 128);
-                    const uint64_t db = umma_sdesc(planes + (uint32_t)(k0 + 2 * kk) * 48, 48, 128);
-                    // consecutive products go to independent accumulators, so
-                    // they need not wait on one another; product mi of the
-                    // segment starts accumulator mi when mi < DS_NACC
-                    umma_i8(acc + 16 * (mi % DS_NACC), da, db, idesc, mi < DS_NACC ? 0u : 1u);
-                }
-                umma_commit(b_empty + 8 * slot);  // the slot is free once these products are done
-                seg_start = false;
-                if (seg_end) {
-                    umma_commit(b_tfull + 8 * buf);  // the segment's sums are complete in TMEM
-                    seg++;
-                    seg_start = true;
-                    mi = 0;
-                }
-                if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
-            }
-            if (failed) ds_sh.abort = 1;
-        }
-    } else if (warp < 4) {
-        uint32_t seg = seg_io;
-        int nmma = 0;  // products of the current segment (the accumulators in use)
-        DsWalk wk(KS, ntiles, G, cta);
-        while (wk.more() && !failed) {
-            int t, k0, nks;
-            wk.next(t, k0, nks);
-            nmma += (nks + 1) >> 1;
-            if (wk.more() && wk.tile == t) continue;  // not the end of a tile segment
-            const uint32_t buf = seg & 1;
-            const bool ok = mbar_wait(b_tfull + 8 * buf, (seg >> 1) & 1);
-            if (__any_sync(0xffffffffu, !ok)) {
-                failed = true;
-                break;
-            }
-            tc_fence_after();
-            uint32_t d[4 * DS_NACC];
-            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16) + buf * (16 * DS_NACC);
-#pragma unroll
-            for (int j = 0; j < DS_NACC; j++) tmem_ld4(lb + 16 * j, d + 4 * j);
-            tmem_wait_ld(d);
-            long long sum = 0;
-#pragma unroll
-            for (int j = 0; j < DS_NACC; j++)
-                if (j < nmma)  // accumulators the segment never reached hold stale sums
-                    sum += (long long)(int)d[4 * j] + ((long long)(int)d[4 * j + 1] << 8) +
-                           ((long long)(int)d[4 * j + 2] << 16);
-            nmma = 0;
-            if (sum != 0)
-                atomicAdd(reinterpret_cast<unsigned long long *>(out + (size_t)t * DS_TN + warp * 32 + lane),
-                          (unsigned long long)sum);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(b_tempty + 8 * buf);  // the segment has left TMEM
-            seg++;
-        }
-        if (failed && lane == 0) ds_sh.abort = 1;
-    }
-    // every thread advances the stage and segment counts by this GEMV's
-    uint32_t ns = 0, nseg = 0;
-    DsWalk wk(KS, ntiles, G, cta);
-    while (wk.more()) {
-        int t, k0, nks;
-        wk.next(t, k0, nks);
-        ns++;
-        if (!wk.more() || wk.tile != t) nseg++;
-    }
-    seg_io += nseg;
-    return it + ns;
-}
-
-// The same products on the CUDA cores: 8 warps, each owning 4 columns x 1
-// k-step of a stage per pass, dp4a of the 16 int8 weights against the three
-// signed digit planes, int32 sums recombined in int64 per tile segment and
-// reduced over the warps in shared memory (red: [8 warps][128] int64).
-__device__ __forceinline__ void dot16s(const uint4 &w, const uint4 &p0, const uint4 &p1, const uint4 &p2, int &a0,
-                                       int &a1, int &a2) {
-    a0 = dp4a_ss(w.x, p0.x, a0);
-    a0 = dp4a_ss(w.y, p0.y, a0);
-    a0 = dp4a_ss(w.z, p0.z, a0);
-    a0 = dp4a_ss(w.w, p0.w, a0);
-    a1 = dp4a_ss(w.x, p1.x, a1);
-    a1 = dp4a_ss(w.y, p1.y, a1);
-    a1 = dp4a_ss(w.z, p1.z, a1);
-    a1 = dp4a_ss(w.w, p1.w, a1);
-    a2 = dp4a_ss(w.x, p2.x, a2);
-    a2 = dp4a_ss(w.y, p2.y, a2);
-    a2 = dp4a_ss(w.z, p2.z, a2);
-    a2 = dp4a_ss(w.w, p2.w, a2);
-}
-
-__device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t bars, int KS, int ntiles,
-                                                  long long *out, int G, int cta, uint32_t pa_off, uint32_t red_off,
-                                                  unsigned long long *ready) {
+// Consumes this CTA's stages of one GEMV and adds the exact column sums into
+// out.  Returns the updated count of consumed ring stages.
+__device__ __noinline__ uint32_t ds_gemv(uint32_t it, int nst, uint32_t bars, int KS, int ntiles, long long *out,
+                                         int G, int cta, uint32_t pa_off, uint32_t red_off,
+                                         unsigned long long *ready) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     DsWalk wk(KS, ntiles, G, cta);
     if (!wk.more()) return it;
@@ -654,7 +406,11 @@ __device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t 
         ds_sync();
     };
     int cur = wk.tile;
+#ifdef SB_STEP_TIMELINE
     bool first = true;
+#else
+    (void)ready;
+#endif
     while (wk.more()) {
         int t, k0, nks;
         wk.next(t, k0, nks);
@@ -666,12 +422,14 @@ __device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t 
             failed = true;
             ds_sh.abort = 1;
         }
+#ifdef SB_STEP_TIMELINE
         if (ready && tid == 0) {  // timeline: first and last weight stage ready
             const unsigned long long tn = global_ns();
             if (first) ready[0] = tn;
             ready[1] = tn;
         }
         first = false;
+#endif
         if (!failed) {
             const uint4 *wst = ring4 + (size_t)slot * (DS_STAGE / 16) + warp * DS_TN + lane;
 #pragma unroll
@@ -682,9 +440,9 @@ __device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t 
                     uint4 w[4];
 #pragma unroll
                     for (int j = 0; j < 4; j++) w[j] = wst[kk * 8 * DS_TN + 32 * j];
-                    const uint4 p0 = planes4[3 * ks], p1 = planes4[3 * ks + 1], p2 = planes4[3 * ks + 2];
+                    const uint4 p0 = planes4[ks], p1 = planes4[KS + ks], p2 = planes4[2 * KS + ks];
 #pragma unroll
-                    for (int j = 0; j < 4; j++) dot16s(w[j], p0, p1, p2, acc[j][0], acc[j][1], acc[j][2]);
+                    for (int j = 0; j < 4; j++) dot16(w[j], p0, p1, p2, acc[j][0], acc[j][1], acc[j][2]);
                 }
             }
         }
@@ -695,14 +453,6 @@ __device__ __forceinline__ uint32_t ds_gemv_simt(uint32_t it, int nst, uint32_t 
     }
     flush(cur);
     return it;
-}
-
-// One GEMV of the step: the tensor-core or the CUDA-core consumer.
-__device__ __noinline__ uint32_t ds_gemv(uint32_t it, uint32_t &seg, int nst, uint32_t bars, int KS, int ntiles,
-                                         long long *out, int G, int cta, uint32_t pa_off, uint32_t red_off,
-                                         unsigned long long *ready) {
-    if constexpr (DS_TC_GEMV) return ds_gemv_tc(it, seg, nst, bars, KS, ntiles, out, G, cta, pa_off, ready);
-    else return ds_gemv_simt(it, nst, bars, KS, ntiles, out, G, cta, pa_off, red_off, ready);
 }
 
 // ---- attention consumer -------------------------------------------------------
@@ -720,8 +470,7 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                                               const float *cos_row, const float *sin_row, KV *kcl, KV *vcl,
                                               const int *page_table, float *part, int nkv, int q_dim, int kv_dim,
                                               int page_size, int chunk, float q_scale, int G, int cta,
-                                              uint32_t qs_off, uint32_t kvnew_off, uint32_t pa_off,
-                                              unsigned *bound_word) {
+                                              uint32_t qs_off, uint32_t kvnew_off, uint32_t pa_off) {
     using KL = DsKv<KV>;
     constexpr int DPL = HD / 32;  // dims per lane
     constexpr int BR = 4;         // rows per warp per shuffle round
@@ -735,7 +484,6 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
     uint32_t slot = it % nst, par = (it / nst) & 1;
     float q[REP][DPL], o[REP][DPL], m[REP], ls[REP];
     int cur = -1;
-    float bmax = 0.f;  // max over this CTA's records of |o / l| (a bound on every attention output)
     // RoPE of the element pair (d, d^1) of a head whose columns start at
     // col (rope_with_freqs_preloaded, cpu.rs:650-661).
     auto roped = [&](int col, int d) {
@@ -803,7 +551,6 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                 Lz = fmaf(aw[HD + 1], sw, Lz);
             }
             rec[(size_t)r * DS_REC(HD) + d] = O;
-            if (Lz > 0.f) bmax = fmaxf(bmax, fabsf(O / Lz));
             if (d == 0) {
                 rec[(size_t)r * DS_REC(HD) + HD] = M;
                 rec[(size_t)r * DS_REC(HD) + HD + 1] = Lz;
@@ -886,26 +633,12 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
                 }
             }
         }
-        if constexpr (DS_TC_GEMV) {
-            ds_sync();  // every warp has read the slot
-            if (tid == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
-        } else {
-            __syncwarp();
-            if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
-        }
+        __syncwarp();
+        if (lane == 0 && !failed) mbar_arrive(bars + 8 * (nst + slot));
         if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
         it++;
     }
     if (cur >= 0) finish(cur);
-    // publish the bound: positive floats order like their bit patterns
-    bmax = warp_max_f(bmax);
-    if (lane == 0) ds_sh.red_f[warp] = bmax;
-    ds_sync();
-    if (tid == 0) {
-        float b = 0.f;
-        for (int w = 0; w < DS_CONSUMERS / 32; w++) b = fmaxf(b, ds_sh.red_f[w]);
-        if (b > 0.f) atomicMax(bound_word, __float_as_uint(b));
-    }
     return it;
 }
 
@@ -922,35 +655,22 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     const int nst = a.nst;
     const int ksmax = max(max(a.ks_h, a.ks_q), a.ks_f);
     const DsSmem L = ds_layout(nst, ksmax, REP, HD, a.chunk, a.mtab_bytes);
-    // full[nst], empty[nst], TMEM full[2], TMEM empty[2], MMA done
-    const uint32_t bars = smem_u32(smem + L.bars);
-    const uint32_t b_done = bars + 8 * (2 * nst + 4);
+    const uint32_t bars = smem_u32(smem + L.bars);  // full[nst], empty[nst]
     const uint32_t ring = smem_u32(smem + L.ring);
     unsigned *const abort_flag = a.sync + 2;
 
     if (tid == 0) {
         for (int i = 0; i < nst; i++) {
             mbar_init(bars + 8 * i, 1);
-            // tensor-core consumer: released by one arrival, the tensor core's
-            // commit (weights) or one thread after all warps read the slot
-            // (K/V rows); CUDA-core consumer: one arrival per warp
-            mbar_init(bars + 8 * (nst + i), DS_TC_GEMV ? 1 : DS_CONSUMERS / 32);
+            mbar_init(bars + 8 * (nst + i), DS_CONSUMERS / 32);
         }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(bars + 8 * (2 * nst + i), 1);      // TMEM full: the issuer's commit
-            mbar_init(bars + 8 * (2 * nst + 2 + i), 4);  // TMEM empty: one arrival per draining warp
-        }
-        mbar_init(b_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         sh.abort = 0;
         sh.shift = 0;
         sh.rstd = 1.0;
         sh.last = 0;
     }
-    if (warp == 0) tmem_alloc(&sh.tmem, 2 * 16 * DS_NACC);  // two buffers of DS_NACC 16-column accumulators
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
 
     // Step constants: the position decoded, the context and its KV chunks.
     const int pos = a.seq.pos[0];
@@ -1024,18 +744,25 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
 
     // ---- consumers (warps 0-7)
     uint32_t it = 0;     // stages consumed; mirrors the producer's count
-    uint32_t seg = 0;    // tensor-core tile segments completed (TMEM barrier phases)
     unsigned phase = 0;  // phases completed by this CTA
 
     // Optional timeline, per phase p and CTA: %globaltimer at the phase's
     // start (after its barrier), after its input stage, when its first and
     // its last weight stage were ready (GEMV phases), and at its end (before
     // the arrival): stamps[(p * G + cta) * DS_STAMPS + i], i = 0, 1, 2, 3, 4.
+    // Compiled in only with SB_STEP_TIMELINE (a profiling build): the default
+    // kernel carries no trace of it.
     auto mark = [&](int i) {
+#ifdef SB_STEP_TIMELINE
         if (a.stamps && tid == 0) a.stamps[((size_t)phase * G + cta) * DS_STAMPS + i] = global_ns();
+#endif
     };
     auto ready_slot = [&]() -> unsigned long long * {
+#ifdef SB_STEP_TIMELINE
         return a.stamps ? a.stamps + ((size_t)phase * G + cta) * DS_STAMPS + 2 : nullptr;
+#else
+        return nullptr;
+#endif
     };
     // Arrive at the end of the current phase.
     auto arrive = [&]() {
@@ -1092,7 +819,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             reinterpret_cast<KV *>(static_cast<char *>(a.kc) + (size_t)l * a.layer_kv_bytes),
             reinterpret_cast<KV *>(static_cast<char *>(a.vc) + (size_t)l * a.layer_kv_bytes), a.page_table, a.part,
             a.nkv, a.q_dim, a.kv_dim, a.page_size, a.chunk, a.q_scale, G, cta, (uint32_t)L.qs, (uint32_t)L.kvnew,
-            (uint32_t)L.pa, a.sync + DS_SYNC_ATT_BOUND + (l & 1));
+            (uint32_t)L.pa);
     };
 
     auto accbuf = [&](int j) { return a.acc + (size_t)(j % 3) * a.acc_n; };
@@ -1122,10 +849,6 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         // ---- QKV: input = RMSNorm(x) (x = embedding, or x + down of the previous layer)
         if (go && l > 0) go = wait_all();
         if (go) {
-            if (writer && tid == 0) {  // the next layer's bounds start at zero (last read two layers ago)
-                a.sync[DS_SYNC_ATT_BOUND + ((l + 1) & 1)] = 0u;
-                a.sync[DS_SYNC_ACT_BOUND + ((l + 1) & 1)] = 0u;
-            }
             if (j >= 2) zero_acc(accbuf(j - 2), npad_gu);
             const float *nw = a.norm_in + (size_t)l * a.h;
             if (l == 0) {
@@ -1139,7 +862,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 xv ^= 1;
             }
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off, red_off, ready_slot());
+            it = ds_gemv(it, nst, bars, a.ks_h, a.nt_qkv, accbuf(j), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- attention
@@ -1154,10 +877,12 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) go = wait_all();
         if (go) {
             if (l > 0) zero_acc(accbuf(j - 1), npad_down);
-            const float ab = __uint_as_float(ld_acquire(a.sync + DS_SYNC_ATT_BOUND + (l & 1)));
-            ds_in_att_part<HD, REP>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, a.nt_o, rmax, ab, pa_off);
+            if (a.q_dim <= 4 * DS_CONSUMERS * 4)
+                ds_in_att<HD, REP, 4>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
+            else
+                ds_in_att<HD, REP, DS_QMAX_H>(a.part, (unsigned)att_U, nch, G, a.nh, a.q_dim, a.ks_q, rmax, pa_off);
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off, red_off, ready_slot());
+            it = ds_gemv(it, nst, bars, a.ks_q, a.nt_o, accbuf(j + 1), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- gate/up: input = RMSNorm(x + o)
@@ -1169,7 +894,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                    writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
             xv ^= 1;
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off, red_off, ready_slot());
+            it = ds_gemv(it, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
         // ---- SwiGLU (llama.rs:490-500), this CTA's share of the F outputs
@@ -1179,24 +904,12 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             const long long *gu = accbuf(j + 2);
             const int f0 = (int)((long long)a.F * cta / G), f1 = (int)((long long)a.F * (cta + 1) / G);
             const double fg = gemv_factor(sh.shift, ly.scale[2], sh.rstd), fu = gemv_factor(sh.shift, ly.scale_up, sh.rstd);
-            float amx = 0.f;
             for (int f = f0 + tid; f < f1; f += DS_CONSUMERS) {
                 const int col = (f >> 4) * 32 + (f & 15);
                 const long long tg = __ldcg(gu + col), tu = __ldcg(gu + col + 16);
                 const float yg = gemv_out(tg, fg);
                 const float yu = gemv_out(tu, fu);
-                const float v = __fmul_rn(silu_f64(yg), yu);
-                a.act[f] = v;
-                amx = fmaxf(amx, fabsf(v));
-            }
-            // max|act| over the row, for the down projection's exponent
-            amx = warp_max_f(amx);
-            if (lane == 0) sh.red_f[warp] = amx;
-            ds_sync();
-            if (tid == 0) {
-                float b = 0.f;
-                for (int w = 0; w < DS_CONSUMERS / 32; w++) b = fmaxf(b, sh.red_f[w]);
-                if (b > 0.f) atomicMax(a.sync + DS_SYNC_ACT_BOUND + (l & 1), __float_as_uint(b));
+                a.act[f] = __fmul_rn(silu_f64(yg), yu);
             }
         }
         arrive();
@@ -1205,10 +918,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) go = wait_all();
         if (go) {
             zero_acc(accbuf(j + 1), npad_o);
-            const float fb = __uint_as_float(ld_acquire(a.sync + DS_SYNC_ACT_BOUND + (l & 1)));
-            ds_in_rows_part(a.act, a.F, a.ks_f, a.nt_down, G, fb, pa_off);
+            ds_in_rows<DS_QMAX_F>(a.act, false, nullptr, a.F, a.ks_f, a.eps, nullptr, pa_off);
             mark(1);
-            it = ds_gemv(it, seg, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off, red_off, ready_slot());
+            it = ds_gemv(it, nst, bars, a.ks_f, a.nt_down, accbuf(j + 3), G, cta, pa_off, red_off, ready_slot());
         }
         arrive();
     }
@@ -1221,7 +933,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                                a.norm_final, a.h, a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
                                (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
         mark(1);
-        it = ds_gemv(it, seg, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off, red_off, ready_slot());
+        it = ds_gemv(it, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off, red_off, ready_slot());
     }
     arrive();
     // ---- logits and this CTA's argmax candidate (ties -> larger index,
@@ -1293,17 +1005,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         }
         a.sync[0] = 0;
         a.sync[1] = 0;
-        for (int i = DS_SYNC_ATT_BOUND; i < DS_SYNC_WORDS; i++) a.sync[i] = 0;  // layer 0's bounds, next step
     }
-    // ---- release the tensor memory once no tensor-core work is in flight
-    if (warp == 4 && lane == 0) {
-        umma_commit(b_done);  // completes when every product this thread issued has
-        if (!mbar_wait(b_done, 0)) atomicExch(abort_flag, 1u);
-    }
-    tc_fence_before();
-    ds_sync();
-    tc_fence_after();
-    if (warp == 0) tmem_dealloc(sh.tmem, 2 * 16 * DS_NACC);
 }
 
 template <int HD, int REP, typename KV>

@@ -714,7 +714,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
         if ((rc = dalloc_t(m, &m->ds_part, ds_part_floats(m->nkv, m->nh / m->nkv, m->hd))) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_cand_val, (size_t)G)) != SB_OK) return fail(rc);
         if ((rc = dalloc_t(m, &m->ds_cand_idx, (size_t)G)) != SB_OK) return fail(rc);
-        if ((rc = dalloc_t(m, &m->ds_sync, DS_SYNC_WORDS)) != SB_OK) return fail(rc);
+        if ((rc = dalloc_t(m, &m->ds_sync, 4)) != SB_OK) return fail(rc);
     }
     if (B > QG_MAX_M) {
         int nt = m->lm.ntiles;
@@ -1481,6 +1481,9 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
 sb_status sb_llama_set_timeline(sb_llama *m, int enabled) {
     SB_CHECK(m, SB_ERR_ARG, "sb_llama_set_timeline: null model");
     SB_CHECK(m->ds_ok, SB_ERR_UNSUPPORTED, "sb_llama_set_timeline: this model does not run the persistent step");
+    SB_CHECK(!enabled || ds_timeline_built(), SB_ERR_UNSUPPORTED,
+             "sb_llama_set_timeline: this library was built without the step timeline (build with "
+             "SB_STEP_TIMELINE=1 in the environment)");
     if (enabled && !m->ds_stamps) {
         const size_t n = (size_t)(6 * m->L + 2) * ds_grid() * DS_STAMPS;
         SB_TRY(dalloc_t(m, &m->ds_stamps, n));

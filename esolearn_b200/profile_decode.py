@@ -16,7 +16,8 @@ before it captures the graph, so a profiler that should see decode steps at
     python -m esolearn_b200.profile_decode --shape llama3_8b_shape --batch 32 --layers 2 --ctx 2068
     python -m esolearn_b200.profile_decode --ctx 584 --steps 4 --timeline
 
---timeline (batch 1, persistent step) records the step kernel's per-phase
+--timeline (batch 1, persistent step; needs the profiling build of the
+library, `SB_STEP_TIMELINE=1 python -m esolearn_b200.build --force`) records the step kernel's per-phase
 %globaltimer stamps (sb_llama_set_timeline) in the last step and prints, per
 phase kind, the mean over layers of: the grid-barrier wait (a CTA's end of the
 previous phase to its start of this one, mean over CTAs), the input stage and

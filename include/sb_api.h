@@ -343,7 +343,10 @@ sb_status sb_llama_attn_plan(sb_llama *m, int batch, int *splits, int *tensor_ma
  * and its last weight stage were ready (GEMV phases; 0 otherwise), and its
  * end before the arrival: out[(p * ctas + c) * 5 + i].  SB_ERR_UNSUPPORTED when the model
  * does not run the persistent step.  get: *phases and *ctas always; out
- * (cap slots) when non-NULL, for the last step. */
+ * (cap slots) when non-NULL, for the last step.  The timeline is compiled
+ * into the step kernel only in a profiling build (SB_STEP_TIMELINE=1 in the
+ * environment of `python -m esolearn_b200.build`); otherwise enabling it
+ * returns SB_ERR_UNSUPPORTED. */
 sb_status sb_llama_set_timeline(sb_llama *m, int enabled);
 sb_status sb_llama_get_timeline(sb_llama *m, uint64_t *out, size_t cap, int *phases, int *ctas);
 
