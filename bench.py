@@ -345,11 +345,11 @@ def measure_decode(wl_name: str, B: int, prompt: int, K: int, W: int, rank: int,
 def quant_linear_sweep_summary(iters: int = 5):
     """The quantized-linear sweep on this GPU, compact:
     GB/s (fraction of measured HBM) per (K, N, group, M) cell, M in {1, 8, 32,
-    128}, per-tensor scale and group 32 (group 64 times within a few % of 32)."""
+    128}, per-tensor scale and groups 32 and 64."""
     from esolearn_b200 import linear_sweep
 
     peak, kind = read_peaks()
-    cells = linear_sweep.run(iters=iters, peak_gbs=peak, groups=[0, 32])
+    cells = linear_sweep.run(iters=iters, peak_gbs=peak, groups=[0, 32, 64])
     out = {"timing": f"CUDA events, L2 flushed before each call, median of {iters}",
            "bytes": "K*N int8 + 4*K*N/g scales + 2*M*K bf16 in + 4*M*N f32 out", "peak_gbs": peak,
            "peak_source": kind, "cells": []}

@@ -44,6 +44,7 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--timeline", action="store_true", help="per-phase timeline of the last persistent step")
+    ap.add_argument("--timeline-out", default=None, help="also save the raw stamps [phases, ctas, 5] (.npy)")
     args = ap.parse_args(argv)
 
     cfg = getattr(LlamaConfig, args.shape)()
@@ -62,7 +63,12 @@ def main(argv=None):
     out = {"shape": args.shape, "layers": cfg.n_layers, "batch": B, "ctx": args.ctx, "steps": args.steps,
            "launches_per_step": model.step_launches(B), "host_ms_per_call": times}
     if args.timeline:
-        out["timeline_us"] = timeline_summary(model.timeline(), cfg.n_layers)
+        ts = model.timeline()
+        out["timeline_us"] = timeline_summary(ts, cfg.n_layers)
+        if args.timeline_out:
+            import numpy as np
+
+            np.save(args.timeline_out, ts)
     print(json.dumps(out))
 
 
@@ -80,10 +86,17 @@ def timeline_summary(ts, n_layers: int) -> dict:
     kinds.append(("lm_head", [6 * n_layers]))
     for name, idx in kinds:
         wait, inp, work, span, r0, r1, tail = [], [], [], [], [], [], []
+        prop, lag, spread = [], [], []
         for p in idx:
             if p == 0 or p >= P:
                 continue
             wait.append(np.mean(t[p, :, 0] - t[p - 1, :, 4]))
+            # the grid barrier before phase p: last arrival -> first start
+            # (propagation), last arrival - median arrival (imbalance), and
+            # the spread of the start stamps
+            prop.append(t[p, :, 0].min() - t[p - 1, :, 4].max())
+            lag.append(t[p - 1, :, 4].max() - np.median(t[p - 1, :, 4]))
+            spread.append(t[p, :, 0].max() - t[p, :, 0].min())
             inp.append(np.mean(t[p, :, 1] - t[p, :, 0]))
             work.append(np.mean(t[p, :, 4] - t[p, :, 1]))
             span.append(np.max(t[p, :, 4]) - np.max(t[p - 1, :, 4]))
@@ -94,7 +107,8 @@ def timeline_summary(ts, n_layers: int) -> dict:
                 tail.append(np.mean(t[p, g, 4] - t[p, g, 3]))
         if span:
             res[name] = {"barrier": np.mean(wait) / 1e3, "input": np.mean(inp) / 1e3, "work": np.mean(work) / 1e3,
-                         "span": np.mean(span) / 1e3}
+                         "span": np.mean(span) / 1e3, "barrier_propagation": np.mean(prop) / 1e3,
+                         "arrival_lag": np.mean(lag) / 1e3, "start_spread": np.mean(spread) / 1e3}
             if r0:  # input done -> first / last weight stage ready, last stage ready -> phase end
                 res[name].update({"first_ready": np.mean(r0) / 1e3, "last_ready": np.mean(r1) / 1e3,
                                   "after_last": np.mean(tail) / 1e3})
