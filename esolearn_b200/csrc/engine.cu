@@ -260,6 +260,22 @@ int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, boo
 
 // Enqueue one decode step for M sequences on st.
 int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, StepProfiler *prof = nullptr) {
+    // Batches of 5+ rows on one GPU chain the tensor-core linears: the finish
+    // of o, gate/up and down (whose output row is the next linear's input)
+    // also writes the next linear's planes, one launch instead of two.
+    const bool chain = M > QG_MAX_M && m->tp == 1;
+    bool planes_ready = false;  // the previous link wrote this linear's planes
+    auto linear = [&](int epi, const QGemvArgs &a, const float *next_norm) -> int {
+        if (!chain) return engine_linear(m, epi, a, st, pdl);
+        const bool chained = epi == QEPI_RESID || epi == QEPI_SWIGLU;
+        QGemmNext nx;
+        nx.norm_w = next_norm;
+        nx.eps = m->cfg.rms_norm_eps;
+        nx.planes_bytes = qgemm_planes_bytes(std::max({m->h, m->F, m->q_dim}), m->B);
+        const bool need = !planes_ready;
+        planes_ready = chained;
+        return qgemm_launch_chained(epi, a, m->gws, st, pdl, need, chained ? &nx : nullptr);
+    };
     SB_PROF(prof, 2, embed_launch(m->embed, m->h, m->V, m->seq, M, m->x, st, pdl));
     for (int l = 0; l < m->L; l++) {
         const sb_llama::Layer &ly = m->layers[l];
@@ -284,7 +300,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.rope_cos = m->rope_cos;
             a.rope_sin = m->rope_sin;
             a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
-            SB_PROF(prof, 0, engine_linear(m, QEPI_QKV, a, st, pdl));
+            SB_PROF(prof, 0, linear(QEPI_QKV, a, nullptr));
         }
         {
             AttnArgs a;
@@ -317,7 +333,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             QGemvArgs a = gemv_common(ly.o, M, m->attn, m->q_dim);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, engine_linear(m, resid_epi(m), a, st, pdl));
+            SB_PROF(prof, 0, linear(resid_epi(m), a, m->norm_post + (size_t)l * m->h));
             SB_TRY(tp_reduce_residual(m, M, st));
         }
         {
@@ -327,13 +343,13 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.out = m->act;
             a.ldo = m->F;
             a.F = m->F;
-            SB_PROF(prof, 0, engine_linear(m, QEPI_SWIGLU, a, st, pdl));
+            SB_PROF(prof, 0, linear(QEPI_SWIGLU, a, nullptr));
         }
         {
             QGemvArgs a = gemv_common(ly.down, M, m->act, m->F);
             a.out = m->x;
             a.ldo = m->h;
-            SB_PROF(prof, 0, engine_linear(m, resid_epi(m), a, st, pdl));
+            SB_PROF(prof, 0, linear(resid_epi(m), a, l + 1 < m->L ? m->norm_in + (size_t)(l + 1) * m->h : m->norm_final));
             SB_TRY(tp_reduce_residual(m, M, st));
         }
         if (trace)
@@ -348,7 +364,7 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
         a.ldo = m->Vl;
         a.cand_val = m->cand_val;
         a.cand_idx = m->cand_idx;
-        SB_PROF(prof, 0, engine_linear(m, QEPI_LOGITS, a, st, pdl));
+        SB_PROF(prof, 0, linear(QEPI_LOGITS, a, nullptr));
     }
     if (m->tp > 1) {
         // every rank's per-tile candidates [rank][row][tile]; rank r's columns start at r * Vl
@@ -1471,6 +1487,11 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
     SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
     if (batch == 1 && m->ds_ok)
         *launches = 1;  // the persistent step kernel
+    else if (batch > QG_MAX_M && m->tp == 1)
+        // embed; per layer GEMM + finish for qkv (plus the planes in layer 0),
+        // attention, planes + GEMM + row finish for o, GEMM + row finish for
+        // gate/up and down; lm_head GEMM + finish; argmax
+        *launches = 5 + 10 * m->L;
     else if (batch > QG_MAX_M)
         *launches = 5 + 13 * m->L;  // embed, 4 linears x 3 + attention per layer, lm_head x 3, argmax
     else

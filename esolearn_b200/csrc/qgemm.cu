@@ -32,12 +32,15 @@
 // the CTA stops issuing, waits for its tensor-core work and frees TMEM.
 #include "qgemm.cuh"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "pipeline.cuh"
 #include "tcgen05.cuh"
 
 namespace sb {
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -274,25 +277,43 @@ __global__ void __launch_bounds__(QGM_THREADS, 1)
         if (lane == 0) {
             QgmWalk wk(w.KS, w.ntiles, G, cta, ups);
             uint32_t it = 0, slot = 0, par = 0;
-            bool waited = false;
+            // Fill every slot with its weights first: under programmatic
+            // dependent launch this runs while the previous kernels finish.
+            // The planes come from the previous kernel, so their copies into
+            // the same slots follow griddepcontrol.wait.
+            int pk0[QGM_MAX_NST], pnks[QGM_MAX_NST];
+            while (it < (uint32_t)nst && wk.more()) {
+                int t, k0, nks;
+                bool se;
+                wk.next(t, k0, nks, se);
+                const uint32_t wbytes = (uint32_t)nks * QGM_TN * 16, pbytes = (uint32_t)nks * np * 16;
+                mbar_expect_tx(b_full + 8 * it, wbytes + pbytes);
+                tma_load_1d(ring + it * slot_bytes,
+                            reinterpret_cast<const uint8_t *>(w.w) + ((size_t)t * w.KS + k0) * QGM_TN * 16, wbytes,
+                            b_full + 8 * it);
+                pk0[it] = k0, pnks[it] = nks;
+                it++;
+            }
+            pdl_wait();
+            for (uint32_t i = 0; i < it; i++)
+                tma_load_1d(ring + i * slot_bytes + wslot, ws.planes + (size_t)pk0[i] * np * 16,
+                            (uint32_t)pnks[i] * np * 16, b_full + 8 * i);
+            slot = it % (uint32_t)nst;
+            par = it / (uint32_t)nst;
             while (wk.more()) {
                 int t, k0, nks;
                 bool se;
                 wk.next(t, k0, nks, se);
-                if (it >= (uint32_t)nst) {
-                    if (!waited) pdl_wait(), waited = true;
-                    if (*(volatile int *)&s_abort || !mbar_wait(b_empty + 8 * slot, par ^ 1)) {
-                        atomicOr(&qgm_error_flag, 1u);
-                        s_abort = 1;
-                        break;
-                    }
+                if (*(volatile int *)&s_abort || !mbar_wait(b_empty + 8 * slot, par ^ 1)) {
+                    atomicOr(&qgm_error_flag, 1u);
+                    s_abort = 1;
+                    break;
                 }
                 const uint32_t wbytes = (uint32_t)nks * QGM_TN * 16, pbytes = (uint32_t)nks * np * 16;
                 const uint32_t dst = ring + slot * slot_bytes;
                 mbar_expect_tx(b_full + 8 * slot, wbytes + pbytes);
                 tma_load_1d(dst, reinterpret_cast<const uint8_t *>(w.w) + ((size_t)t * w.KS + k0) * QGM_TN * 16, wbytes,
                             b_full + 8 * slot);
-                if (!waited) pdl_wait(), waited = true;  // the planes come from the previous kernel
                 tma_load_1d(dst + wslot, ws.planes + (size_t)k0 * np * 16, pbytes, b_full + 8 * slot);
                 it++;
                 if (++slot == (uint32_t)nst) slot = 0, par ^= 1;
@@ -572,6 +593,168 @@ __global__ void __launch_bounds__(QGM_FIN_THREADS) qgm_finish_kernel(const QGemv
             a.cand_idx[(size_t)(m0 + tid) * a.w.ntiles + tile] = bj;
         }
     }
+}
+
+// ---- finish + the next linear's planes, one row per cluster ----------------------
+// When a linear's output row is the next linear's input (o -> gate/up with the
+// post-attention RMSNorm, gate/up -> down, down -> the next layer's qkv or the
+// lm_head with their RMSNorm), one launch finishes the sums and writes the
+// next GEMM's byte planes.  The QGF_CLUSTER CTAs of a cluster own one row:
+// each finishes a contiguous run of whole 16-feature chunks (sums -> f32,
+// residual add or SwiGLU, store; clears the sums) and keeps the values in
+// shared memory; the CTAs exchange their partial sum of squares and maximum
+// through distributed shared memory and add them in rank order, so every CTA
+// derives the same exponent and RMSNorm factor (the planes kernel's rules);
+// then each quantizes its run into the planes.
+constexpr int QGF_CLUSTER = 8;
+constexpr int QGF_THREADS = 256;
+constexpr int QGF_J = 16;                                     // features per thread
+constexpr int QGF_MAX_PER = QGF_THREADS * QGF_J;             // per CTA
+constexpr int QGF_MAX_K = QGF_CLUSTER * QGF_MAX_PER;         // 32768 features per row
+
+template <int EPI>
+__global__ void __cluster_dims__(QGF_CLUSTER, 1, 1) __launch_bounds__(QGF_THREADS)
+    qgm_finish_planes_kernel(const QGemvArgs a, const QGemmWs ws, const float *norm_next, float eps, int np) {
+    static_assert(EPI == QEPI_RESID || EPI == QEPI_SWIGLU, "row finish: residual or SwiGLU");
+    __shared__ float vals[QGF_MAX_PER];
+    __shared__ double w_ssq[QGF_THREADS / 32];
+    __shared__ float w_amx[QGF_THREADS / 32];
+    __shared__ double c_ssq;  // this CTA's partials, read by the cluster
+    __shared__ float c_amx;
+    __shared__ int s_shift;
+    pdl_launch_dependents();
+    pdl_wait();
+    cg::cluster_group cl = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m = blockIdx.y;
+    const int rank = (int)cl.block_rank();
+    const int K = EPI == QEPI_SWIGLU ? a.F : a.w.N;  // features of the row = the next linear's K
+    const int nchunk = (K + 15) >> 4, cpc = (nchunk + QGF_CLUSTER - 1) / QGF_CLUSTER;
+    const int kc0 = min(nchunk, rank * cpc), kc1 = min(nchunk, kc0 + cpc);
+    const int f0 = kc0 * 16, f1 = min(K, kc1 * 16), nf = f1 - f0;
+    long long *acc = ws.acc + (size_t)m * ws.ld_acc;
+    float *out = a.out + (size_t)m * a.ldo;
+    const int sh0 = ws.shift[m];
+    const double rs0 = ws.rstd[m];
+    // 1. finish: every load of the thread in flight together
+    if (EPI == QEPI_RESID) {
+        long long t[QGF_J];
+        float x[QGF_J];
+#pragma unroll
+        for (int j = 0; j < QGF_J; j++) {
+            const int i = tid + QGF_THREADS * j;
+            if (i < nf) t[j] = __ldcg(acc + f0 + i), x[j] = out[f0 + i];
+        }
+        const double f = gemv_factor(sh0, a.w.scale, rs0);
+#pragma unroll
+        for (int j = 0; j < QGF_J; j++) {
+            const int i = tid + QGF_THREADS * j;
+            if (i < nf) {
+                acc[f0 + i] = 0;
+                const float v = __fadd_rn(x[j], gemv_out(t[j], f));  // x + proj (llama.rs:564,568)
+                out[f0 + i] = v;
+                vals[i] = v;
+            }
+        }
+    } else {
+        long long tg[QGF_J], tu[QGF_J];
+#pragma unroll
+        for (int j = 0; j < QGF_J; j++) {
+            const int i = tid + QGF_THREADS * j;
+            if (i < nf) {
+                const int fi = f0 + i, col = (fi >> 4) * 32 + (fi & 15);
+                tg[j] = __ldcg(acc + col), tu[j] = __ldcg(acc + col + 16);
+            }
+        }
+        const double fg = gemv_factor(sh0, a.w.scale, rs0), fu = gemv_factor(sh0, a.w.scale_up, rs0);
+#pragma unroll
+        for (int j = 0; j < QGF_J; j++) {
+            const int i = tid + QGF_THREADS * j;
+            if (i < nf) {
+                const int fi = f0 + i, col = (fi >> 4) * 32 + (fi & 15);
+                acc[col] = 0, acc[col + 16] = 0;
+                const float v = __fmul_rn(silu_f64(gemv_out(tg[j], fg)), gemv_out(tu[j], fu));
+                out[fi] = v;
+                vals[i] = v;
+            }
+        }
+    }
+    // padded columns past the last feature hold zero sums (zero weights); the
+    // last CTA clears them anyway so the buffer is all zero for the next call
+    if (rank == QGF_CLUSTER - 1) {
+        const int used = EPI == QEPI_SWIGLU ? ((K + 15) >> 4) * 32 : K;
+        for (int n = used + tid; n < a.w.ntiles * QGM_TN; n += QGF_THREADS) acc[n] = 0;
+    }
+    __syncthreads();
+    // 2. this CTA's sum of squares (before the norm weight) and max |value|
+    // (after it), as the planes kernel forms them
+    float ssq = 0.f, amx = 0.f;
+    for (int i = tid; i < nf; i += QGF_THREADS) {
+        float v = vals[i];
+        if (norm_next) {
+            ssq = fmaf(v, v, ssq);
+            v = __fmul_rn(v, __ldg(norm_next + f0 + i));
+            vals[i] = v;
+        }
+        amx = fmaxf(amx, fabsf(v));
+    }
+    const double s = warp_sum_d((double)ssq);
+    const float mx = warp_max_f(amx);
+    if (lane == 0) w_ssq[warp] = s, w_amx[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        double st = 0.0;
+        float mt = 0.f;
+        for (int w = 0; w < QGF_THREADS / 32; w++) st += w_ssq[w], mt = fmaxf(mt, w_amx[w]);
+        c_ssq = st, c_amx = mt;
+    }
+    cl.sync();  // partials visible cluster-wide
+    if (tid == 0) {
+        double st = 0.0, mt = 0.0;
+        for (int r = 0; r < QGF_CLUSTER; r++) {  // rank order: the same totals in every CTA
+            st += *cl.map_shared_rank(&c_ssq, r);
+            mt = fmax(mt, (double)*cl.map_shared_rank(&c_amx, r));
+        }
+        int e = 0;
+        if (mt > 0.0) frexp(mt, &e);
+        const int sh = (mt > 0.0) ? 22 - e : 0;  // |a * 2^sh| < 2^22
+        s_shift = sh < -126 ? -126 : (sh > 126 ? 126 : sh);
+        if (rank == 0) {
+            // rmsnorm (cpu.rs:582-588): rstd = 1/sqrt(mean(x^2) + eps) in f64
+            ws.rstd[m] = norm_next ? 1.0 / sqrt(st / (double)K + (double)eps) : 1.0;
+            ws.shift[m] = s_shift;
+        }
+    }
+    __syncthreads();
+    // 3. planes of this CTA's chunks (U = A + 2^23, three unsigned bytes)
+    const float sc = __int_as_float((s_shift + 127) << 23);
+    for (int kc = kc0 + tid; kc < kc1; kc += QGF_THREADS) {
+        const int i0 = (kc - kc0) * 16;
+        uint32_t w[3][4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int k = i0 + q * 4 + i;
+                const float v = f0 + k < K ? vals[k] : 0.f;
+                const int A = __float_as_int(__fadd_rn(__fmul_rn(v, sc), 12582912.0f)) - 0x4B400000;
+                const uint32_t U = (uint32_t)(A + (1 << 23));
+                b0 |= (U & 0xffu) << (8 * i);
+                b1 |= ((U >> 8) & 0xffu) << (8 * i);
+                b2 |= ((U >> 16) & 0xffu) << (8 * i);
+            }
+            w[0][q] = b0, w[1][q] = b1, w[2][q] = b2;
+        }
+        uint4 *row = reinterpret_cast<uint4 *>(ws.planes) + (size_t)kc * np;
+#pragma unroll
+        for (int p = 0; p < 3; p++) row[1 + 3 * m + p] = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
+        if (m == 0) {  // the all-ones row and the zero padding rows of this chunk
+            row[0] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+            for (int r = 3 * a.M + 1; r < np; r++) row[r] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    cl.sync();  // no CTA leaves while another may still read its partials
 }
 
 // ---- grouped scales (g = 32 or 64 rows of K per f32 scale and column) -------------
@@ -872,6 +1055,11 @@ int qgemm_check_error() {
 }
 
 int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
+    return qgemm_launch_chained(epi, a, ws, st, pdl, true, nullptr);
+}
+
+int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl, bool planes,
+                         const QGemmNext *next) {
     SB_CHECK(qgemm_supported(a.w, a.M), SB_ERR_UNSUPPORTED, "qgemm: weight/rows not supported (TN %d, group %d, M %d)",
              a.w.TN, a.w.group, a.M);
     SB_CHECK(ws.planes && ws.acc && ws.shift && ws.rstd && ws.ld_acc >= a.w.ntiles * QGM_TN, SB_ERR_ARG,
@@ -882,12 +1070,29 @@ int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st
     int limit = 0;
     const int nst = qgm_nst(np, &limit);
     SB_CHECK(nst >= 2, SB_ERR_SHAPE, "qgemm: %d rows need %d B per stage (limit %d)", a.M, qgm_slot_bytes(np), limit);
-    SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + ceil_div(a.w.KS, 16)), dim3(QGM_PL_THREADS), 0, st, pdl, a, ws,
-                       np));
+    if (next) {
+        SB_CHECK(epi == QEPI_RESID || epi == QEPI_SWIGLU, SB_ERR_ARG, "qgemm: epilogue %d has no row finish", epi);
+        const int K = epi == QEPI_SWIGLU ? a.F : a.w.N;
+        SB_CHECK(K <= QGF_MAX_K, SB_ERR_SHAPE, "qgemm: row finish of %d features (max %d)", K, QGF_MAX_K);
+        SB_CHECK((size_t)ceil_div(K, 16) * np * 16 <= next->planes_bytes, SB_ERR_SHAPE,
+                 "qgemm: planes of %d features x %d rows exceed the scratch", K, a.M);
+    }
+    if (planes)
+        SB_CUDA_TRY(launch(qgm_planes_kernel, dim3(a.M + ceil_div(a.w.KS, 16)), dim3(QGM_PL_THREADS), 0, st, pdl, a,
+                           ws, np));
     const int upt = ceil_div(a.w.KS, QGM_UNIT_KS);
     const int G = std::max(1, std::min(device_props().sm_count, a.w.ntiles * upt / 2));
     SB_CUDA_TRY(launch(qgm_gemm_kernel, dim3(G), dim3(QGM_THREADS), (size_t)nst * qgm_slot_bytes(np), st, pdl, a.w, ws,
                        a.M, np, nst));
+    if (next) {
+        if (epi == QEPI_RESID)
+            SB_CUDA_TRY(launch(qgm_finish_planes_kernel<QEPI_RESID>, dim3(QGF_CLUSTER, a.M), dim3(QGF_THREADS), 0, st,
+                               pdl, a, ws, next->norm_w, next->eps, np));
+        else
+            SB_CUDA_TRY(launch(qgm_finish_planes_kernel<QEPI_SWIGLU>, dim3(QGF_CLUSTER, a.M), dim3(QGF_THREADS), 0, st,
+                               pdl, a, ws, next->norm_w, next->eps, np));
+        return SB_OK;
+    }
     switch (epi) {
     case QEPI_STORE: return finish_launch<QEPI_STORE>(a, ws, st, pdl);
     case QEPI_BIAS: return finish_launch<QEPI_BIAS>(a, ws, st, pdl);

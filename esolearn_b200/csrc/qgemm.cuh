@@ -31,6 +31,22 @@ bool qgemm_supported(const QWeightDesc &w, int M);
 // through the tensor cores into exact int64 column sums, finish (scale +
 // epilogue; clears the sums).  pdl enables programmatic dependent launch.
 int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl);
+// The next linear of a chain, when this linear's output row is its input:
+// its fused RMSNorm weight (nullptr: none) and eps, and the size of the
+// planes scratch.
+struct QGemmNext {
+    const float *norm_w = nullptr;
+    float eps = 1e-5f;
+    size_t planes_bytes = 0;
+};
+// qgemm_launch as one link of a chain.  planes = false skips the planes
+// kernel (the previous link already wrote this input's planes, shift and
+// rstd into ws).  With next, the finish is one launch of clusters (one row
+// each; epilogues RESID and SWIGLU, at most 32768 output features) that
+// also writes the next linear's planes, shift and rstd into ws, so the next
+// link runs with planes = false.
+int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl, bool planes,
+                         const QGemmNext *next);
 // Group-scaled weights (g = 32 or 64) on the tensor cores, 5 to 32 rows per
 // launch: one TMEM accumulator per group, the group scales applied in f64 as
 // the groups are drained; per-(tile, piece) f64 partials in `part`
