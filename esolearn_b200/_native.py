@@ -94,6 +94,9 @@ SIGNATURES = {
     "sb_llama_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
     "sb_llama_forward_seq": (C.c_int, [vp, vp, C.c_int, vp]),
     "sb_llama_sample": (C.c_int, [vp, C.c_int, C.c_float, C.c_int, C.c_float, vp, vp]),
+    "sb_llama_set_sampling": (C.c_int, [vp, C.c_int, C.c_float, C.c_int, C.c_float, C.c_int, vp]),
+    "sb_llama_clear_sampling": (C.c_int, [vp]),
+    "sb_llama_get_rng": (C.c_int, [vp, C.c_int, vp]),
     "sb_llama_generate_greedy": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, vp]),
     "sb_llama_set_trace": (C.c_int, [vp, C.c_int]),
     "sb_llama_get_trace": (C.c_int, [vp, vp]),

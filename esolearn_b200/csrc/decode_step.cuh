@@ -85,6 +85,7 @@ struct DsArgs {
     unsigned *sync = nullptr;   // [0] phase arrivals, [1] exits, [2] abort flag (zeroed by the host)
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
     unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
+    int greedy = 1;  // 1: the last CTA records the argmax and advances the sequence; 0: a sampler follows
     int nst = 0;                // ring stages
     int mtab_bytes = 0;         // attention-combine table (ds_mtab_bytes)
 };

@@ -983,7 +983,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     ds_sync();
     if (sh.last && tid == 0) {
         __threadfence();
-        if (!ld_acquire(abort_flag)) {
+        if (a.greedy && !ld_acquire(abort_flag)) {
             float best = -INFINITY;
             int bi = -1;
             for (int c = 0; c < G; c++) {

@@ -103,8 +103,13 @@ struct sb_llama {
     int active = 0;  // batch of the current begin()
     int steps = 0;   // steps queued since begin()
 
-    // graphs per batch size
-    std::vector<cudaGraphExec_t> graphs;
+    // graphs per batch size: greedy steps, and steps ending in the device sampler
+    std::vector<cudaGraphExec_t> graphs, sgraphs;
+    // device sampling loop (sb_llama_set_sampling)
+    bool samp_on = false;
+    SampleCfg samp;
+    int *d_state_bak = nullptr;  // [4][B] sequence state saved around a graph capture's warm-up
+    std::vector<DsLayer> ds_tab;  // the layer table last uploaded for the step kernel
     bool trace = false;
     float *trace_buf = nullptr;
     int trace_batch = 0;
@@ -259,7 +264,8 @@ int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, boo
     } while (0)
 
 // Enqueue one decode step for M sequences on st.
-int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, StepProfiler *prof = nullptr) {
+int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, StepProfiler *prof = nullptr,
+                 bool sampled = false) {
     // Batches of 5+ rows on one GPU chain the tensor-core linears: the finish
     // of o, gate/up and down (whose output row is the next linear's input)
     // also writes the next linear's planes, one launch instead of two.
@@ -373,6 +379,8 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
         SB_TRY(tp_allgather32(m->comm, m->cand_idx, m->cand_all_idx, n, st));
         SB_PROF(prof, 2, argmax_step_launch(m->cand_all_val, m->cand_all_idx, m->lm.ntiles, m->seq, M, st, pdl,
                                             m->tp, (int)n, m->Vl));
+    } else if (sampled) {
+        SB_PROF(prof, 2, sample_step_launch(m->logits, M, m->V, m->Vl, m->samp, m->d_rng, m->samp_prob, m->seq, st));
     } else {
         SB_PROF(prof, 2, argmax_step_launch(m->cand_val, m->cand_idx, m->lm.ntiles, m->seq, M, st, pdl));
     }
@@ -390,7 +398,7 @@ int check_ready(sb_llama *m) {
 int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const int32_t *plen);
 
 // One batch-1 step as the persistent kernel (m->ds_ok).
-int ds_step(sb_llama *m) {
+int ds_step(sb_llama *m, bool sampled = false) {
     std::vector<DsLayer> tab(m->L);
     for (int l = 0; l < m->L; l++) {
         const sb_llama::Layer &ly = m->layers[l];
@@ -401,7 +409,14 @@ int ds_step(sb_llama *m) {
         }
         tab[l].scale_up = ly.gu.scale_up;
     }
-    SB_CUDA_TRY(cudaMemcpyAsync(m->ds_layers, tab.data(), sizeof(DsLayer) * tab.size(), cudaMemcpyHostToDevice, m->st));
+    if (m->ds_tab.size() != tab.size() ||
+        std::memcmp(m->ds_tab.data(), tab.data(), sizeof(DsLayer) * tab.size()) != 0) {
+        // weights were (re)loaded: upload the table once, not every step
+        SB_CUDA_TRY(cudaMemcpyAsync(m->ds_layers, tab.data(), sizeof(DsLayer) * tab.size(), cudaMemcpyHostToDevice,
+                                    m->st));
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));  // tab is a local: the copy must finish before it goes
+        m->ds_tab = tab;
+    }
     DsArgs a;
     a.L = m->L;
     a.h = m->h;
@@ -455,7 +470,10 @@ int ds_step(sb_llama *m) {
     a.nst = m->ds_nst;
     a.mtab_bytes = ds_mtab_bytes(m->nh, m->nkv);
     a.stamps = m->ds_stamps;
-    return ds_launch(a, m->nh / m->nkv, m->st);
+    a.greedy = sampled ? 0 : 1;
+    SB_TRY(ds_launch(a, m->nh / m->nkv, m->st));
+    if (sampled) SB_TRY(sample_step_launch(m->logits, 1, m->V, m->Vl, m->samp, m->d_rng, m->samp_prob, m->seq, m->st));
+    return SB_OK;
 }
 
 // Errors a bounded device wait may have left behind.
@@ -467,22 +485,33 @@ int check_device_errors(sb_llama *m) {
     return qgemv_check_error();
 }
 
-int get_graph(sb_llama *m, int M, cudaGraphExec_t *out) {
-    if (m->graphs[M]) {
-        *out = m->graphs[M];
+int get_graph(sb_llama *m, int M, cudaGraphExec_t *out, bool sampled = false) {
+    std::vector<cudaGraphExec_t> &cache = sampled ? m->sgraphs : m->graphs;
+    if (cache[M]) {
+        *out = cache[M];
         return SB_OK;
     }
     // Warm up once outside capture (sets kernel attributes, loads modules)
-    // at position -1, which writes no K/V row and reads no context, so the
-    // caches of live sequences are untouched; callers set their own state
-    // afterwards.
+    // at position -1, which writes no K/V row, reads no context and draws
+    // nothing, so the caches of live sequences are untouched; the sequence
+    // state of rows 0..M-1 is saved around it and put back.
+    const size_t sb = sizeof(int) * M;
+    int *bak = m->d_state_bak;
+    SB_CUDA_TRY(cudaMemcpyAsync(bak, m->d_tok, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(bak + m->B, m->d_pos, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(bak + 2 * m->B, m->d_plen, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(bak + 3 * m->B, m->d_ngen, sizeof(int) * m->B, cudaMemcpyDeviceToDevice, m->st));
     std::vector<int32_t> zero(M, 0), before(M, -1);
     SB_TRY(set_state(m, M, zero.data(), before.data(), zero.data()));
-    SB_TRY(enqueue_step(m, M, m->st, true, false));
+    SB_TRY(enqueue_step(m, M, m->st, true, false, nullptr, sampled));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, bak, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_pos, bak + m->B, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_plen, bak + 2 * m->B, sb, cudaMemcpyDeviceToDevice, m->st));
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_ngen, bak + 3 * m->B, sizeof(int) * m->B, cudaMemcpyDeviceToDevice, m->st));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     cudaGraph_t g = nullptr;
     SB_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, M, m->st, true, false);
+    int rc = enqueue_step(m, M, m->st, true, false, nullptr, sampled);
     cudaError_t e = cudaStreamEndCapture(m->st, &g);
     if (rc != SB_OK) {
         if (g) cudaGraphDestroy(g);
@@ -493,7 +522,7 @@ int get_graph(sb_llama *m, int M, cudaGraphExec_t *out) {
     e = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     SB_CUDA_TRY(e);
-    m->graphs[M] = ge;
+    cache[M] = ge;
     *out = ge;
     return SB_OK;
 }
@@ -609,6 +638,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     m->pps = ceil_div(c.max_seq_len, m->P);
     m->kv_f32 = c.kv_dtype == SB_KV_F32;
     m->graphs.assign(m->B + 1, nullptr);
+    m->sgraphs.assign(m->B + 1, nullptr);
     auto fail = [&](int rc) {
         sb_llama_destroy(m);
         return rc;
@@ -710,6 +740,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     if ((rc = dalloc_t(m, &m->d_out, (size_t)B * c.max_seq_len)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->d_ngen, B)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->d_last, B)) != SB_OK) return fail(rc);
+    if ((rc = dalloc_t(m, &m->d_state_bak, (size_t)4 * B)) != SB_OK) return fail(rc);
     m->seq.tok = m->d_tok;
     m->seq.pos = m->d_pos;
     m->seq.prompt = m->d_prompt;
@@ -786,6 +817,8 @@ sb_status sb_llama_destroy(sb_llama *m) {
     if (m->st) cudaStreamSynchronize(m->st);
     for (auto g : m->graphs)
         if (g) cudaGraphExecDestroy(g);  // graphs hold NCCL calls: release them before the communicator
+    for (auto g : m->sgraphs)
+        if (g) cudaGraphExecDestroy(g);
     tp_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     if (m->raw) cudaFree(m->raw);
@@ -1245,6 +1278,71 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
     return check_device_errors(m);
 }
 
+namespace {
+// Scratch of the device sampler: [B][V] probabilities, [B] generator states, [B] tokens.
+int samp_buffers(sb_llama *m) {
+    if (m->samp_prob) return SB_OK;
+    void *a = nullptr, *b = nullptr, *c = nullptr;
+    cudaError_t e = cudaMalloc(&a, sizeof(double) * (size_t)m->B * m->V);
+    if (e == cudaSuccess) m->allocs.push_back(a), e = cudaMalloc(&b, sizeof(uint64_t) * m->B);
+    if (e == cudaSuccess) m->allocs.push_back(b), e = cudaMalloc(&c, sizeof(int) * m->B);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(SB_ERR_OOM, "device sampler scratch: %s", cudaGetErrorString(e));
+    }
+    m->allocs.push_back(c);
+    m->samp_prob = static_cast<double *>(a);
+    m->d_rng = static_cast<uint64_t *>(b);
+    m->d_samp = static_cast<int *>(c);
+    return SB_OK;
+}
+}  // namespace
+
+sb_status sb_llama_set_sampling(sb_llama *m, int batch, float temperature, int top_k, float top_p, int max_draws,
+                                const uint64_t *rng_state) {
+    SB_CHECK(m && rng_state, SB_ERR_ARG, "sb_llama_set_sampling: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    SB_CHECK(m->tp == 1, SB_ERR_UNSUPPORTED,
+             "sb_llama_set_sampling: a tensor-parallel rank holds a vocabulary slice; sample on the host");
+    SB_CHECK(!std::isnan(temperature) && !std::isnan(top_p) && top_k >= 0 && max_draws >= 1, SB_ERR_ARG,
+             "sb_llama_set_sampling: temperature %g, top_k %d, top_p %g, max_draws %d", (double)temperature, top_k,
+             (double)top_p, max_draws);
+    SB_TRY(samp_buffers(m));
+    SampleCfg c;
+    c.temperature = temperature;
+    c.top_k = top_k;
+    c.top_p = top_p;
+    c.max_draws = max_draws;
+    if (c.temperature != m->samp.temperature || c.top_k != m->samp.top_k || c.top_p != m->samp.top_p ||
+        c.max_draws != m->samp.max_draws) {
+        // the sampled graphs hold the parameters: capture them again
+        SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+        for (auto &g : m->sgraphs)
+            if (g) cudaGraphExecDestroy(g), g = nullptr;
+        m->samp = c;
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(m->d_rng, rng_state, sizeof(uint64_t) * batch, cudaMemcpyHostToDevice, m->st));
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    m->samp_on = true;
+    return SB_OK;
+}
+
+sb_status sb_llama_clear_sampling(sb_llama *m) {
+    SB_CHECK(m, SB_ERR_ARG, "sb_llama_clear_sampling: null model");
+    m->samp_on = false;
+    return SB_OK;
+}
+
+sb_status sb_llama_get_rng(sb_llama *m, int batch, uint64_t *rng_state) {
+    SB_CHECK(m && rng_state, SB_ERR_ARG, "sb_llama_get_rng: null argument");
+    SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
+    SB_CHECK(m->d_rng, SB_ERR_STATE, "sb_llama_get_rng: the device sampler has not run");
+    SB_CUDA_TRY(cudaStreamSynchronize(m->st));
+    SB_TRY(check_device_errors(m));
+    SB_CUDA_TRY(cudaMemcpy(rng_state, m->d_rng, sizeof(uint64_t) * batch, cudaMemcpyDeviceToHost));
+    return SB_OK;
+}
+
 sb_status sb_llama_sample(sb_llama *m, int batch, float temperature, int top_k, float top_p, uint64_t *rng_state,
                           int32_t *tokens) {
     SB_CHECK(m && rng_state && tokens, SB_ERR_ARG, "sb_llama_sample: null argument");
@@ -1254,20 +1352,7 @@ sb_status sb_llama_sample(sb_llama *m, int batch, float temperature, int top_k, 
              "sb_llama_forward and sample on the host");
     SB_CHECK(!std::isnan(temperature) && !std::isnan(top_p) && top_k >= 0, SB_ERR_ARG,
              "sb_llama_sample: temperature %g, top_k %d, top_p %g", (double)temperature, top_k, (double)top_p);
-    if (!m->samp_prob) {
-        void *a = nullptr, *b = nullptr, *c = nullptr;
-        cudaError_t e = cudaMalloc(&a, sizeof(double) * (size_t)m->B * m->V);
-        if (e == cudaSuccess) m->allocs.push_back(a), e = cudaMalloc(&b, sizeof(uint64_t) * m->B);
-        if (e == cudaSuccess) m->allocs.push_back(b), e = cudaMalloc(&c, sizeof(int) * m->B);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return set_error(SB_ERR_OOM, "sb_llama_sample: %s", cudaGetErrorString(e));
-        }
-        m->allocs.push_back(c);
-        m->samp_prob = static_cast<double *>(a);
-        m->d_rng = static_cast<uint64_t *>(b);
-        m->d_samp = static_cast<int *>(c);
-    }
+    SB_TRY(samp_buffers(m));
     SB_CUDA_TRY(cudaMemcpyAsync(m->d_rng, rng_state, sizeof(uint64_t) * batch, cudaMemcpyHostToDevice, m->st));
     SB_TRY(sample_rows_launch(m->logits, batch, m->V, m->Vl, temperature, top_k, top_p, m->d_rng, m->samp_prob,
                               m->d_samp, m->st));
@@ -1286,7 +1371,7 @@ sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_p
     SB_TRY(check_ready(m));
     if (!(batch == 1 && m->ds_ok)) {
         cudaGraphExec_t g = nullptr;
-        SB_TRY(get_graph(m, batch, &g));
+        SB_TRY(get_graph(m, batch, &g, m->samp_on));
     }
     for (int b = 0; b < batch; b++)
         SB_CUDA_TRY(cudaMemcpyAsync(m->d_prompt + (size_t)b * m->cfg.max_seq_len, prompts + (size_t)b * n_prompt,
@@ -1311,7 +1396,7 @@ sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n
     // Capture every step shape used here and by the decode steps that follow
     // before any state is set: a capture's warm-up step resets the sequence state.
     cudaGraphExec_t g_full = nullptr, g_tail = nullptr, g_dec = nullptr;
-    if (!(batch == 1 && m->ds_ok)) SB_TRY(get_graph(m, batch, &g_dec));
+    if (!(batch == 1 && m->ds_ok)) SB_TRY(get_graph(m, batch, &g_dec, m->samp_on));
     if (n_prompt >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full));
     if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail));
     std::vector<int> pt((size_t)m->B * m->pps);
@@ -1331,8 +1416,16 @@ sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n
             else
                 SB_CUDA_TRY(cudaGraphLaunch(M == C ? g_full : g_tail, m->st));
         }
-        // the argmax after the last prompt token is the first generated token
-        SB_CUDA_TRY(cudaMemcpyAsync(&first[b], m->d_last + (M - 1), sizeof(int), cudaMemcpyDeviceToHost, m->st));
+        // the token after the last prompt position is the first generated
+        // token: the argmax, or with device sampling a draw from sequence b's
+        // generator on that position's logits (generate.rs:72-75)
+        if (m->samp_on) {
+            SB_TRY(sample_rows_launch(m->logits + (size_t)(M - 1) * m->Vl, 1, m->V, m->Vl, m->samp.temperature,
+                                      m->samp.top_k, m->samp.top_p, m->d_rng + b, m->samp_prob, m->d_samp + b, m->st));
+            SB_CUDA_TRY(cudaMemcpyAsync(&first[b], m->d_samp + b, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+        } else {
+            SB_CUDA_TRY(cudaMemcpyAsync(&first[b], m->d_last + (M - 1), sizeof(int), cudaMemcpyDeviceToHost, m->st));
+        }
     }
     // sequences back on their own pages, positioned after the prompt
     for (int r = 0; r < m->B; r++)
@@ -1419,9 +1512,9 @@ sb_status sb_llama_step(sb_llama *m, int n_steps) {
     SB_CHECK(n_steps >= 0 && (long long)m->steps + n_steps <= m->cfg.max_seq_len, SB_ERR_SHAPE,
              "sb_llama_step: %d + %d steps exceed the cache (%d positions)", m->steps, n_steps, m->cfg.max_seq_len);
     if (m->active == 1 && m->ds_ok) {
-        for (int i = 0; i < n_steps; i++) SB_TRY(ds_step(m));
+        for (int i = 0; i < n_steps; i++) SB_TRY(ds_step(m, m->samp_on));
     } else {
-        SB_TRY(get_graph(m, m->active, &g));
+        SB_TRY(get_graph(m, m->active, &g, m->samp_on));
         for (int i = 0; i < n_steps; i++) SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
     }
     m->steps += n_steps;

@@ -82,7 +82,9 @@ __global__ void argmax_step_kernel(const float *__restrict__ cv, const int *__re
         const int pos = s.pos[b];
         const int plen = s.prompt_len ? s.prompt_len[b] : 0;
         s.last[b] = next;
-        if (pos >= plen - 1) {  // generate.rs:72-75: sample after the last prompt token
+        // generate.rs:72-75: sample after the last prompt token (a step at
+        // position -1 is a graph capture's warm-up and records nothing)
+        if (pos >= 0 && pos >= plen - 1) {
             const int g = s.ngen[b];
             if (g < s.max_gen) s.out[(size_t)b * s.max_gen + g] = next;
             s.ngen[b] = g + 1;

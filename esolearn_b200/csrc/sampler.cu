@@ -113,15 +113,12 @@ __device__ __forceinline__ void sp_amax_merge(float &v, int &i, float ov, int oi
     if (i < 0 || ov > v || (ov == v && oi > i)) v = ov, i = oi;
 }
 
-__global__ void __launch_bounds__(SP_THREADS) sample_rows_kernel(const float *__restrict__ logits, int n, int ld,
-                                                                 float temperature, int top_k, float top_p,
-                                                                 uint64_t *__restrict__ rng, double *__restrict__ prob,
-                                                                 int *__restrict__ out) {
-    __shared__ SpShared sh;
+// One row: the token goes to *token_out (written by thread 0), the draw advances
+// *rng_row.  Every thread of the CTA calls it; p is the row's scratch.
+__device__ __forceinline__ void sp_sample_row(const float *__restrict__ x, int n, float temperature, int top_k,
+                                              float top_p, uint64_t *__restrict__ rng_row, double *__restrict__ p,
+                                              SpShared &sh, int *token_out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int row = blockIdx.x;
-    const float *x = logits + (size_t)row * ld;
-    double *p = prob + (size_t)row * n;
 
     if (temperature < 1e-8f) {  // greedy: no draw
         float v = -INFINITY;
@@ -136,7 +133,7 @@ __global__ void __launch_bounds__(SP_THREADS) sample_rows_kernel(const float *__
         __syncthreads();
         if (tid == 0) {
             for (int w = 1; w < SP_WARPS; w++) sp_amax_merge(v, idx, sh.amax_v[w], sh.amax_i[w]);
-            out[row] = idx < 0 ? 0 : idx;
+            *token_out = idx < 0 ? 0 : idx;
         }
         return;
     }
@@ -334,9 +331,9 @@ __global__ void __launch_bounds__(SP_THREADS) sample_rows_kernel(const float *__
     sh.seg[tid] = ssum;
     __syncthreads();
     if (tid == 0) {
-        uint64_t st = rng[row];
+        uint64_t st = *rng_row;
         const double r = sp_rng_f64(st);
-        rng[row] = st;
+        *rng_row = st;
         int token = n - 1;
         double cum = 0.0;
         int w = 0;
@@ -350,11 +347,60 @@ __global__ void __launch_bounds__(SP_THREADS) sample_rows_kernel(const float *__
             cum += p[i];
             if (r < cum) token = i, found = true;
         }
-        out[row] = token;
+        *token_out = token;
+    }
+}
+
+__global__ void __launch_bounds__(SP_THREADS) sample_rows_kernel(const float *__restrict__ logits, int n, int ld,
+                                                                 float temperature, int top_k, float top_p,
+                                                                 uint64_t *__restrict__ rng, double *__restrict__ prob,
+                                                                 int *__restrict__ out) {
+    __shared__ SpShared sh;
+    const int row = blockIdx.x;
+    sp_sample_row(logits + (size_t)row * ld, n, temperature, top_k, top_p, rng + row, prob + (size_t)row * n, sh,
+                  out + row);
+}
+
+// The token step of a sampled decode loop (generate.rs:68-86), row b per CTA:
+// while b is inside its prompt (pos < prompt_len - 1) nothing is drawn and
+// the next step reads the prompt; from the last prompt position on, the
+// token is sampled from this step's logits, recorded and fed to the next
+// step, until max_draws tokens were drawn (later steps draw nothing and feed
+// token 0).  The position always advances.
+__global__ void __launch_bounds__(SP_THREADS) sample_step_kernel(const float *__restrict__ logits, int n, int ld,
+                                                                 SampleCfg c, uint64_t *__restrict__ rng,
+                                                                 double *__restrict__ prob, SeqState s) {
+    __shared__ SpShared sh;
+    __shared__ int tok;
+    const int b = blockIdx.x;
+    const int pos = s.pos[b], plen = s.prompt_len ? s.prompt_len[b] : 0, g = s.ngen[b];
+    // uniform over the CTA; a step at position -1 (a graph capture's warm-up) draws nothing
+    const bool draw = pos >= 0 && pos >= plen - 1 && g < c.max_draws;
+    if (draw)
+        sp_sample_row(logits + (size_t)b * ld, n, c.temperature, c.top_k, c.top_p, rng + b, prob + (size_t)b * n, sh,
+                      &tok);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int next = draw ? tok : 0;
+        if (draw) {
+            s.last[b] = next;
+            if (g < s.max_gen) s.out[(size_t)b * s.max_gen + g] = next;
+            s.ngen[b] = g + 1;
+        }
+        s.tok[b] = next;
+        s.pos[b] = pos + 1;
     }
 }
 
 }  // namespace
+
+int sample_step_launch(const float *logits, int rows, int n, int ld, const SampleCfg &c, uint64_t *rng, double *prob,
+                       const SeqState &s, cudaStream_t st) {
+    if (rows <= 0) return SB_OK;
+    sample_step_kernel<<<rows, SP_THREADS, 0, st>>>(logits, n, ld, c, rng, prob, s);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+}
 
 int sample_rows_launch(const float *logits, int rows, int n, int ld, float temperature, int top_k, float top_p,
                        uint64_t *rng, double *prob, int *out, cudaStream_t st) {

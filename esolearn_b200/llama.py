@@ -413,6 +413,49 @@ class QuantLlamaB200:
             r.state = int(v)
         return out.tolist()
 
+    def set_sampling(self, config: "SamplingConfig", rngs: Sequence["Rng"], max_draws: int | None = None):
+        """Make every decode step that step() queues end in sample_token on
+        the device for rows 0..len(rngs)-1 (sb_llama_set_sampling): the
+        sampled token feeds the next step with no host round trip; rngs[b]'s
+        state is copied to the device (rng_states() reads it back)."""
+        st = np.array([r.state for r in rngs], np.uint64)
+        md = 0x7FFFFFFF if max_draws is None else int(max_draws)
+        N.check(N.lib().sb_llama_set_sampling(self._h, len(rngs), float(config.temperature), int(config.top_k),
+                                              float(config.top_p), md, _ptr(st)))
+
+    def clear_sampling(self):
+        N.check(N.lib().sb_llama_clear_sampling(self._h))
+
+    def rng_states(self, batch: int) -> np.ndarray:
+        st = np.empty(batch, np.uint64)
+        N.check(N.lib().sb_llama_get_rng(self._h, batch, _ptr(st)))
+        return st
+
+    def generate_sampled(self, prompts, config: "SamplingConfig", rngs: Sequence["Rng"],
+                         batched_prefill: bool = False) -> np.ndarray:
+        """generate() (generate.rs:51-89) with sampling, for equal-length
+        prompts, as one device loop: max(1, max_tokens) tokens per prompt,
+        [B, n]; rngs[b] ends where sampling on the host would leave it."""
+        pr = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, n_out = pr.shape[0], max(1, config.max_tokens)
+        if len(rngs) != B:
+            raise ValueError("generate_sampled: one generator per prompt")
+        self.set_sampling(config, rngs, n_out)
+        try:
+            if batched_prefill:
+                self.prefill(pr)
+                self.step(n_out - 1)
+            else:
+                self.begin(pr)
+                self.step(pr.shape[1] + n_out - 1)
+            out = self.tokens(B, n_out)
+            st = self.rng_states(B)
+        finally:
+            self.clear_sampling()
+        for r, v in zip(rngs, st):
+            r.state = int(v)
+        return out
+
     def set_trace(self, on: bool):
         N.check(N.lib().sb_llama_set_trace(self._h, int(on)))
 
@@ -567,15 +610,19 @@ def sample_token(logits: np.ndarray, config: SamplingConfig, rng: Rng) -> int:
 
 
 def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: SamplingConfig, rng: Rng,
-             device_sampling: bool = True) -> list:
+             device_sampling: bool = True, device_loop: bool = True) -> list:
     """generate.rs:51-89.  Greedy runs entirely on the device.  Sampled
-    generation samples on the device (only the token crosses to the host)
-    unless device_sampling is False or the model is tensor-parallel, in which
-    case the logits come back and sample_token runs on the host."""
+    generation runs as one device loop (every step samples on the device and
+    feeds its token to the next step) unless device_loop is False, where each
+    token is sampled on the device but passes through the host, or
+    device_sampling is False or the model is tensor-parallel, where the logits
+    come back and sample_token runs on the host."""
     if len(prompt_tokens) == 0:
         raise ValueError("generate: prompt_tokens must not be empty")
     if config.temperature < 1e-8:
         return model.generate_greedy([list(prompt_tokens)], config.max_tokens)[0].tolist()
+    if device_sampling and device_loop and model.tp_size == 1:
+        return model.generate_sampled([list(prompt_tokens)], config, [rng])[0].tolist()
     max_seq = len(prompt_tokens) + config.max_tokens
     cache = model.new_kv_cache(max_seq)
     V = model.vocab_size()
@@ -600,7 +647,7 @@ def generate(model: QuantLlamaB200, prompt_tokens: Sequence[int], config: Sampli
 
 
 def generate_batch(model: QuantLlamaB200, prompts: Sequence[Sequence[int]], config: SamplingConfig,
-                   rngs: Sequence[Rng], device_sampling: bool = True) -> list:
+                   rngs: Sequence[Rng], device_sampling: bool = True, device_loop: bool = True) -> list:
     """generate() (generate.rs:51-89) for several prompts at once, one engine
     row per sequence: sequence b's tokens, and the final state of rngs[b],
     equal generate(model, prompts[b], config, rngs[b]).  Prompts may differ in
@@ -608,7 +655,8 @@ def generate_batch(model: QuantLlamaB200, prompts: Sequence[Sequence[int]], conf
     step of its last prompt token on (max(1, max_tokens) tokens, like the
     reference loop); a row that is done keeps stepping without drawing from
     its generator.  Sampling runs on the device unless device_sampling is
-    False or the model is tensor-parallel."""
+    False or the model is tensor-parallel; prompts of equal length then run
+    as one device loop (generate_sampled) unless device_loop is False."""
     B = len(prompts)
     if len(rngs) != B:
         raise ValueError("generate_batch: one generator per prompt")
@@ -620,6 +668,10 @@ def generate_batch(model: QuantLlamaB200, prompts: Sequence[Sequence[int]], conf
         raise N.SbError(4, f"generate_batch: {B} prompts exceed the engine's max_batch {model.max_batch}")
     lens = [len(p) for p in prompts]
     n_out = max(1, config.max_tokens)
+    if device_sampling and device_loop and model.tp_size == 1 and len(set(lens)) == 1:
+        if config.temperature < 1e-8:
+            return model.generate_greedy([list(p) for p in prompts], n_out).tolist()
+        return model.generate_sampled([list(p) for p in prompts], config, rngs).tolist()
     steps = max(lens) + n_out - 1
     cache = model.new_kv_cache(steps)
     V = model.vocab_size()

@@ -289,6 +289,25 @@ sb_status sb_llama_forward_seq(sb_llama *m, const int32_t *tokens, int n, float 
  * (SB_ERR_UNSUPPORTED under tensor parallelism). */
 sb_status sb_llama_sample(sb_llama *m, int batch, float temperature, int top_k, float top_p,
                           uint64_t *rng_state, int32_t *tokens);
+/* Sampled generation as a device loop (generate.rs:68-86 with
+ * temperature > 0): from this call on, every decode step that sb_llama_step
+ * queues ends in sample_token on the device for rows 0..batch-1 instead of
+ * the argmax, and feeds the sampled token to the next step with no host
+ * round trip.  A row draws nothing while it is inside its prompt; from its
+ * last prompt position on it draws one token per step from its own fastrand
+ * state, until max_draws tokens were drawn (later steps draw nothing).
+ * sb_llama_prefill also samples the first generated token.  rng_state: host
+ * [batch] states, copied to the device; sb_llama_get_rng reads the advanced
+ * states back, sb_llama_tokens the tokens.  sb_llama_forward and
+ * sb_llama_forward_batch keep returning argmax tokens.  Single-GPU models
+ * only (SB_ERR_UNSUPPORTED under tensor parallelism).  Replaces the host
+ * loop around sb_llama_sample. */
+sb_status sb_llama_set_sampling(sb_llama *m, int batch, float temperature, int top_k, float top_p,
+                                int max_draws, const uint64_t *rng_state);
+/* Back to greedy (argmax) steps. */
+sb_status sb_llama_clear_sampling(sb_llama *m);
+/* The device generators of rows 0..batch-1 (host out [batch]). */
+sb_status sb_llama_get_rng(sb_llama *m, int batch, uint64_t *rng_state);
 /* generate (generate.rs:51-89) with temperature 0, for `batch` prompts of
  * equal length: prompts [batch, n_prompt], out [batch, max_tokens]. */
 sb_status sb_llama_generate_greedy(sb_llama *m, int batch, const int32_t *prompts, int n_prompt,

@@ -61,7 +61,7 @@ class FakeModel:
 
     def generate_greedy(self, prompts, max_tokens):
         p = list(np.atleast_2d(prompts)[0])
-        return np.array([generate(self, p, SamplingConfig(1.0, 1, 1.0, max_tokens), Rng(0))])
+        return np.array([generate(self, p, SamplingConfig(1.0, 1, 1.0, max_tokens), Rng(0), device_loop=False)])
 
 
 CONFIGS = [SamplingConfig(0.8, 10, 0.9, 7), SamplingConfig(1.3, 0, 1.0, 5), SamplingConfig(0.0, 0, 1.0, 6),

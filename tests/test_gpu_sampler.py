@@ -145,3 +145,61 @@ def test_engine_sample_batch_rows_match_oracle():
     assert got == want
     assert [r.state for r in rngs] == [int(r.state.value) for r in refs]
     e.close()
+
+
+def _oracle_sampled(om, prompt, cfg, seed, max_seq):
+    """The oracle model's generate() with sampling: tokens and the final state."""
+    oc = om.new_cache(max_seq)
+    rng = O.Rng(seed)
+    for pos, t in enumerate(prompt):
+        lg = om.forward_with_cache(oc, int(t), pos)
+    out = [O.sample_token(lg, cfg.temperature, cfg.top_k, cfg.top_p, rng)]
+    for i in range(1, max(1, cfg.max_tokens)):
+        lg = om.forward_with_cache(oc, out[-1], len(prompt) + i - 1)
+        out.append(O.sample_token(lg, cfg.temperature, cfg.top_k, cfg.top_p, rng))
+    return out, int(rng.state.value)
+
+
+@pytest.mark.parametrize("B,batched_prefill", [(1, False), (1, True), (3, False), (3, True), (6, False), (6, True)])
+def test_device_sampling_loop_matches_oracle(B, batched_prefill):
+    # generate() with sampling as one device loop (sb_llama_set_sampling +
+    # sb_llama_step): every step samples on the device and feeds its token to
+    # the next one.  Batch 1 runs the persistent step kernel, 3 the GEMV graph,
+    # 6 the chained tensor-core graph; with batched_prefill the first token is
+    # sampled after sb_llama_prefill.  Tokens and generator states equal the
+    # oracle model's generate() per sequence.
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 96), 6)
+    e = engine_from_oracle(om, c, max_seq=96, max_batch=max(B, 4), kv_dtype="f32")
+    cfg = SamplingConfig(0.8, 20, 0.9, 16)
+    prompts = np.stack([O.prompt_ids(500 + b, 7, c.vocab_size) for b in range(B)])
+    rngs = [Rng(50 + b) for b in range(B)]
+    got = e.generate_sampled(prompts, cfg, rngs, batched_prefill=batched_prefill)
+    for b in range(B):
+        want, state = _oracle_sampled(om, prompts[b], cfg, 50 + b, 96)
+        assert got[b].tolist() == want, b
+        assert rngs[b].state == state, b
+    e.close()
+
+
+def test_device_sampling_loop_draw_cap_and_state_kept_across_capture():
+    # Sampling switched on after sb_llama_begin (the sampled step graph is
+    # captured then: its warm-up must leave the sequence state alone), and
+    # max_draws = 5: steps after the fifth draw leave the generators as they
+    # are.
+    c = small_config(layers=2, heads=8, kv=2)
+    om = O.OracleLlama(orc_config(c, 96), 6)
+    e = engine_from_oracle(om, c, max_seq=96, max_batch=3, kv_dtype="f32")
+    cfg = SamplingConfig(1.1, 0, 0.95, 5)
+    prompts = np.stack([O.prompt_ids(600 + b, 6, c.vocab_size) for b in range(3)])
+    e.begin(prompts)
+    e.set_sampling(cfg, [Rng(90 + b) for b in range(3)], max_draws=5)
+    e.step(6 + 12)  # the prompt, then 13 steps: 5 draw, 8 draw nothing
+    got = e.tokens(3, 5)
+    st = e.rng_states(3)
+    e.clear_sampling()
+    for b in range(3):
+        want, state = _oracle_sampled(om, prompts[b], cfg, 90 + b, 96)
+        assert got[b].tolist() == want, b
+        assert int(st[b]) == state, b
+    e.close()
