@@ -30,6 +30,24 @@ struct AttnArgs {
     CUtensorMap tmk, tmv;
 };
 
+// Causal attention of a prefill chunk (attention_prefill.cu): rows 0..M-1
+// are positions pos[r] of one sequence whose pages are page_table[0 ..
+// max_pages); row r attends to positions 0..pos[r].  q: [M, n_heads*hd]
+// (RoPE'd, scaled by 1/sqrt(hd)); out: [M, n_heads*hd].  bf16 cache, head_dim
+// 64 or 128.  Each K/V tile is read once per 16 rows and q head.
+struct PrefillAttnArgs {
+    const float *q = nullptr;
+    const void *kc = nullptr, *vc = nullptr;  // this layer's [pages][n_kv][page_size][hd]
+    int kv_f32 = 0;
+    const int *page_table = nullptr;  // the sequence's pages
+    int max_pages = 0;
+    const int *pos = nullptr;  // [M] device
+    int M = 0, n_heads = 0, n_kv = 0, hd = 0, page_size = 0;
+    float *out = nullptr;
+};
+bool attn_prefill_supported(int hd, int kv_f32);
+int attn_prefill_launch(const PrefillAttnArgs &a, cudaStream_t st, bool pdl);
+
 // Reports (and clears) a timed-out wait of the tensor-map kernel.
 int attn_tc_check_error();
 // Encode a [rows][hd] bf16 tensor map over a KV cache for the tensor-map path.

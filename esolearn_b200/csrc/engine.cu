@@ -104,7 +104,7 @@ struct sb_llama {
     int steps = 0;   // steps queued since begin()
 
     // graphs per batch size: greedy steps, and steps ending in the device sampler
-    std::vector<cudaGraphExec_t> graphs, sgraphs;
+    std::vector<cudaGraphExec_t> graphs, sgraphs, pgraphs;  // + prefill chunks (rows = positions of one sequence)
     // device sampling loop (sb_llama_set_sampling)
     bool samp_on = false;
     SampleCfg samp;
@@ -264,8 +264,21 @@ int engine_linear(sb_llama *m, int epi, const QGemvArgs &a, cudaStream_t st, boo
     } while (0)
 
 // Enqueue one decode step for M sequences on st.
+// What a queued step ends in, and how its attention runs: greedy (argmax),
+// sampled (the device sampler), or a prefill chunk -- rows are consecutive
+// prompt positions of one sequence (page-table row 0 holds its pages), the
+// attention may read each K/V tile once for all rows (attention_prefill.cu),
+// and the step ends in the argmax.
+enum StepKind { STEP_GREEDY = 0, STEP_SAMPLED = 1, STEP_PREFILL = 2 };
+
 int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, StepProfiler *prof = nullptr,
-                 bool sampled = false) {
+                 int kind = STEP_GREEDY) {
+    const bool sampled = kind == STEP_SAMPLED;
+    // The prefill kernel replaces the per-row attention where that runs on the
+    // SIMT kernel (one query head per kv head); with 2-8 heads per kv head the
+    // tensor-map kernel is as fast or faster (its grid has 8x more CTAs).
+    const bool flash =
+        kind == STEP_PREFILL && M > 1 && m->nh == m->nkv && attn_prefill_supported(m->hd, m->kv_f32);
     // Batches of 5+ rows on one GPU chain the tensor-core linears: the finish
     // of o, gate/up and down (whose output row is the next linear's input)
     // also writes the next linear's planes, one launch instead of two.
@@ -308,7 +321,23 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
             a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
             SB_PROF(prof, 0, linear(QEPI_QKV, a, nullptr));
         }
-        {
+        if (flash) {
+            PrefillAttnArgs a;
+            a.q = m->q;
+            a.kc = (char *)m->kc + kvoff;
+            a.vc = (char *)m->vc + kvoff;
+            a.kv_f32 = m->kv_f32;
+            a.page_table = m->page_table;
+            a.max_pages = m->pps;
+            a.pos = m->d_pos;
+            a.M = M;
+            a.n_heads = m->nh;
+            a.n_kv = m->nkv;
+            a.hd = m->hd;
+            a.page_size = m->P;
+            a.out = m->attn;
+            SB_PROF(prof, 1, attn_prefill_launch(a, st, pdl));
+        } else {
             AttnArgs a;
             a.q = m->q;
             a.kc = (char *)m->kc + kvoff;
@@ -485,8 +514,8 @@ int check_device_errors(sb_llama *m) {
     return qgemv_check_error();
 }
 
-int get_graph(sb_llama *m, int M, cudaGraphExec_t *out, bool sampled = false) {
-    std::vector<cudaGraphExec_t> &cache = sampled ? m->sgraphs : m->graphs;
+int get_graph(sb_llama *m, int M, cudaGraphExec_t *out, int kind = STEP_GREEDY) {
+    std::vector<cudaGraphExec_t> &cache = kind == STEP_SAMPLED ? m->sgraphs : kind == STEP_PREFILL ? m->pgraphs : m->graphs;
     if (cache[M]) {
         *out = cache[M];
         return SB_OK;
@@ -503,7 +532,7 @@ int get_graph(sb_llama *m, int M, cudaGraphExec_t *out, bool sampled = false) {
     SB_CUDA_TRY(cudaMemcpyAsync(bak + 3 * m->B, m->d_ngen, sizeof(int) * m->B, cudaMemcpyDeviceToDevice, m->st));
     std::vector<int32_t> zero(M, 0), before(M, -1);
     SB_TRY(set_state(m, M, zero.data(), before.data(), zero.data()));
-    SB_TRY(enqueue_step(m, M, m->st, true, false, nullptr, sampled));
+    SB_TRY(enqueue_step(m, M, m->st, true, false, nullptr, kind));
     SB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, bak, sb, cudaMemcpyDeviceToDevice, m->st));
     SB_CUDA_TRY(cudaMemcpyAsync(m->d_pos, bak + m->B, sb, cudaMemcpyDeviceToDevice, m->st));
     SB_CUDA_TRY(cudaMemcpyAsync(m->d_plen, bak + 2 * m->B, sb, cudaMemcpyDeviceToDevice, m->st));
@@ -511,7 +540,7 @@ int get_graph(sb_llama *m, int M, cudaGraphExec_t *out, bool sampled = false) {
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     cudaGraph_t g = nullptr;
     SB_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, M, m->st, true, false, nullptr, sampled);
+    int rc = enqueue_step(m, M, m->st, true, false, nullptr, kind);
     cudaError_t e = cudaStreamEndCapture(m->st, &g);
     if (rc != SB_OK) {
         if (g) cudaGraphDestroy(g);
@@ -639,6 +668,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     m->kv_f32 = c.kv_dtype == SB_KV_F32;
     m->graphs.assign(m->B + 1, nullptr);
     m->sgraphs.assign(m->B + 1, nullptr);
+    m->pgraphs.assign(m->B + 1, nullptr);
     auto fail = [&](int rc) {
         sb_llama_destroy(m);
         return rc;
@@ -732,6 +762,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     m->att_splits = attn_pick_splits(B, m->nkv, c.max_seq_len);
     if ((rc = dalloc_t(m, &m->att_part, attn_scratch_floats(B, m->nh, m->att_splits, hd))) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->att_cnt, (size_t)B * m->nkv)) != SB_OK) return fail(rc);
+
     // sequence state
     if ((rc = dalloc_t(m, &m->d_tok, B)) != SB_OK) return fail(rc);
     if ((rc = dalloc_t(m, &m->d_pos, B)) != SB_OK) return fail(rc);
@@ -818,6 +849,8 @@ sb_status sb_llama_destroy(sb_llama *m) {
     for (auto g : m->graphs)
         if (g) cudaGraphExecDestroy(g);  // graphs hold NCCL calls: release them before the communicator
     for (auto g : m->sgraphs)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto g : m->pgraphs)
         if (g) cudaGraphExecDestroy(g);
     tp_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
@@ -1371,7 +1404,7 @@ sb_status sb_llama_begin(sb_llama *m, int batch, const int32_t *prompts, int n_p
     SB_TRY(check_ready(m));
     if (!(batch == 1 && m->ds_ok)) {
         cudaGraphExec_t g = nullptr;
-        SB_TRY(get_graph(m, batch, &g, m->samp_on));
+        SB_TRY(get_graph(m, batch, &g, m->samp_on ? STEP_SAMPLED : STEP_GREEDY));
     }
     for (int b = 0; b < batch; b++)
         SB_CUDA_TRY(cudaMemcpyAsync(m->d_prompt + (size_t)b * m->cfg.max_seq_len, prompts + (size_t)b * n_prompt,
@@ -1396,9 +1429,9 @@ sb_status sb_llama_prefill(sb_llama *m, int batch, const int32_t *prompts, int n
     // Capture every step shape used here and by the decode steps that follow
     // before any state is set: a capture's warm-up step resets the sequence state.
     cudaGraphExec_t g_full = nullptr, g_tail = nullptr, g_dec = nullptr;
-    if (!(batch == 1 && m->ds_ok)) SB_TRY(get_graph(m, batch, &g_dec, m->samp_on));
-    if (n_prompt >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full));
-    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail));
+    if (!(batch == 1 && m->ds_ok)) SB_TRY(get_graph(m, batch, &g_dec, m->samp_on ? STEP_SAMPLED : STEP_GREEDY));
+    if (n_prompt >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full, STEP_PREFILL));
+    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail, STEP_PREFILL));
     std::vector<int> pt((size_t)m->B * m->pps);
     std::vector<int32_t> tok(C), pos(C), zero(C, 0), first(batch);
     for (int b = 0; b < batch; b++) {
@@ -1456,8 +1489,8 @@ sb_status sb_llama_forward_seq(sb_llama *m, const int32_t *tokens, int n, float 
     const int tail = n % C;
     // capture the chunk shapes first (a capture's warm-up resets the state)
     cudaGraphExec_t g_full = nullptr, g_tail = nullptr;
-    if (n >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full));
-    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail));
+    if (n >= C && !(C == 1 && m->ds_ok)) SB_TRY(get_graph(m, C, &g_full, STEP_PREFILL));
+    if (tail > 0 && !(tail == 1 && m->ds_ok)) SB_TRY(get_graph(m, tail, &g_tail, STEP_PREFILL));
     // every row of a chunk is a position of sequence 0: all rows use its pages
     std::vector<int> pt((size_t)m->B * m->pps);
     for (int r = 0; r < m->B; r++)
@@ -1514,7 +1547,7 @@ sb_status sb_llama_step(sb_llama *m, int n_steps) {
     if (m->active == 1 && m->ds_ok) {
         for (int i = 0; i < n_steps; i++) SB_TRY(ds_step(m, m->samp_on));
     } else {
-        SB_TRY(get_graph(m, m->active, &g, m->samp_on));
+        SB_TRY(get_graph(m, m->active, &g, m->samp_on ? STEP_SAMPLED : STEP_GREEDY));
         for (int i = 0; i < n_steps; i++) SB_CUDA_TRY(cudaGraphLaunch(g, m->st));
     }
     m->steps += n_steps;

@@ -191,3 +191,24 @@ def test_seventy_b_head_layout_one_layer(B):
     lg, _ = _rewound_logits(e, prompts, got, steps)
     for b in range(B):
         assert rel_err(lg[b], ref_logits[b][steps[b]]) < TOL, (b, steps[b])
+
+
+@pytest.mark.parametrize("max_batch,n_prompt", [(64, 600), (16, 203)])
+def test_seven_b_head_layout_prefill_attention(max_batch, n_prompt):
+    # One query head per kv head (the 7B layout: 32 heads of 128): a batched
+    # prefill runs the prefill attention kernel, every chunk of max_batch
+    # prompt positions reading each K/V tile once for all its rows under the
+    # causal mask (10 chunks of 64 over a 600-position prompt; 203 = 12
+    # chunks of 16 plus a ragged tail of 11).  The greedy stream and the
+    # logits of the steps after it equal the oracle's token-by-token run.
+    cfg = LlamaConfig(1024, 4096, 512, 1, 32, 32, 4096, 1e-5, 10000.0, False, None)
+    max_seq = 704
+    om = O.OracleLlama(orc_config(cfg, max_seq), 31)
+    e = engine_from_oracle(om, cfg, max_seq=max_seq, max_batch=max_batch, kv_dtype="bf16")
+    prompt = O.prompt_ids(77, n_prompt, cfg.vocab_size)
+    got = e.generate_greedy(prompt, 16, batched_prefill=True)[0]
+    ref, ref_logits = _streams(om, prompt[:-1], prompt[None, -1:], 16, max_seq)
+    assert greedy_agreement(got, ref[0], ref_logits[0], TOL) == 16
+    for j in (0, 9, 15):
+        lg, _ = _rewound_logits(e, prompt[None, :], got[None, :], [j])
+        assert rel_err(lg[0], ref_logits[0][j]) < TOL, j
