@@ -69,7 +69,9 @@ struct Workspace {
 // WS_GEMM_SUMS only ever holds the tensor-core GEMM's int64 column sums,
 // which must read zero before every call: a grown buffer is zero-filled and
 // every call clears what it used.
-enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_SAMPLE = 4, WS_GROUPED = 5, WS_KINDS = 6 };
+// WS_SPLITK: the split-K GEMV's int64 sums and tile counters, zero between calls.
+enum { WS_QUANT = 0, WS_ATTN = 1, WS_GEMM = 2, WS_GEMM_SUMS = 3, WS_SAMPLE = 4, WS_GROUPED = 5, WS_SPLITK = 6,
+       WS_KINDS = 7 };
 constexpr size_t WS_ATTN_COUNTER_BYTES = 64 * 1024;
 
 static int workspace_get(int kind, size_t bytes, void **out, cudaStream_t st) {
@@ -419,6 +421,13 @@ static sb_status matmul_desc(const QWeightDesc &wd, const void *a, int a_dtype, 
         g.out = c + (size_t)r0 * wd.N;
         g.ldo = wd.N;
         g.bias = bias;
+        if (qgemv_splitk_wanted(wd, g.M)) {
+            // few 128-column tiles: split K over the SMs
+            void *ws = nullptr;
+            SB_TRY(workspace_get(WS_SPLITK, qgemv_splitk_ws_bytes(wd, QG_MAX_M), &ws, st));
+            SB_TRY(qgemv_splitk_launch(bias ? QEPI_BIAS : QEPI_STORE, g, ws, st));
+            continue;
+        }
         SB_TRY(qgemv_launch(bias ? QEPI_BIAS : QEPI_STORE, g, st, false));
     }
     return SB_OK;

@@ -3,6 +3,7 @@
 #pragma once
 
 #include "misc.cuh"
+#include "tp_comm.cuh"
 #include "qgemv.cuh"
 
 namespace sb {
@@ -59,6 +60,7 @@ struct DsLayer {
 
 struct DsArgs {
     int L = 0, h = 0, F = 0, V = 0, nh = 0, nkv = 0, hd = 0, q_dim = 0, kv_dim = 0;
+    int V_lm = 0;  // lm_head rows (logits) of this rank: V, or the rank's slice under tensor parallelism
     int ks_h = 0, ks_q = 0, ks_f = 0;                        // input widths / 16, rounded up
     int nt_qkv = 0, nt_o = 0, nt_gu = 0, nt_down = 0, nt_lm = 0;  // 128-column tiles
     const DsLayer *layers = nullptr;                         // [L] (device)
@@ -86,6 +88,16 @@ struct DsArgs {
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
     unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
     int greedy = 1;  // 1: the last CTA records the argmax and advances the sequence; 0: a sampler follows
+    // Tensor parallelism (tp > 1): shapes above are this rank's shard (heads,
+    // ffn columns, vocabulary rows); the o and down partial products and the
+    // argmax candidates travel through cells[r] = rank r's [2][tp][h + 2]
+    // 8-byte cells (value, epoch), mapped into every rank.  The exchanges of
+    // one step use epochs epoch0 + 1 .. epoch0 + 2L + 1 (one per o, one per
+    // down, one for the argmax); slot parity = epoch & 1.
+    int tp = 1, tp_rank = 0;
+    uint2 *cells[TP_MAX_RANKS] = {};
+    unsigned epoch0 = 0;
+    int v_off = 0;  // first vocabulary index of this rank's lm_head rows
     int nst = 0;                // ring stages
     int mtab_bytes = 0;         // attention-combine table (ds_mtab_bytes)
 };

@@ -247,6 +247,95 @@ __device__ __noinline__ void ds_in_resid(const float *x_src, const long long *ac
     ds_quantize<QMAX>(v, ssq, amx, K, nq, norm != nullptr, eps, pa_off);
 }
 
+// Input stage after a tensor-parallel row projection (o or down): the
+// residual x plus every rank's partial product, read from this rank's cells
+// (cells + src * ld + k holds rank src's y_k, written with epoch e), waiting
+// -- bounded -- for cells not yet written.  The ranks' values are added in
+// rank order, (x + y_0) + y_1 + ..., so every rank gets the same bits.  Then
+// RMSNorm and quantization as ds_in_resid.  Returns false when a wait ran
+// out (the step is then abandoned).
+template <int QMAX>
+__device__ __noinline__ bool ds_in_resid_tp(const float *x_src, const uint2 *cells, int T, int ld, unsigned e,
+                                            const float *norm, int K, int KS, float eps, float *x_dst, float *trace,
+                                            size_t pa_off) {
+    const int tid = threadIdx.x, nq = KS * 4;
+    float4 v[QMAX];
+    float ssq = 0.f, amx = 0.f;
+    bool ok = true;
+    uint64_t t0 = 0;
+    uint32_t spins = 0;
+#pragma unroll
+    for (int j0 = 0; j0 < QMAX; j0 += 4) {
+        // every load of four quads in flight together: x, the norm weight,
+        // then one rank's 16 cells at a time (one round trip per rank)
+        float4 xb[4], wb[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            const int k0 = (tid + (j0 + jj) * DS_CONSUMERS) * 4;
+            xb[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+            wb[jj] = xb[jj];
+            if (k0 < K) {
+                xb[jj] = ldcg4(x_src + k0);
+                if (norm) wb[jj] = __ldg(reinterpret_cast<const float4 *>(norm + k0));
+            }
+        }
+        // cells of two quads of one rank per round trip (register budget)
+        for (int r = 0; r < T; r++) {
+#pragma unroll
+            for (int jp = 0; jp < 4; jp += 2) {
+                uint2 c[2][4];
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        c[u][q] = k0 < K ? ld_cell(cells + (size_t)r * ld + k0 + q) : make_uint2(0u, e);
+                }
+                for (;;) {
+                    bool all = true;
+#pragma unroll
+                    for (int u = 0; u < 2; u++)
+#pragma unroll
+                        for (int q = 0; q < 4; q++) all = all && c[u][q].y == e;
+                    if (all || !ok) break;
+                    if ((spins++ & 63) == 0) {
+                        const uint64_t t = global_ns();
+                        if (t0 == 0) t0 = t;
+                        else if (t - t0 > SB_WAIT_NS) ok = false;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+#pragma unroll
+                        for (int q = 0; q < 4; q++)
+                            if (c[u][q].y != e) c[u][q] = ld_cell(cells + (size_t)r * ld + k0 + q);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    float4 &x = xb[jp + u];
+                    x.x = __fadd_rn(x.x, __uint_as_float(c[u][0].x));
+                    x.y = __fadd_rn(x.y, __uint_as_float(c[u][1].x));
+                    x.z = __fadd_rn(x.z, __uint_as_float(c[u][2].x));
+                    x.w = __fadd_rn(x.w, __uint_as_float(c[u][3].x));
+                }
+            }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            const int k0 = (tid + (j0 + jj) * DS_CONSUMERS) * 4;
+            if (k0 < K) {
+                if (x_dst) *reinterpret_cast<float4 *>(x_dst + k0) = xb[jj];
+                if (trace) *reinterpret_cast<float4 *>(trace + k0) = xb[jj];
+            }
+            ds_accum(xb[jj], wb[jj], norm != nullptr, ssq, amx, v[j0 + jj]);
+        }
+    }
+    if (!ok) ds_sh.abort = 1;  // seen by the GEMV after the reductions below
+    ds_quantize<QMAX>(v, ssq, amx, K, nq, norm != nullptr, eps, pa_off);
+    return ok;
+}
+
 // Input = the attention output: each q head's partial records (one per CTA
 // that worked on its kv head) combined in CTA order,
 //   out = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c,  M = max_c m_c.
@@ -643,7 +732,59 @@ __device__ __noinline__ uint32_t ds_attention(uint32_t it, int nst, uint32_t bar
 }
 
 // ---- the kernel ----------------------------------------------------------------
-template <int HD, int REP, typename KV>
+// Tensor parallelism: this CTA's slice of a row projection's h outputs,
+// y = sum * f (this rank's partial product), into slot [e & 1][rank] of
+// every rank's cells, each value paired with the exchange's epoch e in one
+// store.
+__device__ __forceinline__ void ds_tp_push(const DsArgs &a, const long long *sums, double f, unsigned e, int G, int cta) {
+    const int tid = threadIdx.x, ld = a.h + 2;
+    const int c0 = (int)((long long)a.h * cta / G), c1 = (int)((long long)a.h * (cta + 1) / G);
+    const size_t slot = ((size_t)(e & 1u) * a.tp + a.tp_rank) * ld;
+    for (int col = c0 + tid; col < c1; col += DS_CONSUMERS) {
+        const float y = gemv_out(__ldcg(sums + col), f);
+        for (int r = 0; r < a.tp; r++) st_cell(a.cells[r] + slot + col, y, e);
+    }
+}
+
+// Tensor parallelism, one thread: this rank's argmax candidate (best, bi
+// local to its vocabulary rows) to every rank, then every rank's candidate
+// merged in rank order with the argmax tie rule (ties -> the larger index);
+// best / bi become the global argmax.  The argmax exchange of the step uses
+// cells h and h+1 of slot [e & 1][rank].  Returns false when a wait ran out.
+__device__ __forceinline__ bool ds_tp_argmax(const DsArgs &a, float &best, int &bi) {
+    const unsigned e = a.epoch0 + 2 * a.L + 1;
+    const int ld = a.h + 2;
+    const size_t slot = ((size_t)(e & 1u) * a.tp + a.tp_rank) * ld + a.h;
+    const unsigned gi = bi < 0 ? 0xffffffffu : (unsigned)(bi + a.v_off);
+    for (int r = 0; r < a.tp; r++) {
+        st_cell(a.cells[r] + slot, best, e);
+        st_cell_u(a.cells[r] + slot + 1, gi, e);
+    }
+    best = -INFINITY;
+    bi = -1;
+    const uint2 *mine = a.cells[a.tp_rank] + (size_t)(e & 1u) * a.tp * ld;
+    uint64_t t0 = 0;
+    for (int r = 0; r < a.tp; r++) {
+        const uint2 *c = mine + (size_t)r * ld + a.h;
+        uint2 cv = ld_cell(c), ci = ld_cell(c + 1);
+        for (uint32_t it = 0; cv.y != e || ci.y != e; it++) {
+            if ((it & 63) == 0) {
+                const uint64_t t = global_ns();
+                if (it == 0) t0 = t;
+                else if (t - t0 > SB_WAIT_NS) return false;
+            }
+            if (cv.y != e) cv = ld_cell(c);
+            if (ci.y != e) ci = ld_cell(c + 1);
+        }
+        const float ov = __uint_as_float(cv.x);
+        const int oi = ci.x == 0xffffffffu ? -1 : (int)ci.x;
+        if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
+    }
+    return true;
+}
+
+// TP: the tensor-parallel variant (a.tp > 1); the single-GPU kernel carries none of its code.
+template <int HD, int REP, typename KV, bool TP>
 __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs a) {
     using KL = DsKv<KV>;
     static_assert(HD % 64 == 0, "head_dim must give each lane 2 or 4 dims");
@@ -808,6 +949,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         for (int i = z0 + tid; i < z1; i += DS_CONSUMERS) buf[i] = 0;
     };
 
+    // Tensor parallelism: this CTA's slice of a row projection's h outputs,
+    // y = sum * f (this rank's partial product), into slot [e & 1][rank] of
+    // every rank's cells, paired with the exchange's epoch e in one store.
+    const int tp_ld = a.h + 2;
+    auto tp_push = [&](const long long *sums, double f, unsigned e) { ds_tp_push(a, sums, f, e, G, cta); };
+    // This rank's cells of exchange e: [src][tp_ld].
+    auto tp_cells = [&](unsigned e) -> const uint2 * {
+        return a.cells[a.tp_rank] + (size_t)(e & 1u) * a.tp * tp_ld;
+    };
+
     // Attention over this CTA's (kv head, chunk) units of layer l.
     auto attention = [&](int l) {
         const long long u0 = att_U * cta / G, u1 = att_U * (cta + 1) / G;
@@ -855,6 +1006,13 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 ds_in_rows<DS_QMAX_H>(a.embed + (size_t)tok * a.h, true, nw, a.h, a.ks_h, a.eps,
                                       writer ? a.x : nullptr, pa_off);
                 xv = 0;
+            } else if constexpr (TP) {
+                const unsigned e = a.epoch0 + 2 * l;  // the down exchange of layer l - 1
+                tp_push(accbuf(j - 1), gemv_factor(sh.shift, a.layers[l - 1].scale[3], sh.rstd), e);
+                ds_in_resid_tp<DS_QMAX_H>(a.x + (size_t)xv * a.h, tp_cells(e), a.tp, tp_ld, e, nw, a.h, a.ks_h, a.eps,
+                                          writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
+                                          (writer && a.trace) ? a.trace + (size_t)(l - 1) * a.h : nullptr, pa_off);
+                xv ^= 1;
             } else {
                 ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(j - 1), a.layers[l - 1].scale[3], sh.shift,
                                        sh.rstd, nw, a.h, a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
@@ -889,9 +1047,17 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         if (go) go = wait_all();
         if (go) {
             zero_acc(accbuf(j), npad_qkv);
-            ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(j + 1), ly.scale[1], sh.shift, sh.rstd,
-                                   a.norm_post + (size_t)l * a.h, a.h, a.ks_h, a.eps,
-                                   writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
+            if constexpr (TP) {
+                const unsigned e = a.epoch0 + 2 * l + 1;  // the o exchange of layer l
+                tp_push(accbuf(j + 1), gemv_factor(sh.shift, ly.scale[1], sh.rstd), e);
+                ds_in_resid_tp<DS_QMAX_H>(a.x + (size_t)xv * a.h, tp_cells(e), a.tp, tp_ld, e,
+                                          a.norm_post + (size_t)l * a.h, a.h, a.ks_h, a.eps,
+                                          writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
+            } else {
+                ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(j + 1), ly.scale[1], sh.shift, sh.rstd,
+                                       a.norm_post + (size_t)l * a.h, a.h, a.ks_h, a.eps,
+                                       writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr, nullptr, pa_off);
+            }
             xv ^= 1;
             mark(1);
             it = ds_gemv(it, nst, bars, a.ks_h, a.nt_gu, accbuf(j + 2), G, cta, pa_off, red_off, ready_slot());
@@ -929,9 +1095,18 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     if (go) go = wait_all();
     if (go) {
         zero_acc(accbuf(jl - 2), npad_gu);
-        ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(jl - 1), a.layers[a.L - 1].scale[3], sh.shift, sh.rstd,
-                               a.norm_final, a.h, a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
-                               (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
+        if constexpr (TP) {
+            const unsigned e = a.epoch0 + 2 * a.L;  // the down exchange of the last layer
+            tp_push(accbuf(jl - 1), gemv_factor(sh.shift, a.layers[a.L - 1].scale[3], sh.rstd), e);
+            ds_in_resid_tp<DS_QMAX_H>(a.x + (size_t)xv * a.h, tp_cells(e), a.tp, tp_ld, e, a.norm_final, a.h,
+                                      a.ks_h, a.eps, writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
+                                      (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
+        } else {
+            ds_in_resid<DS_QMAX_H>(a.x + (size_t)xv * a.h, accbuf(jl - 1), a.layers[a.L - 1].scale[3], sh.shift,
+                                   sh.rstd, a.norm_final, a.h, a.ks_h, a.eps,
+                                   writer ? a.x + (size_t)(xv ^ 1) * a.h : nullptr,
+                                   (writer && a.trace) ? a.trace + (size_t)(a.L - 1) * a.h : nullptr, pa_off);
+        }
         mark(1);
         it = ds_gemv(it, nst, bars, a.ks_h, a.nt_lm, accbuf(jl), G, cta, pa_off, red_off, ready_slot());
     }
@@ -948,7 +1123,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
         for (int n = n0 + tid; n < n1; n += DS_CONSUMERS) {
             const long long t = __ldcg(lm + n);
             lm[n] = 0;
-            if (n < a.V) {
+            if (n < a.V_lm) {
                 const float y = gemv_out(t, fl);
                 a.logits[n] = y;
                 if (bi < 0 || y >= best) best = y, bi = n;
@@ -991,30 +1166,47 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
                 const int oi = __ldcg(a.cand_idx + c);
                 if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) best = ov, bi = oi;
             }
-            const int next = bi < 0 ? 0 : bi;
-            const SeqState &s = a.seq;
-            const int plen = s.prompt_len ? s.prompt_len[0] : 0;
-            s.last[0] = next;
-            if (pos >= plen - 1) {  // generate.rs:72-75: sample after the last prompt token
-                const int gcount = s.ngen[0];
-                if (gcount < s.max_gen) s.out[gcount] = next;
-                s.ngen[0] = gcount + 1;
+            bool ok = true;
+            if constexpr (TP) {
+                ok = ds_tp_argmax(a, best, bi);
+                if (!ok) atomicExch(abort_flag, 1u);
             }
-            s.tok[0] = next;
-            s.pos[0] = pos + 1;
+            if (ok) {
+                const int next = bi < 0 ? 0 : bi;
+                const SeqState &s = a.seq;
+                const int plen = s.prompt_len ? s.prompt_len[0] : 0;
+                s.last[0] = next;
+                if (pos >= plen - 1) {  // generate.rs:72-75: sample after the last prompt token
+                    const int gcount = s.ngen[0];
+                    if (gcount < s.max_gen) s.out[gcount] = next;
+                    s.ngen[0] = gcount + 1;
+                }
+                s.tok[0] = next;
+                s.pos[0] = pos + 1;
+            }
         }
         a.sync[0] = 0;
         a.sync[1] = 0;
     }
 }
 
-template <int HD, int REP, typename KV>
-inline int ds_limit(int *limit) {
+template <int HD, int REP, typename KV, bool TP>
+inline int ds_limit_k(int *limit) {
     static int lim[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!lim[dev & 63]) SB_TRY(allow_max_dynamic_smem(decode_step_kernel<HD, REP, KV>, &lim[dev & 63]));
+    if (!lim[dev & 63]) SB_TRY(allow_max_dynamic_smem(decode_step_kernel<HD, REP, KV, TP>, &lim[dev & 63]));
     *limit = lim[dev & 63];
+    return SB_OK;
+}
+// Dynamic shared memory the step kernels of this shape may use (the single-GPU
+// and tensor-parallel variants declare the same static shared memory).
+template <int HD, int REP, typename KV>
+inline int ds_limit(int *limit) {
+    int l1 = 0, l2 = 0;
+    SB_TRY((ds_limit_k<HD, REP, KV, false>(&l1)));
+    SB_TRY((ds_limit_k<HD, REP, KV, true>(&l2)));
+    *limit = std::min(l1, l2);
     return SB_OK;
 }
 
@@ -1031,7 +1223,7 @@ inline int ds_limit_rep(int rep, int *limit) {
 
 template <int HD, int REP, typename KV>
 inline int ds_inst(const DsArgs &a, cudaStream_t st) {
-    auto kern = decode_step_kernel<HD, REP, KV>;
+    auto kern = a.tp > 1 ? decode_step_kernel<HD, REP, KV, true> : decode_step_kernel<HD, REP, KV, false>;
     int limit = 0;
     const int lrc = ds_limit<HD, REP, KV>(&limit);
     SB_TRY(lrc);

@@ -116,6 +116,7 @@ struct sb_llama {
 
     // persistent batch-1 step
     bool ds_ok = false;
+    unsigned ds_epoch = 0;  // tensor parallelism: epochs of the step kernel's exchanges so far
     int ds_chunk = 0, ds_nst = 0;
     DsLayer *ds_layers = nullptr;  // device copy of the per-layer weight table
     float *ds_x = nullptr;
@@ -451,6 +452,7 @@ int ds_step(sb_llama *m, bool sampled = false) {
     a.h = m->h;
     a.F = m->F;
     a.V = m->V;
+    a.V_lm = m->Vl;
     a.nh = m->nh;
     a.nkv = m->nkv;
     a.hd = m->hd;
@@ -500,6 +502,14 @@ int ds_step(sb_llama *m, bool sampled = false) {
     a.mtab_bytes = ds_mtab_bytes(m->nh, m->nkv);
     a.stamps = m->ds_stamps;
     a.greedy = sampled ? 0 : 1;
+    if (m->tp > 1) {
+        a.tp = m->tp;
+        a.tp_rank = m->tp_rank;
+        for (int r = 0; r < m->tp; r++) a.cells[r] = m->comm.cells[r];
+        a.epoch0 = m->ds_epoch;
+        a.v_off = m->tp_rank * m->Vl;
+        m->ds_epoch += 2 * m->L + 1;  // the exchanges of this step
+    }
     SB_TRY(ds_launch(a, m->nh / m->nkv, m->st));
     if (sampled) SB_TRY(sample_step_launch(m->logits, 1, m->V, m->Vl, m->samp, m->d_rng, m->samp_prob, m->seq, m->st));
     return SB_OK;
@@ -679,7 +689,7 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     int rc = SB_OK;
     if (tp_size > 1 && (rc = tp_init(m->comm, tp_id, tp_rank, tp_size, 120.0)) != SB_OK) return fail(rc);
     if (tp_size > 1 && (rc = tp_setup_p2p(m->comm, m->B * m->h, m->st)) != SB_OK) return fail(rc);
-    if (tp_size == 1) {
+    {
         int chunk = 0;
         if (ds_supported(m->h, m->F, m->q_dim, hd, m->nh / m->nkv, m->kv_f32, m->P, &chunk)) {
             const int ksmax = ceil_div(std::max(std::max(m->h, m->F), m->q_dim), 16);
@@ -693,6 +703,33 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
                 m->ds_chunk = chunk;
                 m->ds_nst = nst;
             }
+        }
+    }
+    if (tp_size > 1) {
+        // The persistent step under tensor parallelism exchanges through cells
+        // in every rank's memory: all ranks must have peer access and the
+        // kernel; they agree (one all-gather) before sharing the cells.
+        int *flags = nullptr;
+        int mine = (m->ds_ok && m->comm.p2p) ? 1 : 0;
+        std::vector<int> all(tp_size, 0);
+        if (cudaMalloc(&flags, sizeof(int) * (tp_size + 1)) != cudaSuccess) return fail(set_error(SB_ERR_OOM, "flags"));
+        rc = SB_OK;
+        if (cudaMemcpyAsync(flags + tp_size, &mine, sizeof(int), cudaMemcpyHostToDevice, m->st) != cudaSuccess)
+            rc = set_error(SB_ERR_CUDA, "sb_llama_create: flag upload failed");
+        if (rc == SB_OK) rc = tp_allgather32(m->comm, flags + tp_size, flags, 1, m->st);
+        if (rc == SB_OK && (cudaMemcpyAsync(all.data(), flags, sizeof(int) * tp_size, cudaMemcpyDeviceToHost, m->st) !=
+                                cudaSuccess ||
+                            cudaStreamSynchronize(m->st) != cudaSuccess))
+            rc = set_error(SB_ERR_CUDA, "sb_llama_create: flag exchange failed");
+        cudaFree(flags);
+        if (rc != SB_OK) return fail(rc);
+        bool every = true;
+        for (int v : all) every = every && v == 1;
+        m->ds_ok = every;
+        if (every) {
+            uint2 *mapped[TP_MAX_RANKS] = {};
+            if ((rc = tp_share_cells(m->comm, (size_t)2 * tp_size * (m->h + 2), m->st, mapped)) != SB_OK)
+                return fail(rc);
         }
     }
     m->layers.resize(m->L);

@@ -74,6 +74,14 @@ size_t qgemv_smem_bytes(int M, int KS, int TN, bool norm);
 // qgemv_check_error() reports (and clears) a timed-out pipeline wait.
 int qgemv_check_error();
 int qgemv_launch(int epi, const QGemvArgs &a, cudaStream_t st, bool pdl);
+// Split-K GEMV (qgemv_sk.cu) for 1-4 rows of a per-tensor weight with
+// 128-column tiles and fewer tiles than SMs (STORE / BIAS epilogues): CTA
+// (tile, k range), exact int64 sums in a workspace of qgemv_splitk_ws_bytes
+// (zero before the first call; every call leaves it zero), the last split of
+// a tile applies the epilogue.  Bit-identical to qgemv_launch.
+bool qgemv_splitk_wanted(const QWeightDesc &w, int M);
+size_t qgemv_splitk_ws_bytes(const QWeightDesc &w, int M);
+int qgemv_splitk_launch(int epi, const QGemvArgs &a, void *ws, cudaStream_t st);
 
 // Permute a device [K,N] int8 matrix into the packed layout.  With
 // pair_F > 0 the source is two [K,F] matrices (gate then up, concatenated

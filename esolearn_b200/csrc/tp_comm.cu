@@ -98,18 +98,6 @@ int enqueued(const TpComm &c, ncclResult_t r, const char *what) {
     return nccl_fail(what, r);
 }
 
-// A cell is one aligned 64-bit word (epoch << 32 | value bits): scalar 64-bit
-// accesses are single-copy atomic, so a reader sees a value only together
-// with the epoch it was written for.
-__device__ __forceinline__ void st_cell(uint2 *p, float v, unsigned e) {
-    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ uint2 ld_cell(const uint2 *p) {
-    unsigned long long w;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return make_uint2((unsigned)w, (unsigned)(w >> 32));
-}
 
 __global__ void __launch_bounds__(256) tp_ar_kernel(float *x, int n, TpPeers P, int rank, int T) {
     pdl_launch_dependents();
@@ -163,21 +151,15 @@ __global__ void __launch_bounds__(256) tp_ar_kernel(float *x, int n, TpPeers P, 
 
 }  // namespace
 
-int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st) {
+namespace {
+// Every rank's `local` buffer mapped into this process over CUDA IPC
+// (handles exchanged with an NCCL all-gather): mapped[r] is rank r's buffer
+// (mapped[rank] = local).  *ok = false, with nothing left open, when some
+// peer's memory cannot be mapped.
+int share_buffer(const TpComm &c, void *local, cudaStream_t st, void **mapped, bool *ok) {
     const int T = c.size;
-    SB_CHECK(T >= 2 && T <= TP_MAX_RANKS, SB_ERR_ARG, "peer all-reduce: %d ranks", T);
-    uint2 *recv = nullptr;
-    unsigned *misc = nullptr;
-    const size_t rbytes = sizeof(uint2) * 2 * (size_t)T * cap;
-    SB_CUDA_TRY(cudaMalloc(&recv, rbytes));
-    c.own[0] = recv;
-    SB_CUDA_TRY(cudaMalloc(&misc, sizeof(unsigned) * (TP_AR_CTAS + 1)));
-    c.own[1] = misc;
-    SB_CUDA_TRY(cudaMemsetAsync(recv, 0, rbytes, st));  // epoch 0: no call has written yet
-    SB_CUDA_TRY(cudaMemsetAsync(misc, 0, sizeof(unsigned) * (TP_AR_CTAS + 1), st));
-    // exchange the IPC handles through the communicator
     cudaIpcMemHandle_t mine;
-    SB_CUDA_TRY(cudaIpcGetMemHandle(&mine, recv));
+    SB_CUDA_TRY(cudaIpcGetMemHandle(&mine, local));
     const size_t hb = sizeof mine;
     static_assert(sizeof(mine) % 4 == 0, "handles are gathered as 32-bit words");
     uint8_t *dev = nullptr;
@@ -193,31 +175,63 @@ int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st) {
         rc = set_error(SB_ERR_CUDA, "peer all-reduce: handle exchange failed");
     cudaFree(dev);
     SB_TRY(rc);
+    *ok = true;
+    for (int r = 0; r < T; r++) mapped[r] = r == c.rank ? local : nullptr;
+    for (int r = 0; r < T && *ok; r++) {
+        if (r == c.rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + hb * r, hb);
+        if (cudaIpcOpenMemHandle(&mapped[r], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            mapped[r] = nullptr;
+            *ok = false;  // no peer access between these GPUs
+        }
+    }
+    if (!*ok)
+        for (int r = 0; r < T; r++)
+            if (r != c.rank && mapped[r]) cudaIpcCloseMemHandle(mapped[r]), mapped[r] = nullptr;
+    return SB_OK;
+}
+}  // namespace
+
+int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st) {
+    const int T = c.size;
+    SB_CHECK(T >= 2 && T <= TP_MAX_RANKS, SB_ERR_ARG, "peer all-reduce: %d ranks", T);
+    uint2 *recv = nullptr;
+    unsigned *misc = nullptr;
+    const size_t rbytes = sizeof(uint2) * 2 * (size_t)T * cap;
+    SB_CUDA_TRY(cudaMalloc(&recv, rbytes));
+    c.own[0] = recv;
+    SB_CUDA_TRY(cudaMalloc(&misc, sizeof(unsigned) * (TP_AR_CTAS + 1)));
+    c.own[1] = misc;
+    SB_CUDA_TRY(cudaMemsetAsync(recv, 0, rbytes, st));  // epoch 0: no call has written yet
+    SB_CUDA_TRY(cudaMemsetAsync(misc, 0, sizeof(unsigned) * (TP_AR_CTAS + 1), st));
+    void *mapped[TP_MAX_RANKS] = {};
+    bool ok = false;
+    SB_TRY(share_buffer(c, recv, st, mapped, &ok));
     TpPeers P;
     P.cap = cap;
     P.epoch = misc;
     P.error = misc + TP_AR_CTAS;
-    bool ok = true;
-    for (int r = 0; r < T && ok; r++) {
-        if (r == c.rank) {
-            P.recv[r] = recv;
-            continue;
-        }
-        cudaIpcMemHandle_t h;
-        std::memcpy(&h, all.data() + hb * r, hb);
-        void *pr = nullptr;
-        if (cudaIpcOpenMemHandle(&pr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-            cudaGetLastError();
-            ok = false;  // no peer access between these GPUs: NCCL carries the sums
-            break;
-        }
-        P.recv[r] = static_cast<uint2 *>(pr);
-    }
+    for (int r = 0; r < T; r++) P.recv[r] = static_cast<uint2 *>(mapped[r]);
     c.peers = P;
-    c.p2p = ok;
-    if (!ok)
-        for (int r = 0; r < T; r++)
-            if (r != c.rank && P.recv[r]) cudaIpcCloseMemHandle(P.recv[r]);
+    c.p2p = ok;  // without peer access NCCL carries the sums
+    return SB_OK;
+}
+
+int tp_share_cells(TpComm &c, size_t cells, cudaStream_t st, uint2 **mapped) {
+    SB_CHECK(c.size >= 2 && c.size <= TP_MAX_RANKS && c.p2p, SB_ERR_UNSUPPORTED,
+             "shared cells: needs peer access between %d ranks", c.size);
+    SB_CHECK(!c.own[2], SB_ERR_STATE, "shared cells: already set up");
+    void *buf = nullptr;
+    SB_CUDA_TRY(cudaMalloc(&buf, sizeof(uint2) * cells));
+    c.own[2] = buf;
+    SB_CUDA_TRY(cudaMemsetAsync(buf, 0, sizeof(uint2) * cells, st));  // epoch 0: nothing written yet
+    void *m[TP_MAX_RANKS] = {};
+    bool ok = false;
+    SB_TRY(share_buffer(c, buf, st, m, &ok));
+    SB_CHECK(ok, SB_ERR_UNSUPPORTED, "shared cells: a peer's memory cannot be mapped");
+    for (int r = 0; r < c.size; r++) c.cells[r] = mapped[r] = static_cast<uint2 *>(m[r]);
     return SB_OK;
 }
 
@@ -309,6 +323,9 @@ void tp_destroy(TpComm &c) {
     if (c.p2p)
         for (int r = 0; r < c.size; r++)
             if (r != c.rank) cudaIpcCloseMemHandle(c.peers.recv[r]);
+    for (int r = 0; r < c.size; r++)
+        if (r != c.rank && c.cells[r]) cudaIpcCloseMemHandle(c.cells[r]);
+    for (uint2 *&p : c.cells) p = nullptr;
     c.p2p = false;
     for (void *&p : c.own)
         if (p) cudaFree(p), p = nullptr;

@@ -33,8 +33,26 @@ struct TpComm {
     int rank = 0, size = 1;
     TpPeers peers;
     bool p2p = false;                    // peer all-reduce usable
-    void *own[2] = {};                   // local allocations (recv, epoch+error)
+    void *own[3] = {};                   // local allocations (recv, epoch+error, shared cells)
+    uint2 *cells[TP_MAX_RANKS] = {};     // tp_share_cells: rank r's cells, mapped here
 };
+
+// A cell is one aligned 64-bit word (epoch << 32 | value bits): scalar 64-bit
+// accesses are single-copy atomic, so a reader sees a value only together
+// with the epoch it was written for.
+__device__ __forceinline__ void st_cell(uint2 *p, float v, unsigned e) {
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void st_cell_u(uint2 *p, unsigned v, unsigned e) {
+    const unsigned long long w = ((unsigned long long)e << 32) | v;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint2 ld_cell(const uint2 *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return make_uint2((unsigned)w, (unsigned)(w >> 32));
+}
 
 // Fresh unique id for a new communicator (rank 0 makes it, the caller sends
 // it to the other ranks).
@@ -50,6 +68,10 @@ int tp_allreduce_f32(const TpComm &c, float *buf, size_t count, cudaStream_t st)
 // process over CUDA IPC (handles exchanged with an NCCL all-gather).  Leaves
 // p2p off (NCCL only) when the GPUs cannot reach each other's memory.
 int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st);
+// `cells` zeroed 8-byte cells in this rank's memory, mapped into every rank:
+// afterwards c.cells[r] (= mapped[r]) is rank r's array.  Needs peer access
+// (tp_setup_p2p found it); SB_ERR_UNSUPPORTED otherwise.  Once per comm.
+int tp_share_cells(TpComm &c, size_t cells, cudaStream_t st, uint2 **mapped);
 // Reports (and clears) a timed-out flag wait of the peer all-reduce.
 int tp_check_error(const TpComm &c);
 // Runs the peer all-reduce against a peer that never writes (one device);

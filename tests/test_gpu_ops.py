@@ -122,6 +122,38 @@ def test_matmul_beyond_64_rows_runs_in_tensor_core_chunks(M, K, N_, bf16):
     assert rel_err(out, O.matmul_i8_f32(a, q, s, M, K, N_)) < TOL_F32
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("K,N_,bf16,bias", [(4096, 4096, True, False), (11008, 4096, True, False),
+                                             (4096, 11008, False, True), (1000, 640, False, False),
+                                             (4096, 32000, True, True)])
+def test_split_k_gemv_equals_one_cta_per_tile_gemv(M, K, N_, bf16, bias):
+    # 1-4 rows of a 128-column-tile weight with fewer tiles than SMs take the
+    # split-K GEMV (CTA per (tile, k range), int64 sums, the tile's last split
+    # applies the epilogue); its output must equal bit for bit the one-CTA-per-
+    # tile GEMV on the same int8 values (a narrower tiling, below), and the
+    # oracle within the GEMV bar.  4096 x 32000 (250 tiles) stays on the plain
+    # GEMV.  K = 1000 ends in a partial k-step.
+    rng = np.random.default_rng(M + K + N_)
+    q = rng.integers(-127, 128, (K, N_), dtype=np.int8)
+    s = np.float32(1.3e-4)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    if bf16:
+        xt = torch.from_numpy(x).to(torch.bfloat16)
+        x = xt.float().numpy()
+        xd = xt.cuda()
+    else:
+        xd = dev(x)
+    b = rng.standard_normal(N_).astype(np.float32) if bias else None
+    ref = O.matmul_i8_f32(x, q, s, M, K, N_) + (b[None, :] if bias else 0)
+    wide = QWeight(q, s, tile_n=128)
+    narrow = QWeight(q, s, tile_n=16)
+    kw = {"bias": dev(b)} if bias else {}
+    out = matmul_i8_f32(xd, wide, **kw).cpu().numpy()
+    assert np.array_equal(out, matmul_i8_f32(xd, narrow, **kw).cpu().numpy())
+    assert np.array_equal(out, matmul_i8_f32(xd, wide, **kw).cpu().numpy())  # the workspace was left clean
+    assert rel_err(out, ref) < TOL_GEMV
+
+
 @pytest.mark.parametrize("group", [32, 64])
 @pytest.mark.parametrize("M", [1, 4, 8, 32, 128])
 @pytest.mark.parametrize("K,N_", [(4096, 4096), (11008, 4096), (4096, 11008), (4096, 32000)])
