@@ -132,8 +132,10 @@ def test_row_and_column_splits_over_gloo_ranks():
 # ---------------------------------------------------------------------------
 # the NCCL tensor-parallel engine on 2 GPUs
 
-def _tp_config():
-    # GQA 8 query / 4 kv heads, head_dim 64
+def _tp_config(size=2):
+    # GQA 8 query / 4 kv heads, head_dim 64; 16 / 8 heads for 8 ranks (one kv head each)
+    if size > 4:
+        return small_config(h=1024, layers=2, heads=16, kv=8, ffn=1024, vocab=1024)
     return small_config(h=512, layers=2, heads=8, kv=4, ffn=512, vocab=1024)
 
 
@@ -178,12 +180,12 @@ def _tp_engine_run(rank, size, tid, mode):
         e.close()
         return rank, outs, None, None
     if mode == "oracle":
-        c = _tp_config()
+        c = _tp_config(size)
         om = O.OracleLlama(orc_config(c, 128), 5)
         e = engine_from_oracle(om, c, max_seq=128, max_batch=4, kv_dtype="bf16", tp_rank=rank, tp_size=size,
                                tp_id=tid)
     else:  # on-device random init, checked shard by shard against the oracle's generator
-        c = _tp_config()
+        c = _tp_config(size)
         e = QuantLlamaB200.new_random(c, 3, max_seq=128, max_batch=4, kv_dtype="bf16", tp_rank=rank, tp_size=size,
                                       tp_id=tid)
         om = O.OracleLlama(orc_config(c, 128), 3)
@@ -206,12 +208,13 @@ def _tp_engine_run(rank, size, tid, mode):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("size", [2, 4])
+@pytest.mark.parametrize("size", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["oracle", "random"])
 def test_tensor_parallel_engine_matches_oracle(mode, size):
-    # 2 or 4 ranks (NCCL over NVLink, peer-memory all-reduce): greedy streams
-    # for 1 and 3 sequences equal the unsharded oracle's for 32 tokens,
-    # logits within the f32 bar, on every rank.
+    # 2, 4 or 8 ranks (NCCL over NVLink, peer-memory exchanges): greedy
+    # streams for 1 sequence (the persistent step, exchanging inside the
+    # kernel) and 3 sequences (per-operation kernels) equal the unsharded
+    # oracle's for 32 tokens, logits within the f32 bar, on every rank.
     import torch
     import torch.multiprocessing as mp
 
@@ -238,7 +241,7 @@ def test_tensor_parallel_engine_matches_oracle(mode, size):
         for p in procs:  # a rank left waiting on a failed peer ends with the test
             if p.is_alive():
                 p.kill()
-    c = _tp_config()
+    c = _tp_config(size)
     om = O.OracleLlama(orc_config(c, 128), 5 if mode == "oracle" else 3)
     prompt = O.prompt_ids(11, 8, c.vocab_size)
     ref1 = om.generate_greedy(prompt, 32, kv_bf16=True)
