@@ -45,14 +45,26 @@ def main(argv=None):
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--timeline", action="store_true", help="per-phase timeline of the last persistent step")
     ap.add_argument("--timeline-out", default=None, help="also save the raw stamps [phases, ctas, 5] (.npy)")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="instead of decode steps: prefill one prompt of this many seeded tokens (chunks of --batch)")
     args = ap.parse_args(argv)
 
     cfg = getattr(LlamaConfig, args.shape)()
     if args.layers:
         cfg = dataclasses.replace(cfg, n_layers=args.layers)
     N.check(N.lib().sb_init(args.device))
-    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=args.ctx + args.steps + 8, max_batch=args.batch)
+    max_seq = max(args.ctx + args.steps, args.prefill) + 8
+    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=args.batch)
     B = args.batch
+    if args.prefill:
+        import numpy as np
+
+        prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, args.prefill)).astype(np.int32)
+        t0 = time.perf_counter()
+        model.prefill(prompt)
+        print(json.dumps({"shape": args.shape, "layers": cfg.n_layers, "prefill": args.prefill, "chunk": B,
+                          "host_ms": (time.perf_counter() - t0) * 1e3}))
+        return
     if args.timeline:
         model.set_timeline(True)
     times = []
