@@ -279,24 +279,31 @@ __device__ __noinline__ bool ds_in_resid_tp(const float *x_src, const uint2 *cel
                 if (norm) wb[jj] = __ldg(reinterpret_cast<const float4 *>(norm + k0));
             }
         }
-        // cells of two quads of one rank per round trip (register budget)
-        for (int r = 0; r < T; r++) {
+        // cells of two quads of two ranks per round trip (register budget);
+        // the ranks' values are still added in rank order
 #pragma unroll
-            for (int jp = 0; jp < 4; jp += 2) {
-                uint2 c[2][4];
+        for (int jp = 0; jp < 4; jp += 2) {
+            for (int r0 = 0; r0 < T; r0 += 2) {
+                const int nr = min(2, T - r0);
+                uint2 c[2][2][4];
 #pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+                for (int rr = 0; rr < 2; rr++)
 #pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        c[u][q] = k0 < K ? ld_cell(cells + (size_t)r * ld + k0 + q) : make_uint2(0u, e);
-                }
+                    for (int u = 0; u < 2; u++) {
+                        const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+#pragma unroll
+                        for (int q = 0; q < 4; q++)
+                            c[rr][u][q] = (rr < nr && k0 < K) ? ld_cell(cells + (size_t)(r0 + rr) * ld + k0 + q)
+                                                              : make_uint2(0u, e);
+                    }
                 for (;;) {
                     bool all = true;
 #pragma unroll
-                    for (int u = 0; u < 2; u++)
+                    for (int rr = 0; rr < 2; rr++)
 #pragma unroll
-                        for (int q = 0; q < 4; q++) all = all && c[u][q].y == e;
+                        for (int u = 0; u < 2; u++)
+#pragma unroll
+                            for (int q = 0; q < 4; q++) all = all && c[rr][u][q].y == e;
                     if (all || !ok) break;
                     if ((spins++ & 63) == 0) {
                         const uint64_t t = global_ns();
@@ -304,20 +311,26 @@ __device__ __noinline__ bool ds_in_resid_tp(const float *x_src, const uint2 *cel
                         else if (t - t0 > SB_WAIT_NS) ok = false;
                     }
 #pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+                    for (int rr = 0; rr < 2; rr++)
 #pragma unroll
-                        for (int q = 0; q < 4; q++)
-                            if (c[u][q].y != e) c[u][q] = ld_cell(cells + (size_t)r * ld + k0 + q);
-                    }
+                        for (int u = 0; u < 2; u++) {
+                            const int k0 = (tid + (j0 + jp + u) * DS_CONSUMERS) * 4;
+#pragma unroll
+                            for (int q = 0; q < 4; q++)
+                                if (c[rr][u][q].y != e) c[rr][u][q] = ld_cell(cells + (size_t)(r0 + rr) * ld + k0 + q);
+                        }
                 }
 #pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    float4 &x = xb[jp + u];
-                    x.x = __fadd_rn(x.x, __uint_as_float(c[u][0].x));
-                    x.y = __fadd_rn(x.y, __uint_as_float(c[u][1].x));
-                    x.z = __fadd_rn(x.z, __uint_as_float(c[u][2].x));
-                    x.w = __fadd_rn(x.w, __uint_as_float(c[u][3].x));
+                for (int rr = 0; rr < 2; rr++) {
+                    if (rr >= nr) break;
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        float4 &x = xb[jp + u];
+                        x.x = __fadd_rn(x.x, __uint_as_float(c[rr][u][0].x));
+                        x.y = __fadd_rn(x.y, __uint_as_float(c[rr][u][1].x));
+                        x.z = __fadd_rn(x.z, __uint_as_float(c[rr][u][2].x));
+                        x.w = __fadd_rn(x.w, __uint_as_float(c[rr][u][3].x));
+                    }
                 }
             }
         }
