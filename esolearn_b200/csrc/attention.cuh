@@ -28,6 +28,20 @@ struct AttnArgs {
     int tma = 0;
     long long tm_row0 = 0;
     CUtensorMap tmk, tmv;
+    // Tensor-map path with one split: the q|k|v projection's epilogue done
+    // here instead of in its own kernel.  q, k and v of row b come from the
+    // GEMM's exact int64 column sums qkv_sums[b * ld_sums + n] (cleared after
+    // use), y = sum * 2^-shift[b] * qkv_scale * rstd[b]; RoPE from the
+    // rope_cos / rope_sin rows of the position, q scaled by q_scale; the new
+    // K/V row is written to the cache at position len[b] (when 0 <= it <
+    // max_pos) before the tile holding it is loaded.
+    const long long *qkv_sums = nullptr;
+    int ld_sums = 0;
+    const int *shift = nullptr;
+    const double *rstd = nullptr;
+    float qkv_scale = 0.f, q_scale = 1.f;
+    const float *rope_cos = nullptr, *rope_sin = nullptr;
+    int max_pos = 0;
 };
 
 // Causal attention of a prefill chunk (attention_prefill.cu): rows 0..M-1

@@ -357,7 +357,81 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// ---- the q|k|v epilogue fused into the tensor-map kernel (one split) -------
+// Producer warp: the new K and V rows of kv head g for sequence b, from the
+// projection's int64 sums (RoPE on K, rope_with_freqs_preloaded, cpu.rs:
+// 650-661), written as bf16 to the cache at position pos when 0 <= pos <
+// max_pos; their sums are cleared either way.  The stores are then made
+// visible to the async proxy, so a tensor-map load issued after this sees them.
+template <int HD>
+__device__ __forceinline__ void atm_new_kv(const AttnArgs &a, int b, int g, int pos) {
+    const int lane = threadIdx.x & 31;
+    const double f = gemv_factor(a.shift[b], a.qkv_scale, a.rstd[b]);
+    long long *ks = const_cast<long long *>(a.qkv_sums) + (size_t)b * a.ld_sums + (size_t)a.n_heads * HD +
+                    (size_t)g * HD;
+    long long *vs = ks + (size_t)a.n_kv * HD;
+    const bool live = pos >= 0 && pos < a.max_pos;
+    size_t row = 0;
+    if (live) {
+        const int page = a.page_table[(size_t)b * a.max_pages + pos / a.page_size];
+        row = (((size_t)page * a.n_kv + g) * a.page_size + pos % a.page_size) * HD;
+    }
+    __nv_bfloat16 *kc = reinterpret_cast<__nv_bfloat16 *>(const_cast<void *>(a.kc)) + row;
+    __nv_bfloat16 *vc = reinterpret_cast<__nv_bfloat16 *>(const_cast<void *>(a.vc)) + row;
+    for (int d0 = 2 * lane; d0 < HD; d0 += 64) {
+        const long long t0 = __ldcg(ks + d0), t1 = __ldcg(ks + d0 + 1);
+        const long long u0 = __ldcg(vs + d0), u1 = __ldcg(vs + d0 + 1);
+        ks[d0] = 0, ks[d0 + 1] = 0, vs[d0] = 0, vs[d0 + 1] = 0;
+        if (live) {
+            const float y0 = gemv_out(t0, f), y1 = gemv_out(t1, f);
+            const float cs = a.rope_cos[(size_t)pos * (HD / 2) + (d0 >> 1)];
+            const float sn = a.rope_sin[(size_t)pos * (HD / 2) + (d0 >> 1)];
+            kc[d0] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn)));
+            kc[d0 + 1] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs)));
+            vc[d0] = __float2bfloat16_rn(gemv_out(u0, f));
+            vc[d0 + 1] = __float2bfloat16_rn(gemv_out(u1, f));
+        }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+}
+
+// Consumer lanes: the query fragments of head g * REP + grp (as atc_load_q)
+// from the projection's sums: y = sum * factor, RoPE at the position, times
+// q_scale (the projection epilogue's arithmetic, qgemm.cu QEPI_QKV).
 template <int HD, int REP>
+__device__ __forceinline__ void atm_load_q_sums(const AttnArgs &a, int b, int g, int grp, int qd, int pos,
+                                                uint32_t (&qa)[HD / 16][4]) {
+    const bool live = grp < REP;
+    const double f = gemv_factor(a.shift[b], a.qkv_scale, a.rstd[b]);
+    const long long *qs = a.qkv_sums + (size_t)b * a.ld_sums + ((size_t)g * REP + grp) * HD;
+    const int rp = min(max(pos, 0), a.max_pos - 1);  // outside the cache the output is unused
+    const float *cr = a.rope_cos + (size_t)rp * (HD / 2), *sr = a.rope_sin + (size_t)rp * (HD / 2);
+#pragma unroll
+    for (int k = 0; k < HD / 16; k++) {
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+#pragma unroll
+            for (int hlf = 0; hlf < 2; hlf++) {
+                const int d0 = k * 16 + 8 * hlf + 2 * qd;
+                const float y0 = gemv_out(__ldcg(qs + d0), f), y1 = gemv_out(__ldcg(qs + d0 + 1), f);
+                const float cs = cr[d0 >> 1], sn = sr[d0 >> 1];
+                x[2 * hlf] = __fmul_rn(__fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn)), a.q_scale);
+                x[2 * hlf + 1] = __fmul_rn(__fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs)), a.q_scale);
+            }
+        }
+        __nv_bfloat16 h[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) split_bf16(x[i], h[i], l[i]);
+        qa[k][0] = pack_bf16(h[0], h[1]);
+        qa[k][1] = pack_bf16(l[0], l[1]);
+        qa[k][2] = pack_bf16(h[2], h[3]);
+        qa[k][3] = pack_bf16(l[2], l[3]);
+    }
+}
+
+// FUSED: the q|k|v projection's epilogue runs here (a.qkv_sums; one split).
+template <int HD, int REP, bool FUSED>
 __global__ void __launch_bounds__(ATC_THREADS + 32) attn_tc_tma_kernel(const __grid_constant__ AttnArgs a) {
     static_assert(REP == 2 || REP == 4 || REP == 8, "tensor-core attention takes 2, 4 or 8 heads per group");
     static_assert(HD % 64 == 0, "head_dim is whole 64-element boxes");
@@ -397,40 +471,66 @@ __global__ void __launch_bounds__(ATC_THREADS + 32) attn_tc_tma_kernel(const __g
     const int ntiles = (p1 - p0 + ATC_T - 1) / ATC_T;
 
     if (warp == ATC_WARPS) {
-        // ---- producer: one elected lane issues every tile's boxes
+        // ---- producer: one elected lane issues every tile's boxes; with
+        // FUSED the whole warp writes the new K/V row before the tile that
+        // holds it is requested (ahead of tile min(its tile, NST - 1): writing
+        // it once the ring is full instead measured slower)
+        const int pos = FUSED ? a.len[b] : -1;
+        const int t_row = (FUSED && pos >= p0 && pos < p1) ? min((pos - p0) / ATC_T, ATM_NST - 1) : -1;
+        bool row_done = false;
+        const uint64_t pol = l2_evict_first_policy();  // every row is read once per step
+        const int *ptab = a.page_table + (size_t)b * a.max_pages;
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.tmk)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.tmv)) : "memory");
-            const uint64_t pol = l2_evict_first_policy();  // every row is read once per step
-            const int *ptab = a.page_table + (size_t)b * a.max_pages;
-            int t = 0;
-            for (; t < ntiles; t++) {
-                const int st = t % ATM_NST;
+        }
+        int t = 0;
+        for (; t < ntiles; t++) {
+            if (FUSED && t == t_row) {
+                atm_new_kv<HD>(a, b, g, pos);
+                row_done = true;
+            }
+            const int st = t % ATM_NST;
+            int stop = 0;
+            if (lane == 0) {
                 if (t >= ATM_NST && (s_abort || !mbar_wait(b_empty + 8 * st, ((t / ATM_NST) - 1) & 1))) {
                     atomicOr(&atc_error_flag, 1u);
                     s_abort = 1;
-                    break;
-                }
-                const int p = p0 + t * ATC_T;
-                const int pg = ptab[p / a.page_size], slot = p % a.page_size;
-                const int row = (int)(a.tm_row0 + ((long long)pg * a.n_kv + g) * a.page_size + slot);
-                const uint32_t kdst = sbase + (uint32_t)st * atm_stage_bytes<HD>();
-                mbar_expect_tx(b_full + 8 * st, 2 * KVB);
+                    stop = 1;
+                } else {
+                    const int p = p0 + t * ATC_T;
+                    const int pg = ptab[p / a.page_size], slot = p % a.page_size;
+                    const int row = (int)(a.tm_row0 + ((long long)pg * a.n_kv + g) * a.page_size + slot);
+                    const uint32_t kdst = sbase + (uint32_t)st * atm_stage_bytes<HD>();
+                    mbar_expect_tx(b_full + 8 * st, 2 * KVB);
 #pragma unroll
-                for (int bx = 0; bx < NBOX; bx++) {
-                    tma_load_2d(kdst + bx * ATM_BOX, &a.tmk, 64 * bx, row, b_full + 8 * st, pol);
-                    tma_load_2d(kdst + KVB + bx * ATM_BOX, &a.tmv, 64 * bx, row, b_full + 8 * st, pol);
+                    for (int bx = 0; bx < NBOX; bx++) {
+                        tma_load_2d(kdst + bx * ATM_BOX, &a.tmk, 64 * bx, row, b_full + 8 * st, pol);
+                        tma_load_2d(kdst + KVB + bx * ATM_BOX, &a.tmv, 64 * bx, row, b_full + 8 * st, pol);
+                    }
                 }
             }
-            // leave no copy in flight: the last stages issued have landed
+            if (__shfl_sync(0xffffffffu, stop, 0)) break;
+        }
+        if (FUSED && !row_done) atm_new_kv<HD>(a, b, g, pos);  // the sums are cleared in every case
+        // leave no copy in flight: the last stages issued have landed
+        if (lane == 0)
             for (int u = max(0, t - ATM_NST); u < t; u++)
                 if (!mbar_wait(b_full + 8 * (u % ATM_NST), (u / ATM_NST) & 1)) atomicOr(&atc_error_flag, 1u);
-        }
         return;  // the consumer warps combine and write
     }
 
     uint32_t qa[HD / 16][4];
-    atc_load_q<HD, REP>(a, b, g, grp, qd, qa);
+    if (FUSED) {
+        atm_load_q_sums<HD, REP>(a, b, g, grp, qd, a.len[b], qa);
+        consumer_sync();  // every consumer warp has its query; clear its sums
+        if (warp == 0) {
+            long long *qs = const_cast<long long *>(a.qkv_sums) + (size_t)b * a.ld_sums + (size_t)g * REP * HD;
+            for (int i = lane; i < REP * HD; i += 32) qs[i] = 0;
+        }
+    } else {
+        atc_load_q<HD, REP>(a, b, g, grp, qd, qa);
+    }
     float o[NB][4];
 #pragma unroll
     for (int j = 0; j < NB; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -465,11 +565,11 @@ __global__ void __launch_bounds__(ATC_THREADS + 32) attn_tc_tma_kernel(const __g
                         s_l, s_fm, s_fl, &s_last);
 }
 
-template <int HD, int REP>
-int atm_inst(const AttnArgs &a, cudaStream_t st, bool pdl) {
+template <int HD, int REP, bool FUSED>
+int atm_inst_k(const AttnArgs &a, cudaStream_t st, bool pdl) {
     constexpr size_t smem = atm_smem_bytes<HD>();
     static_assert((size_t)ATC_WARPS * REP * HD * 4 + 1024 <= smem, "combine buffer must fit the stages");
-    auto kern = attn_tc_tma_kernel<HD, REP>;
+    auto kern = attn_tc_tma_kernel<HD, REP, FUSED>;
     static int limit[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -478,6 +578,16 @@ int atm_inst(const AttnArgs &a, cudaStream_t st, bool pdl) {
              limit[dev & 63]);
     SB_CUDA_TRY(launch(kern, dim3(a.n_kv, a.n_splits, a.B), dim3(ATC_THREADS + 32), smem, st, pdl, a));
     return SB_OK;
+}
+
+template <int HD, int REP>
+int atm_inst(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    if (a.qkv_sums) {
+        SB_CHECK(a.n_splits == 1 && a.shift && a.rstd && a.rope_cos && a.rope_sin && a.max_pos > 0, SB_ERR_ARG,
+                 "attention: the fused q|k|v epilogue needs one split and the projection's scratch");
+        return atm_inst_k<HD, REP, true>(a, st, pdl);
+    }
+    return atm_inst_k<HD, REP, false>(a, st, pdl);
 }
 
 template <int HD>

@@ -287,8 +287,16 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
     // also writes the next linear's planes, one launch instead of two.
     const bool chain = M > QG_MAX_M && m->tp == 1;
     bool planes_ready = false;  // the previous link wrote this linear's planes
+    // With the tensor-map attention in one split, the q|k|v GEMM's epilogue
+    // (RoPE, q scale, the K/V row write) runs inside the attention kernel,
+    // which reads the GEMM's sums: one launch less per layer.
+    const bool fuse_qkv = M > QG_MAX_M && m->att_tma && tma_splits(m, M) == 1 && kind != STEP_PREFILL;
     auto linear = [&](int epi, const QGemvArgs &a, const float *next_norm) -> int {
-        if (!chain) return engine_linear(m, epi, a, st, pdl);
+        if (!chain) {
+            if (epi == QEPI_QKV && fuse_qkv)
+                return qgemm_launch_chained(epi, a, m->gws, st, pdl, true, nullptr, true);
+            return engine_linear(m, epi, a, st, pdl);
+        }
         const bool chained = epi == QEPI_RESID || epi == QEPI_SWIGLU;
         QGemmNext nx;
         nx.norm_w = next_norm;
@@ -296,7 +304,8 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
         nx.planes_bytes = qgemm_planes_bytes(std::max({m->h, m->F, m->q_dim}), m->B);
         const bool need = !planes_ready;
         planes_ready = chained;
-        return qgemm_launch_chained(epi, a, m->gws, st, pdl, need, chained ? &nx : nullptr);
+        return qgemm_launch_chained(epi, a, m->gws, st, pdl, need, chained ? &nx : nullptr,
+                                    epi == QEPI_QKV && fuse_qkv);
     };
     SB_PROF(prof, 2, embed_launch(m->embed, m->h, m->V, m->seq, M, m->x, st, pdl));
     for (int l = 0; l < m->L; l++) {
@@ -364,6 +373,17 @@ int enqueue_step(sb_llama *m, int M, cudaStream_t st, bool pdl, bool trace, Step
                 a.tmk = m->att_tmk;
                 a.tmv = m->att_tmv;
                 a.tm_row0 = (long long)l * (long long)(m->layer_kv_elems / m->hd);
+            }
+            if (fuse_qkv) {
+                a.qkv_sums = m->gws.acc;
+                a.ld_sums = m->gws.ld_acc;
+                a.shift = m->gws.shift;
+                a.rstd = m->gws.rstd;
+                a.qkv_scale = ly.qkv.scale;
+                a.q_scale = (float)(1.0 / std::sqrt((double)m->hd));  // llama.rs:394
+                a.rope_cos = m->rope_cos;
+                a.rope_sin = m->rope_sin;
+                a.max_pos = m->cfg.max_seq_len;
             }
             SB_PROF(prof, 1, attn_launch(a, st, pdl));
         }

@@ -1055,11 +1055,11 @@ int qgemm_check_error() {
 }
 
 int qgemm_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl) {
-    return qgemm_launch_chained(epi, a, ws, st, pdl, true, nullptr);
+    return qgemm_launch_chained(epi, a, ws, st, pdl, true, nullptr, false);
 }
 
 int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl, bool planes,
-                         const QGemmNext *next) {
+                         const QGemmNext *next, bool skip_finish) {
     SB_CHECK(qgemm_supported(a.w, a.M), SB_ERR_UNSUPPORTED, "qgemm: weight/rows not supported (TN %d, group %d, M %d)",
              a.w.TN, a.w.group, a.M);
     SB_CHECK(ws.planes && ws.acc && ws.shift && ws.rstd && ws.ld_acc >= a.w.ntiles * QGM_TN, SB_ERR_ARG,
@@ -1084,6 +1084,7 @@ int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStr
     const int G = std::max(1, std::min(device_props().sm_count, a.w.ntiles * upt / 2));
     SB_CUDA_TRY(launch(qgm_gemm_kernel, dim3(G), dim3(QGM_THREADS), (size_t)nst * qgm_slot_bytes(np), st, pdl, a.w, ws,
                        a.M, np, nst));
+    if (skip_finish) return SB_OK;  // the consumer of the sums finishes them (and clears them)
     if (next) {
         if (epi == QEPI_RESID)
             SB_CUDA_TRY(launch(qgm_finish_planes_kernel<QEPI_RESID>, dim3(QGF_CLUSTER, a.M), dim3(QGF_THREADS), 0, st,

@@ -45,8 +45,11 @@ struct QGemmNext {
 // each; epilogues RESID and SWIGLU, at most 32768 output features) that
 // also writes the next linear's planes, shift and rstd into ws, so the next
 // link runs with planes = false.
+// skip_finish: only the planes (if asked) and the GEMM; the caller's next
+// kernel consumes and clears the int64 sums (the attention's fused q|k|v
+// epilogue).
 int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStream_t st, bool pdl, bool planes,
-                         const QGemmNext *next);
+                         const QGemmNext *next, bool skip_finish = false);
 // Group-scaled weights (g = 32 or 64) on the tensor cores, 5 to 32 rows per
 // launch: one TMEM accumulator per group, the group scales applied in f64 as
 // the groups are drained; per-(tile, piece) f64 partials in `part`
