@@ -15,6 +15,7 @@ before it captures the graph, so a profiler that should see decode steps at
     python -m esolearn_b200.profile_decode --ctx 584 --steps 2
     python -m esolearn_b200.profile_decode --shape llama3_8b_shape --batch 32 --layers 2 --ctx 2068
     python -m esolearn_b200.profile_decode --ctx 584 --steps 4 --timeline
+    torchrun --nproc-per-node 2 -m esolearn_b200.profile_decode --timeline   (tensor parallel, one rank per GPU)
 
 --timeline (batch 1, persistent step; needs the profiling build of the
 library, `SB_STEP_TIMELINE=1 python -m esolearn_b200.build --force`) records the step kernel's per-phase
@@ -52,9 +53,25 @@ def main(argv=None):
     cfg = getattr(LlamaConfig, args.shape)()
     if args.layers:
         cfg = dataclasses.replace(cfg, n_layers=args.layers)
+    # under torchrun: tensor parallelism over the ranks (one GPU each)
+    import os
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    tp_kw = {}
+    if world > 1:
+        import torch.distributed as dist
+
+        from .llama import tp_unique_id
+
+        args.device = int(os.environ.get("LOCAL_RANK", "0"))
+        dist.init_process_group("gloo")
+        obj = [tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp_kw = {"tp_rank": rank, "tp_size": world, "tp_id": obj[0]}
     N.check(N.lib().sb_init(args.device))
     max_seq = max(args.ctx + args.steps, args.prefill) + 8
-    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=args.batch)
+    model = QuantLlamaB200.new_random(cfg, seed=0, max_seq=max_seq, max_batch=args.batch, **tp_kw)
     B = args.batch
     if args.prefill:
         import numpy as np
@@ -73,15 +90,20 @@ def main(argv=None):
         model.forward_batch([1] * B, [args.ctx + i] * B, want_logits=False)
         times.append((time.perf_counter() - t0) * 1e3)
     out = {"shape": args.shape, "layers": cfg.n_layers, "batch": B, "ctx": args.ctx, "steps": args.steps,
-           "launches_per_step": model.step_launches(B), "host_ms_per_call": times}
+           "tp": world, "rank": rank, "launches_per_step": model.step_launches(B), "host_ms_per_call": times}
     if args.timeline:
         ts = model.timeline()
         out["timeline_us"] = timeline_summary(ts, cfg.n_layers)
         if args.timeline_out:
             import numpy as np
 
-            np.save(args.timeline_out, ts)
+            np.save(args.timeline_out if world == 1 else f"{args.timeline_out}.rank{rank}.npy", ts)
     print(json.dumps(out))
+    if world > 1:
+        model.close()
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 PHASES = ("qkv", "attention", "o", "gate_up", "swiglu", "down")
