@@ -1672,13 +1672,19 @@ sb_status sb_llama_step_launches(sb_llama *m, int batch, int *launches) {
     SB_CHECK(batch >= 1 && batch <= m->B, SB_ERR_SHAPE, "batch %d outside 1..%d", batch, m->B);
     if (batch == 1 && m->ds_ok)
         *launches = 1;  // the persistent step kernel
-    else if (batch > QG_MAX_M && m->tp == 1)
-        // embed; per layer GEMM + finish for qkv (plus the planes in layer 0),
-        // attention, planes + GEMM + row finish for o, GEMM + row finish for
-        // gate/up and down; lm_head GEMM + finish; argmax
-        *launches = 5 + 10 * m->L;
-    else if (batch > QG_MAX_M)
-        *launches = 5 + 13 * m->L;  // embed, 4 linears x 3 + attention per layer, lm_head x 3, argmax
+    else if (batch > QG_MAX_M) {
+        // the q|k|v epilogue inside the one-split tensor-map attention
+        const bool fuse = m->att_tma && tma_splits(m, batch) == 1;
+        if (m->tp == 1)
+            // embed; per layer the q|k|v GEMM (+ its finish unless fused; the
+            // planes in layer 0), attention, o planes + GEMM + row finish,
+            // gate/up and down GEMM + row finish; lm_head GEMM + finish; argmax
+            *launches = fuse ? 5 + 9 * m->L : 5 + 10 * m->L;
+        else
+            // embed, 4 linears x 3 (q|k|v x 2 when fused) + attention per layer,
+            // lm_head x 3, argmax
+            *launches = fuse ? 5 + 12 * m->L : 5 + 13 * m->L;
+    }
     else
         *launches = 3 + 5 * m->L;  // embed, 5 per layer, lm_head, argmax
     return SB_OK;

@@ -212,3 +212,27 @@ def test_seven_b_head_layout_prefill_attention(max_batch, n_prompt):
     for j in (0, 9, 15):
         lg, _ = _rewound_logits(e, prompt[None, :], got[None, :], [j])
         assert rel_err(lg[0], ref_logits[0][j]) < TOL, j
+
+
+def test_one_split_attention_with_fused_projection_epilogue():
+    # 32 sequences x 8 kv heads fill the GPU with one context split each, so
+    # the batched step runs the tensor-map attention with the q|k|v
+    # projection's epilogue inside it (q, RoPE and the new K/V row from the
+    # GEMM's int64 sums): 9 launches per layer.  Greedy streams (near-tie
+    # rule) and rewound logits against the oracle.
+    cfg = small_config(h=1024, heads=16, kv=8, layers=2, ffn=512, vocab=1024, theta=500000.0)
+    B, n_prompt, n_gen, max_seq = 32, 70, 16, 128
+    om = O.OracleLlama(orc_config(cfg, max_seq), 41)
+    e = engine_from_oracle(om, cfg, max_seq=max_seq, max_batch=B, kv_dtype="bf16")
+    splits, tmap, _ = e.attn_plan(B)
+    assert tmap and splits == 1, splits
+    assert e.step_launches(B) == 5 + 9 * cfg.n_layers
+    prompts = np.stack([O.prompt_ids(7000 + b, n_prompt, cfg.vocab_size) for b in range(B)])
+    got = e.generate_greedy(prompts, n_gen, batched_prefill=True)
+    ref, ref_logits = _streams(om, np.zeros(0, np.int32), prompts, n_gen, max_seq)
+    agree = [greedy_agreement(got[b], ref[b], ref_logits[b], TOL) for b in range(B)]
+    assert sum(a == n_gen for a in agree) >= B - 2, agree
+    steps = [min((5 * b + 3) % n_gen, agree[b]) for b in range(B)]
+    lg, _ = _rewound_logits(e, prompts, got, steps)
+    for b in range(B):
+        assert rel_err(lg[b], ref_logits[b][steps[b]]) < TOL, (b, steps[b])
