@@ -332,7 +332,9 @@ def measure_decode(wl_name: str, B: int, prompt: int, K: int, W: int, rank: int,
             tt = torch.tensor([e2e_s], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e2e_s = float(tt.item())
-        e2e = {"value": n_jobs * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+        # batch 1 (the persistent step): token and position travel as launch
+        # arguments; batches: token, position and prompt length copied per row
+        e2e = {"value": n_jobs * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 if B == 1 else 12 * B,
                "d2h_bytes_per_step": 4 * B, "steps": K,
                "api": "sb_llama_forward (token, position in; argmax out; stream-synchronous)"}
     model.close()

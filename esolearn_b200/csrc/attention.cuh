@@ -62,6 +62,8 @@ struct PrefillAttnArgs {
 bool attn_prefill_supported(int hd, int kv_f32);
 int attn_prefill_launch(const PrefillAttnArgs &a, cudaStream_t st, bool pdl);
 
+// Queues a copy of the tensor-map kernel's error word into *host (pinned) on st.
+int attn_tc_error_peek(unsigned *host, cudaStream_t st);
 // Reports (and clears) a timed-out wait of the tensor-map kernel.
 int attn_tc_check_error();
 // Encode a [rows][hd] bf16 tensor map over a KV cache for the tensor-map path.

@@ -632,6 +632,11 @@ bool attn_tc_supported(const AttnArgs &a) {
     return !a.kv_f32 && (a.hd == 64 || a.hd == 128) && (rep == 2 || rep == 4 || rep == 8);
 }
 
+int attn_tc_error_peek(unsigned *host, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemcpyFromSymbolAsync(host, atc_error_flag, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, st));
+    return SB_OK;
+}
+
 int attn_tc_check_error() {
     unsigned f = 0;
     SB_CUDA_TRY(cudaMemcpyFromSymbol(&f, atc_error_flag, sizeof f));

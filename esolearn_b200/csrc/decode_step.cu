@@ -103,6 +103,11 @@ int ds_launch(const DsArgs &a, int rep, cudaStream_t st) {
     return set_error(SB_ERR_UNSUPPORTED, "decode step: head_dim %d", a.hd);
 }
 
+int ds_error_peek(const unsigned *sync_dev, unsigned *host, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemcpyAsync(host, sync_dev + 2, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    return SB_OK;
+}
+
 int ds_check_error(unsigned *sync_dev, cudaStream_t st) {
     unsigned f = 0;
     SB_CUDA_TRY(cudaMemcpyAsync(&f, sync_dev + 2, sizeof f, cudaMemcpyDeviceToHost, st));

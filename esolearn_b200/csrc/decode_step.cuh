@@ -88,6 +88,9 @@ struct DsArgs {
     float *trace = nullptr;     // [L][h] residual after each layer, or nullptr
     unsigned long long *stamps = nullptr;  // optional timeline [phases][grid][DS_STAMPS] (%globaltimer ns)
     int greedy = 1;  // 1: the last CTA records the argmax and advances the sequence; 0: a sampler follows
+    // >= 0: this step's token and position, given at launch (the host wrote no
+    // sequence state for it; the prompt is then empty); else read from seq
+    int tok_in = -1, pos_in = -1;
     // Tensor parallelism (tp > 1): shapes above are this rank's shard (heads,
     // ffn columns, vocabulary rows); the o and down partial products and the
     // argmax candidates travel through cells[r] = rank r's [2][tp][h + 2]
@@ -114,6 +117,9 @@ bool ds_timeline_built();
 size_t ds_part_floats(int nkv, int rep, int hd);
 int ds_mtab_bytes(int nh, int nkv);
 int ds_launch(const DsArgs &a, int rep, cudaStream_t st);
+// Queues a copy of the abort flag into *host (pinned) on st, for a check after the
+// caller's next synchronisation.
+int ds_error_peek(const unsigned *sync_dev, unsigned *host, cudaStream_t st);
 // Reads and clears the abort flag; SB_ERR_TIMEOUT when a bounded wait ran out.
 int ds_check_error(unsigned *sync_dev, cudaStream_t st);
 

@@ -827,7 +827,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     __syncthreads();
 
     // Step constants: the position decoded, the context and its KV chunks.
-    const int pos = a.seq.pos[0];
+    const int pos = a.pos_in >= 0 ? a.pos_in : a.seq.pos[0];
     const int cap = min(a.max_pos, a.max_pages * a.page_size);
     const bool has_new = pos >= 0 && pos < cap;
     const int ctx = max(1, min(pos + 1, cap));
@@ -994,7 +994,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
     const int rmax = G / a.nkv + 2;  // records per head: a head's units span at most this many CTAs
 
     // token of this step (embedding lookup, cpu.rs:485-498)
-    int tok = (a.seq.prompt_len && pos < a.seq.prompt_len[0]) ? a.seq.prompt[pos] : a.seq.tok[0];
+    int tok = a.tok_in >= 0 ? a.tok_in
+                            : ((a.seq.prompt_len && pos < a.seq.prompt_len[0]) ? a.seq.prompt[pos] : a.seq.tok[0]);
     tok = min(max(tok, 0), a.V - 1);
 
     {
@@ -1187,7 +1188,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const DsArgs
             if (ok) {
                 const int next = bi < 0 ? 0 : bi;
                 const SeqState &s = a.seq;
-                const int plen = s.prompt_len ? s.prompt_len[0] : 0;
+                const int plen = (a.pos_in < 0 && s.prompt_len) ? s.prompt_len[0] : 0;
                 s.last[0] = next;
                 if (pos >= plen - 1) {  // generate.rs:72-75: sample after the last prompt token
                     const int gcount = s.ngen[0];

@@ -117,6 +117,7 @@ struct sb_llama {
     // persistent batch-1 step
     bool ds_ok = false;
     unsigned ds_epoch = 0;  // tensor parallelism: epochs of the step kernel's exchanges so far
+    unsigned *err_host = nullptr;  // pinned [5]: the kernels' error words, read with a step's own sync
     int ds_chunk = 0, ds_nst = 0;
     DsLayer *ds_layers = nullptr;  // device copy of the per-layer weight table
     float *ds_x = nullptr;
@@ -450,7 +451,9 @@ int check_ready(sb_llama *m) {
 int set_state(sb_llama *m, int M, const int32_t *tok, const int32_t *pos, const int32_t *plen);
 
 // One batch-1 step as the persistent kernel (m->ds_ok).
-int ds_step(sb_llama *m, bool sampled = false) {
+// tok_in / pos_in >= 0: the step's token and position as launch arguments
+// (no sequence state uploaded first).
+int ds_step(sb_llama *m, bool sampled = false, int tok_in = -1, int pos_in = -1) {
     std::vector<DsLayer> tab(m->L);
     for (int l = 0; l < m->L; l++) {
         const sb_llama::Layer &ly = m->layers[l];
@@ -524,6 +527,8 @@ int ds_step(sb_llama *m, bool sampled = false) {
     a.mtab_bytes = ds_mtab_bytes(m->nh, m->nkv);
     a.stamps = m->ds_stamps;
     a.greedy = sampled ? 0 : 1;
+    a.tok_in = tok_in;
+    a.pos_in = pos_in;
     if (m->tp > 1) {
         a.tp = m->tp;
         a.tp_rank = m->tp_rank;
@@ -538,6 +543,21 @@ int ds_step(sb_llama *m, bool sampled = false) {
 }
 
 // Errors a bounded device wait may have left behind.
+// Queue copies of every kernel error word into the pinned err_host, so the
+// caller's one synchronisation also brings them back (no extra round trips).
+// step_only: the call ran only the persistent step kernel, whose abort flag
+// is then the only word it can have set.
+int queue_error_peeks(sb_llama *m, bool step_only = false) {
+    unsigned *h = m->err_host;
+    h[0] = h[1] = h[2] = h[3] = h[4] = 0;
+    if (m->ds_ok) SB_TRY(ds_error_peek(m->ds_sync, h + 0, m->st));
+    if (step_only) return SB_OK;
+    SB_TRY(qgemm_error_peek(h + 1, m->st));
+    SB_TRY(attn_tc_error_peek(h + 2, m->st));
+    if (m->tp > 1) SB_TRY(tp_error_peek(m->comm, h + 3, m->st));
+    return qgemv_error_peek(h + 4, m->st);
+}
+
 int check_device_errors(sb_llama *m) {
     if (m->ds_ok) SB_TRY(ds_check_error(m->ds_sync, m->st));
     SB_TRY(qgemm_check_error());
@@ -707,6 +727,8 @@ int llama_create(const sb_llama_config *cfg, int tp_rank, int tp_size, const uin
     };
     if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess)
         return fail(set_error(SB_ERR_CUDA, "cudaStreamCreate failed"));
+    if (cudaMallocHost(&m->err_host, 8 * sizeof(unsigned)) != cudaSuccess)
+        return fail(set_error(SB_ERR_OOM, "cudaMallocHost failed"));
 
     int rc = SB_OK;
     if (tp_size > 1 && (rc = tp_init(m->comm, tp_id, tp_rank, tp_size, 120.0)) != SB_OK) return fail(rc);
@@ -914,6 +936,7 @@ sb_status sb_llama_destroy(sb_llama *m) {
     tp_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     if (m->raw) cudaFree(m->raw);
+    if (m->err_host) cudaFreeHost(m->err_host);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
     return SB_OK;
@@ -1334,11 +1357,12 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
     }
     SB_TRY(check_ready(m));
     std::vector<int32_t> zero(batch, 0);
-    SB_TRY(set_state(m, batch, tokens, pos, zero.data()));
     if (batch == 1 && m->ds_ok) {
-        SB_TRY(ds_step(m));
+        // token and position go to the kernel as launch arguments: no copies
+        SB_TRY(ds_step(m, false, tokens[0], pos[0]));
         if (m->trace) m->trace_batch = 1;
     } else if (m->trace) {
+        SB_TRY(set_state(m, batch, tokens, pos, zero.data()));
         SB_TRY(enqueue_step(m, batch, m->st, false, true));
         m->trace_batch = batch;
     } else {
@@ -1361,13 +1385,16 @@ sb_status sb_llama_forward(sb_llama *m, int batch, const int32_t *tokens, const 
                                     m->st));
     }
     if (argmax) SB_CUDA_TRY(cudaMemcpyAsync(argmax, m->d_last, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
+    SB_TRY(queue_error_peeks(m, batch == 1 && m->ds_ok));
     SB_CUDA_TRY(cudaStreamSynchronize(m->st));
     if (!lg_all.empty())
         for (int t = 0; t < m->tp; t++)
             for (int b = 0; b < batch; b++)
                 std::memcpy(logits + (size_t)b * m->V + (size_t)t * m->Vl,
                             lg_all.data() + ((size_t)t * batch + b) * m->Vl, sizeof(float) * m->Vl);
-    return check_device_errors(m);
+    const unsigned *h = m->err_host;
+    if (h[0] | h[1] | h[2] | h[3] | h[4]) return check_device_errors(m);  // reports and clears
+    return SB_OK;
 }
 
 namespace {

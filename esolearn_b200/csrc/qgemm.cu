@@ -1043,6 +1043,11 @@ int qgemm_grouped_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, double 
     return SB_OK;
 }
 
+int qgemm_error_peek(unsigned *host, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemcpyFromSymbolAsync(host, qgm_error_flag, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, st));
+    return SB_OK;
+}
+
 int qgemm_check_error() {
     unsigned f = 0;
     SB_CUDA_TRY(cudaMemcpyFromSymbol(&f, qgm_error_flag, sizeof f));

@@ -58,6 +58,8 @@ int qgemm_launch_chained(int epi, const QGemvArgs &a, const QGemmWs &ws, cudaStr
 bool qgemm_grouped_supported(const QWeightDesc &w, int M);
 size_t qgemm_grouped_part_doubles(const QWeightDesc &w);
 int qgemm_grouped_launch(int epi, const QGemvArgs &a, const QGemmWs &ws, double *part, cudaStream_t st, bool pdl);
+// Queues a copy of the GEMM kernels' error word into *host (pinned) on st.
+int qgemm_error_peek(unsigned *host, cudaStream_t st);
 // Reports (and clears) a timed-out pipeline wait of the GEMM kernel.
 int qgemm_check_error();
 

@@ -599,6 +599,11 @@ int qgemv_pick_tn(int N, int K, int min_tn) {
     return 256;
 }
 
+int qgemv_error_peek(unsigned *host, cudaStream_t st) {
+    SB_CUDA_TRY(cudaMemcpyFromSymbolAsync(host, qg_error_flag, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, st));
+    return SB_OK;
+}
+
 int qgemv_check_error() {
     unsigned f = 0;
     SB_CUDA_TRY(cudaMemcpyFromSymbol(&f, qg_error_flag, sizeof f));

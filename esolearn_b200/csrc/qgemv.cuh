@@ -73,6 +73,8 @@ size_t qgemv_smem_bytes(int M, int KS, int TN, bool norm);
 // Launch one GEMV.  pdl enables programmatic dependent launch.
 // qgemv_check_error() reports (and clears) a timed-out pipeline wait.
 int qgemv_check_error();
+// Queues a copy of the GEMV's error word into *host (pinned) on st.
+int qgemv_error_peek(unsigned *host, cudaStream_t st);
 int qgemv_launch(int epi, const QGemvArgs &a, cudaStream_t st, bool pdl);
 // Split-K GEMV (qgemv_sk.cu) for 1-4 rows of a per-tensor weight with
 // 128-column tiles and fewer tiles than SMs (STORE / BIAS epilogues): CTA

@@ -276,6 +276,15 @@ int tp_probe_timeout(int *timed_out, double *seconds) {
     return rc;
 }
 
+int tp_error_peek(const TpComm &c, unsigned *host, cudaStream_t st) {
+    if (!c.p2p) {
+        *host = 0;
+        return SB_OK;
+    }
+    SB_CUDA_TRY(cudaMemcpyAsync(host, c.peers.error, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    return SB_OK;
+}
+
 int tp_check_error(const TpComm &c) {
     if (!c.p2p) return SB_OK;
     unsigned f = 0;

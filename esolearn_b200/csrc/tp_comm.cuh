@@ -72,6 +72,8 @@ int tp_setup_p2p(TpComm &c, int cap, cudaStream_t st);
 // afterwards c.cells[r] (= mapped[r]) is rank r's array.  Needs peer access
 // (tp_setup_p2p found it); SB_ERR_UNSUPPORTED otherwise.  Once per comm.
 int tp_share_cells(TpComm &c, size_t cells, cudaStream_t st, uint2 **mapped);
+// Queues a copy of the peer exchanges' error word into *host (pinned) on st.
+int tp_error_peek(const TpComm &c, unsigned *host, cudaStream_t st);
 // Reports (and clears) a timed-out flag wait of the peer all-reduce.
 int tp_check_error(const TpComm &c);
 // Runs the peer all-reduce against a peer that never writes (one device);
