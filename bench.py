@@ -41,9 +41,12 @@ steps of the full model (stopped early, and the step count reported, if the
 timed loop passes 150 s).  The reference is Rust and cannot be built here;
 the oracle restates it operation by operation.
 Multi-GPU (torchrun, N ranks): tensor parallelism over the N GPUs -- every
-rank holds 1/N of every projection and of the KV heads, the partial o and
-down products are summed with an NCCL all-reduce over NVLink, and the greedy
-token is the argmax over all ranks' vocabulary slices.  The workload (model,
+rank holds 1/N of every projection and of the KV heads.  At batch 1 each
+rank runs the persistent step kernel, which sums the partial o and down
+products and picks the greedy token (the argmax over all ranks' vocabulary
+slices) through stores into the other GPUs' memory over NVLink inside the
+kernel; larger batches run the per-operation graph with a peer all-reduce
+after o and down.  The workload (model,
 batch, prompt) is the same at every N ("scaling": "strong"); value is the
 job's tokens/s from the slowest rank's CUDA-event time.  --replicas runs N
 independent single-GPU replicas instead (weak scaling).
