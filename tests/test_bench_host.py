@@ -3,8 +3,10 @@
 bench.py's workloads must be BASELINE's configurations (shape, batch,
 prompt); the clock record must report the throttle reasons that reject a run;
 the quantized-linear sweep must cover the configs[1] grid with its stated
-byte count; and the CPU reference leg must time whole decode steps of the
-shape it is given.  None of this needs a GPU.
+byte count; the CPU reference leg must time whole decode steps of the
+shape it is given; and the step-timeline summary (the per-phase barrier,
+input-stage and work times of the persistent step) must read its stamps
+correctly.  None of this needs a GPU.
 """
 import time
 
@@ -83,3 +85,33 @@ def test_cpu_reference_leg_times_whole_steps():
     tok_s, cores, n, sample = bench.cpu_reference_decode(shape, 16, 1, 3)
     assert n == 3 and tok_s > 0 and cores >= 1
     assert "all 2 layers + lm_head" in sample and "contexts 16-19" in sample
+
+
+def test_step_timeline_summary():
+    # A synthetic 1-layer timeline of two CTAs, CTA 1 100 ns behind CTA 0:
+    # every phase starts 2 us after the CTA's previous phase ended, spends
+    # 3 us on its input stage and 5 us on its work, with the first and last
+    # weight stages ready 0.5 and 1.5 us after the input stage.
+    import numpy as np
+
+    from esolearn_b200.profile_decode import PHASES, timeline_summary
+
+    P, C = 7, 2  # six phases per layer + lm_head
+    t = np.zeros((P, C, 5), dtype=np.int64)
+    for p in range(P):
+        for c in range(C):
+            t[p, c, 0] = 100 * c if p == 0 else t[p - 1, c, 4] + 2000
+            t[p, c, 1] = t[p, c, 0] + 3000
+            t[p, c, 2] = t[p, c, 1] + 500
+            t[p, c, 3] = t[p, c, 1] + 1500
+            t[p, c, 4] = t[p, c, 1] + 5000
+    r = timeline_summary(t, 1)
+    assert PHASES[0] not in r  # the first phase has no barrier before it
+    for name in list(PHASES[1:]) + ["lm_head"]:
+        got = r[name]
+        want = {"barrier": 2.0, "input": 3.0, "work": 5.0, "span": 10.0, "barrier_propagation": 1.9,
+                "arrival_lag": 0.05, "start_spread": 0.1, "first_ready": 0.5, "last_ready": 1.5, "after_last": 3.5}
+        for k, v in want.items():
+            assert abs(got[k] - v) < 1e-9, (name, k, got[k])
+    assert abs(r["layers_total"] - 58.1) < 1e-9 and abs(r["per_layer"] - 58.1) < 1e-9
+    assert abs(r["step_to_lm_end"] - 68.1) < 1e-9
