@@ -18,14 +18,17 @@ from esolearn_b200 import _native as N
 from gpu_util import engine_from_oracle, orc_config, rel_err, small_config
 
 
-def _cfg():
-    # GQA 8 query / 4 kv heads, hd 32, ffn 96, vocab 64
+def _cfg(T=1):
+    # GQA 8 query / 4 kv heads, hd 32, ffn 96, vocab 64; for 8 ranks 16 query /
+    # 8 kv heads of 16
+    if T == 8:
+        return LlamaConfig(64, 256, 96, 2, 16, 8, 128, 1e-5, 10000.0, False, None)
     return LlamaConfig(64, 256, 96, 2, 8, 4, 128, 1e-5, 10000.0, False, None)
 
 
-@pytest.mark.parametrize("T", [1, 2, 4])
+@pytest.mark.parametrize("T", [1, 2, 4, 8])
 def test_shards_partition_every_weight(T):
-    c = _cfg()
+    c = _cfg(T)
     hd = c.head_dim()
     Qf, KVf = c.n_heads * hd, c.n_kv_heads * hd
     rng = np.random.default_rng(T)
