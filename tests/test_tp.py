@@ -112,8 +112,9 @@ def _gloo_worker(rank, size, port, out):
         dist.destroy_process_group()
 
 
-def test_row_and_column_splits_over_gloo_ranks():
-    # World size 2 on the CPU: the o projection's row split summed by an
+@pytest.mark.parametrize("size", [2, 4])
+def test_row_and_column_splits_over_gloo_ranks(size):
+    # World size 2 or 4 on the CPU: the o projection's row split summed by an
     # all-reduce equals the unsharded product within f32 rounding, and the
     # gate projection's column split gathered equals it bit for bit.
     import torch.multiprocessing as mp
@@ -121,7 +122,7 @@ def test_row_and_column_splits_over_gloo_ranks():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gloo_worker, args=(r, size, port, q)) for r in range(size)]
     for p in procs:
         p.start()
     for p in procs:
